@@ -1,0 +1,351 @@
+"""LEMA prefill match on B200 -- the benchmark line.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl b200|reference]
+
+Workload ("kernel-level prefill on 1 B200"): B=8 x H=64 = 512 streams of
+T=16384 positions, 32-bit codes (per-stream pool of 8192 codes, Zipf 1.1, 10% fresh), value
+rows of 24 bf16 (48 bytes). One step = the exact op over the whole batch: for every position,
+the latest earlier position whose key code equals its query code, and its value row gathered
+(zeros on a miss) -- code/lema/attention.py:100-158 -- through lema_prefill_match (K2).
+
+Metric: Mpos/s (positions per second, whole job). Inputs are resident in HBM when the timed
+region starts; codes + values + outputs (~0.9 GB) exceed the 126 MB L2, so no flush is
+needed between steps. `e2e` is the same metric through the C ABI with host buffers: every
+step copies its codes and values host->device from pinned memory and its outputs back.
+
+Multi-GPU (torchrun, one process per GPU): the streams are independent, so every rank runs
+its own full batch (different seeds) with no collective on the data path ("scaling": weak);
+the time is the max over ranks of CUDA-event time.
+
+--impl reference: the reference's own CPU implementation of the path -- its C++ store
+(code/lema/csrc/store.cpp, built from source into oracle/_ref) exchanging every stream's
+positions in one call on all host cores, as code/lema/cache.py:184-201 does -- timed on a
+bounded sample of the same workload. Rank 0 alone runs it.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import tempfile
+import time
+from pathlib import Path
+
+import numpy as np
+
+ROOT = Path(__file__).resolve().parent
+sys.path.insert(0, str(ROOT))
+
+B, H, T, D_V = 8, 64, 16384, 24
+N_STREAMS = B * H
+VBYTES = D_V * 2
+METRIC = "LEMA prefill Mpos/s/GPU & batched decode tok/s; % of HBM roofline"
+UNIT = "Mpos/s"
+WORKLOAD = "cfg2: kernel-level prefill, B=8 H=64 T=16384, 32-bit codes, d_v 24 bf16"
+
+
+def peaks():
+    p = ROOT / "MEASURED_PEAKS.json"
+    if p.exists():
+        d = json.loads(p.read_text())
+        return float(d["hbm_gbs"]), "measured"
+    return 6650.0, "fallback"
+
+
+class ClockSampler:
+    """nvidia-smi clocks and throttle reasons sampled every 200 ms during the timed region."""
+
+    QUERY = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+             "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+             "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, index: int):
+        self.index = index
+        self.file = tempfile.NamedTemporaryFile("w+", suffix=".csv", delete=False)
+        self.proc = None
+
+    def __enter__(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--id={self.index}", f"--query-gpu={self.QUERY}",
+                 "--format=csv,noheader,nounits", "-lms", "200"],
+                stdout=self.file, stderr=subprocess.DEVNULL)
+        except OSError:
+            self.proc = None
+        time.sleep(0.3)
+        return self
+
+    def __exit__(self, *exc):
+        if self.proc is not None:
+            self.proc.terminate()
+            try:
+                self.proc.wait(timeout=5)
+            except subprocess.TimeoutExpired:
+                self.proc.kill()
+
+    def summary(self) -> dict:
+        self.file.flush()
+        rows = [r.split(",") for r in Path(self.file.name).read_text().splitlines() if r.strip()]
+        os.unlink(self.file.name)
+        sm, mx, reasons = [], [], set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for r in rows:
+            r = [x.strip() for x in r]
+            try:
+                sm.append(float(r[1]))
+                mx.append(float(r[2]))
+            except (ValueError, IndexError):
+                continue
+            for name, val in zip(names, r[5:9]):
+                if val.lower() == "active":
+                    reasons.add(name)
+        if not sm:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["unsampled"]}
+        return {"sm_mhz": statistics.median(sm), "sm_max_mhz": max(mx), "reasons": sorted(reasons),
+                "samples": len(sm)}
+
+
+def dist_setup(n_gpus: int):
+    rank, world = int(os.environ.get("RANK", "0")), int(os.environ.get("WORLD_SIZE", "1"))
+    if world != n_gpus:
+        raise SystemExit(f"--gpus {n_gpus} but WORLD_SIZE={world}: launch N>1 with torchrun")
+    if world > 1:
+        import datetime
+
+        import torch.distributed as dist
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120))
+    return rank, world
+
+
+def make_inputs(rank: int, device):
+    import torch
+
+    from latest_exact_match_attention_b200 import synth
+    qc, kc = synth.code_streams(N_STREAMS, T, synth.CONFIG2, seed=rank, config_id=2)
+    q = torch.from_numpy(qc.view(np.int32)).to(device)
+    k = torch.from_numpy(kc.view(np.int32)).to(device)
+    v = synth.values_torch(N_STREAMS, T, D_V, torch.bfloat16, device, seed=rank, config_id=2)
+    return qc, kc, q, k, v
+
+
+def cpu_reference_sample(qc: np.ndarray, kc: np.ndarray, n_streams: int, reps: int = 1):
+    """The reference's C++ store exchange (oracle/_ref) over `n_streams` full streams in one
+    call on all host cores: returns (Mpos/s, cores, kind, sample description)."""
+    import torch
+
+    import oracle
+    cores = len(os.sched_getaffinity(0))
+    torch.set_num_threads(cores)
+    ref = oracle.ref_store()
+    qs, ks = qc[:n_streams].astype(np.int64), kc[:n_streams].astype(np.int64)
+    n = n_streams * T
+    vals = torch.from_numpy(np.random.default_rng(0).integers(0, 1 << 16, size=(n, D_V), dtype=np.uint16))
+    out = torch.empty_like(vals)
+    q64, k64 = torch.from_numpy(qs.reshape(-1)), torch.from_numpy(ks.reshape(-1))
+    if ref is not None:
+        cap = int(n * 1.6)
+        times = []
+        for _ in range(reps + 1):          # one warm-up: OpenMP team, page touch
+            table = torch.zeros((cap, 16 + VBYTES), dtype=torch.uint8)
+            t0 = time.perf_counter()
+            ref.exchange(table, q64, k64, vals, out, T, 0, cap, VBYTES)
+            times.append(time.perf_counter() - t0)
+        dt = min(times[1:])
+        return n / dt / 1e6, cores, "reference", (
+            f"code/lema/csrc/store.cpp exchange, {n_streams} streams x {T} positions in one call "
+            f"(P={n_streams}, T={T}), {cores} OpenMP threads, table load {n / cap:.2f}")
+    # no reference build: the oracle port (single-threaded dictionary sweep + gather)
+    t0 = time.perf_counter()
+    src = oracle.latest_prev_match(qs, ks)
+    oracle.gather(src, vals.numpy().reshape(n_streams, T, D_V))
+    dt = time.perf_counter() - t0
+    return n / dt / 1e6, 1, "port", f"oracle latest_prev_match + gather, {n_streams} streams x {T}"
+
+
+def run_reference(args):
+    rank = int(os.environ.get("RANK", "0"))
+    if rank != 0:
+        return
+    from latest_exact_match_attention_b200 import synth
+    sample = 32                                   # streams per step: ~0.5M positions
+    qc, kc = synth.code_streams(sample, T, synth.CONFIG2, seed=0, config_id=2)
+    vals = []
+    for _ in range(args.warmup):
+        cpu_reference_sample(qc, kc, sample, reps=0)
+    t0 = time.perf_counter()
+    for _ in range(args.steps):
+        v, cores, kind, desc = cpu_reference_sample(qc, kc, sample, reps=0)
+        vals.append(v)
+    wall = time.perf_counter() - t0
+    value = statistics.median(vals)
+    print(json.dumps({
+        "impl": "reference", "metric": METRIC, "value": round(value, 3), "unit": UNIT,
+        "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
+        "ms_per_step": round(1e3 * wall / max(1, args.steps), 3), "higher_is_better": True,
+        "scaling": "weak", "vs_baseline": None, "dtype": "u32", "data": "synthetic",
+        "config": {"workload": WORKLOAD, "sample_streams": sample, "global_batch": N_STREAMS,
+                   "seq_len": T, "parallelism": "cpu"},
+        "cpu_baseline": {"value": round(value, 3), "unit": UNIT, "cores": cores, "kind": kind,
+                         "sample": desc},
+        "e2e": {"value": round(value, 3), "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }), flush=True)
+
+
+def run_b200(args):
+    import torch
+
+    from latest_exact_match_attention_b200 import _lib
+    from latest_exact_match_attention_b200._lib import call, ptr
+
+    rank, world = dist_setup(args.gpus)
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    qc, kc, q, k, v = make_inputs(rank, dev)
+    n_pos = N_STREAMS * T
+    src = torch.empty((N_STREAMS, T), dtype=torch.int32, device=dev)
+    out = torch.empty_like(v)
+    status = torch.zeros(1, dtype=torch.int32, device=dev)
+    ws_bytes = int(_lib.lib().lema_prefill_workspace_bytes(N_STREAMS, T, 4))
+    ws = torch.empty(max(ws_bytes, 1), dtype=torch.uint8, device=dev)
+    stream = torch.cuda.current_stream(dev)
+
+    def step():
+        call("lema_prefill_match", ptr(q), ptr(k), 4, N_STREAMS, T, ptr(src), ptr(v), VBYTES,
+             ptr(out), ptr(ws), ws_bytes, ptr(status), stream.cuda_stream)
+
+    def barrier():
+        if world > 1:
+            import torch.distributed as dist
+            dist.barrier()
+
+    for _ in range(max(3, args.warmup)):
+        step()
+    torch.cuda.synchronize()
+    assert int(status.item()) == 0, "device status raised during warm-up"
+
+    # algorithmic bytes per step: codes in, index + row out, each distinct source row read once
+    s = src.to(torch.int64)
+    hit = s >= 0
+    ids = (torch.arange(N_STREAMS, device=dev, dtype=torch.int64)[:, None] * T + s)[hit]
+    U = int(torch.unique(ids).numel())
+    alg_bytes = n_pos * (4 + 4 + VBYTES + 4) + U * VBYTES
+    hit_rate = float(hit.float().mean())
+    del s, hit, ids
+
+    ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
+          for _ in range(args.steps)]
+    barrier()
+    torch.cuda.synchronize()
+    with ClockSampler(local) as clk:
+        t0 = torch.cuda.Event(enable_timing=True)
+        t1 = torch.cuda.Event(enable_timing=True)
+        t0.record(stream)
+        for i in range(args.steps):
+            ev[i][0].record(stream)
+            step()
+            ev[i][1].record(stream)
+        t1.record(stream)
+        torch.cuda.synchronize()
+    barrier()
+    clocks = clk.summary()
+    total_ms = t0.elapsed_time(t1)
+    per_launch_ms = statistics.mean(a.elapsed_time(b) for a, b in ev)
+    if world > 1:
+        import torch.distributed as dist
+        tt = torch.tensor([total_ms], device=dev)
+        dist.all_reduce(tt, op=dist.ReduceOp.MAX)
+        total_ms = float(tt.item())
+    assert int(status.item()) == 0, "device status raised during the timed region"
+    ms_per_step = total_ms / args.steps
+    value = world * n_pos * args.steps / (total_ms / 1e3) / 1e6
+
+    # end to end through the C ABI with host buffers (pinned), copies inside the timed region
+    e2e_steps = max(1, min(args.steps, 5))
+    hq = torch.from_numpy(qc.view(np.int32)).pin_memory()
+    hk = torch.from_numpy(kc.view(np.int32)).pin_memory()
+    hv = v.cpu().pin_memory()
+    ho = torch.empty_like(hv).pin_memory()
+    hs = torch.empty((N_STREAMS, T), dtype=torch.int32).pin_memory()
+    h2d = hq.numel() * 4 + hk.numel() * 4 + hv.numel() * 2
+    d2h = ho.numel() * 2 + hs.numel() * 4
+    barrier()
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    for _ in range(e2e_steps):
+        q.copy_(hq, non_blocking=True)
+        k.copy_(hk, non_blocking=True)
+        v.copy_(hv, non_blocking=True)
+        step()
+        ho.copy_(out, non_blocking=True)
+        hs.copy_(src, non_blocking=True)
+    e1.record(stream)
+    torch.cuda.synchronize()
+    e2e_ms = e0.elapsed_time(e1)
+    if world > 1:
+        import torch.distributed as dist
+        tt = torch.tensor([e2e_ms], device=dev)
+        dist.all_reduce(tt, op=dist.ReduceOp.MAX)
+        e2e_ms = float(tt.item())
+    e2e_value = world * n_pos * e2e_steps / (e2e_ms / 1e3) / 1e6
+
+    cpu = None
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        cv, cores, kind, desc = cpu_reference_sample(qc, kc, 32, reps=1)
+        cpu = {"value": round(cv, 3), "unit": UNIT, "cores": cores, "kind": kind, "sample": desc}
+
+    peak, peak_src = peaks()
+    achieved = alg_bytes / (per_launch_ms / 1e3) / 1e9
+    traffic = None
+    tf = ROOT / "profiles" / "prefill_match_cfg2_traffic.json"
+    if tf.exists():
+        traffic = json.loads(tf.read_text()).get("dram_bytes_per_launch")
+    if world > 1:
+        import torch.distributed as dist
+        dist.destroy_process_group()
+    if rank != 0:
+        return
+    line = {
+        "metric": METRIC, "value": round(value, 2), "unit": UNIT, "n_gpus": world,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms_per_step, 4),
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "u32",
+        "data": "synthetic (seeded Zipf-pool codes, N(0,1) bf16 values)",
+        "config": {"workload": WORKLOAD, "streams_per_gpu": N_STREAMS, "positions_per_gpu": n_pos,
+                   "seq_len": T, "value_bytes": VBYTES, "parallelism": f"streams x{world}, no collective",
+                   "l2": "inputs+outputs 0.9 GB > 126 MB L2 (no flush)", "hit_rate": round(hit_rate, 4),
+                   "distinct_sources": U},
+        "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
+                     "frac": round(achieved / peak, 4), "traffic": traffic,
+                     "peak_source": peak_src, "alg_bytes_per_launch": alg_bytes,
+                     "launch_ms": round(per_launch_ms, 4)},
+        "e2e": {"value": round(e2e_value, 2), "unit": UNIT, "h2d_bytes_per_step": h2d,
+                "d2h_bytes_per_step": d2h, "steps": e2e_steps},
+        "cpu_baseline": cpu,
+        "gpu_launches": args.steps * (2 if ws_bytes else 1),
+        "clocks": clocks,
+    }
+    print(json.dumps(line), flush=True)
+
+
+def main():
+    ap = argparse.ArgumentParser(description=__doc__.split("\n")[0])
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", choices=["b200", "reference"], default="b200")
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    args = ap.parse_args()
+    if args.warmup < 3 and args.impl == "b200":
+        args.warmup = 3
+    if args.impl == "reference":
+        run_reference(args)
+    else:
+        run_b200(args)
+
+
+if __name__ == "__main__":
+    main()

@@ -1,0 +1,164 @@
+/*
+ * lema_b200.h -- C ABI of the B200 (sm_100a) LEMA inference hot path.
+ *
+ * LEMA ("latest exact match attention"): a head turns its query and key
+ * pre-activations into sign codes, code(z) = sum_d [z_d >= 0] << d, and query i
+ * reads the value row of the LARGEST j < i (strictly causal) whose key code
+ * equals its query code, or zeros when there is none.
+ *
+ * Every entry point:
+ *   - takes plain device pointers and sizes (no framework types), and a CUDA
+ *     stream as `void*` (NULL = the legacy default stream);
+ *   - is asynchronous and stream-ordered: it validates its arguments on the host,
+ *     launches, and returns; it never synchronises and never allocates device
+ *     memory, so it can be captured into a CUDA graph after the first call on a
+ *     device (which sets kernel attributes);
+ *   - returns LEMA_OK or an error code; lema_last_error() gives the message of the
+ *     last failing call on this host thread;
+ *   - reports conditions found ON THE DEVICE (a full store, an exhausted probe)
+ *     by OR-ing LEMA_STATUS_* bits into a caller-owned, zero-initialised uint32
+ *     status word in device memory. Kernels never trap.
+ *
+ * Codes are unsigned integers of `code_bytes` = 4 (d_qk <= 32) or 8 (d_qk <= 64)
+ * bytes; only equality is ever used, so the int64 codes of the reference (uint64
+ * bit patterns) are passed as code_bytes = 8 unchanged.
+ *
+ * Value rows are opaque byte rows of `vbytes` bytes: the library copies them and
+ * never interprets them, so fp32, fp16 and bf16 rows are all the same call.
+ */
+#ifndef LEMA_B200_H
+#define LEMA_B200_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* ------------------------------------------------------------------ status */
+enum {
+  LEMA_OK = 0,
+  LEMA_ERR_INVALID_ARGUMENT = 1, /* shapes, sizes, alignment or null pointers */
+  LEMA_ERR_CUDA = 2,             /* a CUDA runtime call failed                 */
+  LEMA_ERR_WORKSPACE = 3,        /* workspace smaller than *_workspace_bytes() */
+  LEMA_ERR_UNSUPPORTED = 4       /* no kernel for this device or this case     */
+};
+
+/* Bits OR-ed into the device status word by kernels. */
+#define LEMA_STATUS_TABLE_FULL 0x1u  /* store: an insert probed every slot       */
+#define LEMA_STATUS_PROBE_LIMIT 0x2u /* internal: a bounded probe or wait ran out */
+
+/* Message of the last failing call on the calling host thread ("" if none). */
+const char* lema_last_error(void);
+
+/* Library version, major * 10000 + minor * 100 + patch. */
+int lema_version(void);
+
+/* ------------------------------------------------------------ (a) codes */
+/* Element type tags of pre-activations. */
+enum { LEMA_F32 = 0, LEMA_BF16 = 1, LEMA_F16 = 2 };
+
+/*
+ * pack_codes: one code per row of a strided [d0, d1, d2, d_qk] pre-activation
+ * tensor (the innermost dimension contiguous), written densely as codes[d0][d1][d2].
+ * Bit d of a code is (z[..., d] >= 0); NaN packs to 0 and -0.0 to 1, exactly as a
+ * float comparison `z >= 0` does.
+ *
+ * Replaces: code/lema/attention.py:82-97 (`pack_codes`), applied to the
+ * [B, H, T, d_qk] views that code/lema/model.py:168-175 (`Attention.project`)
+ * returns and code/lema/model.py:224-227 (`Block.gpu_pre`) packs.
+ *   z           device pointer, element type `dtype`
+ *   s0, s1, s2  strides of the three outer dimensions, in elements
+ *   d_qk        1..32 for code_bytes = 4, 1..64 for code_bytes = 8
+ */
+int lema_pack_codes(const void* z, int dtype, int64_t d0, int64_t d1, int64_t d2,
+                    int64_t s0, int64_t s1, int64_t s2, int d_qk, void* codes,
+                    int code_bytes, void* stream);
+
+/*
+ * Code projection (K1): for rows x[M][K] (bf16, row-major) and the stacked query
+ * and key projection weights w_qk[(hq + hk) * d_qk][K] (bf16, row-major, nn.Linear
+ * layout), computes z = x * w_qk^T with fp32 accumulation on the tcgen05 tensor
+ * cores and packs the signs of each head's d_qk = 32 columns in the epilogue, so
+ * z never reaches memory. Row m = b * T + t; the codes are written head-major,
+ * as the matcher consumes them:
+ *   qcodes[(b * hq + h) * T + t], kcodes[(b * hk + h) * T + t]   (uint32)
+ * Requires d_qk = 32, K % 64 == 0, M % T == 0, 16-byte aligned x and w_qk.
+ *
+ * Replaces: the q_proj/k_proj GEMMs of code/lema/model.py:160-175 plus
+ * code/lema/attention.py:82-97, i.e. code/lema/model.py:224-227 minus the norm
+ * and the value projection.
+ */
+int lema_proj_codes(const void* x, const void* w_qk, int64_t M, int64_t K,
+                    int64_t T, int hq, int hk, int d_qk, uint32_t* qcodes,
+                    uint32_t* kcodes, void* stream);
+
+/* ---------------------------------------------- (b) prefill latest match */
+/*
+ * Bytes of device workspace lema_prefill_match needs for n_streams x T
+ * positions (0 is a valid answer: then `workspace` may be NULL).
+ */
+size_t lema_prefill_workspace_bytes(int64_t n_streams, int64_t T, int code_bytes);
+
+/*
+ * Latest exact match over n_streams independent streams (batch x heads) of T
+ * positions each, stream-major:
+ *   src[n][i] = max { j < i : kcodes[n][j] == qcodes[n][i] }, or -1
+ *   out[n][i] = values[n][src[n][i]]  (vbytes bytes), or zeros when src is -1
+ * src (int32) and out are each optional (NULL skips it); values may be NULL
+ * only when out is. vbytes must be a positive multiple of 2.
+ *
+ * Replaces: code/lema/attention.py:100-132 (`latest_prev_match`, int64 indices
+ * there) and the gather of code/lema/attention.py:150-158 (`lema_hard` without
+ * a store).
+ */
+int lema_prefill_match(const void* qcodes, const void* kcodes, int code_bytes,
+                       int64_t n_streams, int64_t T, int32_t* src,
+                       const void* values, int64_t vbytes, void* out,
+                       void* workspace, size_t workspace_bytes, uint32_t* status,
+                       void* stream);
+
+/* ---------------------------------------------------- (c) the HBM store */
+/*
+ * The store is ONE open-addressing table in device memory shared by every
+ * (layer, stream, head) partition ("group"), keyed by (group, code), holding the
+ * value row of the latest key written under that key. The caller owns the table:
+ * cap slots of lema_store_slot_bytes(vbytes) bytes each, ZERO-FILLED before first
+ * use (a zeroed table is an empty table). It never grows; an insert that finds
+ * no free slot sets LEMA_STATUS_TABLE_FULL.
+ *
+ * Replaces: the host table of code/lema/cache.py:129-201 (`HashStore`), whose
+ * slots are [code | state | value] at code/lema/csrc/store.cpp:3-16.
+ */
+int64_t lema_store_slot_bytes(int64_t vbytes);
+
+/* Bytes of device workspace lema_store_exchange needs for n = P * T items. */
+size_t lema_store_workspace_bytes(int64_t n, int64_t T, int code_bytes);
+
+/*
+ * One exchange of P = n / T partitions x T positions against the store. Item i
+ * is position i % T of partition i / T, group g0 + i / T. Each partition, in
+ * position order, looks qcodes[i] up into out[i] (zeros on a miss) and then
+ * inserts kcodes[i] -> values[i] (latest write wins), so a query sees every
+ * earlier key of its partition -- this call's and all earlier calls' -- and not
+ * its own. A prefill chunk (T > 1) and a decode step (T = 1) are the same call.
+ * counts[p] (int64, device, P entries) is increased by the number of slots
+ * partition p newly claimed.
+ *
+ * Replaces: code/lema/csrc/store.cpp:127-162 (`exchange`, which returns the
+ * per-partition `added` the caller adds into code/lema/cache.py:200's counts).
+ *   table      device, cap * lema_store_slot_bytes(vbytes) bytes
+ *   vbytes     positive multiple of 8 (as code/lema/cache.py:161-165 requires)
+ */
+int lema_store_exchange(void* table, int64_t cap, int64_t vbytes,
+                        const void* qcodes, const void* kcodes, int code_bytes,
+                        const void* values, void* out, int64_t n, int64_t T,
+                        int64_t g0, int64_t* counts, uint32_t* status,
+                        void* workspace, size_t workspace_bytes, void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* LEMA_B200_H */

@@ -1,0 +1,98 @@
+"""ctypes binding of liblema_b200.so (the C ABI in include/lema_b200.h).
+
+The library is loaded from this package's directory, where build.py writes it. There is no
+fallback: if it is missing or fails to load, every entry point raises LemaError.
+"""
+from __future__ import annotations
+
+import ctypes
+import threading
+from pathlib import Path
+
+import torch
+
+LIB_PATH = Path(__file__).resolve().with_name("liblema_b200.so")
+
+LEMA_OK = 0
+LEMA_STATUS_TABLE_FULL = 0x1
+LEMA_STATUS_PROBE_LIMIT = 0x2
+F32, BF16, F16 = 0, 1, 2
+DTYPE_TAG = {torch.float32: F32, torch.bfloat16: BF16, torch.float16: F16}
+
+
+class LemaError(RuntimeError):
+    """A failing call into liblema_b200.so."""
+
+
+_lib = None
+_lock = threading.Lock()
+
+_P, _I64, _I, _SZ = ctypes.c_void_p, ctypes.c_int64, ctypes.c_int, ctypes.c_size_t
+_SIGNATURES = {
+    "lema_last_error": ([], ctypes.c_char_p),
+    "lema_version": ([], _I),
+    "lema_pack_codes": ([_P, _I, _I64, _I64, _I64, _I64, _I64, _I64, _I, _P, _I, _P], _I),
+    "lema_proj_codes": ([_P, _P, _I64, _I64, _I64, _I, _I, _I, _P, _P, _P], _I),
+    "lema_prefill_workspace_bytes": ([_I64, _I64, _I], _SZ),
+    "lema_prefill_match": ([_P, _P, _I, _I64, _I64, _P, _P, _I64, _P, _P, _SZ, _P, _P], _I),
+    "lema_store_slot_bytes": ([_I64], _I64),
+    "lema_store_workspace_bytes": ([_I64, _I64, _I], _SZ),
+    "lema_store_exchange": ([_P, _I64, _I64, _P, _P, _I, _P, _P, _I64, _I64, _I64, _P, _P, _P,
+                             _SZ, _P], _I),
+}
+
+
+def lib() -> ctypes.CDLL:
+    """The loaded library (raises LemaError when it is not built)."""
+    global _lib
+    if _lib is None:
+        with _lock:
+            if _lib is None:
+                if not LIB_PATH.exists():
+                    raise LemaError(
+                        f"{LIB_PATH.name} is not built: run `python -m "
+                        f"latest_exact_match_attention_b200.build` (needs nvcc); there is no "
+                        f"CPU fallback")
+                try:
+                    L = ctypes.CDLL(str(LIB_PATH))
+                except OSError as e:
+                    raise LemaError(f"could not load {LIB_PATH}: {e}") from e
+                for name, (args, res) in _SIGNATURES.items():
+                    fn = getattr(L, name)
+                    fn.argtypes = args
+                    fn.restype = res
+                _lib = L
+    return _lib
+
+
+def call(name: str, *args) -> None:
+    """Call an entry point that returns a status code; raise LemaError on failure."""
+    rc = getattr(lib(), name)(*args)
+    if rc != LEMA_OK:
+        msg = lib().lema_last_error().decode(errors="replace")
+        raise LemaError(f"{name} failed (code {rc}): {msg}")
+
+
+def stream_handle(device: torch.device | None = None) -> int:
+    """The raw cudaStream_t of torch's current stream on `device`."""
+    return torch.cuda.current_stream(device).cuda_stream
+
+
+def ptr(t: torch.Tensor | None) -> int | None:
+    return None if t is None else t.data_ptr()
+
+
+def require_cuda(*tensors: torch.Tensor) -> torch.device:
+    """All tensors on one CUDA device; the product path has no CPU implementation."""
+    dev = None
+    for t in tensors:
+        if t is None:
+            continue
+        if not t.is_cuda:
+            raise LemaError("LEMA B200 kernels take CUDA tensors only (there is no CPU path); "
+                            f"got a tensor on {t.device}")
+        if dev is None:
+            dev = t.device
+        elif t.device != dev:
+            raise LemaError(f"tensors on different devices: {dev} and {t.device}")
+    return dev

@@ -1,0 +1,131 @@
+"""The exact LEMA op on the B200: the inference half of code/lema/attention.py.
+
+    pack_codes(z)              code/lema/attention.py:82-97    sign bits -> one code per row
+    latest_prev_match(qc, kc)  code/lema/attention.py:100-132  latest earlier matching key
+    lema_hard(q, k, v, store)  code/lema/attention.py:135-158  the exact op, dense or stored
+
+Same names, argument meanings and results as the reference; the work runs in the sm_100a
+kernels of liblema_b200.so (K2 for the match and gather, the pack kernel for the codes).
+Conventions are the reference's: codes are sum_d [z_d >= 0] << d (sign(0) = +1), matching
+is STRICTLY causal (a query never sees its own key), and no match gives -1 / zeros.
+
+Differences, all deliberate:
+  * CUDA tensors only -- there is no CPU path (a CPU tensor raises);
+  * inference only -- the outputs carry no autograd graph (the reference's gather keeps a
+    value gradient for training, which is out of scope here);
+  * with d_qk <= 32 the op works on 32-bit codes internally (pack_codes(z, narrow=True));
+    `pack_codes(z)` itself still returns int64 like the reference.
+The training-time surrogates (hard_sign, binarize, lema_soft, lema) are not part of this
+package.
+"""
+from __future__ import annotations
+
+import torch
+
+from . import _lib
+from ._lib import DTYPE_TAG, LemaError, call, ptr, require_cuda, stream_handle
+
+__all__ = ["pack_codes", "latest_prev_match", "lema_hard", "prefill_match", "code_bytes_of"]
+
+
+def code_bytes_of(codes: torch.Tensor) -> int:
+    if codes.dtype == torch.int32:
+        return 4
+    if codes.dtype == torch.int64:
+        return 8
+    raise LemaError(f"codes must be int32 (uint32 bit patterns) or int64 (uint64 bit "
+                    f"patterns), got {codes.dtype}")
+
+
+def pack_codes(z: torch.Tensor, narrow: bool = False) -> torch.Tensor:
+    """[..., D] -> one integer code per row, on z's device: bit d is (z[..., d] >= 0).
+
+    Returns int64 like the reference (at D = 64 the top bit makes the value negative;
+    only equality is ever used). `narrow=True` with D <= 32 returns int32 holding the
+    uint32 bit pattern instead, the form the kernels prefer.
+    """
+    require_cuda(z)
+    D = z.shape[-1]
+    if D > 64:
+        raise ValueError(f"d_qk {D} > 64 cannot pack into a uint64")
+    if z.dtype not in DTYPE_TAG:
+        z = z.float()
+    if z.stride(-1) != 1:
+        z = z.contiguous()
+    lead = tuple(z.shape[:-1])
+    if len(lead) > 3:
+        z = z.reshape(-1, D)
+    dims = list(z.shape[:-1])
+    strides = list(z.stride()[:-1])
+    while len(dims) < 3:
+        dims.insert(0, 1)
+        strides.insert(0, 0)
+    narrow = narrow and D <= 32
+    out = torch.empty(lead, dtype=torch.int32 if narrow else torch.int64, device=z.device)
+    if out.numel() == 0:
+        return out
+    call("lema_pack_codes", ptr(z), DTYPE_TAG[z.dtype], dims[0], dims[1], dims[2],
+         strides[0], strides[1], strides[2], D, ptr(out), 4 if narrow else 8,
+         stream_handle(z.device))
+    return out
+
+
+def _workspace(nbytes: int, device) -> torch.Tensor | None:
+    # the caching allocator hands out 512-byte aligned blocks, above the 256 required
+    return torch.empty(nbytes, dtype=torch.uint8, device=device) if nbytes else None
+
+
+def prefill_match(qc: torch.Tensor, kc: torch.Tensor, v: torch.Tensor | None = None, *,
+                  want_src: bool = True, status: torch.Tensor | None = None):
+    """The native K2 call: `qc`, `kc` [N, T] codes (int32 or int64, one dtype), `v` [N, T,
+    ...] value rows (optional). Returns (src, out): src [N, T] int32 (latest j < i with an
+    equal key code, else -1) when want_src, out like v with the gathered rows (zeros on a
+    miss) when v is given. Device status bits are OR-ed into `status` (an int32 [1] device
+    tensor) when given."""
+    dev = require_cuda(qc, kc, v, status)
+    if qc.dim() != 2 or qc.shape != kc.shape:
+        raise ValueError(f"qc and kc must be [N, T] of one shape, got {tuple(qc.shape)} and "
+                         f"{tuple(kc.shape)}")
+    if qc.dtype != kc.dtype:
+        raise ValueError(f"qc and kc must share a dtype, got {qc.dtype} and {kc.dtype}")
+    cb = code_bytes_of(qc)
+    N, T = qc.shape
+    qc, kc = qc.contiguous(), kc.contiguous()
+    src = torch.empty((N, T), dtype=torch.int32, device=dev) if want_src else None
+    out = vbytes = None
+    if v is not None:
+        if v.shape[:2] != (N, T):
+            raise ValueError(f"values must be [N, T, ...] = [{N}, {T}, ...], got {tuple(v.shape)}")
+        v = v.contiguous()
+        out = torch.empty_like(v)
+        vbytes = v[0, 0].numel() * v.element_size() if N * T else 0
+    ws = _workspace(_lib.lib().lema_prefill_workspace_bytes(N, T, cb), dev)
+    call("lema_prefill_match", ptr(qc), ptr(kc), cb, N, T, ptr(src), ptr(v), vbytes or 0,
+         ptr(out), ptr(ws), 0 if ws is None else ws.numel(), ptr(status), stream_handle(dev))
+    return src, out
+
+
+def latest_prev_match(qc: torch.Tensor, kc: torch.Tensor) -> torch.Tensor:
+    """For each i, the largest j < i with kc[j] == qc[i], else -1 (int64 [N, T], as
+    code/lema/attention.py:100-132 returns)."""
+    src, _ = prefill_match(qc, kc)
+    return src.to(torch.int64)
+
+
+def lema_hard(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, store=None) -> torch.Tensor:
+    """Exact latest match: o_i = v_j for the largest j < i with k_j == q_i, else 0.
+
+    q, k: [B, H, T, d_qk] binarized codes OR raw pre-activations (only their signs are
+    read); v: [B, H, T, d_v]. With a `store` (a LayerStore) the rule is one exchange
+    against it, so this window's queries also see every key fed before; without one it is
+    a self-contained forward over the window. Returns [B, H, T, d_v] in v's dtype.
+    """
+    B, H, T, D = q.shape
+    narrow = D <= 32
+    qc, kc = pack_codes(q, narrow=narrow), pack_codes(k, narrow=narrow)
+    if store is not None:
+        return store.exchange(qc, kc, v)
+    d_v = v.shape[-1]
+    _, out = prefill_match(qc.view(B * H, T), kc.view(B * H, T),
+                           v.reshape(B * H, T, d_v), want_src=False)
+    return out.view(B, H, T, d_v)

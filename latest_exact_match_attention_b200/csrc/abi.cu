@@ -1,0 +1,147 @@
+// The C ABI of liblema_b200.so (declared in include/lema_b200.h): argument checks, error
+// reporting, per-device facts, and dispatch to the kernels.
+#include <cuda_runtime.h>
+
+#include <cstdarg>
+#include <cstdio>
+#include <mutex>
+
+#include "common.cuh"
+#include "match.cuh"
+
+namespace lema {
+
+// Implemented next to their kernels.
+int pack_codes(const void* z, int dtype, int64_t d0, int64_t d1, int64_t d2, int64_t s0, int64_t s1,
+               int64_t s2, int D, void* codes, int code_bytes, cudaStream_t stream);
+int64_t store_slot_bytes(int64_t vbytes);
+size_t store_workspace_bytes(int64_t n, int64_t T, int code_bytes);
+int store_exchange(void* table, int64_t cap, int64_t vbytes, const void* qc, const void* kc,
+                   int code_bytes, const void* values, void* out, int64_t n, int64_t T, int64_t g0,
+                   int64_t* counts, uint32_t* status, void* ws, size_t ws_bytes, cudaStream_t stream);
+int proj_codes(const void* x, const void* w_qk, int64_t M, int64_t K, int64_t T, int hq, int hk,
+               int d_qk, uint32_t* qcodes, uint32_t* kcodes, cudaStream_t stream);
+
+namespace {
+thread_local char g_err[512] = {0};
+constexpr int kMaxDevices = 64;
+DeviceInfo g_dev[kMaxDevices];
+std::once_flag g_dev_once[kMaxDevices];
+}  // namespace
+
+void set_error(const char* fmt, ...) {
+  va_list ap;
+  va_start(ap, fmt);
+  vsnprintf(g_err, sizeof(g_err), fmt, ap);
+  va_end(ap);
+}
+
+void clear_error() { g_err[0] = 0; }
+
+int fail(int code, const char* fmt, ...) {
+  va_list ap;
+  va_start(ap, fmt);
+  vsnprintf(g_err, sizeof(g_err), fmt, ap);
+  va_end(ap);
+  return code;
+}
+
+int cuda_fail(cudaError_t e, const char* what) {
+  snprintf(g_err, sizeof(g_err), "CUDA error %d (%s) in %s", static_cast<int>(e),
+           cudaGetErrorString(e), what);
+  return LEMA_ERR_CUDA;
+}
+
+const DeviceInfo* current_device_info() {
+  int dev = -1;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) {
+    cuda_fail(e, "cudaGetDevice");
+    return nullptr;
+  }
+  if (dev < 0 || dev >= kMaxDevices) {
+    fail(LEMA_ERR_UNSUPPORTED, "device index %d out of range", dev);
+    return nullptr;
+  }
+  std::call_once(g_dev_once[dev], [dev]() {
+    DeviceInfo d;
+    d.device = dev;
+    if (cudaDeviceGetAttribute(&d.sms, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess ||
+        cudaDeviceGetAttribute(&d.max_smem_optin, cudaDevAttrMaxSharedMemoryPerBlockOptin, dev) != cudaSuccess ||
+        cudaDeviceGetAttribute(&d.cc_major, cudaDevAttrComputeCapabilityMajor, dev) != cudaSuccess ||
+        cudaDeviceGetAttribute(&d.cc_minor, cudaDevAttrComputeCapabilityMinor, dev) != cudaSuccess) {
+      d.sms = 0;
+    }
+    g_dev[dev] = d;
+  });
+  if (g_dev[dev].sms <= 0) {
+    fail(LEMA_ERR_CUDA, "could not query device %d", dev);
+    return nullptr;
+  }
+  return &g_dev[dev];
+}
+
+}  // namespace lema
+
+extern "C" {
+
+const char* lema_last_error(void) { return lema::g_err; }
+
+int lema_version(void) { return 100; }
+
+int lema_pack_codes(const void* z, int dtype, int64_t d0, int64_t d1, int64_t d2, int64_t s0, int64_t s1,
+                    int64_t s2, int d_qk, void* codes, int code_bytes, void* stream) {
+  lema::clear_error();
+  return lema::pack_codes(z, dtype, d0, d1, d2, s0, s1, s2, d_qk, codes, code_bytes,
+                          static_cast<cudaStream_t>(stream));
+}
+
+int lema_proj_codes(const void* x, const void* w_qk, int64_t M, int64_t K, int64_t T, int hq, int hk,
+                    int d_qk, uint32_t* qcodes, uint32_t* kcodes, void* stream) {
+  lema::clear_error();
+  return lema::proj_codes(x, w_qk, M, K, T, hq, hk, d_qk, qcodes, kcodes,
+                          static_cast<cudaStream_t>(stream));
+}
+
+size_t lema_prefill_workspace_bytes(int64_t n_streams, int64_t T, int code_bytes) {
+  return lema::match_workspace_bytes(n_streams, T, code_bytes);
+}
+
+int lema_prefill_match(const void* qcodes, const void* kcodes, int code_bytes, int64_t n_streams,
+                       int64_t T, int32_t* src, const void* values, int64_t vbytes, void* out,
+                       void* workspace, size_t workspace_bytes, uint32_t* status, void* stream) {
+  lema::clear_error();
+  lema::MatchLaunch m;
+  m.qc = qcodes;
+  m.kc = kcodes;
+  m.code_bytes = code_bytes;
+  m.N = n_streams;
+  m.T = T;
+  m.src = src;
+  m.v = values;
+  m.vbytes = vbytes;
+  m.out = out;
+  m.ws = workspace;
+  m.ws_bytes = workspace_bytes;
+  m.status = status;
+  m.stream = static_cast<cudaStream_t>(stream);
+  return lema::launch_match(m);
+}
+
+int64_t lema_store_slot_bytes(int64_t vbytes) { return lema::store_slot_bytes(vbytes); }
+
+size_t lema_store_workspace_bytes(int64_t n, int64_t T, int code_bytes) {
+  return lema::store_workspace_bytes(n, T, code_bytes);
+}
+
+int lema_store_exchange(void* table, int64_t cap, int64_t vbytes, const void* qcodes, const void* kcodes,
+                        int code_bytes, const void* values, void* out, int64_t n, int64_t T, int64_t g0,
+                        int64_t* counts, uint32_t* status, void* workspace, size_t workspace_bytes,
+                        void* stream) {
+  lema::clear_error();
+  return lema::store_exchange(table, cap, vbytes, qcodes, kcodes, code_bytes, values, out, n, T, g0,
+                              counts, status, workspace, workspace_bytes,
+                              static_cast<cudaStream_t>(stream));
+}
+
+}  // extern "C"

@@ -1,0 +1,117 @@
+// Shared helpers of the LEMA B200 kernels: hashing, warp utilities, status
+// reporting and host-side error handling.
+#pragma once
+
+#include <cuda_runtime.h>
+
+#include <cstddef>
+#include <cstdint>
+
+#include "lema_b200.h"
+
+namespace lema {
+
+constexpr unsigned kFullMask = 0xFFFFFFFFu;
+
+// MurmurHash3's 32- and 64-bit finalizers (Appleby, public domain): cheap
+// full-avalanche mixers. Codes are what a model chose, not random bits, so they
+// are mixed before they index a table.
+__host__ __device__ __forceinline__ uint32_t fmix32(uint32_t h) {
+  h ^= h >> 16;
+  h *= 0x85EBCA6Bu;
+  h ^= h >> 13;
+  h *= 0xC2B2AE35u;
+  h ^= h >> 16;
+  return h;
+}
+
+__host__ __device__ __forceinline__ uint64_t fmix64(uint64_t k) {
+  k ^= k >> 33;
+  k *= 0xFF51AFD7ED558CCDull;
+  k ^= k >> 33;
+  k *= 0xC4CEB9FE1A85EC53ull;
+  k ^= k >> 33;
+  return k;
+}
+
+template <typename CodeT>
+__device__ __forceinline__ uint32_t code_hash32(CodeT c);
+template <>
+__device__ __forceinline__ uint32_t code_hash32<uint32_t>(uint32_t c) {
+  return fmix32(c);
+}
+template <>
+__device__ __forceinline__ uint32_t code_hash32<uint64_t>(uint64_t c) {
+  return static_cast<uint32_t>(fmix64(c) >> 32);
+}
+
+__device__ __forceinline__ uint32_t lanemask_lt() {
+  uint32_t m;
+  asm("mov.u32 %0, %%lanemask_lt;" : "=r"(m));
+  return m;
+}
+
+__device__ __forceinline__ void raise_status(uint32_t* status, uint32_t bits) {
+  if (status != nullptr) atomicOr(status, bits);
+}
+
+// Streaming (evict-first) store of one vector word: outputs are written once
+// and never re-read by the kernel that writes them.
+template <typename Vec>
+__device__ __forceinline__ void store_stream(Vec* p, const Vec& v) {
+  __stcs(p, v);
+}
+template <>
+__device__ __forceinline__ void store_stream<unsigned short>(unsigned short* p,
+                                                             const unsigned short& v) {
+  *p = v;
+}
+
+template <typename Vec>
+__device__ __forceinline__ Vec zero_vec() {
+  Vec v;
+  memset(&v, 0, sizeof(Vec));
+  return v;
+}
+
+// ------------------------------------------------------------------ host side
+// Thread-local message of the last failing entry point (lema_last_error()).
+void set_error(const char* fmt, ...);
+void clear_error();
+int fail(int code, const char* fmt, ...);
+int cuda_fail(cudaError_t e, const char* what);
+
+struct DeviceInfo {
+  int device = -1;
+  int sms = 0;
+  int max_smem_optin = 0;
+  int cc_major = 0, cc_minor = 0;
+};
+// Cached per device; queried once. Returns nullptr (and sets the error) on failure.
+const DeviceInfo* current_device_info();
+
+#define LEMA_CUDA_TRY(expr)                                \
+  do {                                                     \
+    cudaError_t _e = (expr);                               \
+    if (_e != cudaSuccess) return ::lema::cuda_fail(_e, #expr); \
+  } while (0)
+
+inline bool aligned(const void* p, size_t a) {
+  return (reinterpret_cast<uintptr_t>(p) % a) == 0;
+}
+
+inline uint64_t next_pow2(uint64_t x) {
+  uint64_t p = 1;
+  while (p < x) p <<= 1;
+  return p;
+}
+
+inline int log2_exact(uint64_t p) {
+  int l = 0;
+  while ((uint64_t(1) << l) < p) ++l;
+  return l;
+}
+
+inline size_t round_up(size_t x, size_t a) { return (x + a - 1) / a * a; }
+
+}  // namespace lema

@@ -1,0 +1,308 @@
+// K3 -- the HBM-resident LEMA store and its exchange.
+//
+// Semantics are those of code/lema/csrc/store.cpp:122-162: one open-addressing table shared
+// by every (layer, stream, head) partition, keyed by (group, code); each partition, in
+// position order, looks its query up (zeros on a miss) and then inserts its key (latest write
+// wins); counts[p] grows by the slots partition p newly claims; a table with no free slot
+// left reports "full" instead of growing.
+//
+// Slot layout (stride = 16 + vbytes rounded up to 16, so value rows are 16-byte aligned):
+//   [0, 8)    code (zero-extended to 64 bits)
+//   [8, 16)   state: 0 = EMPTY, 1 = LOCKED (being claimed), group + 2 = published
+//   [16, ..)  value row, opaque bytes
+// A zero-filled allocation is an empty table. Claims are a compare-and-swap EMPTY -> LOCKED,
+// then the code and value are written and the state is published with a release store;
+// probers read the state with acquire loads, so a published slot's code and value are
+// complete when seen. The home slot is a 64-bit mix of (group, code) mapped onto [0, cap)
+// by a multiply-high (Lemire's range reduction), so the capacity is any slot count.
+//
+// Exchange on the GPU:
+//   T == 1 (decode step): every item is its own partition; one thread per item looks up and
+//           then inserts. No ordering between items is needed.
+//   T > 1 (prefill chunk): the order inside a partition only matters between equal codes, so
+//           the call is decomposed exactly:
+//             (1) the matcher (K2) finds each query's latest earlier key INSIDE the chunk and
+//                 each key code's last position in the chunk;
+//             (2) a query with an in-chunk match copies that value row; any other query
+//                 looks the store up (the state before this call);
+//             (3) each partition's distinct key codes are inserted once, with the value row
+//                 of their last position -- what a position-ordered sequence of overwrites
+//                 leaves behind.
+//           Kernel boundaries order (2) before (3).
+#include <cuda_runtime.h>
+
+#include <algorithm>
+
+#include "common.cuh"
+#include "match.cuh"
+
+namespace lema {
+namespace k3 {
+
+constexpr uint64_t kEmpty = 0, kLocked = 1;
+constexpr int kThreads = 256;
+
+struct Args {
+  unsigned char* table;
+  uint64_t cap;
+  int64_t stride;
+  int64_t vbytes;
+  const void* qc;
+  const void* kc;
+  const unsigned char* v;
+  unsigned char* out;
+  int64_t n, T;
+  uint64_t g0;
+  int64_t* counts;
+  uint32_t* status;
+  const int32_t* src;
+  const void* lt_code;
+  const int32_t* lt_pos;
+  const int32_t* lt_count;
+};
+
+__device__ __forceinline__ uint64_t home(uint64_t code, uint64_t group, uint64_t cap) {
+  const uint64_t h = fmix64(code ^ fmix64(group ^ 0x5851F42D4C957F2Dull));
+  return __umul64hi(h, cap);
+}
+
+__device__ __forceinline__ uint64_t ld_acquire(const uint64_t* p) {
+  uint64_t v;
+  asm volatile("ld.acquire.gpu.global.u64 %0, [%1];" : "=l"(v) : "l"(p) : "memory");
+  return v;
+}
+
+__device__ __forceinline__ void st_release(uint64_t* p, uint64_t v) {
+  asm volatile("st.release.gpu.global.u64 [%0], %1;" ::"l"(p), "l"(v) : "memory");
+}
+
+template <typename Vec>
+__device__ __forceinline__ void copy_row(Vec* dst, const Vec* src, int wpr) {
+  for (int k = 0; k < wpr; ++k) dst[k] = src[k];
+}
+
+template <typename Vec>
+__device__ __forceinline__ void zero_row(Vec* dst, int wpr) {
+  const Vec z = zero_vec<Vec>();
+  for (int k = 0; k < wpr; ++k) dst[k] = z;
+}
+
+// Copies the value stored under (group, code) into dst, or zeros. Returns whether it hit.
+template <typename Vec>
+__device__ bool lookup(const Args& a, uint64_t code, uint64_t group, Vec* dst) {
+  const int wpr = static_cast<int>(a.vbytes / static_cast<int64_t>(sizeof(Vec)));
+  const uint64_t tag = group + 2;
+  uint64_t s = home(code, group, a.cap);
+  for (uint64_t t = 0; t < a.cap; ++t) {
+    uint64_t* hdr = reinterpret_cast<uint64_t*>(a.table + s * a.stride);
+    const uint64_t st = ld_acquire(hdr + 1);
+    if (st == kEmpty) break;
+    if (st == tag && hdr[0] == code) {
+      copy_row(dst, reinterpret_cast<const Vec*>(hdr + 2), wpr);
+      return true;
+    }
+    s = (s + 1 == a.cap) ? 0 : s + 1;
+  }
+  zero_row(dst, wpr);
+  return false;
+}
+
+// (group, code) -> row, latest write wins. Returns 1 for a newly claimed slot, 0 for an
+// overwrite, -1 when every slot was probed (the table is full).
+template <typename Vec>
+__device__ int insert(const Args& a, uint64_t code, uint64_t group, const Vec* row) {
+  const int wpr = static_cast<int>(a.vbytes / static_cast<int64_t>(sizeof(Vec)));
+  const uint64_t tag = group + 2;
+  uint64_t s = home(code, group, a.cap);
+  for (uint64_t t = 0; t < a.cap; ++t) {
+    uint64_t* hdr = reinterpret_cast<uint64_t*>(a.table + s * a.stride);
+    uint64_t st = ld_acquire(hdr + 1);
+    if (st == kEmpty) {
+      st = atomicCAS(reinterpret_cast<unsigned long long*>(hdr + 1), kEmpty, kLocked);
+      if (st == kEmpty) {
+        hdr[0] = code;
+        copy_row(reinterpret_cast<Vec*>(hdr + 2), row, wpr);
+        st_release(hdr + 1, tag);
+        return 1;
+      }
+    }
+    if (st == tag && hdr[0] == code) {
+      copy_row(reinterpret_cast<Vec*>(hdr + 2), row, wpr);
+      return 0;
+    }
+    s = (s + 1 == a.cap) ? 0 : s + 1;
+  }
+  return -1;
+}
+
+template <typename CodeT>
+__device__ __forceinline__ uint64_t load_code(const void* p, int64_t i) {
+  return static_cast<uint64_t>(static_cast<const CodeT*>(p)[i]);
+}
+
+// T == 1: item i is partition i; look up, then insert.
+template <typename CodeT, typename Vec>
+__global__ void __launch_bounds__(kThreads) exchange_step(const Args a) {
+  const int64_t i = static_cast<int64_t>(blockIdx.x) * kThreads + threadIdx.x;
+  if (i >= a.n) return;
+  const int64_t wpr = a.vbytes / static_cast<int64_t>(sizeof(Vec));
+  const uint64_t g = a.g0 + static_cast<uint64_t>(i);
+  lookup<Vec>(a, load_code<CodeT>(a.qc, i), g, reinterpret_cast<Vec*>(a.out) + i * wpr);
+  const int r = insert<Vec>(a, load_code<CodeT>(a.kc, i), g, reinterpret_cast<const Vec*>(a.v) + i * wpr);
+  if (r < 0) {
+    raise_status(a.status, LEMA_STATUS_TABLE_FULL);
+  } else if (r > 0) {
+    atomicAdd(reinterpret_cast<unsigned long long*>(a.counts + i), 1ull);
+  }
+}
+
+// T > 1, phase (2): in-chunk match or store lookup.
+template <typename CodeT, typename Vec>
+__global__ void __launch_bounds__(kThreads) exchange_resolve(const Args a) {
+  const int64_t i = static_cast<int64_t>(blockIdx.x) * kThreads + threadIdx.x;
+  if (i >= a.n) return;
+  const int64_t wpr = a.vbytes / static_cast<int64_t>(sizeof(Vec));
+  const int64_t p = i / a.T;
+  Vec* dst = reinterpret_cast<Vec*>(a.out) + i * wpr;
+  const int32_t s = a.src[i];
+  if (s >= 0) {
+    copy_row(dst, reinterpret_cast<const Vec*>(a.v) + (p * a.T + s) * wpr, static_cast<int>(wpr));
+  } else {
+    lookup<Vec>(a, load_code<CodeT>(a.qc, i), a.g0 + static_cast<uint64_t>(p), dst);
+  }
+}
+
+// T > 1, phase (3): insert each partition's distinct key codes with their last row.
+template <typename CodeT, typename Vec>
+__global__ void __launch_bounds__(kThreads) exchange_insert(const Args a) {
+  const int64_t i = static_cast<int64_t>(blockIdx.x) * kThreads + threadIdx.x;
+  if (i >= a.n) return;
+  const int64_t p = i / a.T;
+  const int64_t e = i - p * a.T;
+  if (e >= a.lt_count[p]) return;
+  const int64_t wpr = a.vbytes / static_cast<int64_t>(sizeof(Vec));
+  const int32_t pos = a.lt_pos[i];
+  const int r = insert<Vec>(a, load_code<CodeT>(a.lt_code, i), a.g0 + static_cast<uint64_t>(p),
+                            reinterpret_cast<const Vec*>(a.v) + (p * a.T + pos) * wpr);
+  if (r < 0) {
+    raise_status(a.status, LEMA_STATUS_TABLE_FULL);
+  } else if (r > 0) {
+    atomicAdd(reinterpret_cast<unsigned long long*>(a.counts + p), 1ull);
+  }
+}
+
+struct WsLayout {
+  size_t src = 0, lt_code = 0, lt_pos = 0, lt_count = 0, match = 0, total = 0;
+};
+
+WsLayout layout(int64_t n, int64_t T, int code_bytes) {
+  WsLayout w;
+  if (T <= 1 || n <= 0) return w;
+  const int64_t P = n / T;
+  size_t off = 0;
+  w.src = off;
+  off = round_up(off + 4 * static_cast<size_t>(n), 256);
+  w.lt_code = off;
+  off = round_up(off + static_cast<size_t>(code_bytes) * n, 256);
+  w.lt_pos = off;
+  off = round_up(off + 4 * static_cast<size_t>(n), 256);
+  w.lt_count = off;
+  off = round_up(off + 4 * static_cast<size_t>(P), 256);
+  w.match = off;
+  off += match_workspace_bytes(P, T, code_bytes);
+  w.total = off;
+  return w;
+}
+
+template <typename CodeT, typename Vec>
+int run(Args a, int64_t T, void* ws, size_t ws_bytes, int code_bytes, cudaStream_t stream) {
+  const unsigned blocks = static_cast<unsigned>((a.n + kThreads - 1) / kThreads);
+  if (T == 1) {
+    exchange_step<CodeT, Vec><<<blocks, kThreads, 0, stream>>>(a);
+    LEMA_CUDA_TRY(cudaGetLastError());
+    return LEMA_OK;
+  }
+  const WsLayout w = layout(a.n, T, code_bytes);
+  unsigned char* base = static_cast<unsigned char*>(ws);
+  MatchLaunch m;
+  m.qc = a.qc;
+  m.kc = a.kc;
+  m.code_bytes = code_bytes;
+  m.N = a.n / T;
+  m.T = T;
+  m.src = reinterpret_cast<int32_t*>(base + w.src);
+  m.lt_code = base + w.lt_code;
+  m.lt_pos = reinterpret_cast<int32_t*>(base + w.lt_pos);
+  m.lt_count = reinterpret_cast<int32_t*>(base + w.lt_count);
+  m.ws = (ws_bytes > w.match) ? base + w.match : nullptr;
+  m.ws_bytes = ws_bytes - w.match;
+  m.status = a.status;
+  m.stream = stream;
+  const int rc = launch_match(m);
+  if (rc != LEMA_OK) return rc;
+  a.src = m.src;
+  a.lt_code = m.lt_code;
+  a.lt_pos = m.lt_pos;
+  a.lt_count = m.lt_count;
+  exchange_resolve<CodeT, Vec><<<blocks, kThreads, 0, stream>>>(a);
+  LEMA_CUDA_TRY(cudaGetLastError());
+  exchange_insert<CodeT, Vec><<<blocks, kThreads, 0, stream>>>(a);
+  LEMA_CUDA_TRY(cudaGetLastError());
+  return LEMA_OK;
+}
+
+}  // namespace k3
+
+int64_t store_slot_bytes(int64_t vbytes) {
+  return 16 + static_cast<int64_t>(round_up(static_cast<size_t>(vbytes), 16));
+}
+
+size_t store_workspace_bytes(int64_t n, int64_t T, int code_bytes) {
+  return k3::layout(n, T, code_bytes).total;
+}
+
+int store_exchange(void* table, int64_t cap, int64_t vbytes, const void* qc, const void* kc,
+                   int code_bytes, const void* values, void* out, int64_t n, int64_t T, int64_t g0,
+                   int64_t* counts, uint32_t* status, void* ws, size_t ws_bytes,
+                   cudaStream_t stream) {
+  if (code_bytes != 4 && code_bytes != 8) return fail(LEMA_ERR_INVALID_ARGUMENT, "code_bytes must be 4 or 8, got %d", code_bytes);
+  if (vbytes <= 0 || vbytes % 8 != 0) return fail(LEMA_ERR_INVALID_ARGUMENT, "value row of %lld bytes: vbytes must be a positive multiple of 8", (long long)vbytes);
+  if (cap < 1) return fail(LEMA_ERR_INVALID_ARGUMENT, "capacity must be >= 1 slot, got %lld", (long long)cap);
+  if (n < 0 || T <= 0 || n % T != 0) return fail(LEMA_ERR_INVALID_ARGUMENT, "items must be partitions x T (n = %lld, T = %lld)", (long long)n, (long long)T);
+  if (g0 < 0) return fail(LEMA_ERR_INVALID_ARGUMENT, "negative group offset");
+  if (n == 0) return LEMA_OK;
+  if (table == nullptr || !aligned(table, 16)) return fail(LEMA_ERR_INVALID_ARGUMENT, "table must be a 16-byte aligned device pointer");
+  if (qc == nullptr || kc == nullptr || values == nullptr || out == nullptr || counts == nullptr) return fail(LEMA_ERR_INVALID_ARGUMENT, "null pointer argument");
+  if (!aligned(qc, code_bytes) || !aligned(kc, code_bytes)) return fail(LEMA_ERR_INVALID_ARGUMENT, "codes not aligned to their width");
+  if (!aligned(values, 8) || !aligned(out, 8) || !aligned(counts, 8)) return fail(LEMA_ERR_INVALID_ARGUMENT, "values, out and counts must be 8-byte aligned");
+  const size_t need = store_workspace_bytes(n, T, code_bytes);
+  if (ws_bytes < need || (need > 0 && ws == nullptr)) return fail(LEMA_ERR_WORKSPACE, "workspace of %zu bytes, %zu needed", ws_bytes, need);
+  if (need > 0 && !aligned(ws, 256)) return fail(LEMA_ERR_INVALID_ARGUMENT, "workspace must be 256-byte aligned");
+  const DeviceInfo* dev = current_device_info();
+  if (dev == nullptr) return LEMA_ERR_CUDA;
+  if (dev->cc_major != 10) return fail(LEMA_ERR_UNSUPPORTED, "built for sm_100a; device is sm_%d%d", dev->cc_major, dev->cc_minor);
+
+  k3::Args a{};
+  a.table = static_cast<unsigned char*>(table);
+  a.cap = static_cast<uint64_t>(cap);
+  a.stride = store_slot_bytes(vbytes);
+  a.vbytes = vbytes;
+  a.qc = qc;
+  a.kc = kc;
+  a.v = static_cast<const unsigned char*>(values);
+  a.out = static_cast<unsigned char*>(out);
+  a.n = n;
+  a.T = T;
+  a.g0 = static_cast<uint64_t>(g0);
+  a.counts = counts;
+  a.status = status;
+  const bool v16 = vbytes % 16 == 0 && aligned(values, 16) && aligned(out, 16);
+  if (code_bytes == 4) {
+    return v16 ? k3::run<uint32_t, uint4>(a, T, ws, ws_bytes, code_bytes, stream)
+               : k3::run<uint32_t, uint2>(a, T, ws, ws_bytes, code_bytes, stream);
+  }
+  return v16 ? k3::run<uint64_t, uint4>(a, T, ws, ws_bytes, code_bytes, stream)
+             : k3::run<uint64_t, uint2>(a, T, ws, ws_bytes, code_bytes, stream);
+}
+
+}  // namespace lema

@@ -1,0 +1,129 @@
+"""K3, the HBM store, on the GPU through the C ABI: the reference's store tests
+(code/tests/test_store.py shapes, golden outputs of its C++ store), config 1's prefill +
+512 decode steps, the overfull error, and chunking invariance against the dense op
+(code/tests/test_gpu.py:68-90's claim, at the op level)."""
+import numpy as np
+import pytest
+import torch
+
+import oracle
+from latest_exact_match_attention_b200.cache import HashStore
+from tests import golden_data as G
+
+pytestmark = pytest.mark.gpu
+
+
+def dev_codes(a, dev):
+    a = np.ascontiguousarray(a)
+    if a.dtype.itemsize <= 4:
+        return torch.from_numpy(a.astype(np.uint32).view(np.int32)).to(dev)
+    return torch.from_numpy(a.astype(np.int64)).to(dev)
+
+
+@pytest.mark.parametrize("name", sorted(G.store_cases()))
+def test_reference_store_cases(cuda, name):
+    c = G.store_cases()[name]
+    P, T, chunk = c["P"], c["T"], c["chunk"]
+    vals = G.store_case_values(P, T, 8, c["seed"])
+    st = HashStore(8, groups=P, dtype=torch.float16, capacity=c["cap"], device=cuda)
+    v16 = torch.from_numpy(vals.view(np.float16))
+    outs = np.empty_like(vals)
+    for lo in range(0, T, chunk):
+        hi = min(T, lo + chunk)
+        q = dev_codes(c["codes"][0, :, lo:hi].reshape(-1), cuda)
+        k = dev_codes(c["codes"][1, :, lo:hi].reshape(-1), cuda)
+        vv = v16[:, lo:hi].reshape(-1, 8).contiguous().to(cuda)
+        o = torch.empty_like(vv)
+        st.exchange(q, k, vv, o, hi - lo, 0)
+        outs[:, lo:hi] = o.cpu().numpy().view(np.uint16).reshape(P, hi - lo, 8)
+    np.testing.assert_array_equal(st.counts.cpu().numpy(), c["counts"])
+    assert G.sha(outs) == c["out_sha"]
+
+
+def test_overfull_raises(cuda):
+    rng = np.random.default_rng(3)
+    codes = rng.integers(0, 100, size=(2, 50, 100), dtype=np.int64) * 7919 % 102
+    st = HashStore(8, groups=50, dtype=torch.float16, capacity=1000, device=cuda)
+    v = torch.randn(5000, 8, device=cuda, dtype=torch.float16)
+    with pytest.raises(RuntimeError, match="full"):
+        st.exchange(dev_codes(codes[0].reshape(-1), cuda), dev_codes(codes[1].reshape(-1), cuda),
+                    v, torch.empty_like(v), 100, 0)
+    # decode-sized steps raise too
+    st = HashStore(8, groups=64, dtype=torch.float16, capacity=16, device=cuda)
+    with pytest.raises(RuntimeError, match="full"):
+        for t in range(3):
+            c = torch.arange(64, device=cuda, dtype=torch.int32) + 64 * t
+            st.exchange(c, c, v[:64], torch.empty_like(v[:64]), 1, 0)
+
+
+@pytest.mark.parametrize("width", [4, 8])
+def test_config1_prefill_then_decode(cuda, width):
+    g = G.load("config1")
+    v = G.config1_values()
+    T0 = int(g["prefill_T"])
+    qc, kc = g["qc"], g["kc"]
+    if width == 8:
+        qc, kc = qc.astype(np.int64), kc.astype(np.int64)
+    st = HashStore(64, groups=8, dtype=torch.float32, capacity=8 * 4608 * 2, device=cuda)
+    vd = torch.from_numpy(v).to(cuda)
+    outs = torch.empty_like(vd)
+    o = torch.empty(8 * T0, 64, device=cuda)
+    st.exchange(dev_codes(qc[:, :T0].reshape(-1), cuda), dev_codes(kc[:, :T0].reshape(-1), cuda),
+                vd[:, :T0].reshape(-1, 64), o, T0, 0)
+    outs[:, :T0] = o.view(8, T0, 64)
+    np.testing.assert_array_equal(st.counts.cpu().numpy(), g["counts_prefill"])
+    qd, kd = dev_codes(qc, cuda), dev_codes(kc, cuda)
+    step_out = torch.empty(8, 64, device=cuda)
+    for t in range(T0, 4608):
+        st.exchange(qd[:, t].contiguous(), kd[:, t].contiguous(), vd[:, t].contiguous(), step_out, 1, 0,
+                    check=False)
+        outs[:, t] = step_out
+    st.check()
+    np.testing.assert_array_equal(st.counts.cpu().numpy(), g["counts_final"])
+    assert G.sha(outs.cpu().numpy()) == str(g["out_sha"])
+
+
+@pytest.mark.parametrize("chunk", [1300, 64, 7, 1])
+def test_chunking_invariance(cuda, chunk):
+    """Fed in any chunking, the store reproduces the dense one-shot op exactly."""
+    rng = np.random.default_rng(chunk)
+    P, T = 12, 1300
+    qc = rng.integers(0, 60, size=(P, T)).astype(np.uint32)
+    kc = rng.integers(0, 60, size=(P, T)).astype(np.uint32)
+    v = rng.standard_normal((P, T, 24)).astype(np.float32)
+    dense = oracle.lema_hard(qc, kc, v)
+    st = HashStore(24, groups=P + 5, dtype=torch.float32, capacity=P * T, device=cuda)
+    vd = torch.from_numpy(v).to(cuda)
+    got = torch.empty_like(vd)
+    for lo in range(0, T, chunk):
+        hi = min(T, lo + chunk)
+        o = torch.empty(P * (hi - lo), 24, device=cuda)
+        st.exchange(dev_codes(qc[:, lo:hi].reshape(-1), cuda), dev_codes(kc[:, lo:hi].reshape(-1), cuda),
+                    vd[:, lo:hi].reshape(-1, 24), o, hi - lo, 5, check=False)
+        got[:, lo:hi] = o.view(P, hi - lo, 24)
+    st.check()
+    np.testing.assert_array_equal(got.cpu().numpy(), dense)
+    want_counts = [len(set(kc[p].tolist())) for p in range(P)]
+    np.testing.assert_array_equal(st.counts.cpu().numpy()[5:], want_counts)
+    assert st.counts[:5].sum().item() == 0
+
+
+def test_store_vs_oracle_store_random(cuda):
+    """Many partitions sharing a small code space, capacity tight: the GPU store and the
+    oracle store agree call by call, including the counts."""
+    rng = np.random.default_rng(17)
+    P, T, cap = 300, 40, 14000
+    tab = oracle.new_table(cap, 16)
+    st = HashStore(8, groups=P, dtype=torch.float16, capacity=cap, device=cuda)
+    for step in range(6):
+        qc = rng.integers(0, 50, size=(P, T)).astype(np.int64)
+        kc = rng.integers(0, 50, size=(P, T)).astype(np.int64)
+        v = rng.integers(0, 1 << 16, size=(P * T, 8), dtype=np.uint16)
+        want, added, full = oracle.store_exchange(tab, qc, kc, v, T, 0)
+        assert not full
+        vd = torch.from_numpy(v.view(np.float16)).to(cuda)
+        o = torch.empty_like(vd)
+        st.exchange(dev_codes(qc.reshape(-1), cuda), dev_codes(kc.reshape(-1), cuda), vd, o, T, 0)
+        np.testing.assert_array_equal(o.cpu().numpy().view(np.uint16), want)
+    counts = st.counts.cpu().numpy()
+    assert counts.sum() == int((tab.view(np.uint64).reshape(cap, -1)[:, 1] != 0).sum())
