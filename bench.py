@@ -40,7 +40,7 @@ ROOT = Path(__file__).resolve().parent
 sys.path.insert(0, str(ROOT))
 
 B, H, T, D_V = 8, 64, 16384, 24
-N_STREAMS = B * H
+N_STREAMS = B * H          # --streams overrides (smaller cases for profiling)
 VBYTES = D_V * 2
 METRIC = "LEMA prefill Mpos/s/GPU & batched decode tok/s; % of HBM roofline"
 UNIT = "Mpos/s"
@@ -120,14 +120,14 @@ def dist_setup(n_gpus: int):
     return rank, world
 
 
-def make_inputs(rank: int, device):
+def make_inputs(rank: int, device, n_streams: int):
     import torch
 
     from latest_exact_match_attention_b200 import synth
-    qc, kc = synth.code_streams(N_STREAMS, T, synth.CONFIG2, seed=rank, config_id=2)
+    qc, kc = synth.code_streams(n_streams, T, synth.CONFIG2, seed=rank, config_id=2)
     q = torch.from_numpy(qc.view(np.int32)).to(device)
     k = torch.from_numpy(kc.view(np.int32)).to(device)
-    v = synth.values_torch(N_STREAMS, T, D_V, torch.bfloat16, device, seed=rank, config_id=2)
+    v = synth.values_torch(n_streams, T, D_V, torch.bfloat16, device, seed=rank, config_id=2)
     return qc, kc, q, k, v
 
 
@@ -204,7 +204,8 @@ def run_b200(args):
     local = int(os.environ.get("LOCAL_RANK", "0"))
     torch.cuda.set_device(local)
     dev = torch.device("cuda", local)
-    qc, kc, q, k, v = make_inputs(rank, dev)
+    N_STREAMS = args.streams
+    qc, kc, q, k, v = make_inputs(rank, dev, N_STREAMS)
     n_pos = N_STREAMS * T
     src = torch.empty((N_STREAMS, T), dtype=torch.int32, device=dev)
     out = torch.empty_like(v)
@@ -264,7 +265,7 @@ def run_b200(args):
     value = world * n_pos * args.steps / (total_ms / 1e3) / 1e6
 
     # end to end through the C ABI with host buffers (pinned), copies inside the timed region
-    e2e_steps = max(1, min(args.steps, 5))
+    e2e_steps = 0 if args.no_e2e else max(1, min(args.steps, 5))
     hq = torch.from_numpy(qc.view(np.int32)).pin_memory()
     hk = torch.from_numpy(kc.view(np.int32)).pin_memory()
     hv = v.cpu().pin_memory()
@@ -276,6 +277,8 @@ def run_b200(args):
     torch.cuda.synchronize()
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     e0.record(stream)
+    if e2e_steps == 0:
+        step()
     for _ in range(e2e_steps):
         q.copy_(hq, non_blocking=True)
         k.copy_(hk, non_blocking=True)
@@ -291,7 +294,7 @@ def run_b200(args):
         tt = torch.tensor([e2e_ms], device=dev)
         dist.all_reduce(tt, op=dist.ReduceOp.MAX)
         e2e_ms = float(tt.item())
-    e2e_value = world * n_pos * e2e_steps / (e2e_ms / 1e3) / 1e6
+    e2e_value = world * n_pos * e2e_steps / (e2e_ms / 1e3) / 1e6 if e2e_steps else None
 
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
@@ -322,7 +325,7 @@ def run_b200(args):
                      "frac": round(achieved / peak, 4), "traffic": traffic,
                      "peak_source": peak_src, "alg_bytes_per_launch": alg_bytes,
                      "launch_ms": round(per_launch_ms, 4)},
-        "e2e": {"value": round(e2e_value, 2), "unit": UNIT, "h2d_bytes_per_step": h2d,
+        "e2e": {"value": e2e_value and round(e2e_value, 2), "unit": UNIT, "h2d_bytes_per_step": h2d,
                 "d2h_bytes_per_step": d2h, "steps": e2e_steps},
         "cpu_baseline": cpu,
         "gpu_launches": args.steps * (2 if ws_bytes else 1),
@@ -338,6 +341,9 @@ def main():
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", choices=["b200", "reference"], default="b200")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-e2e", action="store_true")
+    ap.add_argument("--streams", type=int, default=N_STREAMS,
+                    help="streams per GPU (default: the workload's 512); smaller for profiling")
     args = ap.parse_args()
     if args.warmup < 3 and args.impl == "b200":
         args.warmup = 3

@@ -129,8 +129,16 @@ class HashStore:
         P = n // T if T else 0
         if g0 < 0 or g0 + P > self.groups:
             raise ValueError(f"groups [{g0}, {g0 + P}) outside the store's {self.groups}")
+        if values.dim() != 2 or values.shape[0] != n or out.shape != values.shape:
+            raise ValueError(f"values and out must be [n, d_v] = [{n}, {self.d_v}], got "
+                             f"{tuple(values.shape)} and {tuple(out.shape)}")
+        if values.element_size() * values.shape[1] != self.vbytes:
+            raise ValueError(f"value rows of {values.element_size() * values.shape[1]} bytes, "
+                             f"the store holds {self.vbytes}")
+        if not out.is_contiguous():
+            raise ValueError("out must be contiguous")
         ws = self._workspace(n, T, cb)
-        qcodes, kcodes = qcodes.contiguous(), kcodes.contiguous()
+        qcodes, kcodes, values = qcodes.contiguous(), kcodes.contiguous(), values.contiguous()
         call("lema_store_exchange", ptr(self.table), self.cap, self.vbytes, ptr(qcodes),
              ptr(kcodes), cb, ptr(values), ptr(out), n, T, g0,
              ptr(self.counts) + 8 * g0, ptr(self.status), ptr(ws), 0 if ws is None else ws.numel(),

@@ -6,23 +6,27 @@
 // one pass in position order with a hash table of the stream's key codes in shared memory.
 //
 // One CTA owns one stream at a time (persistent grid-stride over streams) and walks it in
-// chunks of kChunk positions. Per chunk:
-//   1. insert   all warps: each key code is inserted into (or found in) the stream's table,
-//               giving it a SLOT id. Equal codes of a warp are deduplicated with match_any
-//               first, so one lane per distinct code touches the table.
-//   2. lookup   all warps: each query code is looked up; a code that no key up to the end of
-//               this chunk has used gets no slot, and that is already its final answer (-1).
-//   3. in-step  all warps: inside each 32-position step (one warp-wide row), the latest key
-//               lane j < i with the query's slot, by 32 shuffles; and for each key lane,
-//               whether it is the last lane of its slot in the step.
-//   4. sweep    ONE warp, in position order, 32 positions per step: a query with an in-step
-//               match takes it; otherwise it reads meta[slot], the position of the latest key
-//               of its slot swept so far. Then the last key lane of each slot writes its
-//               position into meta[slot]. Two __syncwarp()s per step order the reads before
-//               the step's writes and the writes before the next step's reads. This is the
-//               only ordered part, and it touches one shared-memory word per position.
-//   5. gather   all warps: src to global memory, value rows copied with 16-byte vectors
-//               (streaming stores), zeros for misses.
+// chunks of kChunk positions through a three-stage pipeline of warp roles; stage boundaries are
+// CTA-wide barriers ("rounds"), and in round r:
+//
+//   preparers (7 warps) -- chunk r
+//     1. insert  the chunk's key codes (loaded in one batch) are inserted into -- or found in --
+//                the stream's table, giving each a SLOT id. Equal codes of a warp are first
+//                deduplicated with match_any, so one lane per distinct code touches the table.
+//     2. lookup  each query code is looked up; a code that no key up to the end of this chunk
+//                has used gets no slot, and -1 is already its final answer.
+//     3. in-step inside each 32-position step, the latest key lane j < i with the query's
+//                slot (32 shuffles), and whether each key lane is the last of its slot.
+//   sweeper (1 warp) -- chunk r-1, the only ordered part: 32 positions per step, a query with
+//                an in-step match takes it, any other reads meta[slot] (the position of the
+//                latest key of its slot swept so far); then the last key lane of each slot
+//                writes its position into meta[slot]. Two __syncwarp()s per step order the
+//                reads before the step's writes and the writes before the next step's reads.
+//   gatherers (8 warps) -- chunk r-2: indices out, value rows copied with 16-byte vectors,
+//                eight loads in flight per thread, streaming stores; zeros for misses.
+//
+// The stages touch the table without conflict: inserts only claim free words, lookups compare
+// codes only, and the sweep writes the position half of words claimed in earlier rounds.
 //
 // The shared-memory table has a fixed capacity (kSmemCap slots). A stream whose distinct key
 // codes would load it beyond kOverflowFrac is handed over whole to the same kernel running
@@ -41,8 +45,15 @@ namespace lema {
 namespace k2 {
 
 constexpr int kThreads = 512;
-constexpr int kWarps = kThreads / 32;
 constexpr int kChunk = 2048;
+constexpr int kSweepWarp = 0;                        // warp 0: the ordered sweep
+constexpr int kPrepWarp0 = 1, kPrepWarps = 7;        // warps 1..7: insert / lookup / in-step
+constexpr int kGathWarp0 = 8, kGathWarps = 8;        // warps 8..15: indices and rows out
+constexpr int kPrepThreads = kPrepWarps * 32;
+constexpr int kGathThreads = kGathWarps * 32;
+constexpr int kPerPrep = (kChunk + kPrepThreads - 1) / kPrepThreads;
+constexpr int kGatherUnroll = 8;
+static_assert((kPrepWarp0 + kPrepWarps) * 32 <= kThreads && kGathWarp0 * 32 + kGathThreads == kThreads, "roles");
 
 constexpr uint32_t kEmpty = 0xFFFFFFFFu;   // meta of a free slot
 constexpr uint32_t kLocked = 0xFFFFFFFEu;  // meta of a slot being claimed (64-bit codes only)
@@ -117,11 +128,12 @@ struct Table<uint32_t> {
     }
     return kNoSlot;
   }
-  // Find after a barrier that ended all inserts of this chunk.
+  // Find after a barrier that ended all inserts of this chunk (the sweep may be writing
+  // position halves meanwhile; codes never change once claimed).
   __device__ uint32_t find(uint32_t code) const {
     uint32_t s = code_hash32(code) & mask;
     for (uint32_t n = 0; n <= mask; ++n, s = (s + 1) & mask) {
-      const unsigned long long cur = w[s];
+      const unsigned long long cur = *reinterpret_cast<volatile unsigned long long*>(w + s);
       if (cur == ~0ull) return kNoSlot;
       if (static_cast<uint32_t>(cur) == code) return s;
     }
@@ -183,7 +195,7 @@ struct Table<uint64_t> {
   __device__ uint32_t find(uint64_t c) const {
     uint32_t s = code_hash32(c) & mask;
     for (uint32_t n = 0; n <= mask; ++n, s = (s + 1) & mask) {
-      if (m[s] == kEmpty) return kNoSlot;
+      if (*reinterpret_cast<volatile uint32_t*>(m + s) == kEmpty) return kNoSlot;
       if (code[s] == c) return s;
     }
     return kNoSlot;
@@ -213,20 +225,40 @@ struct Params {
   int list_mode;  // global path: 1 = streams from ovf_list, 0 = all streams
 };
 
+__device__ __forceinline__ void prep_barrier() {
+  asm volatile("bar.sync 1, %0;" ::"n"(kPrepThreads) : "memory");
+}
+
+// Gatherers: indices of one chunk to global memory, then its value rows, kGatherUnroll vector
+// loads in flight per thread before the streaming stores.
 template <typename Vec>
 __device__ __forceinline__ void gather_chunk(const Params& p, int64_t row0, int64_t base, int cnt,
-                                             const int32_t* src_s, int tid) {
+                                             const int32_t* src_s, int gtid) {
+  if (p.src != nullptr) {
+    for (int i = gtid; i < cnt; i += kGathThreads) p.src[row0 + base + i] = src_s[i];
+  }
+  if (p.out == nullptr) return;
   const int wpr = static_cast<int>(p.vbytes / static_cast<int64_t>(sizeof(Vec)));
   const int total = cnt * wpr;
   const Vec* v = reinterpret_cast<const Vec*>(p.v) + row0 * wpr;
   Vec* o = reinterpret_cast<Vec*>(p.out) + (row0 + base) * wpr;
-  for (int w = tid; w < total; w += kThreads) {
-    const int r = w / wpr;
-    const int k = w - r * wpr;
-    const int32_t s = src_s[r];
-    Vec val = zero_vec<Vec>();
-    if (s >= 0) val = __ldg(v + static_cast<int64_t>(s) * wpr + k);
-    store_stream(o + w, val);
+  for (int w0 = gtid; w0 < total; w0 += kGathThreads * kGatherUnroll) {
+    Vec val[kGatherUnroll];
+#pragma unroll
+    for (int u = 0; u < kGatherUnroll; ++u) {
+      const int w = w0 + u * kGathThreads;
+      val[u] = zero_vec<Vec>();
+      if (w < total) {
+        const int r = w / wpr;
+        const int32_t s = src_s[r];
+        if (s >= 0) val[u] = __ldg(v + static_cast<int64_t>(s) * wpr + (w - r * wpr));
+      }
+    }
+#pragma unroll
+    for (int u = 0; u < kGatherUnroll; ++u) {
+      const int w = w0 + u * kGathThreads;
+      if (w < total) store_stream(o + w, val[u]);
+    }
   }
 }
 
@@ -235,10 +267,10 @@ __global__ void __launch_bounds__(kThreads) match_kernel(const Params p) {
   extern __shared__ __align__(16) unsigned char smem[];
   constexpr uint32_t kCap = 1u << SmemCap<CodeT>::kLog2;
   const size_t table_bytes = kSmemTable ? kCap * Table<CodeT>::kBytesPerSlot : 0;
-  uint32_t* kslot_s = reinterpret_cast<uint32_t*>(smem + table_bytes);
-  uint32_t* qslot_s = kslot_s + kChunk;
-  int32_t* src_s = reinterpret_cast<int32_t*>(qslot_s + kChunk);
-  __shared__ uint32_t s_used, s_ovf, s_lt;
+  uint32_t* kbuf = reinterpret_cast<uint32_t*>(smem + table_bytes);  // [2][kChunk] key slots
+  uint32_t* qbuf = kbuf + 2 * kChunk;                                // [2][kChunk] query words
+  int32_t* sbuf = reinterpret_cast<int32_t*>(qbuf + 2 * kChunk);     // [2][kChunk] src
+  __shared__ uint32_t s_used, s_ovf, s_abort, s_lt;
 
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const CodeT* qc = static_cast<const CodeT*>(p.qc);
@@ -251,6 +283,7 @@ __global__ void __launch_bounds__(kThreads) match_kernel(const Params p) {
     tab.init(p.gtables + static_cast<int64_t>(blockIdx.x) * p.gtable_bytes, 1u << p.gcap_log2);
   }
   const int64_t n_work = (!kSmemTable && p.list_mode) ? static_cast<int64_t>(*p.ovf_count) : p.N;
+  const int64_t n_chunks = (p.T + kChunk - 1) / kChunk;
 
   for (int64_t wi = blockIdx.x; wi < n_work; wi += gridDim.x) {
     const int64_t n = (!kSmemTable && p.list_mode) ? static_cast<int64_t>(p.ovf_list[wi]) : wi;
@@ -259,77 +292,102 @@ __global__ void __launch_bounds__(kThreads) match_kernel(const Params p) {
     if (tid == 0) {
       s_used = 0;
       s_ovf = 0;
+      s_abort = 0;
       s_lt = 0;
     }
     __syncthreads();
 
-    bool overflowed = false;
-    for (int64_t base = 0; base < p.T; base += kChunk) {
-      const int cnt = static_cast<int>(min(static_cast<int64_t>(kChunk), p.T - base));
-      const int cnt32 = (cnt + 31) & ~31;
-
-      // 1. insert this chunk's key codes
-      for (int i = tid; i < cnt32; i += kThreads) {
-        const bool valid = i < cnt;
-        const CodeT c = valid ? kc[row0 + base + i] : CodeT(0);
-        const uint32_t vm = __ballot_sync(kFullMask, valid);
-        if (valid) {
-          const uint32_t peers = __match_any_sync(vm, c);
-          const int leader = __ffs(peers) - 1;
-          uint32_t slot = kNoSlot, claimed = 0;
-          if (lane == leader) {
-            slot = tab.insert(c, claimed, p.status);
-            if (claimed) atomicAdd(&s_used, 1u);
-            if (slot == kNoSlot) s_ovf = 1;
-          }
-          slot = __shfl_sync(vm, slot, leader);
-          kslot_s[i] = slot;
-        }
-      }
-      __syncthreads();
-      if (s_ovf != 0 || (kSmemTable && s_used > overflow_limit<CodeT>())) {
-        overflowed = true;
-        break;
-      }
-
-      // 2. look up this chunk's query codes
-      for (int i = tid; i < cnt; i += kThreads) qslot_s[i] = tab.find(qc[row0 + base + i]);
-      __syncthreads();
-
-      // 3. in-step matches and last-key-of-slot flags, one warp per 32-position step
-      const int nsteps = cnt32 >> 5;
-      for (int s = warp; s < nsteps; s += kWarps) {
-        const int i = s * 32 + lane;
-        const bool valid = i < cnt;
-        const uint32_t ks = valid ? kslot_s[i] : kBadKey;
-        const uint32_t qs = valid ? qslot_s[i] : kNoSlot;
-        uint32_t mm = 0;
+    bool aborted = false;
+    for (int64_t r = 0; r < n_chunks + 2; ++r) {
+      if (warp >= kPrepWarp0 && warp < kPrepWarp0 + kPrepWarps && r < n_chunks) {
+        // ------------------------------------------------ preparers: chunk r
+        const int ptid = tid - kPrepWarp0 * 32;
+        const int pwarp = warp - kPrepWarp0;
+        const int64_t base = r * kChunk;
+        const int cnt = static_cast<int>(min(static_cast<int64_t>(kChunk), p.T - base));
+        const int cnt32 = (cnt + 31) & ~31;
+        uint32_t* kb = kbuf + (r & 1) * kChunk;
+        uint32_t* qb = qbuf + (r & 1) * kChunk;
+        CodeT kr[kPerPrep], qr[kPerPrep];
 #pragma unroll
-        for (int j = 0; j < 32; ++j) mm |= static_cast<uint32_t>(__shfl_sync(kFullMask, ks, j) == qs) << j;
-        mm &= lanemask_lt();
-        const uint32_t peers = __match_any_sync(kFullMask, ks);
-        const bool klast = (peers >> lane) == 1u;
-        if (valid) {
-          qslot_s[i] = (qs == kNoSlot) ? kNoSlot : (mm ? (kInStep | (31u - __clz(mm))) : qs);
-          kslot_s[i] = klast ? ks : kNoSlot;
+        for (int u = 0; u < kPerPrep; ++u) {
+          const int i = ptid + u * kPrepThreads;
+          kr[u] = i < cnt ? kc[row0 + base + i] : CodeT(0);
+          qr[u] = i < cnt ? qc[row0 + base + i] : CodeT(0);
         }
-      }
-      __syncthreads();
-
-      // 4. the ordered sweep (one warp)
-      if (warp == 0) {
+        // 1. insert the key codes
+#pragma unroll
+        for (int u = 0; u < kPerPrep; ++u) {
+          const int i = ptid + u * kPrepThreads;
+          if (i < cnt32) {  // uniform per warp: a warp covers an aligned run of 32 positions
+            const bool valid = i < cnt;
+            const uint32_t vm = __ballot_sync(kFullMask, valid);
+            if (valid) {
+              const uint32_t peers = __match_any_sync(vm, kr[u]);
+              const int leader = __ffs(peers) - 1;
+              uint32_t slot = kNoSlot, claimed = 0;
+              if (lane == leader) {
+                slot = tab.insert(kr[u], claimed, p.status);
+                if (claimed) atomicAdd(&s_used, 1u);
+                if (slot == kNoSlot) s_ovf = 1;
+              }
+              kb[i] = __shfl_sync(vm, slot, leader);
+            }
+          }
+        }
+        prep_barrier();
+        if (s_ovf != 0 || (kSmemTable && s_used > overflow_limit<CodeT>())) {
+          if (ptid == 0) s_abort = 1;
+        } else {
+          // 2. look up the query codes
+#pragma unroll
+          for (int u = 0; u < kPerPrep; ++u) {
+            const int i = ptid + u * kPrepThreads;
+            if (i < cnt) qb[i] = tab.find(qr[u]);
+          }
+          prep_barrier();
+          // 3. in-step matches and last-key-of-slot flags, one warp per 32-position step
+          const int nsteps = cnt32 >> 5;
+          for (int s = pwarp; s < nsteps; s += kPrepWarps) {
+            const int i = s * 32 + lane;
+            const bool valid = i < cnt;
+            const uint32_t ks = valid ? kb[i] : kBadKey;
+            const uint32_t qs = valid ? qb[i] : kNoSlot;
+            uint32_t mm = 0;
+#pragma unroll
+            for (int j = 0; j < 32; ++j) {
+              mm |= static_cast<uint32_t>(__shfl_sync(kFullMask, ks, j) == qs) << j;
+            }
+            mm &= lanemask_lt();
+            const uint32_t peers = __match_any_sync(kFullMask, ks);
+            const bool klast = (peers >> lane) == 1u;
+            if (valid) {
+              qb[i] = (qs == kNoSlot) ? kNoSlot : (mm ? (kInStep | (31u - __clz(mm))) : qs);
+              kb[i] = klast ? ks : kNoSlot;
+            }
+          }
+        }
+      } else if (warp == kSweepWarp && r >= 1 && r <= n_chunks) {
+        // ------------------------------------------------ sweeper: chunk r-1, in order
+        const int64_t c = r - 1;
+        const int64_t base = c * kChunk;
+        const int cnt = static_cast<int>(min(static_cast<int64_t>(kChunk), p.T - base));
+        const int nsteps = (cnt + 31) >> 5;
+        const uint32_t* kb = kbuf + (c & 1) * kChunk;
+        const uint32_t* qb = qbuf + (c & 1) * kChunk;
+        int32_t* sb = sbuf + (c & 1) * kChunk;
         uint32_t qn = kNoSlot, kn = kNoSlot;
         if (lane < cnt) {
-          qn = qslot_s[lane];
-          kn = kslot_s[lane];
+          qn = qb[lane];
+          kn = kb[lane];
         }
         for (int s = 0; s < nsteps; ++s) {
           const int i = s * 32 + lane;
           const bool valid = i < cnt;
           const uint32_t qv = qn, kv = kn;
           if (i + 32 < cnt) {
-            qn = qslot_s[i + 32];
-            kn = kslot_s[i + 32];
+            qn = qb[i + 32];
+            kn = kb[i + 32];
           }
           int32_t sv = -1;
           if (valid && qv != kNoSlot) {
@@ -340,25 +398,28 @@ __global__ void __launch_bounds__(kThreads) match_kernel(const Params p) {
               sv = (m == kNone) ? -1 : static_cast<int32_t>(m);
             }
           }
-          if (valid) src_s[i] = sv;
+          if (valid) sb[i] = sv;
           __syncwarp();
           if (valid && kv != kNoSlot) {
             *reinterpret_cast<volatile uint32_t*>(tab.meta(kv)) = static_cast<uint32_t>(base + i);
           }
           __syncwarp();
         }
+      } else if (warp >= kGathWarp0 && r >= 2) {
+        // ------------------------------------------------ gatherers: chunk r-2
+        const int64_t c = r - 2;
+        const int64_t base = c * kChunk;
+        const int cnt = static_cast<int>(min(static_cast<int64_t>(kChunk), p.T - base));
+        gather_chunk<Vec>(p, row0, base, cnt, sbuf + (c & 1) * kChunk, tid - kGathWarp0 * 32);
       }
       __syncthreads();
-
-      // 5. indices and values out
-      if (p.src != nullptr) {
-        for (int i = tid; i < cnt; i += kThreads) p.src[row0 + base + i] = src_s[i];
+      if (s_abort != 0) {
+        aborted = true;
+        break;
       }
-      if (p.out != nullptr) gather_chunk<Vec>(p, row0, base, cnt, src_s, tid);
-      __syncthreads();
     }
 
-    if (overflowed) {
+    if (aborted) {
       if (tid == 0) {
         if (kSmemTable) {
           const uint32_t k = atomicAdd(p.ovf_count, 1u);
@@ -393,7 +454,7 @@ __global__ void __launch_bounds__(kThreads) match_kernel(const Params p) {
 }
 
 // ---------------------------------------------------------------- host side
-constexpr size_t kChunkSmem = 3 * kChunk * sizeof(uint32_t);
+constexpr size_t kChunkSmem = 6 * kChunk * sizeof(uint32_t);
 constexpr int64_t kMaxOverflowTables = 64;
 constexpr uint64_t kOverflowTableBudget = uint64_t(1) << 30;  // bytes of global tables
 constexpr int64_t kFastMaxT = int64_t(1) << 20;               // beyond: global path directly
