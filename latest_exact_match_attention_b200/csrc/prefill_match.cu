@@ -53,6 +53,7 @@ constexpr int kPrepThreads = kPrepWarps * 32;
 constexpr int kGathThreads = kGathWarps * 32;
 constexpr int kPerPrep = (kChunk + kPrepThreads - 1) / kPrepThreads;
 constexpr int kGatherUnroll = 8;
+constexpr int kMini = 64;  // per-warp code -> lane-mask hash of one step's key codes
 static_assert((kPrepWarp0 + kPrepWarps) * 32 <= kThreads && kGathWarp0 * 32 + kGathThreads == kThreads, "roles");
 
 constexpr uint32_t kEmpty = 0xFFFFFFFFu;   // meta of a free slot
@@ -223,7 +224,15 @@ struct Params {
   int64_t gtable_bytes;
   uint32_t gcap_log2;
   int list_mode;  // global path: 1 = streams from ovf_list, 0 = all streams
+  int div_shift;       // log2(words per row) when a power of two, else -1
+  uint32_t div_magic;  // floor(2^32 / words per row) + 1 when usable, else 0
 };
+
+template <typename CodeT>
+__device__ __forceinline__ uint32_t mini_hash(CodeT c) {
+  return code_hash32(c) >> (32 - 6);  // top bits: independent of the table's low-bit home
+}
+static_assert(kMini == 64, "mini_hash yields 6 bits");
 
 __device__ __forceinline__ void prep_barrier() {
   asm volatile("bar.sync 1, %0;" ::"n"(kPrepThreads) : "memory");
@@ -242,6 +251,10 @@ __device__ __forceinline__ void gather_chunk(const Params& p, int64_t row0, int6
   const int total = cnt * wpr;
   const Vec* v = reinterpret_cast<const Vec*>(p.v) + row0 * wpr;
   Vec* o = reinterpret_cast<Vec*>(p.out) + (row0 + base) * wpr;
+  // row of word w: a shift for power-of-two rows, else a multiply-high by a magic reciprocal
+  // (exact for w * wpr < 2^32, which the host guarantees), else a division
+  const int dshift = p.div_shift;
+  const uint32_t dmagic = p.div_magic;
   for (int w0 = gtid; w0 < total; w0 += kGathThreads * kGatherUnroll) {
     Vec val[kGatherUnroll];
 #pragma unroll
@@ -249,7 +262,9 @@ __device__ __forceinline__ void gather_chunk(const Params& p, int64_t row0, int6
       const int w = w0 + u * kGathThreads;
       val[u] = zero_vec<Vec>();
       if (w < total) {
-        const int r = w / wpr;
+        const int r = dshift >= 0 ? (w >> dshift)
+                                  : (dmagic ? static_cast<int>(__umulhi(static_cast<uint32_t>(w), dmagic))
+                                            : w / wpr);
         const int32_t s = src_s[r];
         if (s >= 0) val[u] = __ldg(v + static_cast<int64_t>(s) * wpr + (w - r * wpr));
       }
@@ -270,6 +285,8 @@ __global__ void __launch_bounds__(kThreads) match_kernel(const Params p) {
   uint32_t* kbuf = reinterpret_cast<uint32_t*>(smem + table_bytes);  // [2][kChunk] key slots
   uint32_t* qbuf = kbuf + 2 * kChunk;                                // [2][kChunk] query words
   int32_t* sbuf = reinterpret_cast<int32_t*>(qbuf + 2 * kChunk);     // [2][kChunk] src
+  CodeT* mini_key = reinterpret_cast<CodeT*>(sbuf + 2 * kChunk);      // [kPrepWarps][kMini]
+  uint32_t* mini_mask = reinterpret_cast<uint32_t*>(mini_key + kPrepWarps * kMini);
   __shared__ uint32_t s_used, s_ovf, s_abort, s_lt;
 
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
@@ -282,6 +299,7 @@ __global__ void __launch_bounds__(kThreads) match_kernel(const Params p) {
   } else {
     tab.init(p.gtables + static_cast<int64_t>(blockIdx.x) * p.gtable_bytes, 1u << p.gcap_log2);
   }
+  for (int i = tid; i < kPrepWarps * kMini; i += kThreads) mini_mask[i] = 0u;  // 0 = free entry
   const int64_t n_work = (!kSmemTable && p.list_mode) ? static_cast<int64_t>(*p.ovf_count) : p.N;
   const int64_t n_chunks = (p.T + kChunk - 1) / kChunk;
 
@@ -308,6 +326,8 @@ __global__ void __launch_bounds__(kThreads) match_kernel(const Params p) {
         const int cnt32 = (cnt + 31) & ~31;
         uint32_t* kb = kbuf + (r & 1) * kChunk;
         uint32_t* qb = qbuf + (r & 1) * kChunk;
+        CodeT* mkey = mini_key + pwarp * kMini;
+        uint32_t* mmask = mini_mask + pwarp * kMini;
         CodeT kr[kPerPrep], qr[kPerPrep];
 #pragma unroll
         for (int u = 0; u < kPerPrep; ++u) {
@@ -315,13 +335,18 @@ __global__ void __launch_bounds__(kThreads) match_kernel(const Params p) {
           kr[u] = i < cnt ? kc[row0 + base + i] : CodeT(0);
           qr[u] = i < cnt ? qc[row0 + base + i] : CodeT(0);
         }
-        // 1. insert the key codes
+        // 1. One aligned 32-position step per warp-iteration. The lanes holding one key code
+        //    (match_any) elect their lowest lane, which inserts the code into the table and
+        //    publishes code -> lane mask in the warp's 64-entry mini hash; each query lane
+        //    then finds the latest key lane j < i of its code in the step, if any.
+        uint32_t qpend = 0;  // bit u: the query of iteration u needs a table lookup
 #pragma unroll
         for (int u = 0; u < kPerPrep; ++u) {
           const int i = ptid + u * kPrepThreads;
           if (i < cnt32) {  // uniform per warp: a warp covers an aligned run of 32 positions
             const bool valid = i < cnt;
             const uint32_t vm = __ballot_sync(kFullMask, valid);
+            uint32_t mine = kMini;  // mini-hash entry this lane claimed
             if (valid) {
               const uint32_t peers = __match_any_sync(vm, kr[u]);
               const int leader = __ffs(peers) - 1;
@@ -330,41 +355,50 @@ __global__ void __launch_bounds__(kThreads) match_kernel(const Params p) {
                 slot = tab.insert(kr[u], claimed, p.status);
                 if (claimed) atomicAdd(&s_used, 1u);
                 if (slot == kNoSlot) s_ovf = 1;
+                uint32_t h = mini_hash(kr[u]);
+                for (int t = 0; t < kMini; ++t, h = (h + 1) & (kMini - 1)) {
+                  if (atomicCAS(mmask + h, 0u, peers) == 0u) {
+                    mkey[h] = kr[u];
+                    mine = h;
+                    break;
+                  }
+                }
               }
-              kb[i] = __shfl_sync(vm, slot, leader);
+              slot = __shfl_sync(vm, slot, leader);
+              kb[i] = ((peers >> lane) == 1u) ? slot : kNoSlot;  // last key lane of its code
             }
+            __syncwarp();
+            if (valid) {
+              uint32_t mm = 0;
+              uint32_t h = mini_hash(qr[u]);
+              for (int t = 0; t < kMini; ++t, h = (h + 1) & (kMini - 1)) {
+                const uint32_t m = mmask[h];
+                if (m == 0u) break;
+                if (mkey[h] == qr[u]) {
+                  mm = m & lanemask_lt();
+                  break;
+                }
+              }
+              if (mm) {
+                qb[i] = kInStep | (31u - __clz(mm));
+              } else {
+                qpend |= 1u << u;
+              }
+            }
+            __syncwarp();
+            if (mine < kMini) mmask[mine] = 0u;
+            __syncwarp();
           }
         }
         prep_barrier();
         if (s_ovf != 0 || (kSmemTable && s_used > overflow_limit<CodeT>())) {
           if (ptid == 0) s_abort = 1;
         } else {
-          // 2. look up the query codes
+          // 2. queries without an in-step match read their code's slot (or none: then no key
+          //    of the code has appeared up to the end of this chunk, and the answer is -1)
 #pragma unroll
           for (int u = 0; u < kPerPrep; ++u) {
-            const int i = ptid + u * kPrepThreads;
-            if (i < cnt) qb[i] = tab.find(qr[u]);
-          }
-          prep_barrier();
-          // 3. in-step matches and last-key-of-slot flags, one warp per 32-position step
-          const int nsteps = cnt32 >> 5;
-          for (int s = pwarp; s < nsteps; s += kPrepWarps) {
-            const int i = s * 32 + lane;
-            const bool valid = i < cnt;
-            const uint32_t ks = valid ? kb[i] : kBadKey;
-            const uint32_t qs = valid ? qb[i] : kNoSlot;
-            uint32_t mm = 0;
-#pragma unroll
-            for (int j = 0; j < 32; ++j) {
-              mm |= static_cast<uint32_t>(__shfl_sync(kFullMask, ks, j) == qs) << j;
-            }
-            mm &= lanemask_lt();
-            const uint32_t peers = __match_any_sync(kFullMask, ks);
-            const bool klast = (peers >> lane) == 1u;
-            if (valid) {
-              qb[i] = (qs == kNoSlot) ? kNoSlot : (mm ? (kInStep | (31u - __clz(mm))) : qs);
-              kb[i] = klast ? ks : kNoSlot;
-            }
+            if ((qpend >> u) & 1u) qb[ptid + u * kPrepThreads] = tab.find(qr[u]);
           }
         }
       } else if (warp == kSweepWarp && r >= 1 && r <= n_chunks) {
@@ -462,7 +496,7 @@ constexpr int64_t kFastMaxT = int64_t(1) << 20;               // beyond: global 
 template <typename CodeT>
 size_t smem_bytes(bool smem_table) {
   return (smem_table ? (size_t(1) << SmemCap<CodeT>::kLog2) * Table<CodeT>::kBytesPerSlot : 0) +
-         kChunkSmem;
+         kChunkSmem + kPrepWarps * kMini * (sizeof(CodeT) + sizeof(uint32_t));
 }
 
 struct Plan {
@@ -512,6 +546,16 @@ int run(const MatchLaunch& a, const Plan& pl, const DeviceInfo& dev) {
   p.lt_pos = a.lt_pos;
   p.lt_count = a.lt_count;
   p.status = a.status;
+  {
+    const int64_t wpr = a.out ? a.vbytes / static_cast<int64_t>(sizeof(Vec)) : 1;
+    p.div_shift = -1;
+    p.div_magic = 0;
+    if ((wpr & (wpr - 1)) == 0) {
+      p.div_shift = log2_exact(static_cast<uint64_t>(wpr));
+    } else if (static_cast<uint64_t>(kChunk) * wpr * wpr < (uint64_t(1) << 32)) {
+      p.div_magic = static_cast<uint32_t>(0xFFFFFFFFull / static_cast<uint64_t>(wpr) + 1);
+    }
+  }
   unsigned char* ws = static_cast<unsigned char*>(a.ws);
   if (pl.global) {
     p.ovf_count = reinterpret_cast<uint32_t*>(ws);

@@ -112,7 +112,7 @@ def test_store_vs_oracle_store_random(cuda):
     """Many partitions sharing a small code space, capacity tight: the GPU store and the
     oracle store agree call by call, including the counts."""
     rng = np.random.default_rng(17)
-    P, T, cap = 300, 40, 14000
+    P, T, cap = 300, 40, 20000
     tab = oracle.new_table(cap, 16)
     st = HashStore(8, groups=P, dtype=torch.float16, capacity=cap, device=cuda)
     for step in range(6):
