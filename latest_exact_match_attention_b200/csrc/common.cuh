@@ -115,3 +115,7 @@ inline int log2_exact(uint64_t p) {
 inline size_t round_up(size_t x, size_t a) { return (x + a - 1) / a * a; }
 
 }  // namespace lema
+
+namespace lema {
+__host__ __device__ constexpr size_t round_up16(size_t x) { return (x + 15) / 16 * 16; }
+}  // namespace lema

@@ -6,33 +6,39 @@
 // one pass in position order with a hash table of the stream's key codes in shared memory.
 //
 // One CTA owns one stream at a time (persistent grid-stride over streams) and walks it in
-// chunks of kChunk positions through a three-stage pipeline of warp roles; stage boundaries are
-// CTA-wide barriers ("rounds"), and in round r:
+// chunks of kChunk positions through a three-stage pipeline of warp roles. Stage boundaries
+// are CTA-wide barriers ("rounds"); in round r:
 //
-//   preparers (7 warps) -- chunk r
-//     1. insert  the chunk's key codes (loaded in one batch) are inserted into -- or found in --
-//                the stream's table, giving each a SLOT id. Equal codes of a warp are first
-//                deduplicated with match_any, so one lane per distinct code touches the table.
-//     2. lookup  each query code is looked up; a code that no key up to the end of this chunk
-//                has used gets no slot, and -1 is already its final answer.
-//     3. in-step inside each 32-position step, the latest key lane j < i with the query's
-//                slot (32 shuffles), and whether each key lane is the last of its slot.
-//   sweeper (1 warp) -- chunk r-1, the only ordered part: 32 positions per step, a query with
-//                an in-step match takes it, any other reads meta[slot] (the position of the
-//                latest key of its slot swept so far); then the last key lane of each slot
-//                writes its position into meta[slot]. Two __syncwarp()s per step order the
-//                reads before the step's writes and the writes before the next step's reads.
+//   preparers (7 warps) -- chunk r, one aligned 32-position step per warp-iteration:
+//     * the lanes holding one key code (match_any) elect their lowest lane, which inserts the
+//       code into -- or finds it in -- the stream's table, giving it a SLOT id; the step's
+//       last lane of each code is marked (only it writes the sweep state);
+//     * each query lane finds the latest key lane j < i with its code in the same step, by
+//       walking the step's distinct key codes with shuffles;
+//     * after a barrier that ends the chunk's inserts, every query without an in-step match
+//       looks its code up: no slot means no key of that code up to the end of the chunk, so
+//       -1 is already its answer.
+//   sweeper (1 warp) -- chunk r-1, the only ordered part. 32 positions per step: a query with
+//       an in-step match takes it, any other reads meta[slot] (the position of the latest key
+//       of its slot swept so far); then each slot's last key lane writes its position into
+//       meta[slot]. Two __syncwarp()s per step order the reads before the step's writes and
+//       the writes before the next step's reads. The answers overwrite the query words.
 //   gatherers (8 warps) -- chunk r-2: indices out, value rows copied with 16-byte vectors,
-//                eight loads in flight per thread, streaming stores; zeros for misses.
+//       eight loads in flight per thread, streaming stores; zeros for misses.
 //
-// The stages touch the table without conflict: inserts only claim free words, lookups compare
-// codes only, and the sweep writes the position half of words claimed in earlier rounds.
+// The stages touch the table without conflict: inserts only claim free code words, lookups
+// read code words, and the sweep writes the meta words of slots claimed in earlier rounds.
 //
-// The shared-memory table has a fixed capacity (kSmemCap slots). A stream whose distinct key
-// codes would load it beyond kOverflowFrac is handed over whole to the same kernel running
-// with a CTA-private table in global memory sized 2*T (the overflow path): it appends itself
-// to an overflow list in the workspace, and a second launch processes the list. No input
-// can make the result wrong; an unusual one only takes the slower path.
+// The table is bucketed: 8 slots per bucket, read with two (four for 64-bit codes) vector
+// loads, linear probing over buckets. Codes and metas are separate arrays; a claim is one
+// compare-and-swap of a free code word (all ones), and the all-ones code itself lives in a
+// dedicated side slot, so every code value is an ordinary key and no reader ever waits.
+//
+// The shared-memory table has a fixed capacity. A stream whose distinct key codes would load
+// it beyond kOverflowFrac is handed over whole to the same kernel running with a CTA-private
+// table in global memory sized for 2*T (the overflow path): it appends itself to an overflow
+// list in the workspace, and a second launch processes the list. No input can make the result
+// wrong; an unusual one only takes the slower path.
 #include <cuda_runtime.h>
 
 #include <algorithm>
@@ -46,158 +52,154 @@ namespace k2 {
 
 constexpr int kThreads = 512;
 constexpr int kChunk = 2048;
-constexpr int kSweepWarp = 0;                        // warp 0: the ordered sweep
-constexpr int kPrepWarp0 = 1, kPrepWarps = 7;        // warps 1..7: insert / lookup / in-step
-constexpr int kGathWarp0 = 8, kGathWarps = 8;        // warps 8..15: indices and rows out
+constexpr int kSweepWarp = 0;                  // warp 0: the ordered sweep
+constexpr int kPrepWarp0 = 1, kPrepWarps = 7;  // warps 1..7: insert / in-step / lookup
+constexpr int kGathWarp0 = 8, kGathWarps = 8;  // warps 8..15: indices and rows out
 constexpr int kPrepThreads = kPrepWarps * 32;
 constexpr int kGathThreads = kGathWarps * 32;
 constexpr int kPerPrep = (kChunk + kPrepThreads - 1) / kPrepThreads;
 constexpr int kGatherUnroll = 8;
-constexpr int kMini = 64;  // per-warp code -> lane-mask hash of one step's key codes
-static_assert((kPrepWarp0 + kPrepWarps) * 32 <= kThreads && kGathWarp0 * 32 + kGathThreads == kThreads, "roles");
+constexpr int kBucket = 8;  // slots per table bucket
+static_assert((kPrepWarp0 + kPrepWarps) * 32 <= kThreads && kGathWarp0 * 32 + kGathThreads == kThreads,
+              "warp roles");
 
-constexpr uint32_t kEmpty = 0xFFFFFFFFu;   // meta of a free slot
-constexpr uint32_t kLocked = 0xFFFFFFFEu;  // meta of a slot being claimed (64-bit codes only)
-constexpr uint32_t kNone = 0xFFFFFFFDu;    // code present, no key position swept yet
+constexpr uint32_t kNone = 0xFFFFFFFDu;    // meta: code present, no key position swept yet
 constexpr uint32_t kNoSlot = 0xFFFFFFFFu;  // query code absent from the table
-constexpr uint32_t kBadKey = 0xFFFFFFFEu;  // key slot of an out-of-range lane
-constexpr uint32_t kInStep = 0x80000000u;  // query slot word: in-step match, lane in low bits
-constexpr uint32_t kSpinLimit = 1u << 22;  // bound on waiting for a LOCKED slot
+constexpr uint32_t kInStep = 0x80000000u;  // query word: in-step match, lane in the low bits
 
-// Shared-memory table capacity (slots) per code width, and the load above which a stream
+// Shared-memory table capacity (slots) per code width; above kOverflowFrac of it a stream
 // moves to the global-memory path.
 template <typename CodeT>
 struct SmemCap;
 template <>
 struct SmemCap<uint32_t> {
-  static constexpr uint32_t kLog2 = 13;
+  static constexpr uint32_t kSlots = 8192;
 };
 template <>
 struct SmemCap<uint64_t> {
-  static constexpr uint32_t kLog2 = 12;
+  static constexpr uint32_t kSlots = 4096;
 };
 constexpr double kOverflowFrac = 0.75;
 
 template <typename CodeT>
 __host__ __device__ constexpr uint32_t overflow_limit() {
-  return static_cast<uint32_t>((1u << SmemCap<CodeT>::kLog2) * kOverflowFrac);
+  return static_cast<uint32_t>(SmemCap<CodeT>::kSlots * kOverflowFrac);
 }
 
-// ---------------------------------------------------------------- the tables
-// Slot -> (code, meta). meta is kEmpty, kLocked, kNone, or the stream position of the latest
-// key with that code swept so far.
+// ---------------------------------------------------------------- the table
+// Volatile vector loads of one bucket's code words (generic addresses: the table lives in
+// shared memory on the fast path and in global memory on the overflow path).
+__device__ __forceinline__ void load_bucket(const uint32_t* p, uint32_t (&c)[kBucket]) {
+  asm volatile("ld.volatile.v4.u32 {%0, %1, %2, %3}, [%4];"
+               : "=r"(c[0]), "=r"(c[1]), "=r"(c[2]), "=r"(c[3]) : "l"(p) : "memory");
+  asm volatile("ld.volatile.v4.u32 {%0, %1, %2, %3}, [%4];"
+               : "=r"(c[4]), "=r"(c[5]), "=r"(c[6]), "=r"(c[7]) : "l"(p + 4) : "memory");
+}
+__device__ __forceinline__ void load_bucket(const uint64_t* p, uint64_t (&c)[kBucket]) {
+#pragma unroll
+  for (int k = 0; k < kBucket; k += 2) {
+    unsigned long long a, b;
+    asm volatile("ld.volatile.v2.u64 {%0, %1}, [%2];" : "=l"(a), "=l"(b) : "l"(p + k) : "memory");
+    c[k] = a;
+    c[k + 1] = b;
+  }
+}
+__device__ __forceinline__ uint32_t cas_code(uint32_t* p, uint32_t cmp, uint32_t val) {
+  return atomicCAS(p, cmp, val);
+}
+__device__ __forceinline__ uint64_t cas_code(uint64_t* p, uint64_t cmp, uint64_t val) {
+  return atomicCAS(reinterpret_cast<unsigned long long*>(p), static_cast<unsigned long long>(cmp),
+                   static_cast<unsigned long long>(val));
+}
+
+// Slot -> (code, meta). Slots [0, cap) form cap / kBucket buckets; slot `cap` holds the
+// all-ones code, whose presence is the side flag. meta is kNone or the stream position of the
+// latest key with that code swept so far.
 template <typename CodeT>
-struct Table;
+struct Table {
+  static constexpr CodeT kFree = static_cast<CodeT>(~CodeT(0));
+  CodeT* code;     // [cap]
+  uint32_t* meta;  // [cap + 1]
+  uint32_t* side;  // 1 word: the all-ones code is present
+  uint32_t cap;
+  uint32_t bmask;  // buckets - 1
 
-// 32-bit codes: one 64-bit word per slot, code in the low half and meta in the high half, so
-// a claim is a single compare-and-swap of an all-ones (free) word and no reader ever waits.
-template <>
-struct Table<uint32_t> {
-  unsigned long long* w;
-  uint32_t mask;
-  static constexpr size_t kBytesPerSlot = 8;
-
-  __device__ void init(void* base, uint32_t cap) {
-    w = static_cast<unsigned long long*>(base);
-    mask = cap - 1;
+  __host__ __device__ static constexpr size_t bytes(uint32_t slots) {
+    return slots * sizeof(CodeT) + (slots + 1) * sizeof(uint32_t) + 16;
+  }
+  __device__ void init(void* base, uint32_t slots) {
+    cap = slots;
+    bmask = slots / kBucket - 1;
+    code = static_cast<CodeT*>(base);
+    meta = reinterpret_cast<uint32_t*>(code + cap);
+    side = meta + cap + 1;
   }
   __device__ void clear(int tid, int nthr) {
-    for (uint32_t s = tid; s <= mask; s += nthr) w[s] = ~0ull;
+    for (uint32_t s = tid; s < cap; s += nthr) code[s] = kFree;
+    for (uint32_t s = tid; s <= cap; s += nthr) meta[s] = kNone;
+    if (tid == 0) *side = 0;
   }
-  __device__ uint32_t* meta(uint32_t s) const { return reinterpret_cast<uint32_t*>(w + s) + 1; }
-  __device__ bool used(uint32_t s, uint32_t& code, uint32_t& m) const {
-    const unsigned long long x = w[s];
-    code = static_cast<uint32_t>(x);
-    m = static_cast<uint32_t>(x >> 32);
-    return x != ~0ull;
-  }
-  // Insert-or-find. Returns the slot, or kNoSlot when every slot was probed.
-  __device__ uint32_t insert(uint32_t code, uint32_t& claimed, uint32_t*) {
-    const unsigned long long fresh =
-        static_cast<unsigned long long>(code) | (static_cast<unsigned long long>(kNone) << 32);
-    uint32_t s = code_hash32(code) & mask;
-    for (uint32_t n = 0; n <= mask; ++n, s = (s + 1) & mask) {
-      unsigned long long cur = *reinterpret_cast<volatile unsigned long long*>(w + s);
-      if (cur == ~0ull) {
-        cur = atomicCAS(w + s, ~0ull, fresh);
-        if (cur == ~0ull) {
-          claimed = 1;
-          return s;
-        }
-      }
-      if (static_cast<uint32_t>(cur) == code) return s;
+  __device__ uint32_t* meta_of(uint32_t s) const { return meta + s; }
+  __device__ bool used(uint32_t s, CodeT& c, uint32_t& m) const {
+    m = meta[s];
+    if (s == cap) {
+      c = kFree;
+      return *side != 0;
     }
-    return kNoSlot;
-  }
-  // Find after a barrier that ended all inserts of this chunk (the sweep may be writing
-  // position halves meanwhile; codes never change once claimed).
-  __device__ uint32_t find(uint32_t code) const {
-    uint32_t s = code_hash32(code) & mask;
-    for (uint32_t n = 0; n <= mask; ++n, s = (s + 1) & mask) {
-      const unsigned long long cur = *reinterpret_cast<volatile unsigned long long*>(w + s);
-      if (cur == ~0ull) return kNoSlot;
-      if (static_cast<uint32_t>(cur) == code) return s;
-    }
-    return kNoSlot;
-  }
-};
-
-// 64-bit codes: codes and metas in two arrays. A claim CASes meta kEmpty -> kLocked, writes
-// the code, then publishes kNone; a prober that meets kLocked waits (bounded) for it.
-template <>
-struct Table<uint64_t> {
-  unsigned long long* code;
-  uint32_t* m;
-  uint32_t mask;
-  static constexpr size_t kBytesPerSlot = 12;
-
-  __device__ void init(void* base, uint32_t cap) {
-    code = static_cast<unsigned long long*>(base);
-    m = reinterpret_cast<uint32_t*>(code + cap);
-    mask = cap - 1;
-  }
-  __device__ void clear(int tid, int nthr) {
-    for (uint32_t s = tid; s <= mask; s += nthr) m[s] = kEmpty;
-  }
-  __device__ uint32_t* meta(uint32_t s) const { return m + s; }
-  __device__ bool used(uint32_t s, uint64_t& c, uint32_t& mm) const {
-    mm = m[s];
     c = code[s];
-    return mm != kEmpty;
+    return c != kFree;
   }
-  __device__ uint32_t insert(uint64_t c, uint32_t& claimed, uint32_t* status) {
-    uint32_t s = code_hash32(c) & mask;
-    for (uint32_t n = 0; n <= mask; ++n, s = (s + 1) & mask) {
-      uint32_t cur = *reinterpret_cast<volatile uint32_t*>(m + s);
-      if (cur == kEmpty) {
-        cur = atomicCAS(m + s, kEmpty, kLocked);
-        if (cur == kEmpty) {
-          *reinterpret_cast<volatile unsigned long long*>(code + s) = c;
-          __threadfence_block();
-          atomicExch(m + s, kNone);
-          claimed = 1;
-          return s;
+  // Insert-or-find. Returns the slot, or kNoSlot when every bucket was full.
+  __device__ uint32_t insert(CodeT c, uint32_t& claimed) {
+    if (c == kFree) {
+      claimed = atomicCAS(side, 0u, 1u) == 0u;
+      return cap;
+    }
+    uint32_t b = code_hash32(c) & bmask;
+    for (uint32_t n = 0; n <= bmask; ++n, b = (b + 1) & bmask) {
+      CodeT* bk = code + b * kBucket;
+      CodeT w[kBucket];
+      load_bucket(bk, w);
+#pragma unroll
+      for (int k = 0; k < kBucket; ++k) {
+        if (w[k] == c) return b * kBucket + k;
+      }
+#pragma unroll
+      for (int k = 0; k < kBucket; ++k) {
+        if (w[k] == kFree) {
+          const CodeT old = cas_code(bk + k, kFree, c);
+          if (old == kFree) {
+            claimed = 1;
+            return b * kBucket + k;
+          }
+          if (old == c) return b * kBucket + k;
+          // another code took slot k: the later slots are judged by their fresh contents
+#pragma unroll
+          for (int j = k + 1; j < kBucket; ++j) w[j] = *reinterpret_cast<volatile CodeT*>(bk + j);
+#pragma unroll
+          for (int j = k + 1; j < kBucket; ++j) {
+            if (w[j] == c) return b * kBucket + j;
+          }
         }
       }
-      if (cur == kLocked) {
-        uint32_t k = 0;
-        while ((cur = *reinterpret_cast<volatile uint32_t*>(m + s)) == kLocked && ++k < kSpinLimit) {
-        }
-        if (cur == kLocked) {
-          raise_status(status, LEMA_STATUS_PROBE_LIMIT);
-          return kNoSlot;
-        }
-      }
-      __threadfence_block();
-      if (*reinterpret_cast<volatile unsigned long long*>(code + s) == c) return s;
     }
     return kNoSlot;
   }
-  __device__ uint32_t find(uint64_t c) const {
-    uint32_t s = code_hash32(c) & mask;
-    for (uint32_t n = 0; n <= mask; ++n, s = (s + 1) & mask) {
-      if (*reinterpret_cast<volatile uint32_t*>(m + s) == kEmpty) return kNoSlot;
-      if (code[s] == c) return s;
+  // Find. A bucket with a free slot ends the search: codes fill a bucket's slots in order and
+  // reach a bucket only when the buckets before it on their chain were full.
+  __device__ uint32_t find(CodeT c) const {
+    if (c == kFree) return *reinterpret_cast<volatile uint32_t*>(side) ? cap : kNoSlot;
+    uint32_t b = code_hash32(c) & bmask;
+    for (uint32_t n = 0; n <= bmask; ++n, b = (b + 1) & bmask) {
+      CodeT w[kBucket];
+      load_bucket(code + b * kBucket, w);
+      bool open = false;
+#pragma unroll
+      for (int k = 0; k < kBucket; ++k) {
+        if (w[k] == c) return b * kBucket + k;
+        open |= (w[k] == kFree);
+      }
+      if (open) return kNoSlot;
     }
     return kNoSlot;
   }
@@ -222,17 +224,11 @@ struct Params {
   // global-memory tables (overflow path): one per CTA
   unsigned char* gtables;
   int64_t gtable_bytes;
-  uint32_t gcap_log2;
-  int list_mode;  // global path: 1 = streams from ovf_list, 0 = all streams
+  uint32_t gslots;
+  int list_mode;       // global path: 1 = streams from ovf_list, 0 = all streams
   int div_shift;       // log2(words per row) when a power of two, else -1
   uint32_t div_magic;  // floor(2^32 / words per row) + 1 when usable, else 0
 };
-
-template <typename CodeT>
-__device__ __forceinline__ uint32_t mini_hash(CodeT c) {
-  return code_hash32(c) >> (32 - 6);  // top bits: independent of the table's low-bit home
-}
-static_assert(kMini == 64, "mini_hash yields 6 bits");
 
 __device__ __forceinline__ void prep_barrier() {
   asm volatile("bar.sync 1, %0;" ::"n"(kPrepThreads) : "memory");
@@ -280,13 +276,10 @@ __device__ __forceinline__ void gather_chunk(const Params& p, int64_t row0, int6
 template <typename CodeT, bool kSmemTable, typename Vec>
 __global__ void __launch_bounds__(kThreads) match_kernel(const Params p) {
   extern __shared__ __align__(16) unsigned char smem[];
-  constexpr uint32_t kCap = 1u << SmemCap<CodeT>::kLog2;
-  const size_t table_bytes = kSmemTable ? kCap * Table<CodeT>::kBytesPerSlot : 0;
-  uint32_t* kbuf = reinterpret_cast<uint32_t*>(smem + table_bytes);  // [2][kChunk] key slots
-  uint32_t* qbuf = kbuf + 2 * kChunk;                                // [2][kChunk] query words
-  int32_t* sbuf = reinterpret_cast<int32_t*>(qbuf + 2 * kChunk);     // [2][kChunk] src
-  CodeT* mini_key = reinterpret_cast<CodeT*>(sbuf + 2 * kChunk);      // [kPrepWarps][kMini]
-  uint32_t* mini_mask = reinterpret_cast<uint32_t*>(mini_key + kPrepWarps * kMini);
+  constexpr uint32_t kCap = SmemCap<CodeT>::kSlots;
+  constexpr size_t kTableBytes = kSmemTable ? round_up16(Table<CodeT>::bytes(kCap)) : 0;
+  uint32_t* kbuf = reinterpret_cast<uint32_t*>(smem + kTableBytes);  // [2][kChunk] key slots
+  uint32_t* qbuf = kbuf + 2 * kChunk;  // [3][kChunk] query words, then the answers in place
   __shared__ uint32_t s_used, s_ovf, s_abort, s_lt;
 
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
@@ -297,9 +290,8 @@ __global__ void __launch_bounds__(kThreads) match_kernel(const Params p) {
   if (kSmemTable) {
     tab.init(smem, kCap);
   } else {
-    tab.init(p.gtables + static_cast<int64_t>(blockIdx.x) * p.gtable_bytes, 1u << p.gcap_log2);
+    tab.init(p.gtables + static_cast<int64_t>(blockIdx.x) * p.gtable_bytes, p.gslots);
   }
-  for (int i = tid; i < kPrepWarps * kMini; i += kThreads) mini_mask[i] = 0u;  // 0 = free entry
   const int64_t n_work = (!kSmemTable && p.list_mode) ? static_cast<int64_t>(*p.ovf_count) : p.N;
   const int64_t n_chunks = (p.T + kChunk - 1) / kChunk;
 
@@ -320,14 +312,11 @@ __global__ void __launch_bounds__(kThreads) match_kernel(const Params p) {
       if (warp >= kPrepWarp0 && warp < kPrepWarp0 + kPrepWarps && r < n_chunks) {
         // ------------------------------------------------ preparers: chunk r
         const int ptid = tid - kPrepWarp0 * 32;
-        const int pwarp = warp - kPrepWarp0;
         const int64_t base = r * kChunk;
         const int cnt = static_cast<int>(min(static_cast<int64_t>(kChunk), p.T - base));
         const int cnt32 = (cnt + 31) & ~31;
         uint32_t* kb = kbuf + (r & 1) * kChunk;
-        uint32_t* qb = qbuf + (r & 1) * kChunk;
-        CodeT* mkey = mini_key + pwarp * kMini;
-        uint32_t* mmask = mini_mask + pwarp * kMini;
+        uint32_t* qb = qbuf + (r % 3) * kChunk;
         CodeT kr[kPerPrep], qr[kPerPrep];
 #pragma unroll
         for (int u = 0; u < kPerPrep; ++u) {
@@ -335,10 +324,6 @@ __global__ void __launch_bounds__(kThreads) match_kernel(const Params p) {
           kr[u] = i < cnt ? kc[row0 + base + i] : CodeT(0);
           qr[u] = i < cnt ? qc[row0 + base + i] : CodeT(0);
         }
-        // 1. One aligned 32-position step per warp-iteration. The lanes holding one key code
-        //    (match_any) elect their lowest lane, which inserts the code into the table and
-        //    publishes code -> lane mask in the warp's 64-entry mini hash; each query lane
-        //    then finds the latest key lane j < i of its code in the step, if any.
         uint32_t qpend = 0;  // bit u: the query of iteration u needs a table lookup
 #pragma unroll
         for (int u = 0; u < kPerPrep; ++u) {
@@ -346,56 +331,45 @@ __global__ void __launch_bounds__(kThreads) match_kernel(const Params p) {
           if (i < cnt32) {  // uniform per warp: a warp covers an aligned run of 32 positions
             const bool valid = i < cnt;
             const uint32_t vm = __ballot_sync(kFullMask, valid);
-            uint32_t mine = kMini;  // mini-hash entry this lane claimed
+            uint32_t peers = 0;
+            bool leader = false;
             if (valid) {
-              const uint32_t peers = __match_any_sync(vm, kr[u]);
-              const int leader = __ffs(peers) - 1;
+              peers = __match_any_sync(vm, kr[u]);
+              const int lead = __ffs(peers) - 1;
+              leader = lane == lead;
               uint32_t slot = kNoSlot, claimed = 0;
-              if (lane == leader) {
-                slot = tab.insert(kr[u], claimed, p.status);
+              if (leader) {
+                slot = tab.insert(kr[u], claimed);
                 if (claimed) atomicAdd(&s_used, 1u);
                 if (slot == kNoSlot) s_ovf = 1;
-                uint32_t h = mini_hash(kr[u]);
-                for (int t = 0; t < kMini; ++t, h = (h + 1) & (kMini - 1)) {
-                  if (atomicCAS(mmask + h, 0u, peers) == 0u) {
-                    mkey[h] = kr[u];
-                    mine = h;
-                    break;
-                  }
-                }
               }
-              slot = __shfl_sync(vm, slot, leader);
+              slot = __shfl_sync(vm, slot, lead);
               kb[i] = ((peers >> lane) == 1u) ? slot : kNoSlot;  // last key lane of its code
             }
-            __syncwarp();
+            // in-step match: walk the step's distinct key codes (one leader lane each)
+            uint32_t leaders = __ballot_sync(kFullMask, leader);
+            uint32_t mm = 0;
+            while (leaders) {
+              const int j = __ffs(leaders) - 1;
+              leaders &= leaders - 1;
+              const CodeT kj = __shfl_sync(kFullMask, kr[u], j);
+              const uint32_t pj = __shfl_sync(kFullMask, peers, j);
+              if (kj == qr[u]) mm = pj;
+            }
+            mm &= lanemask_lt();
             if (valid) {
-              uint32_t mm = 0;
-              uint32_t h = mini_hash(qr[u]);
-              for (int t = 0; t < kMini; ++t, h = (h + 1) & (kMini - 1)) {
-                const uint32_t m = mmask[h];
-                if (m == 0u) break;
-                if (mkey[h] == qr[u]) {
-                  mm = m & lanemask_lt();
-                  break;
-                }
-              }
               if (mm) {
                 qb[i] = kInStep | (31u - __clz(mm));
               } else {
                 qpend |= 1u << u;
               }
             }
-            __syncwarp();
-            if (mine < kMini) mmask[mine] = 0u;
-            __syncwarp();
           }
         }
         prep_barrier();
         if (s_ovf != 0 || (kSmemTable && s_used > overflow_limit<CodeT>())) {
           if (ptid == 0) s_abort = 1;
         } else {
-          // 2. queries without an in-step match read their code's slot (or none: then no key
-          //    of the code has appeared up to the end of this chunk, and the answer is -1)
 #pragma unroll
           for (int u = 0; u < kPerPrep; ++u) {
             if ((qpend >> u) & 1u) qb[ptid + u * kPrepThreads] = tab.find(qr[u]);
@@ -408,8 +382,7 @@ __global__ void __launch_bounds__(kThreads) match_kernel(const Params p) {
         const int cnt = static_cast<int>(min(static_cast<int64_t>(kChunk), p.T - base));
         const int nsteps = (cnt + 31) >> 5;
         const uint32_t* kb = kbuf + (c & 1) * kChunk;
-        const uint32_t* qb = qbuf + (c & 1) * kChunk;
-        int32_t* sb = sbuf + (c & 1) * kChunk;
+        uint32_t* qb = qbuf + (c % 3) * kChunk;
         uint32_t qn = kNoSlot, kn = kNoSlot;
         if (lane < cnt) {
           qn = qb[lane];
@@ -428,14 +401,14 @@ __global__ void __launch_bounds__(kThreads) match_kernel(const Params p) {
             if (qv & kInStep) {
               sv = static_cast<int32_t>(base + s * 32 + static_cast<int>(qv & 31u));
             } else {
-              const uint32_t m = *reinterpret_cast<volatile uint32_t*>(tab.meta(qv));
+              const uint32_t m = *reinterpret_cast<volatile uint32_t*>(tab.meta_of(qv));
               sv = (m == kNone) ? -1 : static_cast<int32_t>(m);
             }
           }
-          if (valid) sb[i] = sv;
+          if (valid) qb[i] = static_cast<uint32_t>(sv);
           __syncwarp();
           if (valid && kv != kNoSlot) {
-            *reinterpret_cast<volatile uint32_t*>(tab.meta(kv)) = static_cast<uint32_t>(base + i);
+            *reinterpret_cast<volatile uint32_t*>(tab.meta_of(kv)) = static_cast<uint32_t>(base + i);
           }
           __syncwarp();
         }
@@ -444,7 +417,8 @@ __global__ void __launch_bounds__(kThreads) match_kernel(const Params p) {
         const int64_t c = r - 2;
         const int64_t base = c * kChunk;
         const int cnt = static_cast<int>(min(static_cast<int64_t>(kChunk), p.T - base));
-        gather_chunk<Vec>(p, row0, base, cnt, sbuf + (c & 1) * kChunk, tid - kGathWarp0 * 32);
+        gather_chunk<Vec>(p, row0, base, cnt, reinterpret_cast<const int32_t*>(qbuf + (c % 3) * kChunk),
+                          tid - kGathWarp0 * 32);
       }
       __syncthreads();
       if (s_abort != 0) {
@@ -471,7 +445,7 @@ __global__ void __launch_bounds__(kThreads) match_kernel(const Params p) {
     if (p.lt_count != nullptr) {
       CodeT* ltc = static_cast<CodeT*>(p.lt_code) + row0;
       int32_t* ltp = p.lt_pos + row0;
-      for (uint32_t s = tid; s <= tab.mask; s += kThreads) {
+      for (uint32_t s = tid; s <= tab.cap; s += kThreads) {
         CodeT c;
         uint32_t m;
         if (tab.used(s, c, m) && m < kNone) {
@@ -488,22 +462,21 @@ __global__ void __launch_bounds__(kThreads) match_kernel(const Params p) {
 }
 
 // ---------------------------------------------------------------- host side
-constexpr size_t kChunkSmem = 6 * kChunk * sizeof(uint32_t);
+constexpr size_t kChunkSmem = 5 * kChunk * sizeof(uint32_t);  // kbuf[2] + qbuf[3]
 constexpr int64_t kMaxOverflowTables = 64;
 constexpr uint64_t kOverflowTableBudget = uint64_t(1) << 30;  // bytes of global tables
 constexpr int64_t kFastMaxT = int64_t(1) << 20;               // beyond: global path directly
 
 template <typename CodeT>
 size_t smem_bytes(bool smem_table) {
-  return (smem_table ? (size_t(1) << SmemCap<CodeT>::kLog2) * Table<CodeT>::kBytesPerSlot : 0) +
-         kChunkSmem + kPrepWarps * kMini * (sizeof(CodeT) + sizeof(uint32_t));
+  return (smem_table ? round_up16(Table<CodeT>::bytes(SmemCap<CodeT>::kSlots)) : 0) + kChunkSmem;
 }
 
 struct Plan {
   bool fast = false;       // run the shared-memory kernel
   bool global = false;     // run the global-table kernel
   bool list_mode = false;  // global kernel reads the overflow list
-  uint32_t gcap_log2 = 0;
+  uint32_t gslots = 0;
   int64_t gtable_bytes = 0;
   int64_t n_gtables = 0;
   size_t off_list = 0, off_tables = 0, total = 0;
@@ -518,10 +491,9 @@ Plan make_plan(int64_t N, int64_t T, int code_bytes) {
   if (!may_overflow) return pl;
   pl.global = true;
   pl.list_mode = pl.fast;
-  const uint64_t cap = next_pow2(static_cast<uint64_t>(2 * T));
-  pl.gcap_log2 = static_cast<uint32_t>(log2_exact(cap));
-  const size_t per_slot = code_bytes == 4 ? Table<uint32_t>::kBytesPerSlot : Table<uint64_t>::kBytesPerSlot;
-  pl.gtable_bytes = static_cast<int64_t>(round_up(cap * per_slot, 256));
+  pl.gslots = static_cast<uint32_t>(next_pow2(static_cast<uint64_t>(std::max<int64_t>(2 * T, 2 * kBucket))));
+  const size_t tb = code_bytes == 4 ? Table<uint32_t>::bytes(pl.gslots) : Table<uint64_t>::bytes(pl.gslots);
+  pl.gtable_bytes = static_cast<int64_t>(round_up(tb, 256));
   pl.n_gtables = std::max<int64_t>(
       1, std::min<int64_t>({N, kMaxOverflowTables,
                             static_cast<int64_t>(kOverflowTableBudget / pl.gtable_bytes)}));
@@ -562,7 +534,7 @@ int run(const MatchLaunch& a, const Plan& pl, const DeviceInfo& dev) {
     p.ovf_list = reinterpret_cast<uint32_t*>(ws + pl.off_list);
     p.gtables = ws + pl.off_tables;
     p.gtable_bytes = pl.gtable_bytes;
-    p.gcap_log2 = pl.gcap_log2;
+    p.gslots = pl.gslots;
     if (pl.list_mode) LEMA_CUDA_TRY(cudaMemsetAsync(p.ovf_count, 0, sizeof(uint32_t), a.stream));
   }
   if (pl.fast) {
@@ -607,7 +579,7 @@ size_t match_workspace_bytes(int64_t N, int64_t T, int code_bytes) {
 int launch_match(const MatchLaunch& a) {
   if (a.code_bytes != 4 && a.code_bytes != 8) return fail(LEMA_ERR_INVALID_ARGUMENT, "code_bytes must be 4 or 8, got %d", a.code_bytes);
   if (a.N < 0 || a.T < 0) return fail(LEMA_ERR_INVALID_ARGUMENT, "negative shape (%lld, %lld)", (long long)a.N, (long long)a.T);
-  if (a.T > (int64_t(1) << 31) - 16) return fail(LEMA_ERR_INVALID_ARGUMENT, "T = %lld exceeds 2^31 - 16", (long long)a.T);
+  if (a.T > (int64_t(1) << 30)) return fail(LEMA_ERR_INVALID_ARGUMENT, "T = %lld exceeds 2^30", (long long)a.T);
   if (a.N == 0 || a.T == 0) return LEMA_OK;
   if (a.qc == nullptr || a.kc == nullptr) return fail(LEMA_ERR_INVALID_ARGUMENT, "null code pointer");
   if (!aligned(a.qc, a.code_bytes) || !aligned(a.kc, a.code_bytes)) return fail(LEMA_ERR_INVALID_ARGUMENT, "codes not aligned to their width");
