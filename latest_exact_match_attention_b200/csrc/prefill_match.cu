@@ -13,8 +13,8 @@
 //     * the lanes holding one key code (match_any) elect their lowest lane, which inserts the
 //       code into -- or finds it in -- the stream's table, giving it a SLOT id; the step's
 //       last lane of each code is marked (only it writes the sweep state);
-//     * each query lane finds the latest key lane j < i with its code in the same step, by
-//       walking the step's distinct key codes with shuffles;
+//     * each query lane finds the latest key lane j < i with its code in the same step: three
+//       match_any calls over half-steps, keys in the low lanes and queries in the high ones;
 //     * after a barrier that ends the chunk's inserts, every query without an in-step match
 //       looks its code up: no slot means no key of that code up to the end of the chunk, so
 //       -1 is already its answer.
@@ -230,6 +230,13 @@ struct Params {
   uint32_t div_magic;  // floor(2^32 / words per row) + 1 when usable, else 0
 };
 
+__device__ __forceinline__ uint32_t shfl_code(uint32_t v, int src) {
+  return __shfl_sync(kFullMask, v, src);
+}
+__device__ __forceinline__ uint64_t shfl_code(uint64_t v, int src) {
+  return static_cast<uint64_t>(__shfl_sync(kFullMask, static_cast<unsigned long long>(v), src));
+}
+
 __device__ __forceinline__ void prep_barrier() {
   asm volatile("bar.sync 1, %0;" ::"n"(kPrepThreads) : "memory");
 }
@@ -331,14 +338,11 @@ __global__ void __launch_bounds__(kThreads) match_kernel(const Params p) {
           if (i < cnt32) {  // uniform per warp: a warp covers an aligned run of 32 positions
             const bool valid = i < cnt;
             const uint32_t vm = __ballot_sync(kFullMask, valid);
-            uint32_t peers = 0;
-            bool leader = false;
             if (valid) {
-              peers = __match_any_sync(vm, kr[u]);
+              const uint32_t peers = __match_any_sync(vm, kr[u]);
               const int lead = __ffs(peers) - 1;
-              leader = lane == lead;
               uint32_t slot = kNoSlot, claimed = 0;
-              if (leader) {
+              if (lane == lead) {
                 slot = tab.insert(kr[u], claimed);
                 if (claimed) atomicAdd(&s_used, 1u);
                 if (slot == kNoSlot) s_ovf = 1;
@@ -346,20 +350,35 @@ __global__ void __launch_bounds__(kThreads) match_kernel(const Params p) {
               slot = __shfl_sync(vm, slot, lead);
               kb[i] = ((peers >> lane) == 1u) ? slot : kNoSlot;  // last key lane of its code
             }
-            // in-step match: walk the step's distinct key codes (one leader lane each)
-            uint32_t leaders = __ballot_sync(kFullMask, leader);
-            uint32_t mm = 0;
-            while (leaders) {
-              const int j = __ffs(leaders) - 1;
-              leaders &= leaders - 1;
-              const CodeT kj = __shfl_sync(kFullMask, kr[u], j);
-              const uint32_t pj = __shfl_sync(kFullMask, peers, j);
-              if (kj == qr[u]) mm = pj;
+            // In-step match with three match_any calls over half-steps. Lanes 0..15 carry
+            // key codes and lanes 16..31 query codes, so a query lane's peer mask, low half,
+            // is exactly the key positions with its code. A: keys 0..15 / queries 0..15,
+            // B: keys 16..31 / queries 16..31, X: keys 0..15 / queries 16..31.
+            const CodeT qlo = shfl_code(qr[u], lane & 15);   // lanes 16..31: query lane-16
+            const CodeT khi = shfl_code(kr[u], lane | 16);   // lanes 0..15: key lane+16
+            const bool lo = lane < 16;
+            const uint32_t vlo = vm & 0xFFFFu, vhi = vm >> 16;
+            const uint32_t pa = __match_any_sync(kFullMask, lo ? kr[u] : qlo) & (vlo | (vlo << 16));
+            const uint32_t pb = __match_any_sync(kFullMask, lo ? khi : qr[u]) & (vhi | (vhi << 16));
+            const uint32_t px = __match_any_sync(kFullMask, lo ? kr[u] : qr[u]) & (vlo | (vhi << 16));
+            const uint32_t pa_q = __shfl_sync(kFullMask, pa, lane | 16);  // A row of query `lane`
+            uint32_t ans = 0;  // 0 = none, else 1 + key lane
+            if (lo) {
+              const uint32_t m = pa_q & 0xFFFFu & ((1u << lane) - 1u);
+              if (m) ans = 32u - __clz(m);
+            } else {
+              const uint32_t mb = pb & 0xFFFFu & ((1u << (lane - 16)) - 1u);
+              const uint32_t mx = px & 0xFFFFu;
+              if (mb) {
+                ans = 16u + 32u - __clz(mb);
+              } else if (mx) {
+                ans = 32u - __clz(mx);
+              }
             }
-            mm &= lanemask_lt();
+            const uint32_t mm = ans;
             if (valid) {
               if (mm) {
-                qb[i] = kInStep | (31u - __clz(mm));
+                qb[i] = kInStep | (mm - 1u);
               } else {
                 qpend |= 1u << u;
               }
