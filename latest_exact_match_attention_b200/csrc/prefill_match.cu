@@ -2,47 +2,46 @@
 //
 // For stream n and position i:  src[n][i] = max{ j < i : kc[n][j] == qc[n][i] } or -1,
 // out[n][i] = v[n][src] (zeros when -1). This is the rule of code/lema/attention.py:100-158,
-// which the reference computes with two stable argsorts over 2T events per stream; here it is
-// one pass in position order with a hash table of the stream's key codes in shared memory.
+// which the reference computes with two stable argsorts over 2T events per stream. Here a
+// stream is walked in chunks of kChunk positions against a hash table of its key codes, and
+// every phase inside a chunk is parallel; only chunk-to-chunk is ordered.
 //
-// One CTA owns one stream at a time (persistent grid-stride over streams) and walks it in
-// chunks of kChunk positions through a three-stage pipeline of warp roles. Stage boundaries
-// are CTA-wide barriers ("rounds"); in round r:
+// Table state per slot (one slot per distinct key code of the stream):
+//   carry[slot]  position of the latest key with that code BEFORE the current chunk
+//   mask[slot]   bit s set iff a key with that code occurs in step s (32 positions) of the
+//                current chunk
+// A chunk is 32 steps, one aligned 32-position row per warp-iteration, and three phases:
+//   P1 (per step) the lanes holding one key code (match_any) elect their lowest lane, which
+//      inserts the code into -- or finds it in -- the table (slot id) and sets the step's bit
+//      in mask[slot]. Each query's latest earlier key IN THE SAME STEP comes from three
+//      match_any calls over half-steps (keys in the low lanes, queries in the high lanes, so a
+//      query lane's peer mask is the set of key positions with its code).
+//   P2 (per query without an in-step match) look the code up; no slot means no key of that
+//      code so far (-1). Else the highest bit of mask[slot] below the query's step names the
+//      latest earlier step holding the code, and a scan of that step's 32 key slots gives
+//      the lane; with no such step the answer is carry[slot]. Each key that is the last of
+//      its code in its step reads mask[slot] too, to learn whether its step is the code's
+//      last in the chunk.
+//   P3 (per last key of its code in the chunk) carry[slot] = its position, mask[slot] = 0.
+// Warp roles: 8 matcher warps run P1..P3 on chunk r (named barrier between phases) while 8
+// gatherer warps write indices and value rows of chunk r-1 (16-byte vectors, eight loads in
+// flight per thread, streaming stores, zeros for misses); a CTA barrier ends each round.
 //
-//   preparers (7 warps) -- chunk r, one aligned 32-position step per warp-iteration:
-//     * the lanes holding one key code (match_any) elect their lowest lane, which inserts the
-//       code into -- or finds it in -- the stream's table, giving it a SLOT id; the step's
-//       last lane of each code is marked (only it writes the sweep state);
-//     * each query lane finds the latest key lane j < i with its code in the same step: three
-//       match_any calls over half-steps, keys in the low lanes and queries in the high ones;
-//     * after a barrier that ends the chunk's inserts, every query without an in-step match
-//       looks its code up: no slot means no key of that code up to the end of the chunk, so
-//       -1 is already its answer.
-//   sweeper (1 warp) -- chunk r-1, the only ordered part. 32 positions per step: a query with
-//       an in-step match takes it, any other reads meta[slot] (the position of the latest key
-//       of its slot swept so far); then each slot's last key lane writes its position into
-//       meta[slot]. Two __syncwarp()s per step order the reads before the step's writes and
-//       the writes before the next step's reads. The answers overwrite the query words.
-//   gatherers (8 warps) -- chunk r-2: indices out, value rows copied with 16-byte vectors,
-//       eight loads in flight per thread, streaming stores; zeros for misses.
+// The table is bucketed: 8 slots per bucket, read with vector loads, linear probing over
+// buckets; a claim is one compare-and-swap of a free code word (all ones), and the all-ones
+// code itself lives in a dedicated side slot, so every code value is an ordinary key.
 //
-// The stages touch the table without conflict: inserts only claim free code words, lookups
-// read code words, and the sweep writes the meta words of slots claimed in earlier rounds.
-//
-// The table is bucketed: 8 slots per bucket, read with two (four for 64-bit codes) vector
-// loads, linear probing over buckets. Codes and metas are separate arrays; a claim is one
-// compare-and-swap of a free code word (all ones), and the all-ones code itself lives in a
-// dedicated side slot, so every code value is an ordinary key and no reader ever waits.
-//
-// The shared-memory table has a fixed capacity. A stream whose distinct key codes would load
-// it beyond kOverflowFrac is handed over whole to the same kernel running with a CTA-private
-// table in global memory sized for 2*T (the overflow path): it appends itself to an overflow
-// list in the workspace, and a second launch processes the list. No input can make the result
-// wrong; an unusual one only takes the slower path.
+// One CTA owns one stream at a time (persistent grid-stride over streams). The shared-memory
+// table has a fixed capacity and 16-bit carries (T <= 65534). A stream whose distinct key
+// codes would load the table beyond kOverflowFrac is handed over whole to the same kernel
+// running with a CTA-private table in global memory sized for 2*T and 32-bit carries (the
+// overflow path); streams longer than the shared-memory path allows start there. No input
+// can make the result wrong; an unusual one only takes the slower path.
 #include <cuda_runtime.h>
 
 #include <algorithm>
 #include <cstring>
+#include <type_traits>
 
 #include "common.cuh"
 #include "match.cuh"
@@ -51,21 +50,22 @@ namespace lema {
 namespace k2 {
 
 constexpr int kThreads = 512;
-constexpr int kChunk = 2048;
-constexpr int kSweepWarp = 0;                  // warp 0: the ordered sweep
-constexpr int kPrepWarp0 = 1, kPrepWarps = 7;  // warps 1..7: insert / in-step / lookup
+constexpr int kChunk = 1024;                   // positions per chunk: 32 steps of 32
+constexpr int kSteps = kChunk / 32;
+constexpr int kMatchWarps = 8;                 // warps 0..7: P1..P3
 constexpr int kGathWarp0 = 8, kGathWarps = 8;  // warps 8..15: indices and rows out
-constexpr int kPrepThreads = kPrepWarps * 32;
+constexpr int kMatchThreads = kMatchWarps * 32;
 constexpr int kGathThreads = kGathWarps * 32;
-constexpr int kPerPrep = (kChunk + kPrepThreads - 1) / kPrepThreads;
+constexpr int kPerLane = kSteps / kMatchWarps;  // steps per matcher warp
 constexpr int kGatherUnroll = 8;
 constexpr int kBucket = 8;  // slots per table bucket
-static_assert((kPrepWarp0 + kPrepWarps) * 32 <= kThreads && kGathWarp0 * 32 + kGathThreads == kThreads,
-              "warp roles");
+static_assert(kSteps == 32, "step masks are 32-bit");
+static_assert(kSteps % kMatchWarps == 0 && kGathWarp0 * 32 + kGathThreads == kThreads, "warp roles");
 
-constexpr uint32_t kNone = 0xFFFFFFFDu;    // meta: code present, no key position swept yet
-constexpr uint32_t kNoSlot = 0xFFFFFFFFu;  // query code absent from the table
-constexpr uint32_t kInStep = 0x80000000u;  // query word: in-step match, lane in the low bits
+constexpr uint32_t kNoSlot = 0xFFFFFFFFu;
+constexpr uint32_t kSlotBits = 0x3FFFFFFFu;  // key word: slot | klast | last-in-chunk
+constexpr uint32_t kKLast = 0x40000000u;     // last key lane of its code in its step
+constexpr uint32_t kCLast = 0x80000000u;     // ... and that step is the code's last in chunk
 
 // Shared-memory table capacity (slots) per code width; above kOverflowFrac of it a stream
 // moves to the global-memory path.
@@ -80,6 +80,7 @@ struct SmemCap<uint64_t> {
   static constexpr uint32_t kSlots = 4096;
 };
 constexpr double kOverflowFrac = 0.75;
+constexpr int64_t kSmemMaxT = 65534;  // 16-bit carries
 
 template <typename CodeT>
 __host__ __device__ constexpr uint32_t overflow_limit() {
@@ -87,23 +88,6 @@ __host__ __device__ constexpr uint32_t overflow_limit() {
 }
 
 // ---------------------------------------------------------------- the table
-// Volatile vector loads of one bucket's code words (generic addresses: the table lives in
-// shared memory on the fast path and in global memory on the overflow path).
-__device__ __forceinline__ void load_bucket(const uint32_t* p, uint32_t (&c)[kBucket]) {
-  asm volatile("ld.volatile.v4.u32 {%0, %1, %2, %3}, [%4];"
-               : "=r"(c[0]), "=r"(c[1]), "=r"(c[2]), "=r"(c[3]) : "l"(p) : "memory");
-  asm volatile("ld.volatile.v4.u32 {%0, %1, %2, %3}, [%4];"
-               : "=r"(c[4]), "=r"(c[5]), "=r"(c[6]), "=r"(c[7]) : "l"(p + 4) : "memory");
-}
-__device__ __forceinline__ void load_bucket(const uint64_t* p, uint64_t (&c)[kBucket]) {
-#pragma unroll
-  for (int k = 0; k < kBucket; k += 2) {
-    unsigned long long a, b;
-    asm volatile("ld.volatile.v2.u64 {%0, %1}, [%2];" : "=l"(a), "=l"(b) : "l"(p + k) : "memory");
-    c[k] = a;
-    c[k + 1] = b;
-  }
-}
 __device__ __forceinline__ uint32_t cas_code(uint32_t* p, uint32_t cmp, uint32_t val) {
   return atomicCAS(p, cmp, val);
 }
@@ -111,55 +95,65 @@ __device__ __forceinline__ uint64_t cas_code(uint64_t* p, uint64_t cmp, uint64_t
   return atomicCAS(reinterpret_cast<unsigned long long*>(p), static_cast<unsigned long long>(cmp),
                    static_cast<unsigned long long>(val));
 }
-
-// Slot -> (code, meta). Slots [0, cap) form cap / kBucket buckets; slot `cap` holds the
-// all-ones code, whose presence is the side flag. meta is kNone or the stream position of the
-// latest key with that code swept so far.
 template <typename CodeT>
+__device__ __forceinline__ void load_bucket(const CodeT* p, CodeT (&w)[kBucket]) {
+  static_assert(sizeof(CodeT) * kBucket % 16 == 0, "bucket = whole 16-byte vectors");
+  const uint4* v = reinterpret_cast<const uint4*>(p);
+#pragma unroll
+  for (int k = 0; k < static_cast<int>(sizeof(CodeT) * kBucket / 16); ++k) {
+    const uint4 x = v[k];
+    memcpy(reinterpret_cast<char*>(w) + 16 * k, &x, 16);
+  }
+}
+
+// Slot -> (code, carry, mask). Slots [0, cap) form cap / kBucket buckets; slot `cap` holds the
+// all-ones code, whose presence is the side flag.
+template <typename CodeT, typename CarryT>
 struct Table {
   static constexpr CodeT kFree = static_cast<CodeT>(~CodeT(0));
-  CodeT* code;     // [cap]
-  uint32_t* meta;  // [cap + 1]
-  uint32_t* side;  // 1 word: the all-ones code is present
+  static constexpr CarryT kNoCarry = static_cast<CarryT>(~CarryT(0));
+  CodeT* code;      // [cap]
+  CarryT* carry;    // [cap + 1]
+  uint32_t* mask;   // [cap + 1]
+  uint32_t* side;   // 1 word
   uint32_t cap;
-  uint32_t bmask;  // buckets - 1
+  uint32_t bmask;   // buckets - 1
 
   __host__ __device__ static constexpr size_t bytes(uint32_t slots) {
-    return slots * sizeof(CodeT) + (slots + 1) * sizeof(uint32_t) + 16;
+    return round_up16(slots * sizeof(CodeT)) + round_up16((slots + 1) * sizeof(CarryT)) +
+           round_up16((slots + 1) * sizeof(uint32_t)) + 16;
   }
   __device__ void init(void* base, uint32_t slots) {
     cap = slots;
     bmask = slots / kBucket - 1;
-    code = static_cast<CodeT*>(base);
-    meta = reinterpret_cast<uint32_t*>(code + cap);
-    side = meta + cap + 1;
+    unsigned char* b = static_cast<unsigned char*>(base);
+    code = reinterpret_cast<CodeT*>(b);
+    b += round_up16(slots * sizeof(CodeT));
+    carry = reinterpret_cast<CarryT*>(b);
+    b += round_up16((slots + 1) * sizeof(CarryT));
+    mask = reinterpret_cast<uint32_t*>(b);
+    b += round_up16((slots + 1) * sizeof(uint32_t));
+    side = reinterpret_cast<uint32_t*>(b);
   }
   __device__ void clear(int tid, int nthr) {
     for (uint32_t s = tid; s < cap; s += nthr) code[s] = kFree;
-    for (uint32_t s = tid; s <= cap; s += nthr) meta[s] = kNone;
+    for (uint32_t s = tid; s <= cap; s += nthr) {
+      carry[s] = kNoCarry;
+      mask[s] = 0u;
+    }
     if (tid == 0) *side = 0;
   }
-  __device__ uint32_t* meta_of(uint32_t s) const { return meta + s; }
-  __device__ bool used(uint32_t s, CodeT& c, uint32_t& m) const {
-    m = meta[s];
-    if (s == cap) {
-      c = kFree;
-      return *side != 0;
-    }
-    c = code[s];
-    return c != kFree;
-  }
-  // Insert-or-find. Returns the slot, or kNoSlot when every bucket was full.
-  __device__ uint32_t insert(CodeT c, uint32_t& claimed) {
+  __device__ uint32_t home(CodeT c) const { return code_hash32(c) & bmask; }
+  // Insert-or-find from the bucket contents `w` already loaded from `home(c)`; the general
+  // probe (CAS races, full buckets) continues from there. Returns the slot, or kNoSlot when
+  // every bucket was full.
+  __device__ uint32_t insert_from(CodeT c, uint32_t b, CodeT (&w)[kBucket], uint32_t& claimed) {
     if (c == kFree) {
       claimed = atomicCAS(side, 0u, 1u) == 0u;
       return cap;
     }
-    uint32_t b = code_hash32(c) & bmask;
-    for (uint32_t n = 0; n <= bmask; ++n, b = (b + 1) & bmask) {
+    for (uint32_t n = 0; n <= bmask; ++n) {
       CodeT* bk = code + b * kBucket;
-      CodeT w[kBucket];
-      load_bucket(bk, w);
 #pragma unroll
       for (int k = 0; k < kBucket; ++k) {
         if (w[k] == c) return b * kBucket + k;
@@ -182,17 +176,17 @@ struct Table {
           }
         }
       }
+      b = (b + 1) & bmask;
+      load_bucket(code + b * kBucket, w);
     }
     return kNoSlot;
   }
-  // Find. A bucket with a free slot ends the search: codes fill a bucket's slots in order and
-  // reach a bucket only when the buckets before it on their chain were full.
-  __device__ uint32_t find(CodeT c) const {
-    if (c == kFree) return *reinterpret_cast<volatile uint32_t*>(side) ? cap : kNoSlot;
-    uint32_t b = code_hash32(c) & bmask;
-    for (uint32_t n = 0; n <= bmask; ++n, b = (b + 1) & bmask) {
-      CodeT w[kBucket];
-      load_bucket(code + b * kBucket, w);
+  // Find (after a barrier that ended the inserts). A bucket with a free slot ends the search:
+  // codes fill a bucket's slots in order and reach a bucket only when the buckets before it on
+  // their chain were full.
+  __device__ uint32_t find_from(CodeT c, uint32_t b, CodeT (&w)[kBucket]) const {
+    if (c == kFree) return *side ? cap : kNoSlot;
+    for (uint32_t n = 0; n <= bmask; ++n) {
       bool open = false;
 #pragma unroll
       for (int k = 0; k < kBucket; ++k) {
@@ -200,8 +194,19 @@ struct Table {
         open |= (w[k] == kFree);
       }
       if (open) return kNoSlot;
+      b = (b + 1) & bmask;
+      load_bucket(code + b * kBucket, w);
     }
     return kNoSlot;
+  }
+  __device__ bool used(uint32_t s, CodeT& c, CarryT& m) const {
+    m = carry[s];
+    if (s == cap) {
+      c = kFree;
+      return *side != 0;
+    }
+    c = code[s];
+    return c != kFree;
   }
 };
 
@@ -230,15 +235,15 @@ struct Params {
   uint32_t div_magic;  // floor(2^32 / words per row) + 1 when usable, else 0
 };
 
+__device__ __forceinline__ void match_barrier() {
+  asm volatile("bar.sync 1, %0;" ::"n"(kMatchThreads) : "memory");
+}
+
 __device__ __forceinline__ uint32_t shfl_code(uint32_t v, int src) {
   return __shfl_sync(kFullMask, v, src);
 }
 __device__ __forceinline__ uint64_t shfl_code(uint64_t v, int src) {
   return static_cast<uint64_t>(__shfl_sync(kFullMask, static_cast<unsigned long long>(v), src));
-}
-
-__device__ __forceinline__ void prep_barrier() {
-  asm volatile("bar.sync 1, %0;" ::"n"(kPrepThreads) : "memory");
 }
 
 // Gatherers: indices of one chunk to global memory, then its value rows, kGatherUnroll vector
@@ -282,18 +287,20 @@ __device__ __forceinline__ void gather_chunk(const Params& p, int64_t row0, int6
 
 template <typename CodeT, bool kSmemTable, typename Vec>
 __global__ void __launch_bounds__(kThreads) match_kernel(const Params p) {
+  using CarryT = typename std::conditional<kSmemTable, uint16_t, uint32_t>::type;
+  using Tab = Table<CodeT, CarryT>;
   extern __shared__ __align__(16) unsigned char smem[];
   constexpr uint32_t kCap = SmemCap<CodeT>::kSlots;
-  constexpr size_t kTableBytes = kSmemTable ? round_up16(Table<CodeT>::bytes(kCap)) : 0;
-  uint32_t* kbuf = reinterpret_cast<uint32_t*>(smem + kTableBytes);  // [2][kChunk] key slots
-  uint32_t* qbuf = kbuf + 2 * kChunk;  // [3][kChunk] query words, then the answers in place
-  __shared__ uint32_t s_used, s_ovf, s_abort, s_lt;
+  constexpr size_t kTableBytes = kSmemTable ? round_up16(Tab::bytes(kCap)) : 0;
+  uint32_t* kbuf = reinterpret_cast<uint32_t*>(smem + kTableBytes);  // [kChunk] key words
+  int32_t* abuf = reinterpret_cast<int32_t*>(kbuf + kChunk);         // [2][kChunk] answers
+  __shared__ uint32_t s_used, s_ovf, s_lt;
 
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const CodeT* qc = static_cast<const CodeT*>(p.qc);
   const CodeT* kc = static_cast<const CodeT*>(p.kc);
 
-  Table<CodeT> tab;
+  Tab tab;
   if (kSmemTable) {
     tab.init(smem, kCap);
   } else {
@@ -309,33 +316,33 @@ __global__ void __launch_bounds__(kThreads) match_kernel(const Params p) {
     if (tid == 0) {
       s_used = 0;
       s_ovf = 0;
-      s_abort = 0;
       s_lt = 0;
     }
     __syncthreads();
 
     bool aborted = false;
-    for (int64_t r = 0; r < n_chunks + 2; ++r) {
-      if (warp >= kPrepWarp0 && warp < kPrepWarp0 + kPrepWarps && r < n_chunks) {
-        // ------------------------------------------------ preparers: chunk r
-        const int ptid = tid - kPrepWarp0 * 32;
+    for (int64_t r = 0; r <= n_chunks; ++r) {
+      if (warp < kMatchWarps && r < n_chunks) {
+        // ==================================================== matchers: chunk r
         const int64_t base = r * kChunk;
         const int cnt = static_cast<int>(min(static_cast<int64_t>(kChunk), p.T - base));
-        const int cnt32 = (cnt + 31) & ~31;
-        uint32_t* kb = kbuf + (r & 1) * kChunk;
-        uint32_t* qb = qbuf + (r % 3) * kChunk;
-        CodeT kr[kPerPrep], qr[kPerPrep];
+        int32_t* ab = abuf + (r & 1) * kChunk;
+        CodeT kr[kPerLane], qr[kPerLane];
 #pragma unroll
-        for (int u = 0; u < kPerPrep; ++u) {
-          const int i = ptid + u * kPrepThreads;
+        for (int u = 0; u < kPerLane; ++u) {
+          const int i = (warp + u * kMatchWarps) * 32 + lane;
           kr[u] = i < cnt ? kc[row0 + base + i] : CodeT(0);
           qr[u] = i < cnt ? qc[row0 + base + i] : CodeT(0);
         }
-        uint32_t qpend = 0;  // bit u: the query of iteration u needs a table lookup
+        // ---------------------------------------------- P1: insert, step bits, in-step
+        uint32_t kslot[kPerLane];
+        uint32_t pend = 0;  // bit u: the query of step u needs P2
 #pragma unroll
-        for (int u = 0; u < kPerPrep; ++u) {
-          const int i = ptid + u * kPrepThreads;
-          if (i < cnt32) {  // uniform per warp: a warp covers an aligned run of 32 positions
+        for (int u = 0; u < kPerLane; ++u) {
+          const int step = warp + u * kMatchWarps;
+          const int i = step * 32 + lane;
+          kslot[u] = kNoSlot;
+          if (step * 32 < cnt) {  // uniform per warp
             const bool valid = i < cnt;
             const uint32_t vm = __ballot_sync(kFullMask, valid);
             if (valid) {
@@ -343,104 +350,119 @@ __global__ void __launch_bounds__(kThreads) match_kernel(const Params p) {
               const int lead = __ffs(peers) - 1;
               uint32_t slot = kNoSlot, claimed = 0;
               if (lane == lead) {
-                slot = tab.insert(kr[u], claimed);
+                CodeT w[kBucket];
+                const uint32_t b = tab.home(kr[u]);
+                load_bucket(tab.code + b * kBucket, w);
+                slot = tab.insert_from(kr[u], b, w, claimed);
                 if (claimed) atomicAdd(&s_used, 1u);
-                if (slot == kNoSlot) s_ovf = 1;
+                if (slot == kNoSlot) {
+                  s_ovf = 1;
+                } else {
+                  atomicOr(tab.mask + slot, 1u << step);
+                }
               }
               slot = __shfl_sync(vm, slot, lead);
-              kb[i] = ((peers >> lane) == 1u) ? slot : kNoSlot;  // last key lane of its code
+              kslot[u] = slot;
+              kbuf[i] = (slot & kSlotBits) | (((peers >> lane) == 1u) ? kKLast : 0u);
             }
-            // In-step match with three match_any calls over half-steps. Lanes 0..15 carry
-            // key codes and lanes 16..31 query codes, so a query lane's peer mask, low half,
-            // is exactly the key positions with its code. A: keys 0..15 / queries 0..15,
-            // B: keys 16..31 / queries 16..31, X: keys 0..15 / queries 16..31.
-            const CodeT qlo = shfl_code(qr[u], lane & 15);   // lanes 16..31: query lane-16
-            const CodeT khi = shfl_code(kr[u], lane | 16);   // lanes 0..15: key lane+16
+            // in-step: A = keys 0..15 / queries 0..15, B = keys 16..31 / queries 16..31,
+            // X = keys 0..15 / queries 16..31; a query lane's peer mask, low half, is the set of
+            // key positions with its code
+            const CodeT qlo = shfl_code(qr[u], lane & 15);
+            const CodeT khi = shfl_code(kr[u], lane | 16);
             const bool lo = lane < 16;
             const uint32_t vlo = vm & 0xFFFFu, vhi = vm >> 16;
             const uint32_t pa = __match_any_sync(kFullMask, lo ? kr[u] : qlo) & (vlo | (vlo << 16));
             const uint32_t pb = __match_any_sync(kFullMask, lo ? khi : qr[u]) & (vhi | (vhi << 16));
             const uint32_t px = __match_any_sync(kFullMask, lo ? kr[u] : qr[u]) & (vlo | (vhi << 16));
-            const uint32_t pa_q = __shfl_sync(kFullMask, pa, lane | 16);  // A row of query `lane`
-            uint32_t ans = 0;  // 0 = none, else 1 + key lane
+            const uint32_t pa_q = __shfl_sync(kFullMask, pa, lane | 16);
+            int hit = -1;
             if (lo) {
               const uint32_t m = pa_q & 0xFFFFu & ((1u << lane) - 1u);
-              if (m) ans = 32u - __clz(m);
+              if (m) hit = 31 - __clz(m);
             } else {
               const uint32_t mb = pb & 0xFFFFu & ((1u << (lane - 16)) - 1u);
               const uint32_t mx = px & 0xFFFFu;
               if (mb) {
-                ans = 16u + 32u - __clz(mb);
+                hit = 16 + 31 - __clz(mb);
               } else if (mx) {
-                ans = 32u - __clz(mx);
+                hit = 31 - __clz(mx);
               }
             }
-            const uint32_t mm = ans;
             if (valid) {
-              if (mm) {
-                qb[i] = kInStep | (mm - 1u);
+              if (hit >= 0) {
+                ab[i] = static_cast<int32_t>(base + step * 32 + hit);
               } else {
-                qpend |= 1u << u;
+                pend |= 1u << u;
               }
             }
           }
         }
-        prep_barrier();
+        match_barrier();
         if (s_ovf != 0 || (kSmemTable && s_used > overflow_limit<CodeT>())) {
-          if (ptid == 0) s_abort = 1;
+          // the whole CTA learns it after the round barrier; P2/P3 are skipped
         } else {
+          // ---------------------------------------------- P2: queries, and last-in-chunk keys
+          bool clast[kPerLane];
 #pragma unroll
-          for (int u = 0; u < kPerPrep; ++u) {
-            if ((qpend >> u) & 1u) qb[ptid + u * kPrepThreads] = tab.find(qr[u]);
+          for (int u = 0; u < kPerLane; ++u) {
+            const int step = warp + u * kMatchWarps;
+            const int i = step * 32 + lane;
+            clast[u] = false;
+            if (i < cnt && (kbuf[i] & kKLast)) {
+              const uint32_t m = tab.mask[kslot[u]];
+              clast[u] = (31 - __clz(m)) == step;
+            }
+            if ((pend >> u) & 1u) {
+              CodeT w[kBucket];
+              const uint32_t b = tab.home(qr[u]);
+              load_bucket(tab.code + b * kBucket, w);
+              const uint32_t s = tab.find_from(qr[u], b, w);
+              int32_t a = -1;
+              if (s != kNoSlot) {
+                const uint32_t m = tab.mask[s] & ((1u << step) - 1u);
+                if (m) {
+                  // the latest earlier step holding the code: its highest lane with the slot
+                  const int st = 31 - __clz(m);
+                  const uint4* row = reinterpret_cast<const uint4*>(kbuf + st * 32);
+                  int hl = -1;
+#pragma unroll
+                  for (int k = 0; k < 8; ++k) {
+                    const uint4 x = row[k];
+                    if ((x.x & kSlotBits) == s) hl = 4 * k;
+                    if ((x.y & kSlotBits) == s) hl = 4 * k + 1;
+                    if ((x.z & kSlotBits) == s) hl = 4 * k + 2;
+                    if ((x.w & kSlotBits) == s) hl = 4 * k + 3;
+                  }
+                  a = static_cast<int32_t>(base + st * 32 + hl);
+                } else {
+                  const CarryT c = tab.carry[s];
+                  a = (c == Tab::kNoCarry) ? -1 : static_cast<int32_t>(c);
+                }
+              }
+              ab[i] = a;
+            }
+          }
+          match_barrier();
+          // ---------------------------------------------- P3: carries of the chunk's last keys
+#pragma unroll
+          for (int u = 0; u < kPerLane; ++u) {
+            if (clast[u]) {
+              const int i = (warp + u * kMatchWarps) * 32 + lane;
+              tab.carry[kslot[u]] = static_cast<CarryT>(base + i);
+              tab.mask[kslot[u]] = 0u;
+            }
           }
         }
-      } else if (warp == kSweepWarp && r >= 1 && r <= n_chunks) {
-        // ------------------------------------------------ sweeper: chunk r-1, in order
+      } else if (warp >= kGathWarp0 && r >= 1) {
+        // ==================================================== gatherers: chunk r-1
         const int64_t c = r - 1;
         const int64_t base = c * kChunk;
         const int cnt = static_cast<int>(min(static_cast<int64_t>(kChunk), p.T - base));
-        const int nsteps = (cnt + 31) >> 5;
-        const uint32_t* kb = kbuf + (c & 1) * kChunk;
-        uint32_t* qb = qbuf + (c % 3) * kChunk;
-        uint32_t qn = kNoSlot, kn = kNoSlot;
-        if (lane < cnt) {
-          qn = qb[lane];
-          kn = kb[lane];
-        }
-        for (int s = 0; s < nsteps; ++s) {
-          const int i = s * 32 + lane;
-          const bool valid = i < cnt;
-          const uint32_t qv = qn, kv = kn;
-          if (i + 32 < cnt) {
-            qn = qb[i + 32];
-            kn = kb[i + 32];
-          }
-          int32_t sv = -1;
-          if (valid && qv != kNoSlot) {
-            if (qv & kInStep) {
-              sv = static_cast<int32_t>(base + s * 32 + static_cast<int>(qv & 31u));
-            } else {
-              const uint32_t m = *reinterpret_cast<volatile uint32_t*>(tab.meta_of(qv));
-              sv = (m == kNone) ? -1 : static_cast<int32_t>(m);
-            }
-          }
-          if (valid) qb[i] = static_cast<uint32_t>(sv);
-          __syncwarp();
-          if (valid && kv != kNoSlot) {
-            *reinterpret_cast<volatile uint32_t*>(tab.meta_of(kv)) = static_cast<uint32_t>(base + i);
-          }
-          __syncwarp();
-        }
-      } else if (warp >= kGathWarp0 && r >= 2) {
-        // ------------------------------------------------ gatherers: chunk r-2
-        const int64_t c = r - 2;
-        const int64_t base = c * kChunk;
-        const int cnt = static_cast<int>(min(static_cast<int64_t>(kChunk), p.T - base));
-        gather_chunk<Vec>(p, row0, base, cnt, reinterpret_cast<const int32_t*>(qbuf + (c % 3) * kChunk),
-                          tid - kGathWarp0 * 32);
+        gather_chunk<Vec>(p, row0, base, cnt, abuf + (c & 1) * kChunk, tid - kGathWarp0 * 32);
       }
       __syncthreads();
-      if (s_abort != 0) {
+      if (s_ovf != 0 || (kSmemTable && s_used > overflow_limit<CodeT>())) {
         aborted = true;
         break;
       }
@@ -466,8 +488,8 @@ __global__ void __launch_bounds__(kThreads) match_kernel(const Params p) {
       int32_t* ltp = p.lt_pos + row0;
       for (uint32_t s = tid; s <= tab.cap; s += kThreads) {
         CodeT c;
-        uint32_t m;
-        if (tab.used(s, c, m) && m < kNone) {
+        CarryT m;
+        if (tab.used(s, c, m) && m != Tab::kNoCarry) {
           const uint32_t k = atomicAdd(&s_lt, 1u);
           ltc[k] = c;
           ltp[k] = static_cast<int32_t>(m);
@@ -481,14 +503,14 @@ __global__ void __launch_bounds__(kThreads) match_kernel(const Params p) {
 }
 
 // ---------------------------------------------------------------- host side
-constexpr size_t kChunkSmem = 5 * kChunk * sizeof(uint32_t);  // kbuf[2] + qbuf[3]
+constexpr size_t kChunkSmem = 3 * kChunk * sizeof(uint32_t);  // kbuf + abuf[2]
 constexpr int64_t kMaxOverflowTables = 64;
 constexpr uint64_t kOverflowTableBudget = uint64_t(1) << 30;  // bytes of global tables
-constexpr int64_t kFastMaxT = int64_t(1) << 20;               // beyond: global path directly
 
 template <typename CodeT>
 size_t smem_bytes(bool smem_table) {
-  return (smem_table ? round_up16(Table<CodeT>::bytes(SmemCap<CodeT>::kSlots)) : 0) + kChunkSmem;
+  return (smem_table ? round_up16(Table<CodeT, uint16_t>::bytes(SmemCap<CodeT>::kSlots)) : 0) +
+         kChunkSmem;
 }
 
 struct Plan {
@@ -505,13 +527,14 @@ Plan make_plan(int64_t N, int64_t T, int code_bytes) {
   Plan pl;
   if (N <= 0 || T <= 0) return pl;
   const uint32_t limit = code_bytes == 4 ? overflow_limit<uint32_t>() : overflow_limit<uint64_t>();
-  pl.fast = T <= kFastMaxT;
+  pl.fast = T <= kSmemMaxT;
   const bool may_overflow = !pl.fast || T > static_cast<int64_t>(limit);
   if (!may_overflow) return pl;
   pl.global = true;
   pl.list_mode = pl.fast;
   pl.gslots = static_cast<uint32_t>(next_pow2(static_cast<uint64_t>(std::max<int64_t>(2 * T, 2 * kBucket))));
-  const size_t tb = code_bytes == 4 ? Table<uint32_t>::bytes(pl.gslots) : Table<uint64_t>::bytes(pl.gslots);
+  const size_t tb = code_bytes == 4 ? Table<uint32_t, uint32_t>::bytes(pl.gslots)
+                                    : Table<uint64_t, uint32_t>::bytes(pl.gslots);
   pl.gtable_bytes = static_cast<int64_t>(round_up(tb, 256));
   pl.n_gtables = std::max<int64_t>(
       1, std::min<int64_t>({N, kMaxOverflowTables,
