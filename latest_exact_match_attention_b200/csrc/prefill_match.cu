@@ -7,22 +7,21 @@
 // every phase inside a chunk is parallel; only chunk-to-chunk is ordered.
 //
 // Table state per slot (one slot per distinct key code of the stream):
-//   carry[slot]  position of the latest key with that code BEFORE the current chunk
+//   carry[slot]  1 + position of the latest key with that code BEFORE the current chunk (0: none)
 //   mask[slot]   bit s set iff a key with that code occurs in step s (32 positions) of the
 //                current chunk
-// A chunk is 32 steps, one aligned 32-position row per warp-iteration, and three phases:
-//   P1 (per step) the lanes holding one key code (match_any) elect their lowest lane, which
-//      inserts the code into -- or finds it in -- the table (slot id) and sets the step's bit
-//      in mask[slot]. Each query's latest earlier key IN THE SAME STEP comes from three
-//      match_any calls over half-steps (keys in the low lanes, queries in the high lanes, so a
-//      query lane's peer mask is the set of key positions with its code).
-//   P2 (per query without an in-step match) look the code up; no slot means no key of that
-//      code so far (-1). Else the highest bit of mask[slot] below the query's step names the
-//      latest earlier step holding the code, and a scan of that step's 32 key slots gives
-//      the lane; with no such step the answer is carry[slot]. Each key that is the last of
-//      its code in its step reads mask[slot] too, to learn whether its step is the code's
-//      last in the chunk.
-//   P3 (per last key of its code in the chunk) carry[slot] = its position, mask[slot] = 0.
+// A chunk is 32 steps of 32 positions and three phases, all parallel:
+//   P1 (keys)    each key inserts its code into -- or finds it in -- the table (its SLOT),
+//                sets its step's bit in mask[slot], and records the slot in the chunk's key row.
+//   P2 (queries) each query looks its code up; no slot means no key of that code so far (-1).
+//                If its own step holds the code (mask bit), the latest key lane before it comes
+//                from one broadcast read of the step's 32 key slots; otherwise the highest mask
+//                bit below its step names the latest earlier step holding the code, whose row
+//                gives the lane; with no such step the answer is carry[slot]. Each key also
+//                reads mask[slot] to learn whether its step is the code's last in the chunk.
+//   P3 (keys of a code's last step) atomicMax(carry[slot], 1 + position); mask[slot] = 0.
+// No warp-wide match instructions are used: on this part they cost far more than the table
+// traffic they would save.
 // Warp roles: 8 matcher warps run P1..P3 on chunk r (named barrier between phases) while 8
 // gatherer warps write indices and value rows of chunk r-1 (16-byte vectors, eight loads in
 // flight per thread, streaming stores, zeros for misses); a CTA barrier ends each round.
@@ -32,11 +31,10 @@
 // code itself lives in a dedicated side slot, so every code value is an ordinary key.
 //
 // One CTA owns one stream at a time (persistent grid-stride over streams). The shared-memory
-// table has a fixed capacity and 16-bit carries (T <= 65534). A stream whose distinct key
-// codes would load the table beyond kOverflowFrac is handed over whole to the same kernel
-// running with a CTA-private table in global memory sized for 2*T and 32-bit carries (the
-// overflow path); streams longer than the shared-memory path allows start there. No input
-// can make the result wrong; an unusual one only takes the slower path.
+// table has a fixed capacity. A stream whose distinct key codes would load it beyond
+// kOverflowFrac is handed over whole to the same kernel running with a CTA-private table in
+// global memory sized for 2*T (the overflow path). No input can make the result wrong; an
+// unusual one only takes the slower path.
 #include <cuda_runtime.h>
 
 #include <algorithm>
@@ -63,9 +61,6 @@ static_assert(kSteps == 32, "step masks are 32-bit");
 static_assert(kSteps % kMatchWarps == 0 && kGathWarp0 * 32 + kGathThreads == kThreads, "warp roles");
 
 constexpr uint32_t kNoSlot = 0xFFFFFFFFu;
-constexpr uint32_t kSlotBits = 0x3FFFFFFFu;  // key word: slot | klast | last-in-chunk
-constexpr uint32_t kKLast = 0x40000000u;     // last key lane of its code in its step
-constexpr uint32_t kCLast = 0x80000000u;     // ... and that step is the code's last in chunk
 
 // Shared-memory table capacity (slots) per code width; above kOverflowFrac of it a stream
 // moves to the global-memory path.
@@ -80,7 +75,6 @@ struct SmemCap<uint64_t> {
   static constexpr uint32_t kSlots = 4096;
 };
 constexpr double kOverflowFrac = 0.75;
-constexpr int64_t kSmemMaxT = 65534;  // 16-bit carries
 
 template <typename CodeT>
 __host__ __device__ constexpr uint32_t overflow_limit() {
@@ -111,7 +105,7 @@ __device__ __forceinline__ void load_bucket(const CodeT* p, CodeT (&w)[kBucket])
 template <typename CodeT, typename CarryT>
 struct Table {
   static constexpr CodeT kFree = static_cast<CodeT>(~CodeT(0));
-  static constexpr CarryT kNoCarry = static_cast<CarryT>(~CarryT(0));
+  static constexpr CarryT kNoCarry = 0;  // carries hold position + 1
   CodeT* code;      // [cap]
   CarryT* carry;    // [cap + 1]
   uint32_t* mask;   // [cap + 1]
@@ -287,8 +281,7 @@ __device__ __forceinline__ void gather_chunk(const Params& p, int64_t row0, int6
 
 template <typename CodeT, bool kSmemTable, typename Vec>
 __global__ void __launch_bounds__(kThreads) match_kernel(const Params p) {
-  using CarryT = typename std::conditional<kSmemTable, uint16_t, uint32_t>::type;
-  using Tab = Table<CodeT, CarryT>;
+  using Tab = Table<CodeT, uint32_t>;
   extern __shared__ __align__(16) unsigned char smem[];
   constexpr uint32_t kCap = SmemCap<CodeT>::kSlots;
   constexpr size_t kTableBytes = kSmemTable ? round_up16(Tab::bytes(kCap)) : 0;
@@ -334,113 +327,89 @@ __global__ void __launch_bounds__(kThreads) match_kernel(const Params p) {
           kr[u] = i < cnt ? kc[row0 + base + i] : CodeT(0);
           qr[u] = i < cnt ? qc[row0 + base + i] : CodeT(0);
         }
-        // ---------------------------------------------- P1: insert, step bits, in-step
+        // ---------------------------------------------- P1: keys into the table, step bits
         uint32_t kslot[kPerLane];
-        uint32_t pend = 0;  // bit u: the query of step u needs P2
 #pragma unroll
         for (int u = 0; u < kPerLane; ++u) {
           const int step = warp + u * kMatchWarps;
           const int i = step * 32 + lane;
           kslot[u] = kNoSlot;
-          if (step * 32 < cnt) {  // uniform per warp
-            const bool valid = i < cnt;
-            const uint32_t vm = __ballot_sync(kFullMask, valid);
-            if (valid) {
-              const uint32_t peers = __match_any_sync(vm, kr[u]);
-              const int lead = __ffs(peers) - 1;
-              uint32_t slot = kNoSlot, claimed = 0;
-              if (lane == lead) {
-                CodeT w[kBucket];
-                const uint32_t b = tab.home(kr[u]);
-                load_bucket(tab.code + b * kBucket, w);
-                slot = tab.insert_from(kr[u], b, w, claimed);
-                if (claimed) atomicAdd(&s_used, 1u);
-                if (slot == kNoSlot) {
-                  s_ovf = 1;
-                } else {
-                  atomicOr(tab.mask + slot, 1u << step);
-                }
-              }
-              slot = __shfl_sync(vm, slot, lead);
-              kslot[u] = slot;
-              kbuf[i] = (slot & kSlotBits) | (((peers >> lane) == 1u) ? kKLast : 0u);
-            }
-            // in-step: A = keys 0..15 / queries 0..15, B = keys 16..31 / queries 16..31,
-            // X = keys 0..15 / queries 16..31; a query lane's peer mask, low half, is the set of
-            // key positions with its code
-            const CodeT qlo = shfl_code(qr[u], lane & 15);
-            const CodeT khi = shfl_code(kr[u], lane | 16);
-            const bool lo = lane < 16;
-            const uint32_t vlo = vm & 0xFFFFu, vhi = vm >> 16;
-            const uint32_t pa = __match_any_sync(kFullMask, lo ? kr[u] : qlo) & (vlo | (vlo << 16));
-            const uint32_t pb = __match_any_sync(kFullMask, lo ? khi : qr[u]) & (vhi | (vhi << 16));
-            const uint32_t px = __match_any_sync(kFullMask, lo ? kr[u] : qr[u]) & (vlo | (vhi << 16));
-            const uint32_t pa_q = __shfl_sync(kFullMask, pa, lane | 16);
-            int hit = -1;
-            if (lo) {
-              const uint32_t m = pa_q & 0xFFFFu & ((1u << lane) - 1u);
-              if (m) hit = 31 - __clz(m);
+          if (i < cnt) {
+            CodeT w[kBucket];
+            const uint32_t b = tab.home(kr[u]);
+            load_bucket(tab.code + b * kBucket, w);
+            uint32_t claimed = 0;
+            const uint32_t slot = tab.insert_from(kr[u], b, w, claimed);
+            if (claimed) atomicAdd(&s_used, 1u);
+            if (slot == kNoSlot) {
+              s_ovf = 1;
             } else {
-              const uint32_t mb = pb & 0xFFFFu & ((1u << (lane - 16)) - 1u);
-              const uint32_t mx = px & 0xFFFFu;
-              if (mb) {
-                hit = 16 + 31 - __clz(mb);
-              } else if (mx) {
-                hit = 31 - __clz(mx);
-              }
+              atomicOr(tab.mask + slot, 1u << step);
             }
-            if (valid) {
-              if (hit >= 0) {
-                ab[i] = static_cast<int32_t>(base + step * 32 + hit);
-              } else {
-                pend |= 1u << u;
-              }
-            }
+            kslot[u] = slot;
+            kbuf[i] = slot;
           }
         }
         match_barrier();
         if (s_ovf != 0 || (kSmemTable && s_used > overflow_limit<CodeT>())) {
           // the whole CTA learns it after the round barrier; P2/P3 are skipped
         } else {
-          // ---------------------------------------------- P2: queries, and last-in-chunk keys
+          // ---------------------------------------------- P2: queries; keys' last step
           bool clast[kPerLane];
 #pragma unroll
           for (int u = 0; u < kPerLane; ++u) {
             const int step = warp + u * kMatchWarps;
             const int i = step * 32 + lane;
             clast[u] = false;
-            if (i < cnt && (kbuf[i] & kKLast)) {
-              const uint32_t m = tab.mask[kslot[u]];
-              clast[u] = (31 - __clz(m)) == step;
-            }
-            if ((pend >> u) & 1u) {
-              CodeT w[kBucket];
-              const uint32_t b = tab.home(qr[u]);
-              load_bucket(tab.code + b * kBucket, w);
-              const uint32_t s = tab.find_from(qr[u], b, w);
+            if (step * 32 < cnt) {  // uniform per warp
+              const bool valid = i < cnt;
+              if (valid) clast[u] = (31 - __clz(tab.mask[kslot[u]])) == step;
+              uint32_t s = kNoSlot, m = 0;
+              if (valid) {
+                CodeT w[kBucket];
+                const uint32_t b = tab.home(qr[u]);
+                load_bucket(tab.code + b * kBucket, w);
+                s = tab.find_from(qr[u], b, w);
+                if (s != kNoSlot) m = tab.mask[s];
+              }
+              int hit = -1;
+              // own step: every lane reads the same row (a broadcast), keeps key lanes < its own
+              if (__any_sync(kFullMask, (m >> step) & 1u)) {
+                const uint4* row = reinterpret_cast<const uint4*>(kbuf + step * 32);
+                const bool look = (m >> step) & 1u;
+#pragma unroll
+                for (int k = 0; k < 8; ++k) {
+                  const uint4 x = row[k];
+                  if (look && 4 * k + 0 < lane && x.x == s) hit = 4 * k + 0;
+                  if (look && 4 * k + 1 < lane && x.y == s) hit = 4 * k + 1;
+                  if (look && 4 * k + 2 < lane && x.z == s) hit = 4 * k + 2;
+                  if (look && 4 * k + 3 < lane && x.w == s) hit = 4 * k + 3;
+                }
+              }
               int32_t a = -1;
-              if (s != kNoSlot) {
-                const uint32_t m = tab.mask[s] & ((1u << step) - 1u);
-                if (m) {
+              if (hit >= 0) {
+                a = static_cast<int32_t>(base + step * 32 + hit);
+              } else if (s != kNoSlot) {
+                const uint32_t me = m & ((1u << step) - 1u);
+                if (me) {
                   // the latest earlier step holding the code: its highest lane with the slot
-                  const int st = 31 - __clz(m);
+                  const int st = 31 - __clz(me);
                   const uint4* row = reinterpret_cast<const uint4*>(kbuf + st * 32);
-                  int hl = -1;
+                  int hl = 0;
 #pragma unroll
                   for (int k = 0; k < 8; ++k) {
                     const uint4 x = row[k];
-                    if ((x.x & kSlotBits) == s) hl = 4 * k;
-                    if ((x.y & kSlotBits) == s) hl = 4 * k + 1;
-                    if ((x.z & kSlotBits) == s) hl = 4 * k + 2;
-                    if ((x.w & kSlotBits) == s) hl = 4 * k + 3;
+                    if (x.x == s) hl = 4 * k + 0;
+                    if (x.y == s) hl = 4 * k + 1;
+                    if (x.z == s) hl = 4 * k + 2;
+                    if (x.w == s) hl = 4 * k + 3;
                   }
                   a = static_cast<int32_t>(base + st * 32 + hl);
                 } else {
-                  const CarryT c = tab.carry[s];
-                  a = (c == Tab::kNoCarry) ? -1 : static_cast<int32_t>(c);
+                  a = static_cast<int32_t>(tab.carry[s]) - 1;  // 0 (none) gives -1
                 }
               }
-              ab[i] = a;
+              if (valid) ab[i] = a;
             }
           }
           match_barrier();
@@ -449,7 +418,7 @@ __global__ void __launch_bounds__(kThreads) match_kernel(const Params p) {
           for (int u = 0; u < kPerLane; ++u) {
             if (clast[u]) {
               const int i = (warp + u * kMatchWarps) * 32 + lane;
-              tab.carry[kslot[u]] = static_cast<CarryT>(base + i);
+              atomicMax(tab.carry + kslot[u], static_cast<uint32_t>(base + i + 1));
               tab.mask[kslot[u]] = 0u;
             }
           }
@@ -488,11 +457,11 @@ __global__ void __launch_bounds__(kThreads) match_kernel(const Params p) {
       int32_t* ltp = p.lt_pos + row0;
       for (uint32_t s = tid; s <= tab.cap; s += kThreads) {
         CodeT c;
-        CarryT m;
+        uint32_t m;
         if (tab.used(s, c, m) && m != Tab::kNoCarry) {
           const uint32_t k = atomicAdd(&s_lt, 1u);
           ltc[k] = c;
-          ltp[k] = static_cast<int32_t>(m);
+          ltp[k] = static_cast<int32_t>(m - 1);
         }
       }
       __syncthreads();
@@ -509,7 +478,7 @@ constexpr uint64_t kOverflowTableBudget = uint64_t(1) << 30;  // bytes of global
 
 template <typename CodeT>
 size_t smem_bytes(bool smem_table) {
-  return (smem_table ? round_up16(Table<CodeT, uint16_t>::bytes(SmemCap<CodeT>::kSlots)) : 0) +
+  return (smem_table ? round_up16(Table<CodeT, uint32_t>::bytes(SmemCap<CodeT>::kSlots)) : 0) +
          kChunkSmem;
 }
 
@@ -527,8 +496,8 @@ Plan make_plan(int64_t N, int64_t T, int code_bytes) {
   Plan pl;
   if (N <= 0 || T <= 0) return pl;
   const uint32_t limit = code_bytes == 4 ? overflow_limit<uint32_t>() : overflow_limit<uint64_t>();
-  pl.fast = T <= kSmemMaxT;
-  const bool may_overflow = !pl.fast || T > static_cast<int64_t>(limit);
+  pl.fast = true;  // any T: a stream with too many distinct keys moves to the global path
+  const bool may_overflow = T > static_cast<int64_t>(limit);
   if (!may_overflow) return pl;
   pl.global = true;
   pl.list_mode = pl.fast;
