@@ -193,6 +193,17 @@ struct Table {
     }
     return kNoSlot;
   }
+  // Branch-free look at one loaded bucket: index of `c` (or -1) and of the first free slot
+  // (or -1).
+  __device__ static void scan(const CodeT (&w)[kBucket], CodeT c, int& found, int& free_at) {
+    found = -1;
+    free_at = -1;
+#pragma unroll
+    for (int k = kBucket - 1; k >= 0; --k) {
+      found = (w[k] == c) ? k : found;
+      free_at = (w[k] == kFree) ? k : free_at;
+    }
+  }
   __device__ bool used(uint32_t s, CodeT& c, CarryT& m) const {
     m = carry[s];
     if (s == cap) {
@@ -280,7 +291,7 @@ __device__ __forceinline__ void gather_chunk(const Params& p, int64_t row0, int6
 }
 
 template <typename CodeT, bool kSmemTable, typename Vec>
-__global__ void __launch_bounds__(kThreads) match_kernel(const Params p) {
+__global__ void __launch_bounds__(kThreads, sizeof(CodeT) == 4 ? 2 : 1) match_kernel(const Params p) {
   using Tab = Table<CodeT, uint32_t>;
   extern __shared__ __align__(16) unsigned char smem[];
   constexpr uint32_t kCap = SmemCap<CodeT>::kSlots;
@@ -328,18 +339,48 @@ __global__ void __launch_bounds__(kThreads) match_kernel(const Params p) {
           qr[u] = i < cnt ? qc[row0 + base + i] : CodeT(0);
         }
         // ---------------------------------------------- P1: keys into the table, step bits
+        // Two steps at a time: both buckets are loaded, scanned and (if needed) claimed side by
+        // side; a lost claim race or a full bucket takes the general probe.
         uint32_t kslot[kPerLane];
 #pragma unroll
-        for (int u = 0; u < kPerLane; ++u) {
-          const int step = warp + u * kMatchWarps;
-          const int i = step * 32 + lane;
-          kslot[u] = kNoSlot;
-          if (i < cnt) {
-            CodeT w[kBucket];
-            const uint32_t b = tab.home(kr[u]);
-            load_bucket(tab.code + b * kBucket, w);
-            uint32_t claimed = 0;
-            const uint32_t slot = tab.insert_from(kr[u], b, w, claimed);
+        for (int u0 = 0; u0 < kPerLane; u0 += 2) {
+          CodeT w[2][kBucket];
+          uint32_t hb[2];
+          bool valid[2];
+#pragma unroll
+          for (int j = 0; j < 2; ++j) {
+            const int i = (warp + (u0 + j) * kMatchWarps) * 32 + lane;
+            valid[j] = i < cnt;
+            hb[j] = tab.home(kr[u0 + j]);
+            if (valid[j]) load_bucket(tab.code + hb[j] * kBucket, w[j]);
+          }
+          int found[2], free_at[2];
+          CodeT old[2];
+#pragma unroll
+          for (int j = 0; j < 2; ++j) {
+            Tab::scan(w[j], kr[u0 + j], found[j], free_at[j]);
+            old[j] = Tab::kFree;
+            if (valid[j] && found[j] < 0 && free_at[j] >= 0 && kr[u0 + j] != Tab::kFree) {
+              old[j] = cas_code(tab.code + hb[j] * kBucket + free_at[j], Tab::kFree, kr[u0 + j]);
+            }
+          }
+#pragma unroll
+          for (int j = 0; j < 2; ++j) {
+            const int u = u0 + j;
+            const int step = warp + u * kMatchWarps;
+            const int i = step * 32 + lane;
+            kslot[u] = kNoSlot;
+            if (!valid[j]) continue;
+            uint32_t slot, claimed = 0;
+            if (found[j] >= 0) {
+              slot = hb[j] * kBucket + found[j];
+            } else if (kr[u] != Tab::kFree && free_at[j] >= 0 && (old[j] == Tab::kFree || old[j] == kr[u])) {
+              slot = hb[j] * kBucket + free_at[j];
+              claimed = old[j] == Tab::kFree;
+            } else {
+              load_bucket(tab.code + hb[j] * kBucket, w[j]);
+              slot = tab.insert_from(kr[u], hb[j], w[j], claimed);
+            }
             if (claimed) atomicAdd(&s_used, 1u);
             if (slot == kNoSlot) {
               s_ovf = 1;
@@ -355,23 +396,44 @@ __global__ void __launch_bounds__(kThreads) match_kernel(const Params p) {
           // the whole CTA learns it after the round barrier; P2/P3 are skipped
         } else {
           // ---------------------------------------------- P2: queries; keys' last step
+          // Two steps at a time, as in P1.
           bool clast[kPerLane];
 #pragma unroll
-          for (int u = 0; u < kPerLane; ++u) {
-            const int step = warp + u * kMatchWarps;
-            const int i = step * 32 + lane;
-            clast[u] = false;
-            if (step * 32 < cnt) {  // uniform per warp
-              const bool valid = i < cnt;
-              if (valid) clast[u] = (31 - __clz(tab.mask[kslot[u]])) == step;
-              uint32_t s = kNoSlot, m = 0;
-              if (valid) {
-                CodeT w[kBucket];
-                const uint32_t b = tab.home(qr[u]);
-                load_bucket(tab.code + b * kBucket, w);
-                s = tab.find_from(qr[u], b, w);
-                if (s != kNoSlot) m = tab.mask[s];
+          for (int u0 = 0; u0 < kPerLane; u0 += 2) {
+            CodeT w[2][kBucket];
+            uint32_t hb[2], s2[2], m2[2];
+            bool valid[2];
+#pragma unroll
+            for (int j = 0; j < 2; ++j) {
+              const int step = warp + (u0 + j) * kMatchWarps;
+              valid[j] = step * 32 + lane < cnt;
+              hb[j] = tab.home(qr[u0 + j]);
+              if (valid[j]) load_bucket(tab.code + hb[j] * kBucket, w[j]);
+              clast[u0 + j] = valid[j] && (31 - __clz(tab.mask[kslot[u0 + j]])) == step;
+            }
+#pragma unroll
+            for (int j = 0; j < 2; ++j) {
+              int found, free_at;
+              Tab::scan(w[j], qr[u0 + j], found, free_at);
+              s2[j] = kNoSlot;
+              if (valid[j]) {
+                if (qr[u0 + j] == Tab::kFree) {
+                  s2[j] = *tab.side ? tab.cap : kNoSlot;
+                } else if (found >= 0) {
+                  s2[j] = hb[j] * kBucket + found;
+                } else if (free_at < 0) {
+                  s2[j] = tab.find_from(qr[u0 + j], hb[j], w[j]);  // full bucket: keep probing
+                }
               }
+              m2[j] = s2[j] != kNoSlot ? tab.mask[s2[j]] : 0u;
+            }
+#pragma unroll
+            for (int j = 0; j < 2; ++j) {
+              const int u = u0 + j;
+              const int step = warp + u * kMatchWarps;
+              if (step * 32 >= cnt) continue;  // uniform per warp
+              const int i = step * 32 + lane;
+              const uint32_t sl = s2[j], m = m2[j];
               int hit = -1;
               // own step: every lane reads the same row (a broadcast), keeps key lanes < its own
               if (__any_sync(kFullMask, (m >> step) & 1u)) {
@@ -380,16 +442,16 @@ __global__ void __launch_bounds__(kThreads) match_kernel(const Params p) {
 #pragma unroll
                 for (int k = 0; k < 8; ++k) {
                   const uint4 x = row[k];
-                  if (look && 4 * k + 0 < lane && x.x == s) hit = 4 * k + 0;
-                  if (look && 4 * k + 1 < lane && x.y == s) hit = 4 * k + 1;
-                  if (look && 4 * k + 2 < lane && x.z == s) hit = 4 * k + 2;
-                  if (look && 4 * k + 3 < lane && x.w == s) hit = 4 * k + 3;
+                  if (look && 4 * k + 0 < lane && x.x == sl) hit = 4 * k + 0;
+                  if (look && 4 * k + 1 < lane && x.y == sl) hit = 4 * k + 1;
+                  if (look && 4 * k + 2 < lane && x.z == sl) hit = 4 * k + 2;
+                  if (look && 4 * k + 3 < lane && x.w == sl) hit = 4 * k + 3;
                 }
               }
               int32_t a = -1;
               if (hit >= 0) {
                 a = static_cast<int32_t>(base + step * 32 + hit);
-              } else if (s != kNoSlot) {
+              } else if (sl != kNoSlot) {
                 const uint32_t me = m & ((1u << step) - 1u);
                 if (me) {
                   // the latest earlier step holding the code: its highest lane with the slot
@@ -399,17 +461,17 @@ __global__ void __launch_bounds__(kThreads) match_kernel(const Params p) {
 #pragma unroll
                   for (int k = 0; k < 8; ++k) {
                     const uint4 x = row[k];
-                    if (x.x == s) hl = 4 * k + 0;
-                    if (x.y == s) hl = 4 * k + 1;
-                    if (x.z == s) hl = 4 * k + 2;
-                    if (x.w == s) hl = 4 * k + 3;
+                    if (x.x == sl) hl = 4 * k + 0;
+                    if (x.y == sl) hl = 4 * k + 1;
+                    if (x.z == sl) hl = 4 * k + 2;
+                    if (x.w == sl) hl = 4 * k + 3;
                   }
                   a = static_cast<int32_t>(base + st * 32 + hl);
                 } else {
-                  a = static_cast<int32_t>(tab.carry[s]) - 1;  // 0 (none) gives -1
+                  a = static_cast<int32_t>(tab.carry[sl]) - 1;  // 0 (none) gives -1
                 }
               }
-              if (valid) ab[i] = a;
+              if (valid[j]) ab[i] = a;
             }
           }
           match_barrier();
