@@ -50,15 +50,19 @@ namespace k2 {
 constexpr int kThreads = 512;
 constexpr int kChunk = 1024;                   // positions per chunk: 32 steps of 32
 constexpr int kSteps = kChunk / 32;
-constexpr int kMatchWarps = 8;                 // warps 0..7: P1..P3
-constexpr int kGathWarp0 = 8, kGathWarps = 8;  // warps 8..15: indices and rows out
+#ifndef LEMA_K2_MATCH_WARPS
+#define LEMA_K2_MATCH_WARPS 8
+#endif
+constexpr int kMatchWarps = LEMA_K2_MATCH_WARPS;  // warps [0, kMatchWarps): P1..P3
+constexpr int kGathWarp0 = kMatchWarps;            // the rest: indices and rows out
+constexpr int kGathWarps = kThreads / 32 - kMatchWarps;
 constexpr int kMatchThreads = kMatchWarps * 32;
 constexpr int kGathThreads = kGathWarps * 32;
-constexpr int kPerLane = kSteps / kMatchWarps;  // steps per matcher warp
+constexpr int kPerLane = (kSteps + kMatchWarps - 1) / kMatchWarps;  // steps per matcher warp
 constexpr int kGatherUnroll = 8;
 constexpr int kBucket = 8;  // slots per table bucket
 static_assert(kSteps == 32, "step masks are 32-bit");
-static_assert(kSteps % kMatchWarps == 0 && kGathWarp0 * 32 + kGathThreads == kThreads, "warp roles");
+static_assert(kMatchWarps > 0 && kGathWarps > 0, "warp roles");
 
 constexpr uint32_t kNoSlot = 0xFFFFFFFFu;
 
@@ -193,17 +197,6 @@ struct Table {
     }
     return kNoSlot;
   }
-  // Branch-free look at one loaded bucket: index of `c` (or -1) and of the first free slot
-  // (or -1).
-  __device__ static void scan(const CodeT (&w)[kBucket], CodeT c, int& found, int& free_at) {
-    found = -1;
-    free_at = -1;
-#pragma unroll
-    for (int k = kBucket - 1; k >= 0; --k) {
-      found = (w[k] == c) ? k : found;
-      free_at = (w[k] == kFree) ? k : free_at;
-    }
-  }
   __device__ bool used(uint32_t s, CodeT& c, CarryT& m) const {
     m = carry[s];
     if (s == cap) {
@@ -239,6 +232,21 @@ struct Params {
   int div_shift;       // log2(words per row) when a power of two, else -1
   uint32_t div_magic;  // floor(2^32 / words per row) + 1 when usable, else 0
 };
+
+// Lanes of a step's 32-entry key row that hold slot `s`, as a bit mask.
+__device__ __forceinline__ uint32_t row_lanes(const uint32_t* row32, uint32_t s) {
+  const uint4* row = reinterpret_cast<const uint4*>(row32);
+  uint32_t m = 0;
+#pragma unroll
+  for (int k = 0; k < 8; ++k) {
+    const uint4 x = row[k];
+    m |= static_cast<uint32_t>(x.x == s) << (4 * k + 0);
+    m |= static_cast<uint32_t>(x.y == s) << (4 * k + 1);
+    m |= static_cast<uint32_t>(x.z == s) << (4 * k + 2);
+    m |= static_cast<uint32_t>(x.w == s) << (4 * k + 3);
+  }
+  return m;
+}
 
 __device__ __forceinline__ void match_barrier() {
   asm volatile("bar.sync 1, %0;" ::"n"(kMatchThreads) : "memory");
@@ -291,7 +299,7 @@ __device__ __forceinline__ void gather_chunk(const Params& p, int64_t row0, int6
 }
 
 template <typename CodeT, bool kSmemTable, typename Vec>
-__global__ void __launch_bounds__(kThreads, sizeof(CodeT) == 4 ? 2 : 1) match_kernel(const Params p) {
+__global__ void __launch_bounds__(kThreads) match_kernel(const Params p) {
   using Tab = Table<CodeT, uint32_t>;
   extern __shared__ __align__(16) unsigned char smem[];
   constexpr uint32_t kCap = SmemCap<CodeT>::kSlots;
@@ -335,52 +343,22 @@ __global__ void __launch_bounds__(kThreads, sizeof(CodeT) == 4 ? 2 : 1) match_ke
 #pragma unroll
         for (int u = 0; u < kPerLane; ++u) {
           const int i = (warp + u * kMatchWarps) * 32 + lane;
-          kr[u] = i < cnt ? kc[row0 + base + i] : CodeT(0);
-          qr[u] = i < cnt ? qc[row0 + base + i] : CodeT(0);
+          kr[u] = (i < cnt && warp + u * kMatchWarps < kSteps) ? kc[row0 + base + i] : CodeT(0);
+          qr[u] = (i < cnt && warp + u * kMatchWarps < kSteps) ? qc[row0 + base + i] : CodeT(0);
         }
         // ---------------------------------------------- P1: keys into the table, step bits
-        // Two steps at a time: both buckets are loaded, scanned and (if needed) claimed side by
-        // side; a lost claim race or a full bucket takes the general probe.
         uint32_t kslot[kPerLane];
 #pragma unroll
-        for (int u0 = 0; u0 < kPerLane; u0 += 2) {
-          CodeT w[2][kBucket];
-          uint32_t hb[2];
-          bool valid[2];
-#pragma unroll
-          for (int j = 0; j < 2; ++j) {
-            const int i = (warp + (u0 + j) * kMatchWarps) * 32 + lane;
-            valid[j] = i < cnt;
-            hb[j] = tab.home(kr[u0 + j]);
-            if (valid[j]) load_bucket(tab.code + hb[j] * kBucket, w[j]);
-          }
-          int found[2], free_at[2];
-          CodeT old[2];
-#pragma unroll
-          for (int j = 0; j < 2; ++j) {
-            Tab::scan(w[j], kr[u0 + j], found[j], free_at[j]);
-            old[j] = Tab::kFree;
-            if (valid[j] && found[j] < 0 && free_at[j] >= 0 && kr[u0 + j] != Tab::kFree) {
-              old[j] = cas_code(tab.code + hb[j] * kBucket + free_at[j], Tab::kFree, kr[u0 + j]);
-            }
-          }
-#pragma unroll
-          for (int j = 0; j < 2; ++j) {
-            const int u = u0 + j;
-            const int step = warp + u * kMatchWarps;
-            const int i = step * 32 + lane;
-            kslot[u] = kNoSlot;
-            if (!valid[j]) continue;
-            uint32_t slot, claimed = 0;
-            if (found[j] >= 0) {
-              slot = hb[j] * kBucket + found[j];
-            } else if (kr[u] != Tab::kFree && free_at[j] >= 0 && (old[j] == Tab::kFree || old[j] == kr[u])) {
-              slot = hb[j] * kBucket + free_at[j];
-              claimed = old[j] == Tab::kFree;
-            } else {
-              load_bucket(tab.code + hb[j] * kBucket, w[j]);
-              slot = tab.insert_from(kr[u], hb[j], w[j], claimed);
-            }
+        for (int u = 0; u < kPerLane; ++u) {
+          const int step = warp + u * kMatchWarps;
+          const int i = step * 32 + lane;
+          kslot[u] = kNoSlot;
+          if (step < kSteps && i < cnt) {
+            CodeT w[kBucket];
+            const uint32_t b = tab.home(kr[u]);
+            load_bucket(tab.code + b * kBucket, w);
+            uint32_t claimed = 0;
+            const uint32_t slot = tab.insert_from(kr[u], b, w, claimed);
             if (claimed) atomicAdd(&s_used, 1u);
             if (slot == kNoSlot) {
               s_ovf = 1;
@@ -396,82 +374,44 @@ __global__ void __launch_bounds__(kThreads, sizeof(CodeT) == 4 ? 2 : 1) match_ke
           // the whole CTA learns it after the round barrier; P2/P3 are skipped
         } else {
           // ---------------------------------------------- P2: queries; keys' last step
-          // Two steps at a time, as in P1.
           bool clast[kPerLane];
 #pragma unroll
-          for (int u0 = 0; u0 < kPerLane; u0 += 2) {
-            CodeT w[2][kBucket];
-            uint32_t hb[2], s2[2], m2[2];
-            bool valid[2];
-#pragma unroll
-            for (int j = 0; j < 2; ++j) {
-              const int step = warp + (u0 + j) * kMatchWarps;
-              valid[j] = step * 32 + lane < cnt;
-              hb[j] = tab.home(qr[u0 + j]);
-              if (valid[j]) load_bucket(tab.code + hb[j] * kBucket, w[j]);
-              clast[u0 + j] = valid[j] && (31 - __clz(tab.mask[kslot[u0 + j]])) == step;
-            }
-#pragma unroll
-            for (int j = 0; j < 2; ++j) {
-              int found, free_at;
-              Tab::scan(w[j], qr[u0 + j], found, free_at);
-              s2[j] = kNoSlot;
-              if (valid[j]) {
-                if (qr[u0 + j] == Tab::kFree) {
-                  s2[j] = *tab.side ? tab.cap : kNoSlot;
-                } else if (found >= 0) {
-                  s2[j] = hb[j] * kBucket + found;
-                } else if (free_at < 0) {
-                  s2[j] = tab.find_from(qr[u0 + j], hb[j], w[j]);  // full bucket: keep probing
-                }
+          for (int u = 0; u < kPerLane; ++u) {
+            const int step = warp + u * kMatchWarps;
+            const int i = step * 32 + lane;
+            clast[u] = false;
+            if (step < kSteps && step * 32 < cnt) {  // uniform per warp
+              const bool valid = i < cnt;
+              if (valid) clast[u] = (31 - __clz(tab.mask[kslot[u]])) == step;
+              uint32_t s = kNoSlot, m = 0;
+              if (valid) {
+                CodeT w[kBucket];
+                const uint32_t b = tab.home(qr[u]);
+                load_bucket(tab.code + b * kBucket, w);
+                s = tab.find_from(qr[u], b, w);
+                if (s != kNoSlot) m = tab.mask[s];
               }
-              m2[j] = s2[j] != kNoSlot ? tab.mask[s2[j]] : 0u;
-            }
-#pragma unroll
-            for (int j = 0; j < 2; ++j) {
-              const int u = u0 + j;
-              const int step = warp + u * kMatchWarps;
-              if (step * 32 >= cnt) continue;  // uniform per warp
-              const int i = step * 32 + lane;
-              const uint32_t sl = s2[j], m = m2[j];
               int hit = -1;
               // own step: every lane reads the same row (a broadcast), keeps key lanes < its own
               if (__any_sync(kFullMask, (m >> step) & 1u)) {
-                const uint4* row = reinterpret_cast<const uint4*>(kbuf + step * 32);
-                const bool look = (m >> step) & 1u;
-#pragma unroll
-                for (int k = 0; k < 8; ++k) {
-                  const uint4 x = row[k];
-                  if (look && 4 * k + 0 < lane && x.x == sl) hit = 4 * k + 0;
-                  if (look && 4 * k + 1 < lane && x.y == sl) hit = 4 * k + 1;
-                  if (look && 4 * k + 2 < lane && x.z == sl) hit = 4 * k + 2;
-                  if (look && 4 * k + 3 < lane && x.w == sl) hit = 4 * k + 3;
-                }
+                const uint32_t lanes = row_lanes(kbuf + step * 32, s) & lanemask_lt();
+                if (((m >> step) & 1u) && lanes) hit = 31 - __clz(lanes);
               }
               int32_t a = -1;
               if (hit >= 0) {
                 a = static_cast<int32_t>(base + step * 32 + hit);
-              } else if (sl != kNoSlot) {
+              } else if (s != kNoSlot) {
                 const uint32_t me = m & ((1u << step) - 1u);
                 if (me) {
                   // the latest earlier step holding the code: its highest lane with the slot
                   const int st = 31 - __clz(me);
-                  const uint4* row = reinterpret_cast<const uint4*>(kbuf + st * 32);
-                  int hl = 0;
-#pragma unroll
-                  for (int k = 0; k < 8; ++k) {
-                    const uint4 x = row[k];
-                    if (x.x == sl) hl = 4 * k + 0;
-                    if (x.y == sl) hl = 4 * k + 1;
-                    if (x.z == sl) hl = 4 * k + 2;
-                    if (x.w == sl) hl = 4 * k + 3;
-                  }
-                  a = static_cast<int32_t>(base + st * 32 + hl);
+                  const uint32_t lanes = row_lanes(kbuf + st * 32, s);
+                  a = static_cast<int32_t>(base + st * 32 + 31 - __clz(lanes | 1u));
                 } else {
-                  a = static_cast<int32_t>(tab.carry[sl]) - 1;  // 0 (none) gives -1
+                  a = static_cast<int32_t>(tab.carry[s]) - 1;  // 0 (none) gives -1
                 }
               }
-              if (valid[j]) ab[i] = a;
+              if (valid) ab[i] = a;
             }
           }
           match_barrier();
