@@ -11,14 +11,18 @@
 //   mask[slot]   bit s set iff a key with that code occurs in step s (32 positions) of the
 //                current chunk
 // A chunk is 32 steps of 32 positions and three phases, all parallel:
-//   P1 (keys)    each key inserts its code into -- or finds it in -- the table (its SLOT),
-//                sets its step's bit in mask[slot], and records the slot in the chunk's key row.
+//   P1 (keys)    each key inserts its code into -- or finds it in -- the table (its SLOT) and
+//                sets its step's bit in mask[slot]. The step's warp then publishes the step's
+//                key slots BIT-SLICED: word b of the step's row is ballot(bit b of the lane's
+//                slot), plus a word of valid lanes.
 //   P2 (queries) each query looks its code up; no slot means no key of that code so far (-1).
-//                If its own step holds the code (mask bit), the latest key lane before it comes
-//                from one broadcast read of the step's 32 key slots; otherwise the highest mask
-//                bit below its step names the latest earlier step holding the code, whose row
-//                gives the lane; with no such step the answer is carry[slot]. Each key also
-//                reads mask[slot] to learn whether its step is the code's last in the chunk.
+//                The key lanes of a step holding slot s are AND_b (s_b ? row[b] : ~row[b]): a
+//                handful of logic ops instead of 32 compares. If the query's own step holds the
+//                code (mask bit), those lanes below its own give the answer; otherwise the
+//                highest mask bit below its step names the latest earlier step holding the
+//                code, whose highest such lane is the answer; with no such step the answer is
+//                carry[slot]. Each key also reads mask[slot] to learn whether its step is the
+//                code's last in the chunk.
 //   P3 (keys of a code's last step) atomicMax(carry[slot], 1 + position); mask[slot] = 0.
 // No warp-wide match instructions are used: on this part they cost far more than the table
 // traffic they would save.
@@ -79,6 +83,9 @@ struct SmemCap<uint64_t> {
   static constexpr uint32_t kSlots = 4096;
 };
 constexpr double kOverflowFrac = 0.75;
+
+static_assert(SmemCap<uint32_t>::kSlots < (1u << 14) && SmemCap<uint64_t>::kSlots < (1u << 14),
+              "shared-memory slots (and the side slot) fit the 14 bit-sliced slot bits");
 
 template <typename CodeT>
 __host__ __device__ constexpr uint32_t overflow_limit() {
@@ -233,18 +240,23 @@ struct Params {
   uint32_t div_magic;  // floor(2^32 / words per row) + 1 when usable, else 0
 };
 
-// Lanes of a step's 32-entry key row that hold slot `s`, as a bit mask.
-__device__ __forceinline__ uint32_t row_lanes(const uint32_t* row32, uint32_t s) {
-  const uint4* row = reinterpret_cast<const uint4*>(row32);
-  uint32_t m = 0;
+// Key lanes of one step whose slot equals s, from the step's bit-sliced row: word b holds
+// ballot(bit b of each lane's slot) for b < kBits, word kBits the valid lanes.
+template <int kBits>
+__device__ __forceinline__ uint32_t sliced_lanes(const uint32_t* row, uint32_t s) {
+  constexpr int kVec = (kBits + 1 + 3) / 4;
+  uint32_t w[4 * kVec];
 #pragma unroll
-  for (int k = 0; k < 8; ++k) {
-    const uint4 x = row[k];
-    m |= static_cast<uint32_t>(x.x == s) << (4 * k + 0);
-    m |= static_cast<uint32_t>(x.y == s) << (4 * k + 1);
-    m |= static_cast<uint32_t>(x.z == s) << (4 * k + 2);
-    m |= static_cast<uint32_t>(x.w == s) << (4 * k + 3);
+  for (int k = 0; k < kVec; ++k) {
+    const uint4 x = reinterpret_cast<const uint4*>(row)[k];
+    w[4 * k] = x.x;
+    w[4 * k + 1] = x.y;
+    w[4 * k + 2] = x.z;
+    w[4 * k + 3] = x.w;
   }
+  uint32_t m = w[kBits];
+#pragma unroll
+  for (int b = 0; b < kBits; ++b) m &= ((s >> b) & 1u) ? w[b] : ~w[b];
   return m;
 }
 
@@ -304,8 +316,11 @@ __global__ void __launch_bounds__(kThreads) match_kernel(const Params p) {
   extern __shared__ __align__(16) unsigned char smem[];
   constexpr uint32_t kCap = SmemCap<CodeT>::kSlots;
   constexpr size_t kTableBytes = kSmemTable ? round_up16(Tab::bytes(kCap)) : 0;
-  uint32_t* kbuf = reinterpret_cast<uint32_t*>(smem + kTableBytes);  // [kChunk] key words
-  int32_t* abuf = reinterpret_cast<int32_t*>(kbuf + kChunk);         // [2][kChunk] answers
+  // slot bits of the bit-sliced step rows: table slots are < 2^14 on the shared-memory path
+  constexpr int kBits = kSmemTable ? 14 : 32;
+  constexpr int kRowWords = kSmemTable ? 16 : 36;
+  uint32_t* srow = reinterpret_cast<uint32_t*>(smem + kTableBytes);  // [kSteps][kRowWords]
+  int32_t* abuf = reinterpret_cast<int32_t*>(srow + kSteps * kRowWords);  // [2][kChunk] answers
   __shared__ uint32_t s_used, s_ovf, s_lt;
 
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
@@ -366,7 +381,19 @@ __global__ void __launch_bounds__(kThreads) match_kernel(const Params p) {
               atomicOr(tab.mask + slot, 1u << step);
             }
             kslot[u] = slot;
-            kbuf[i] = slot;
+          }
+          if (step < kSteps && step * 32 < cnt) {  // uniform per warp: publish the step's row
+            const uint32_t ks = kslot[u];
+            uint32_t* row = srow + step * kRowWords;
+            uint32_t mine = 0;
+#pragma unroll
+            for (int b = 0; b < kBits; ++b) {
+              const uint32_t x = __ballot_sync(kFullMask, (ks >> b) & 1u);
+              if (lane == b) mine = x;
+            }
+            const uint32_t vlanes = __ballot_sync(kFullMask, ks != kNoSlot);
+            if (lane < kBits) row[lane] = mine;
+            if (lane == 0) row[kBits] = vlanes;
           }
         }
         match_barrier();
@@ -394,7 +421,7 @@ __global__ void __launch_bounds__(kThreads) match_kernel(const Params p) {
               int hit = -1;
               // own step: every lane reads the same row (a broadcast), keeps key lanes < its own
               if (__any_sync(kFullMask, (m >> step) & 1u)) {
-                const uint32_t lanes = row_lanes(kbuf + step * 32, s) & lanemask_lt();
+                const uint32_t lanes = sliced_lanes<kBits>(srow + step * kRowWords, s) & lanemask_lt();
                 if (((m >> step) & 1u) && lanes) hit = 31 - __clz(lanes);
               }
               int32_t a = -1;
@@ -405,7 +432,7 @@ __global__ void __launch_bounds__(kThreads) match_kernel(const Params p) {
                 if (me) {
                   // the latest earlier step holding the code: its highest lane with the slot
                   const int st = 31 - __clz(me);
-                  const uint32_t lanes = row_lanes(kbuf + st * 32, s);
+                  const uint32_t lanes = sliced_lanes<kBits>(srow + st * kRowWords, s);
                   a = static_cast<int32_t>(base + st * 32 + 31 - __clz(lanes | 1u));
                 } else {
                   a = static_cast<int32_t>(tab.carry[s]) - 1;  // 0 (none) gives -1
@@ -474,14 +501,18 @@ __global__ void __launch_bounds__(kThreads) match_kernel(const Params p) {
 }
 
 // ---------------------------------------------------------------- host side
-constexpr size_t kChunkSmem = 3 * kChunk * sizeof(uint32_t);  // kbuf + abuf[2]
+// bit-sliced step rows + answers[2]
+template <bool kSmemTable>
+constexpr size_t chunk_smem() {
+  return kSteps * (kSmemTable ? 16 : 36) * sizeof(uint32_t) + 2 * kChunk * sizeof(int32_t);
+}
 constexpr int64_t kMaxOverflowTables = 64;
 constexpr uint64_t kOverflowTableBudget = uint64_t(1) << 30;  // bytes of global tables
 
 template <typename CodeT>
 size_t smem_bytes(bool smem_table) {
-  return (smem_table ? round_up16(Table<CodeT, uint32_t>::bytes(SmemCap<CodeT>::kSlots)) : 0) +
-         kChunkSmem;
+  return smem_table ? round_up16(Table<CodeT, uint32_t>::bytes(SmemCap<CodeT>::kSlots)) + chunk_smem<true>()
+                    : chunk_smem<false>();
 }
 
 struct Plan {
