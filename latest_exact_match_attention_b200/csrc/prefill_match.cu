@@ -23,7 +23,10 @@
 //                code, whose highest such lane is the answer; with no such step the answer is
 //                carry[slot]. Each key also reads mask[slot] to learn whether its step is the
 //                code's last in the chunk.
-//   P3 (keys of a code's last step) atomicMax(carry[slot], 1 + position); mask[slot] = 0.
+//   P3 (the last key of each code in the chunk) carry[slot] = 1 + position; mask[slot] = 0.
+// Shared-memory atomics are kept uncontended: the step's ballots tell each key lane which
+// lanes share its slot, so one lane per slot and step sets the mask bit, and claims are
+// counted once per warp.
 // No warp-wide match instructions are used: on this part they cost far more than the table
 // traffic they would save.
 // Warp roles: 8 matcher warps run P1..P3 on chunk r (named barrier between phases) while 8
@@ -363,37 +366,43 @@ __global__ void __launch_bounds__(kThreads) match_kernel(const Params p) {
         }
         // ---------------------------------------------- P1: keys into the table, step bits
         uint32_t kslot[kPerLane];
+        uint32_t klast = 0;  // bit u: this lane is the last key of its slot in step u
 #pragma unroll
         for (int u = 0; u < kPerLane; ++u) {
           const int step = warp + u * kMatchWarps;
           const int i = step * 32 + lane;
           kslot[u] = kNoSlot;
-          if (step < kSteps && i < cnt) {
+          if (step >= kSteps || step * 32 >= cnt) continue;  // uniform per warp
+          uint32_t claimed = 0;
+          if (i < cnt) {
             CodeT w[kBucket];
             const uint32_t b = tab.home(kr[u]);
             load_bucket(tab.code + b * kBucket, w);
-            uint32_t claimed = 0;
             const uint32_t slot = tab.insert_from(kr[u], b, w, claimed);
-            if (claimed) atomicAdd(&s_used, 1u);
-            if (slot == kNoSlot) {
-              s_ovf = 1;
-            } else {
-              atomicOr(tab.mask + slot, 1u << step);
-            }
+            if (slot == kNoSlot) s_ovf = 1;
             kslot[u] = slot;
           }
-          if (step < kSteps && step * 32 < cnt) {  // uniform per warp: publish the step's row
-            const uint32_t ks = kslot[u];
-            uint32_t* row = srow + step * kRowWords;
-            uint32_t mine = 0;
+          // publish the step's key slots bit-sliced; the same ballots tell each lane which
+          // lanes share its slot, so only the first sets the step bit and the last is known
+          const uint32_t ks = kslot[u];
+          uint32_t bal[kBits];
 #pragma unroll
-            for (int b = 0; b < kBits; ++b) {
-              const uint32_t x = __ballot_sync(kFullMask, (ks >> b) & 1u);
-              if (lane == b) mine = x;
-            }
-            const uint32_t vlanes = __ballot_sync(kFullMask, ks != kNoSlot);
-            if (lane < kBits) row[lane] = mine;
-            if (lane == 0) row[kBits] = vlanes;
+          for (int b = 0; b < kBits; ++b) bal[b] = __ballot_sync(kFullMask, (ks >> b) & 1u);
+          const uint32_t vlanes = __ballot_sync(kFullMask, ks != kNoSlot);
+          uint32_t same = vlanes;
+#pragma unroll
+          for (int b = 0; b < kBits; ++b) same &= ((ks >> b) & 1u) ? bal[b] : ~bal[b];
+          if (ks != kNoSlot) {
+            if ((same & lanemask_lt()) == 0u) atomicOr(tab.mask + ks, 1u << step);
+            if ((same >> lane) == 1u) klast |= 1u << u;
+          }
+          const uint32_t nclaim = __popc(__ballot_sync(kFullMask, claimed != 0));
+          if (lane == 0) {
+            if (nclaim) atomicAdd(&s_used, nclaim);
+            uint32_t* row = srow + step * kRowWords;
+#pragma unroll
+            for (int b = 0; b < kBits; ++b) row[b] = bal[b];
+            row[kBits] = vlanes;
           }
         }
         match_barrier();
@@ -409,7 +418,7 @@ __global__ void __launch_bounds__(kThreads) match_kernel(const Params p) {
             clast[u] = false;
             if (step < kSteps && step * 32 < cnt) {  // uniform per warp
               const bool valid = i < cnt;
-              if (valid) clast[u] = (31 - __clz(tab.mask[kslot[u]])) == step;
+              if ((klast >> u) & 1u) clast[u] = (31 - __clz(tab.mask[kslot[u]])) == step;
               uint32_t s = kNoSlot, m = 0;
               if (valid) {
                 CodeT w[kBucket];
@@ -447,7 +456,7 @@ __global__ void __launch_bounds__(kThreads) match_kernel(const Params p) {
           for (int u = 0; u < kPerLane; ++u) {
             if (clast[u]) {
               const int i = (warp + u * kMatchWarps) * 32 + lane;
-              atomicMax(tab.carry + kslot[u], static_cast<uint32_t>(base + i + 1));
+              tab.carry[kslot[u]] = static_cast<uint32_t>(base + i + 1);  // the slot's unique last key
               tab.mask[kslot[u]] = 0u;
             }
           }
