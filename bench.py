@@ -328,7 +328,10 @@ def run_b200(args):
         "e2e": {"value": e2e_value and round(e2e_value, 2), "unit": UNIT, "h2d_bytes_per_step": h2d,
                 "d2h_bytes_per_step": d2h, "steps": e2e_steps},
         "cpu_baseline": cpu,
-        "gpu_launches": args.steps * (2 if ws_bytes else 1),
+        # per step: the shared-memory match kernel, the overflow-path kernel (launched whenever a
+        # stream could outgrow the shared table, T > 6144; it exits at once when none did) and
+        # the value gather kernel
+        "gpu_launches": args.steps * (3 if T > 6144 else 2),
         "clocks": clocks,
     }
     print(json.dumps(line), flush=True)

@@ -57,19 +57,10 @@ namespace k2 {
 constexpr int kThreads = 512;
 constexpr int kChunk = 1024;                   // positions per chunk: 32 steps of 32
 constexpr int kSteps = kChunk / 32;
-#ifndef LEMA_K2_MATCH_WARPS
-#define LEMA_K2_MATCH_WARPS 8
-#endif
-constexpr int kMatchWarps = LEMA_K2_MATCH_WARPS;  // warps [0, kMatchWarps): P1..P3
-constexpr int kGathWarp0 = kMatchWarps;            // the rest: indices and rows out
-constexpr int kGathWarps = kThreads / 32 - kMatchWarps;
-constexpr int kMatchThreads = kMatchWarps * 32;
-constexpr int kGathThreads = kGathWarps * 32;
-constexpr int kPerLane = (kSteps + kMatchWarps - 1) / kMatchWarps;  // steps per matcher warp
-constexpr int kGatherUnroll = 8;
+constexpr int kMatchWarps = kThreads / 32;                         // every warp matches
+constexpr int kPerLane = (kSteps + kMatchWarps - 1) / kMatchWarps;  // steps per warp
 constexpr int kBucket = 8;  // slots per table bucket
 static_assert(kSteps == 32, "step masks are 32-bit");
-static_assert(kMatchWarps > 0 && kGathWarps > 0, "warp roles");
 
 constexpr uint32_t kNoSlot = 0xFFFFFFFFu;
 
@@ -224,9 +215,6 @@ struct Params {
   const void* kc;
   int64_t N, T;
   int32_t* src;
-  const unsigned char* v;
-  unsigned char* out;
-  int64_t vbytes;
   void* lt_code;
   int32_t* lt_pos;
   int32_t* lt_count;
@@ -238,9 +226,7 @@ struct Params {
   unsigned char* gtables;
   int64_t gtable_bytes;
   uint32_t gslots;
-  int list_mode;       // global path: 1 = streams from ovf_list, 0 = all streams
-  int div_shift;       // log2(words per row) when a power of two, else -1
-  uint32_t div_magic;  // floor(2^32 / words per row) + 1 when usable, else 0
+  int list_mode;  // global path: 1 = streams from ovf_list, 0 = all streams
 };
 
 // Key lanes of one step whose slot equals s, from the step's bit-sliced row: word b holds
@@ -263,9 +249,7 @@ __device__ __forceinline__ uint32_t sliced_lanes(const uint32_t* row, uint32_t s
   return m;
 }
 
-__device__ __forceinline__ void match_barrier() {
-  asm volatile("bar.sync 1, %0;" ::"n"(kMatchThreads) : "memory");
-}
+__device__ __forceinline__ void match_barrier() { __syncthreads(); }
 
 __device__ __forceinline__ uint32_t shfl_code(uint32_t v, int src) {
   return __shfl_sync(kFullMask, v, src);
@@ -274,46 +258,7 @@ __device__ __forceinline__ uint64_t shfl_code(uint64_t v, int src) {
   return static_cast<uint64_t>(__shfl_sync(kFullMask, static_cast<unsigned long long>(v), src));
 }
 
-// Gatherers: indices of one chunk to global memory, then its value rows, kGatherUnroll vector
-// loads in flight per thread before the streaming stores.
-template <typename Vec>
-__device__ __forceinline__ void gather_chunk(const Params& p, int64_t row0, int64_t base, int cnt,
-                                             const int32_t* src_s, int gtid) {
-  if (p.src != nullptr) {
-    for (int i = gtid; i < cnt; i += kGathThreads) p.src[row0 + base + i] = src_s[i];
-  }
-  if (p.out == nullptr) return;
-  const int wpr = static_cast<int>(p.vbytes / static_cast<int64_t>(sizeof(Vec)));
-  const int total = cnt * wpr;
-  const Vec* v = reinterpret_cast<const Vec*>(p.v) + row0 * wpr;
-  Vec* o = reinterpret_cast<Vec*>(p.out) + (row0 + base) * wpr;
-  // row of word w: a shift for power-of-two rows, else a multiply-high by a magic reciprocal
-  // (exact for w * wpr < 2^32, which the host guarantees), else a division
-  const int dshift = p.div_shift;
-  const uint32_t dmagic = p.div_magic;
-  for (int w0 = gtid; w0 < total; w0 += kGathThreads * kGatherUnroll) {
-    Vec val[kGatherUnroll];
-#pragma unroll
-    for (int u = 0; u < kGatherUnroll; ++u) {
-      const int w = w0 + u * kGathThreads;
-      val[u] = zero_vec<Vec>();
-      if (w < total) {
-        const int r = dshift >= 0 ? (w >> dshift)
-                                  : (dmagic ? static_cast<int>(__umulhi(static_cast<uint32_t>(w), dmagic))
-                                            : w / wpr);
-        const int32_t s = src_s[r];
-        if (s >= 0) val[u] = __ldg(v + static_cast<int64_t>(s) * wpr + (w - r * wpr));
-      }
-    }
-#pragma unroll
-    for (int u = 0; u < kGatherUnroll; ++u) {
-      const int w = w0 + u * kGathThreads;
-      if (w < total) store_stream(o + w, val[u]);
-    }
-  }
-}
-
-template <typename CodeT, bool kSmemTable, typename Vec>
+template <typename CodeT, bool kSmemTable>
 __global__ void __launch_bounds__(kThreads) match_kernel(const Params p) {
   using Tab = Table<CodeT, uint32_t>;
   extern __shared__ __align__(16) unsigned char smem[];
@@ -323,7 +268,6 @@ __global__ void __launch_bounds__(kThreads) match_kernel(const Params p) {
   constexpr int kBits = kSmemTable ? 14 : 32;
   constexpr int kRowWords = kSmemTable ? 16 : 36;
   uint32_t* srow = reinterpret_cast<uint32_t*>(smem + kTableBytes);  // [kSteps][kRowWords]
-  int32_t* abuf = reinterpret_cast<int32_t*>(srow + kSteps * kRowWords);  // [2][kChunk] answers
   __shared__ uint32_t s_used, s_ovf, s_lt;
 
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
@@ -351,12 +295,12 @@ __global__ void __launch_bounds__(kThreads) match_kernel(const Params p) {
     __syncthreads();
 
     bool aborted = false;
-    for (int64_t r = 0; r <= n_chunks; ++r) {
-      if (warp < kMatchWarps && r < n_chunks) {
-        // ==================================================== matchers: chunk r
+    for (int64_t r = 0; r < n_chunks; ++r) {
+      {
+        // ==================================================== chunk r
         const int64_t base = r * kChunk;
         const int cnt = static_cast<int>(min(static_cast<int64_t>(kChunk), p.T - base));
-        int32_t* ab = abuf + (r & 1) * kChunk;
+        int32_t* ab = p.src + row0 + base;
         CodeT kr[kPerLane], qr[kPerLane];
 #pragma unroll
         for (int u = 0; u < kPerLane; ++u) {
@@ -461,12 +405,6 @@ __global__ void __launch_bounds__(kThreads) match_kernel(const Params p) {
             }
           }
         }
-      } else if (warp >= kGathWarp0 && r >= 1) {
-        // ==================================================== gatherers: chunk r-1
-        const int64_t c = r - 1;
-        const int64_t base = c * kChunk;
-        const int cnt = static_cast<int>(min(static_cast<int64_t>(kChunk), p.T - base));
-        gather_chunk<Vec>(p, row0, base, cnt, abuf + (c & 1) * kChunk, tid - kGathWarp0 * 32);
       }
       __syncthreads();
       if (s_ovf != 0 || (kSmemTable && s_used > overflow_limit<CodeT>())) {
@@ -509,11 +447,97 @@ __global__ void __launch_bounds__(kThreads) match_kernel(const Params p) {
   }
 }
 
+
+// ---------------------------------------------------------------- the value gather
+// out[n][i] = v[n][src[n][i]] (vbytes-byte rows), zeros where src is -1. A separate kernel
+// on purpose: value traffic in the same SM as the matcher's shared-memory table multiplies
+// the latency of every table access, so the two do not share SMs. Each CTA owns one
+// contiguous run of output words of one stream (blockIdx.y), kGUnroll loads in flight per
+// thread, streaming stores.
+constexpr int kGThreads = 256;
+constexpr int kGUnroll = 8;
+
+struct GatherParams {
+  const int32_t* src;
+  const unsigned char* v;
+  unsigned char* out;
+  int64_t N, T;
+  uint32_t wpr;        // vector words per row
+  uint32_t words;      // words per stream = T * wpr (< 2^32)
+  int div_shift;       // log2(wpr) when a power of two, else -1
+  uint32_t div_magic;  // floor(2^32 / wpr) + 1 when exact for every word index, else 0
+};
+
+template <typename Vec>
+__global__ void __launch_bounds__(kGThreads) gather_kernel(const GatherParams g) {
+  const uint32_t w0 = blockIdx.x * (kGThreads * kGUnroll) + threadIdx.x;
+  for (int64_t n = blockIdx.y; n < g.N; n += gridDim.y) {
+    const int32_t* src = g.src + n * g.T;
+    const Vec* v = reinterpret_cast<const Vec*>(g.v) + n * static_cast<int64_t>(g.words);
+    Vec* o = reinterpret_cast<Vec*>(g.out) + n * static_cast<int64_t>(g.words);
+    Vec val[kGUnroll];
+#pragma unroll
+    for (int u = 0; u < kGUnroll; ++u) {
+      const uint32_t w = w0 + u * kGThreads;
+      val[u] = zero_vec<Vec>();
+      if (w < g.words) {
+        const uint32_t r = g.div_shift >= 0 ? (w >> g.div_shift)
+                                            : (g.div_magic ? __umulhi(w, g.div_magic) : w / g.wpr);
+        const int32_t s = __ldg(src + r);
+        if (s >= 0) val[u] = __ldg(v + static_cast<int64_t>(s) * g.wpr + (w - r * g.wpr));
+      }
+    }
+#pragma unroll
+    for (int u = 0; u < kGUnroll; ++u) {
+      const uint32_t w = w0 + u * kGThreads;
+      if (w < g.words) store_stream(o + w, val[u]);
+    }
+  }
+}
+
+template <typename Vec>
+int launch_gather(const MatchLaunch& a, const int32_t* src) {
+  GatherParams g{};
+  g.src = src;
+  g.v = static_cast<const unsigned char*>(a.v);
+  g.out = static_cast<unsigned char*>(a.out);
+  g.N = a.N;
+  g.T = a.T;
+  const uint64_t wpr = static_cast<uint64_t>(a.vbytes) / sizeof(Vec);
+  const uint64_t words = static_cast<uint64_t>(a.T) * wpr;
+  if (words >= (uint64_t(1) << 32)) return fail(LEMA_ERR_INVALID_ARGUMENT, "T * row words = %llu exceeds 2^32", (unsigned long long)words);
+  g.wpr = static_cast<uint32_t>(wpr);
+  g.words = static_cast<uint32_t>(words);
+  g.div_shift = -1;
+  g.div_magic = 0;
+  if ((wpr & (wpr - 1)) == 0) {
+    g.div_shift = log2_exact(wpr);
+  } else if (words * wpr < (uint64_t(1) << 32)) {  // multiply-high is exact for w * wpr < 2^32
+    g.div_magic = static_cast<uint32_t>(0xFFFFFFFFull / wpr + 1);
+  }
+  const uint64_t per_cta = kGThreads * kGUnroll;
+  const dim3 grid(static_cast<unsigned>((words + per_cta - 1) / per_cta),
+                  static_cast<unsigned>(std::min<int64_t>(a.N, 65535)));
+  gather_kernel<Vec><<<grid, kGThreads, 0, a.stream>>>(g);
+  LEMA_CUDA_TRY(cudaGetLastError());
+  return LEMA_OK;
+}
+
+int run_gather(const MatchLaunch& a, const int32_t* src) {
+  const bool a16 = a.vbytes % 16 == 0 && aligned(a.v, 16) && aligned(a.out, 16);
+  const bool a8 = a.vbytes % 8 == 0 && aligned(a.v, 8) && aligned(a.out, 8);
+  const bool a4 = a.vbytes % 4 == 0 && aligned(a.v, 4) && aligned(a.out, 4);
+  if (a16) return launch_gather<uint4>(a, src);
+  if (a8) return launch_gather<uint2>(a, src);
+  if (a4) return launch_gather<uint32_t>(a, src);
+  return launch_gather<unsigned short>(a, src);
+}
+
 // ---------------------------------------------------------------- host side
-// bit-sliced step rows + answers[2]
+// bit-sliced step rows
 template <bool kSmemTable>
 constexpr size_t chunk_smem() {
-  return kSteps * (kSmemTable ? 16 : 36) * sizeof(uint32_t) + 2 * kChunk * sizeof(int32_t);
+  return kSteps * (kSmemTable ? 16 : 36) * sizeof(uint32_t);
 }
 constexpr int64_t kMaxOverflowTables = 64;
 constexpr uint64_t kOverflowTableBudget = uint64_t(1) << 30;  // bytes of global tables
@@ -525,6 +549,7 @@ size_t smem_bytes(bool smem_table) {
 }
 
 struct Plan {
+  size_t off_src = 0;      // index scratch (used when the caller passes no src)
   bool fast = false;       // run the shared-memory kernel
   bool global = false;     // run the global-table kernel
   bool list_mode = false;  // global kernel reads the overflow list
@@ -539,6 +564,8 @@ Plan make_plan(int64_t N, int64_t T, int code_bytes) {
   if (N <= 0 || T <= 0) return pl;
   const uint32_t limit = code_bytes == 4 ? overflow_limit<uint32_t>() : overflow_limit<uint64_t>();
   pl.fast = true;  // any T: a stream with too many distinct keys moves to the global path
+  const size_t src_bytes = round_up(4 * static_cast<size_t>(N) * static_cast<size_t>(T), 256);
+  pl.total = src_bytes;
   const bool may_overflow = T > static_cast<int64_t>(limit);
   if (!may_overflow) return pl;
   pl.global = true;
@@ -550,40 +577,27 @@ Plan make_plan(int64_t N, int64_t T, int code_bytes) {
   pl.n_gtables = std::max<int64_t>(
       1, std::min<int64_t>({N, kMaxOverflowTables,
                             static_cast<int64_t>(kOverflowTableBudget / pl.gtable_bytes)}));
-  pl.off_list = 256;
+  pl.off_list = src_bytes + 256;
   pl.off_tables = round_up(pl.off_list + 4 * static_cast<size_t>(N), 256);
   pl.total = pl.off_tables + static_cast<size_t>(pl.n_gtables * pl.gtable_bytes);
   return pl;
 }
 
-template <typename CodeT, typename Vec>
+template <typename CodeT>
 int run(const MatchLaunch& a, const Plan& pl, const DeviceInfo& dev) {
+  unsigned char* ws = static_cast<unsigned char*>(a.ws);
   Params p{};
   p.qc = a.qc;
   p.kc = a.kc;
   p.N = a.N;
   p.T = a.T;
-  p.src = a.src;
-  p.v = static_cast<const unsigned char*>(a.v);
-  p.out = static_cast<unsigned char*>(a.out);
-  p.vbytes = a.vbytes;
+  p.src = a.src ? a.src : reinterpret_cast<int32_t*>(ws + pl.off_src);
   p.lt_code = a.lt_code;
   p.lt_pos = a.lt_pos;
   p.lt_count = a.lt_count;
   p.status = a.status;
-  {
-    const int64_t wpr = a.out ? a.vbytes / static_cast<int64_t>(sizeof(Vec)) : 1;
-    p.div_shift = -1;
-    p.div_magic = 0;
-    if ((wpr & (wpr - 1)) == 0) {
-      p.div_shift = log2_exact(static_cast<uint64_t>(wpr));
-    } else if (static_cast<uint64_t>(kChunk) * wpr * wpr < (uint64_t(1) << 32)) {
-      p.div_magic = static_cast<uint32_t>(0xFFFFFFFFull / static_cast<uint64_t>(wpr) + 1);
-    }
-  }
-  unsigned char* ws = static_cast<unsigned char*>(a.ws);
   if (pl.global) {
-    p.ovf_count = reinterpret_cast<uint32_t*>(ws);
+    p.ovf_count = reinterpret_cast<uint32_t*>(ws + pl.off_list - 256);
     p.ovf_list = reinterpret_cast<uint32_t*>(ws + pl.off_list);
     p.gtables = ws + pl.off_tables;
     p.gtable_bytes = pl.gtable_bytes;
@@ -591,7 +605,7 @@ int run(const MatchLaunch& a, const Plan& pl, const DeviceInfo& dev) {
     if (pl.list_mode) LEMA_CUDA_TRY(cudaMemsetAsync(p.ovf_count, 0, sizeof(uint32_t), a.stream));
   }
   if (pl.fast) {
-    auto kern = match_kernel<CodeT, true, Vec>;
+    auto kern = match_kernel<CodeT, true>;
     const size_t sm = smem_bytes<CodeT>(true);
     LEMA_CUDA_TRY(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(sm)));
     int per_sm = 0;
@@ -602,25 +616,14 @@ int run(const MatchLaunch& a, const Plan& pl, const DeviceInfo& dev) {
   }
   if (pl.global) {
     p.list_mode = pl.list_mode ? 1 : 0;
-    auto kern = match_kernel<CodeT, false, Vec>;
+    auto kern = match_kernel<CodeT, false>;
     const size_t sm = smem_bytes<CodeT>(false);
     LEMA_CUDA_TRY(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(sm)));
     kern<<<static_cast<unsigned>(pl.n_gtables), kThreads, sm, a.stream>>>(p);
     LEMA_CUDA_TRY(cudaGetLastError());
   }
+  if (a.out != nullptr) return run_gather(a, p.src);
   return LEMA_OK;
-}
-
-template <typename CodeT>
-int run_code(const MatchLaunch& a, const Plan& pl, const DeviceInfo& dev) {
-  if (a.out == nullptr) return run<CodeT, uint4>(a, pl, dev);
-  const bool a16 = a.vbytes % 16 == 0 && aligned(a.v, 16) && aligned(a.out, 16);
-  const bool a8 = a.vbytes % 8 == 0 && aligned(a.v, 8) && aligned(a.out, 8);
-  const bool a4 = a.vbytes % 4 == 0 && aligned(a.v, 4) && aligned(a.out, 4);
-  if (a16) return run<CodeT, uint4>(a, pl, dev);
-  if (a8) return run<CodeT, uint2>(a, pl, dev);
-  if (a4) return run<CodeT, uint32_t>(a, pl, dev);
-  return run<CodeT, unsigned short>(a, pl, dev);
 }
 
 }  // namespace k2
@@ -640,7 +643,7 @@ int launch_match(const MatchLaunch& a) {
     if (a.v == nullptr) return fail(LEMA_ERR_INVALID_ARGUMENT, "out given without values");
     if (a.vbytes <= 0 || a.vbytes % 2 != 0) return fail(LEMA_ERR_INVALID_ARGUMENT, "vbytes must be a positive multiple of 2, got %lld", (long long)a.vbytes);
     if (!aligned(a.v, 2) || !aligned(a.out, 2)) return fail(LEMA_ERR_INVALID_ARGUMENT, "value rows must be 2-byte aligned");
-    if (a.vbytes / 2 * k2::kChunk > (int64_t(1) << 31)) return fail(LEMA_ERR_INVALID_ARGUMENT, "vbytes %lld too large", (long long)a.vbytes);
+    if (static_cast<uint64_t>(a.T) * static_cast<uint64_t>(a.vbytes / 2) >= (uint64_t(1) << 32)) return fail(LEMA_ERR_INVALID_ARGUMENT, "T * vbytes too large for one stream (%lld x %lld)", (long long)a.T, (long long)a.vbytes);
   }
   const bool lt_any = a.lt_code || a.lt_pos || a.lt_count;
   if (lt_any && !(a.lt_code && a.lt_pos && a.lt_count)) return fail(LEMA_ERR_INVALID_ARGUMENT, "last-occurrence outputs: all three or none");
@@ -652,7 +655,7 @@ int launch_match(const MatchLaunch& a) {
   const DeviceInfo* dev = current_device_info();
   if (dev == nullptr) return LEMA_ERR_CUDA;
   if (dev->cc_major != 10) return fail(LEMA_ERR_UNSUPPORTED, "built for sm_100a; device is sm_%d%d", dev->cc_major, dev->cc_minor);
-  return a.code_bytes == 4 ? k2::run_code<uint32_t>(a, pl, *dev) : k2::run_code<uint64_t>(a, pl, *dev);
+  return a.code_bytes == 4 ? k2::run<uint32_t>(a, pl, *dev) : k2::run<uint64_t>(a, pl, *dev);
 }
 
 }  // namespace lema
