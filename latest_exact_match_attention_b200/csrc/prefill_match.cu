@@ -198,6 +198,50 @@ struct Table {
     }
     return kNoSlot;
   }
+  // One-bucket fast paths, branch-free in the common case; a full bucket or a lost claim race
+  // falls back to the general probe.
+  __device__ uint32_t insert_fast(CodeT c, uint32_t& claimed) {
+    if (c == kFree) {
+      claimed = atomicCAS(side, 0u, 1u) == 0u;
+      return cap;
+    }
+    const uint32_t b = home(c);
+    CodeT w[kBucket];
+    load_bucket(code + b * kBucket, w);
+    uint32_t eq = 0, fr = 0;
+#pragma unroll
+    for (int k = 0; k < kBucket; ++k) {
+      eq |= static_cast<uint32_t>(w[k] == c) << k;
+      fr |= static_cast<uint32_t>(w[k] == kFree) << k;
+    }
+    if (eq) return b * kBucket + (__ffs(eq) - 1);
+    if (fr) {
+      const int k = __ffs(fr) - 1;
+      const CodeT old = cas_code(code + b * kBucket + k, kFree, c);
+      if (old == kFree) {
+        claimed = 1;
+        return b * kBucket + k;
+      }
+      if (old == c) return b * kBucket + k;
+    }
+    load_bucket(code + b * kBucket, w);
+    return insert_from(c, b, w, claimed);
+  }
+  __device__ uint32_t find_fast(CodeT c) const {
+    if (c == kFree) return *side ? cap : kNoSlot;
+    const uint32_t b = home(c);
+    CodeT w[kBucket];
+    load_bucket(code + b * kBucket, w);
+    uint32_t eq = 0, fr = 0;
+#pragma unroll
+    for (int k = 0; k < kBucket; ++k) {
+      eq |= static_cast<uint32_t>(w[k] == c) << k;
+      fr |= static_cast<uint32_t>(w[k] == kFree) << k;
+    }
+    if (eq) return b * kBucket + (__ffs(eq) - 1);
+    if (fr) return kNoSlot;
+    return find_from(c, b, w);
+  }
   __device__ bool used(uint32_t s, CodeT& c, CarryT& m) const {
     m = carry[s];
     if (s == cap) {
@@ -230,9 +274,28 @@ struct Params {
 };
 
 // Key lanes of one step whose slot equals s, from the step's bit-sliced row: word b holds
-// ballot(bit b of each lane's slot) for b < kBits, word kBits the valid lanes.
+// ballot(bit b of each lane's slot) for b < kBits, word kBits the valid lanes. `sb[b]` is all
+// ones where bit b of s is set, so lanes agreeing on bit b are ~(row[b] ^ sb[b]).
 template <int kBits>
-__device__ __forceinline__ uint32_t sliced_lanes(const uint32_t* row, uint32_t s) {
+__device__ __forceinline__ uint32_t sliced_lanes(const uint32_t* row, const uint32_t (&sb)[kBits]) {
+  constexpr int kVec = (kBits + 1 + 3) / 4;
+  uint32_t w[4 * kVec];
+#pragma unroll
+  for (int k = 0; k < kVec; ++k) {
+    const uint4 x = reinterpret_cast<const uint4*>(row)[k];
+    w[4 * k] = x.x;
+    w[4 * k + 1] = x.y;
+    w[4 * k + 2] = x.z;
+    w[4 * k + 3] = x.w;
+  }
+  uint32_t m = w[kBits];
+#pragma unroll
+  for (int b = 0; b < kBits; ++b) m &= ~(w[b] ^ sb[b]);
+  return m;
+}
+
+template <int kBits>
+__device__ __forceinline__ uint32_t sliced_lanes_unused(const uint32_t* row, uint32_t s) {
   constexpr int kVec = (kBits + 1 + 3) / 4;
   uint32_t w[4 * kVec];
 #pragma unroll
@@ -309,31 +372,32 @@ __global__ void __launch_bounds__(kThreads) match_kernel(const Params p) {
           qr[u] = (i < cnt && warp + u * kMatchWarps < kSteps) ? qc[row0 + base + i] : CodeT(0);
         }
         // ---------------------------------------------- P1: keys into the table, step bits
-        uint32_t kslot[kPerLane];
+        const int32_t base32 = static_cast<int32_t>(base);
+        uint32_t kslot[kPerLane], qslot[kPerLane];
         uint32_t klast = 0;  // bit u: this lane is the last key of its slot in step u
 #pragma unroll
         for (int u = 0; u < kPerLane; ++u) {
           const int step = warp + u * kMatchWarps;
           const int i = step * 32 + lane;
           kslot[u] = kNoSlot;
+          qslot[u] = kNoSlot;
           if (step >= kSteps || step * 32 >= cnt) continue;  // uniform per warp
+          const bool valid = i < cnt;
           uint32_t claimed = 0;
-          if (i < cnt) {
-            CodeT w[kBucket];
-            const uint32_t b = tab.home(kr[u]);
-            load_bucket(tab.code + b * kBucket, w);
-            const uint32_t slot = tab.insert_from(kr[u], b, w, claimed);
-            if (slot == kNoSlot) s_ovf = 1;
-            kslot[u] = slot;
+          if (valid) {
+            kslot[u] = tab.insert_fast(kr[u], claimed);
+            if (kslot[u] == kNoSlot) s_ovf = 1;
           }
           // publish the step's key slots bit-sliced; the same ballots tell each lane which
           // lanes share its slot, so only the first sets the step bit and the last is known
           const uint32_t ks = kslot[u];
-          uint32_t bal[kBits];
+          uint32_t bal[kRowWords];
 #pragma unroll
           for (int b = 0; b < kBits; ++b) bal[b] = __ballot_sync(kFullMask, (ks >> b) & 1u);
-          const uint32_t vlanes = __ballot_sync(kFullMask, ks != kNoSlot);
-          uint32_t same = vlanes;
+          bal[kBits] = __ballot_sync(kFullMask, ks != kNoSlot);
+#pragma unroll
+          for (int b = kBits + 1; b < kRowWords; ++b) bal[b] = 0u;
+          uint32_t same = bal[kBits];
 #pragma unroll
           for (int b = 0; b < kBits; ++b) same &= ((ks >> b) & 1u) ? bal[b] : ~bal[b];
           if (ks != kNoSlot) {
@@ -343,64 +407,67 @@ __global__ void __launch_bounds__(kThreads) match_kernel(const Params p) {
           const uint32_t nclaim = __popc(__ballot_sync(kFullMask, claimed != 0));
           if (lane == 0) {
             if (nclaim) atomicAdd(&s_used, nclaim);
-            uint32_t* row = srow + step * kRowWords;
+            uint4* row = reinterpret_cast<uint4*>(srow + step * kRowWords);
 #pragma unroll
-            for (int b = 0; b < kBits; ++b) row[b] = bal[b];
-            row[kBits] = vlanes;
+            for (int k = 0; k < kRowWords / 4; ++k) row[k] = make_uint4(bal[4 * k], bal[4 * k + 1], bal[4 * k + 2], bal[4 * k + 3]);
           }
+          // the query's slot, looked up after this step's own inserts: a code this step inserted
+          // is always found; a miss may be stale (another warp's concurrent insert) and is
+          // looked up again after the barrier
+          __syncwarp();
+          if (valid) qslot[u] = tab.find_fast(qr[u]);
         }
         match_barrier();
         if (s_ovf != 0 || (kSmemTable && s_used > overflow_limit<CodeT>())) {
           // the whole CTA learns it after the round barrier; P2/P3 are skipped
         } else {
           // ---------------------------------------------- P2: queries; keys' last step
-          bool clast[kPerLane];
+          uint32_t clast = 0;
 #pragma unroll
           for (int u = 0; u < kPerLane; ++u) {
             const int step = warp + u * kMatchWarps;
             const int i = step * 32 + lane;
-            clast[u] = false;
-            if (step < kSteps && step * 32 < cnt) {  // uniform per warp
-              const bool valid = i < cnt;
-              if ((klast >> u) & 1u) clast[u] = (31 - __clz(tab.mask[kslot[u]])) == step;
-              uint32_t s = kNoSlot, m = 0;
-              if (valid) {
-                CodeT w[kBucket];
-                const uint32_t b = tab.home(qr[u]);
-                load_bucket(tab.code + b * kBucket, w);
-                s = tab.find_from(qr[u], b, w);
-                if (s != kNoSlot) m = tab.mask[s];
-              }
-              int hit = -1;
-              // own step: every lane reads the same row (a broadcast), keeps key lanes < its own
-              if (__any_sync(kFullMask, (m >> step) & 1u)) {
-                const uint32_t lanes = sliced_lanes<kBits>(srow + step * kRowWords, s) & lanemask_lt();
-                if (((m >> step) & 1u) && lanes) hit = 31 - __clz(lanes);
-              }
-              int32_t a = -1;
-              if (hit >= 0) {
-                a = static_cast<int32_t>(base + step * 32 + hit);
-              } else if (s != kNoSlot) {
-                const uint32_t me = m & ((1u << step) - 1u);
-                if (me) {
-                  // the latest earlier step holding the code: its highest lane with the slot
-                  const int st = 31 - __clz(me);
-                  const uint32_t lanes = sliced_lanes<kBits>(srow + st * kRowWords, s);
-                  a = static_cast<int32_t>(base + st * 32 + 31 - __clz(lanes | 1u));
-                } else {
-                  a = static_cast<int32_t>(tab.carry[s]) - 1;  // 0 (none) gives -1
-                }
-              }
-              if (valid) ab[i] = a;
+            if (step >= kSteps || step * 32 >= cnt) continue;  // uniform per warp
+            const bool valid = i < cnt;
+            if ((klast >> u) & 1u) {
+              if ((31 - __clz(tab.mask[kslot[u]])) == step) clast |= 1u << u;
             }
+            uint32_t sl = qslot[u];
+            if (valid && sl == kNoSlot) sl = tab.find_fast(qr[u]);
+            const uint32_t m = sl != kNoSlot ? tab.mask[sl] : 0u;
+            uint32_t sb[kBits];
+#pragma unroll
+            for (int b = 0; b < kBits; ++b) sb[b] = 0u - ((sl >> b) & 1u);
+            int32_t a = -1;
+            bool done = !valid || sl == kNoSlot;
+            // own step: every lane reads the same row (a broadcast), keeps key lanes < its own
+            if (__any_sync(kFullMask, !done && ((m >> step) & 1u))) {
+              const uint32_t lanes = sliced_lanes<kBits>(srow + step * kRowWords, sb) & lanemask_lt();
+              if (!done && ((m >> step) & 1u) && lanes) {
+                a = base32 + step * 32 + (31 - __clz(lanes));
+                done = true;
+              }
+            }
+            // the latest earlier step holding the code: its highest lane with the slot
+            const uint32_t me = m & ((1u << step) - 1u);
+            if (__any_sync(kFullMask, !done && me)) {
+              const int st = me ? 31 - __clz(me) : 0;
+              const uint32_t lanes = sliced_lanes<kBits>(srow + st * kRowWords, sb);
+              if (!done && me) {
+                a = base32 + st * 32 + (31 - __clz(lanes | 1u));
+                done = true;
+              }
+            }
+            if (!done) a = static_cast<int32_t>(tab.carry[sl]) - 1;  // 0 (none) gives -1
+            if (valid) ab[i] = a;
           }
           match_barrier();
           // ---------------------------------------------- P3: carries of the chunk's last keys
 #pragma unroll
           for (int u = 0; u < kPerLane; ++u) {
-            if (clast[u]) {
+            if ((clast >> u) & 1u) {
               const int i = (warp + u * kMatchWarps) * 32 + lane;
-              tab.carry[kslot[u]] = static_cast<uint32_t>(base + i + 1);  // the slot's unique last key
+              tab.carry[kslot[u]] = static_cast<uint32_t>(base32 + i + 1);  // the slot's unique last key
               tab.mask[kslot[u]] = 0u;
             }
           }
