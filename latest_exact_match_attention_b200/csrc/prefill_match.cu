@@ -29,9 +29,8 @@
 // counted once per warp.
 // No warp-wide match instructions are used: on this part they cost far more than the table
 // traffic they would save.
-// Warp roles: 8 matcher warps run P1..P3 on chunk r (named barrier between phases) while 8
-// gatherer warps write indices and value rows of chunk r-1 (16-byte vectors, eight loads in
-// flight per thread, streaming stores, zeros for misses); a CTA barrier ends each round.
+// All 16 warps of a CTA run the phases (two steps each per chunk); CTA barriers separate them.
+// The value rows are copied by a separate kernel afterwards (see gather_kernel).
 //
 // The table is bucketed: 8 slots per bucket, read with vector loads, linear probing over
 // buckets; a claim is one compare-and-swap of a free code word (all ones), and the all-ones
@@ -294,32 +293,8 @@ __device__ __forceinline__ uint32_t sliced_lanes(const uint32_t* row, const uint
   return m;
 }
 
-template <int kBits>
-__device__ __forceinline__ uint32_t sliced_lanes_unused(const uint32_t* row, uint32_t s) {
-  constexpr int kVec = (kBits + 1 + 3) / 4;
-  uint32_t w[4 * kVec];
-#pragma unroll
-  for (int k = 0; k < kVec; ++k) {
-    const uint4 x = reinterpret_cast<const uint4*>(row)[k];
-    w[4 * k] = x.x;
-    w[4 * k + 1] = x.y;
-    w[4 * k + 2] = x.z;
-    w[4 * k + 3] = x.w;
-  }
-  uint32_t m = w[kBits];
-#pragma unroll
-  for (int b = 0; b < kBits; ++b) m &= ((s >> b) & 1u) ? w[b] : ~w[b];
-  return m;
-}
-
 __device__ __forceinline__ void match_barrier() { __syncthreads(); }
 
-__device__ __forceinline__ uint32_t shfl_code(uint32_t v, int src) {
-  return __shfl_sync(kFullMask, v, src);
-}
-__device__ __forceinline__ uint64_t shfl_code(uint64_t v, int src) {
-  return static_cast<uint64_t>(__shfl_sync(kFullMask, static_cast<unsigned long long>(v), src));
-}
 
 template <typename CodeT, bool kSmemTable>
 __global__ void __launch_bounds__(kThreads) match_kernel(const Params p) {
