@@ -97,7 +97,9 @@ int lema_proj_codes(const void* x, const void* w_qk, int64_t M, int64_t K,
 /* ---------------------------------------------- (b) prefill latest match */
 /*
  * Bytes of device workspace lema_prefill_match needs for n_streams x T
- * positions (0 is a valid answer: then `workspace` may be NULL).
+ * positions: room for the indices (used when src is NULL) plus, when a stream can
+ * hold more distinct key codes than the on-chip table takes, the overflow-path
+ * tables. 256-byte aligned workspace required.
  */
 size_t lema_prefill_workspace_bytes(int64_t n_streams, int64_t T, int code_bytes);
 
