@@ -121,6 +121,34 @@ int lema_prefill_match(const void* qcodes, const void* kcodes, int code_bytes,
                        void* workspace, size_t workspace_bytes, uint32_t* status,
                        void* stream);
 
+/*
+ * lema_prefill_match_noalloc: lema_prefill_match without a workspace argument, for callers
+ * that cannot allocate device memory -- a plugin that is handed only its input and output
+ * tensors by a host engine owning all device memory, a C program with no device allocator,
+ * or a latency-critical loop in which cudaMalloc (may block) and cudaFree (synchronises the
+ * device) are not allowed. It allocates nothing: its scratch is a fixed array of
+ * LEMA_NOALLOC_SCRATCH_BYTES inside this library, which every GPU that loads the library
+ * holds until the process exits.
+ *   - The first call on a device looks up that array's device address (with the device
+ *     current); make that first call before any CUDA-graph stream capture.
+ *   - All calls share the one array and it keeps the last call's contents: each call
+ *     clears the one counter it needs at zero and assumes nothing else about it. Calls
+ *     that overlap on the GPU -- on different streams, or from different host threads --
+ *     race on it: order them on one stream.
+ *   - A call whose scratch does not fit is rejected with LEMA_ERR_WORKSPACE: the scratch is
+ *     4 * n_streams * T bytes when src is NULL, plus, when T > 6144 (32-bit codes) or
+ *     T > 3072 (64-bit codes), room for at least one overflow-path table of about
+ *     12 * next_pow2(2 * T) bytes (16 * ... for 64-bit codes). Passing src avoids the
+ *     first part.
+ * Same arguments, results and status behaviour as lema_prefill_match otherwise.
+ * No counterpart in the reference: it is an addition for allocation-free callers.
+ */
+#define LEMA_NOALLOC_SCRATCH_BYTES (32u << 20)
+int lema_prefill_match_noalloc(const void* qcodes, const void* kcodes, int code_bytes,
+                               int64_t n_streams, int64_t T, int32_t* src,
+                               const void* values, int64_t vbytes, void* out,
+                               uint32_t* status, void* stream);
+
 /* ---------------------------------------------------- (c) the HBM store */
 /*
  * The store is ONE open-addressing table in device memory shared by every

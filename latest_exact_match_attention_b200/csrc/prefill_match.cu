@@ -45,6 +45,7 @@
 
 #include <algorithm>
 #include <cstring>
+#include <mutex>
 #include <type_traits>
 
 #include "common.cuh"
@@ -700,4 +701,111 @@ int launch_match(const MatchLaunch& a) {
   return a.code_bytes == 4 ? k2::run<uint32_t>(a, pl, *dev) : k2::run<uint64_t>(a, pl, *dev);
 }
 
+
+// ---------------------------------------------------------------- no-allocation variant
+// lema_prefill_match_noalloc: the same latest-match and gather for callers that cannot
+// allocate device memory at all -- a plugin handed only its input and output tensors by a
+// host engine that owns every byte of device memory, a C program without a device allocator,
+// or a latency-critical loop where a cudaMalloc (which may block) or a cudaFree (which
+// synchronises the device) is not allowed. Its scratch (the index scratch when the caller
+// passes no src, the overflow list and the overflow-path tables) lives in the fixed array
+// below: every GPU that loads this library holds these bytes until the process exits.
+namespace k2 {
+
+constexpr size_t kNoallocScratchBytes = size_t(32) << 20;  // 32 MiB, LEMA_NOALLOC_SCRATCH_BYTES
+static __device__ __align__(256) unsigned char g_noalloc_scratch[kNoallocScratchBytes];
+
+// make_plan for a fixed scratch size: the overflow path gets as many CTA-private tables as
+// fit (at least one). `fits` is false when even the index scratch plus one table does not.
+Plan make_plan_within(int64_t N, int64_t T, int code_bytes, bool need_src, size_t budget, bool& fits) {
+  Plan pl;
+  fits = true;
+  if (N <= 0 || T <= 0) return pl;
+  const uint32_t limit = code_bytes == 4 ? overflow_limit<uint32_t>() : overflow_limit<uint64_t>();
+  pl.fast = true;
+  const size_t src_bytes = need_src ? round_up(4 * static_cast<size_t>(N) * static_cast<size_t>(T), 256) : 0;
+  pl.off_src = 0;
+  pl.total = src_bytes;
+  if (T > static_cast<int64_t>(limit)) {
+    pl.global = true;
+    pl.list_mode = true;
+    pl.gslots = static_cast<uint32_t>(next_pow2(static_cast<uint64_t>(std::max<int64_t>(2 * T, 2 * kBucket))));
+    const size_t tb = code_bytes == 4 ? Table<uint32_t, uint32_t>::bytes(pl.gslots)
+                                      : Table<uint64_t, uint32_t>::bytes(pl.gslots);
+    pl.gtable_bytes = static_cast<int64_t>(round_up(tb, 256));
+    pl.off_list = src_bytes + 256;  // the overflow count sits in the 256 bytes before the list
+    pl.off_tables = round_up(pl.off_list + 4 * static_cast<size_t>(N), 256);
+    if (pl.off_tables + static_cast<size_t>(pl.gtable_bytes) > budget) {
+      fits = false;
+      pl.total = pl.off_tables + static_cast<size_t>(pl.gtable_bytes);
+      return pl;
+    }
+    pl.n_gtables = std::min<int64_t>(
+        {N, kMaxOverflowTables, static_cast<int64_t>((budget - pl.off_tables) / pl.gtable_bytes)});
+    pl.total = pl.off_tables + static_cast<size_t>(pl.n_gtables * pl.gtable_bytes);
+  }
+  fits = pl.total <= budget;
+  return pl;
+}
+
+// Device address of the array on each device, looked up once per device with that device
+// current (in host code the array's name is only a host-side stand-in for it).
+std::once_flag g_noalloc_once[64];
+void* g_noalloc_ptr[64];
+cudaError_t g_noalloc_err[64];
+
+}  // namespace k2
 }  // namespace lema
+
+extern "C" int lema_prefill_match_noalloc(const void* qcodes, const void* kcodes, int code_bytes,
+                                          int64_t n_streams, int64_t T, int32_t* src,
+                                          const void* values, int64_t vbytes, void* out,
+                                          uint32_t* status, void* stream) {
+  using namespace lema;
+  clear_error();
+  if (code_bytes != 4 && code_bytes != 8) return fail(LEMA_ERR_INVALID_ARGUMENT, "code_bytes must be 4 or 8, got %d", code_bytes);
+  if (n_streams < 0 || T < 0) return fail(LEMA_ERR_INVALID_ARGUMENT, "negative shape (%lld, %lld)", (long long)n_streams, (long long)T);
+  if (T > (int64_t(1) << 30)) return fail(LEMA_ERR_INVALID_ARGUMENT, "T = %lld exceeds 2^30", (long long)T);
+  if (n_streams == 0 || T == 0) return LEMA_OK;
+  if (qcodes == nullptr || kcodes == nullptr) return fail(LEMA_ERR_INVALID_ARGUMENT, "null code pointer");
+  if (!aligned(qcodes, code_bytes) || !aligned(kcodes, code_bytes)) return fail(LEMA_ERR_INVALID_ARGUMENT, "codes not aligned to their width");
+  if (out != nullptr) {
+    if (values == nullptr) return fail(LEMA_ERR_INVALID_ARGUMENT, "out given without values");
+    if (vbytes <= 0 || vbytes % 2 != 0) return fail(LEMA_ERR_INVALID_ARGUMENT, "vbytes must be a positive multiple of 2, got %lld", (long long)vbytes);
+    if (!aligned(values, 2) || !aligned(out, 2)) return fail(LEMA_ERR_INVALID_ARGUMENT, "value rows must be 2-byte aligned");
+    if (static_cast<uint64_t>(T) * static_cast<uint64_t>(vbytes / 2) >= (uint64_t(1) << 32)) return fail(LEMA_ERR_INVALID_ARGUMENT, "T * vbytes too large for one stream (%lld x %lld)", (long long)T, (long long)vbytes);
+  }
+  bool fits = true;
+  const k2::Plan pl = k2::make_plan_within(n_streams, T, code_bytes, src == nullptr, k2::kNoallocScratchBytes, fits);
+  if (!fits) {
+    return fail(LEMA_ERR_WORKSPACE,
+                "%lld streams x %lld positions need %zu bytes of scratch, more than the %zu of "
+                "lema_prefill_match_noalloc: pass src, split the streams over several calls, or "
+                "use lema_prefill_match with a caller-owned workspace",
+                (long long)n_streams, (long long)T, pl.total, k2::kNoallocScratchBytes);
+  }
+  const DeviceInfo* dev = current_device_info();
+  if (dev == nullptr) return LEMA_ERR_CUDA;
+  if (dev->cc_major != 10) return fail(LEMA_ERR_UNSUPPORTED, "built for sm_100a; device is sm_%d%d", dev->cc_major, dev->cc_minor);
+  const int d = dev->device;
+  if (d < 0 || d >= 64) return fail(LEMA_ERR_UNSUPPORTED, "device ordinal %d: lema_prefill_match_noalloc serves devices 0..63", d);
+  std::call_once(k2::g_noalloc_once[d], [d]() {
+    k2::g_noalloc_err[d] = cudaGetSymbolAddress(&k2::g_noalloc_ptr[d], k2::g_noalloc_scratch);
+  });
+  if (k2::g_noalloc_err[d] != cudaSuccess) return cuda_fail(k2::g_noalloc_err[d], "cudaGetSymbolAddress(noalloc scratch)");
+  MatchLaunch m;
+  m.qc = qcodes;
+  m.kc = kcodes;
+  m.code_bytes = code_bytes;
+  m.N = n_streams;
+  m.T = T;
+  m.src = src;
+  m.v = values;
+  m.vbytes = vbytes;
+  m.out = out;
+  m.ws = k2::g_noalloc_ptr[d];
+  m.ws_bytes = k2::kNoallocScratchBytes;
+  m.status = status;
+  m.stream = static_cast<cudaStream_t>(stream);
+  return code_bytes == 4 ? k2::run<uint32_t>(m, pl, *dev) : k2::run<uint64_t>(m, pl, *dev);
+}
