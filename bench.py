@@ -133,7 +133,8 @@ def make_inputs(rank: int, device, n_streams: int):
 
 def cpu_reference_sample(qc: np.ndarray, kc: np.ndarray, n_streams: int, reps: int = 1):
     """The reference's C++ store exchange (oracle/_ref) over `n_streams` full streams in one
-    call on all host cores: returns (Mpos/s, cores, kind, sample description)."""
+    call on all host cores: returns (Mpos/s, cores, kind, sample description). With reps = 0
+    the one timed call is also the warm-up (the caller has warmed up already)."""
     import torch
 
     import oracle
@@ -153,7 +154,7 @@ def cpu_reference_sample(qc: np.ndarray, kc: np.ndarray, n_streams: int, reps: i
             t0 = time.perf_counter()
             ref.exchange(table, q64, k64, vals, out, T, 0, cap, VBYTES)
             times.append(time.perf_counter() - t0)
-        dt = min(times[1:])
+        dt = min(times[1:] or times)
         return n / dt / 1e6, cores, "reference", (
             f"code/lema/csrc/store.cpp exchange, {n_streams} streams x {T} positions in one call "
             f"(P={n_streams}, T={T}), {cores} OpenMP threads, table load {n / cap:.2f}")
