@@ -85,6 +85,10 @@ int lema_pack_codes(const void* z, int dtype, int64_t d0, int64_t d1, int64_t d2
  * as the matcher consumes them:
  *   qcodes[(b * hq + h) * T + t], kcodes[(b * hk + h) * T + t]   (uint32)
  * Requires d_qk = 32, K % 64 == 0, M % T == 0, 16-byte aligned x and w_qk.
+ * Bit d of a code is (z_d >= 0) for the fp32 z; codes can differ from a bf16
+ * GEMM followed by pack_codes only where |z_d| is within rounding of zero.
+ * status (optional, device): LEMA_STATUS_PROBE_LIMIT is OR-ed in if a pipeline
+ * wait inside the kernel ran out (the codes are then incomplete).
  *
  * Replaces: the q_proj/k_proj GEMMs of code/lema/model.py:160-175 plus
  * code/lema/attention.py:82-97, i.e. code/lema/model.py:224-227 minus the norm
@@ -92,7 +96,7 @@ int lema_pack_codes(const void* z, int dtype, int64_t d0, int64_t d1, int64_t d2
  */
 int lema_proj_codes(const void* x, const void* w_qk, int64_t M, int64_t K,
                     int64_t T, int hq, int hk, int d_qk, uint32_t* qcodes,
-                    uint32_t* kcodes, void* stream);
+                    uint32_t* kcodes, uint32_t* status, void* stream);
 
 /* ---------------------------------------------- (b) prefill latest match */
 /*

@@ -11,7 +11,8 @@ package:
 
 The kernels live in liblema_b200.so (C ABI: include/lema_b200.h), built by `build.py`.
 """
-from .attention import latest_prev_match, lema_hard, pack_codes, prefill_match  # noqa: F401
+from .attention import (latest_prev_match, lema_hard, pack_codes, prefill_match,  # noqa: F401
+                        proj_codes)
 from ._lib import LemaError  # noqa: F401
 
 __version__ = "0.1.0"

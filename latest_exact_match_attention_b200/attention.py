@@ -25,7 +25,8 @@ import torch
 from . import _lib
 from ._lib import DTYPE_TAG, LemaError, call, ptr, require_cuda, stream_handle
 
-__all__ = ["pack_codes", "latest_prev_match", "lema_hard", "prefill_match", "code_bytes_of"]
+__all__ = ["pack_codes", "proj_codes", "latest_prev_match", "lema_hard", "prefill_match",
+           "code_bytes_of"]
 
 
 def code_bytes_of(codes: torch.Tensor) -> int:
@@ -68,6 +69,33 @@ def pack_codes(z: torch.Tensor, narrow: bool = False) -> torch.Tensor:
          strides[0], strides[1], strides[2], D, ptr(out), 4 if narrow else 8,
          stream_handle(z.device))
     return out
+
+
+def proj_codes(x: torch.Tensor, w_qk: torch.Tensor, hq: int, hk: int,
+               status: torch.Tensor | None = None) -> tuple[torch.Tensor, torch.Tensor]:
+    """Query and key codes of `x` [B, T, dim] under the stacked projection weights
+    `w_qk` [(hq + hk) * 32, dim] (q_proj.weight over k_proj.weight), both bf16:
+    the codes of `pack_codes(x @ w_qk.T)` per head, without z ever reaching memory.
+
+    Returns (qcodes [B, hq, T], kcodes [B, hk, T]) as int32 holding uint32 bit patterns.
+    The tensor-core GEMM accumulates in fp32, so a bit can differ from a bf16 GEMM followed
+    by pack_codes only where that pre-activation is within rounding of zero.
+    Mirrors code/lema/model.py:224-227 (`Block.gpu_pre`) minus the norm and v_proj.
+    """
+    dev = require_cuda(x, w_qk)
+    if x.dtype != torch.bfloat16 or w_qk.dtype != torch.bfloat16:
+        raise LemaError("proj_codes takes bf16 x and w_qk")
+    if x.dim() != 3 or w_qk.dim() != 2 or w_qk.shape != ((hq + hk) * 32, x.shape[-1]):
+        raise LemaError(f"shapes x {tuple(x.shape)}, w_qk {tuple(w_qk.shape)} do not fit "
+                        f"hq={hq}, hk={hk}, d_qk=32")
+    x = x.contiguous()
+    w_qk = w_qk.contiguous()
+    B, T, dim = x.shape
+    qc = torch.empty((B, hq, T), dtype=torch.int32, device=dev)
+    kc = torch.empty((B, hk, T), dtype=torch.int32, device=dev)
+    call("lema_proj_codes", ptr(x), ptr(w_qk), B * T, dim, T, hq, hk, 32, ptr(qc), ptr(kc),
+         ptr(status), stream_handle(dev))
+    return qc, kc
 
 
 def _workspace(nbytes: int, device) -> torch.Tensor | None:

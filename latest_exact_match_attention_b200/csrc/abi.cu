@@ -20,7 +20,7 @@ int store_exchange(void* table, int64_t cap, int64_t vbytes, const void* qc, con
                    int code_bytes, const void* values, void* out, int64_t n, int64_t T, int64_t g0,
                    int64_t* counts, uint32_t* status, void* ws, size_t ws_bytes, cudaStream_t stream);
 int proj_codes(const void* x, const void* w_qk, int64_t M, int64_t K, int64_t T, int hq, int hk,
-               int d_qk, uint32_t* qcodes, uint32_t* kcodes, cudaStream_t stream);
+               int d_qk, uint32_t* qcodes, uint32_t* kcodes, uint32_t* status, cudaStream_t stream);
 
 namespace {
 thread_local char g_err[512] = {0};
@@ -97,9 +97,9 @@ int lema_pack_codes(const void* z, int dtype, int64_t d0, int64_t d1, int64_t d2
 }
 
 int lema_proj_codes(const void* x, const void* w_qk, int64_t M, int64_t K, int64_t T, int hq, int hk,
-                    int d_qk, uint32_t* qcodes, uint32_t* kcodes, void* stream) {
+                    int d_qk, uint32_t* qcodes, uint32_t* kcodes, uint32_t* status, void* stream) {
   lema::clear_error();
-  return lema::proj_codes(x, w_qk, M, K, T, hq, hk, d_qk, qcodes, kcodes,
+  return lema::proj_codes(x, w_qk, M, K, T, hq, hk, d_qk, qcodes, kcodes, status,
                           static_cast<cudaStream_t>(stream));
 }
 

@@ -72,8 +72,10 @@ def test_argument_validation_on_host():
     # pack: d_qk too wide for the code width
     assert rc("lema_pack_codes", P, 0, 1, 1, 1, 0, 0, 0, 33, P, 4, None) == 1
     assert rc("lema_pack_codes", P, 0, 1, 1, 1, 0, 0, 0, 65, P, 8, None) == 1
-    # projection: only d_qk = 32
-    assert rc("lema_proj_codes", P, P, 128, 64, 128, 1, 1, 16, P, P, None) != 0
+    # projection: only d_qk = 32; K a multiple of 64; whole sequences of T rows
+    assert rc("lema_proj_codes", P, P, 128, 64, 128, 1, 1, 16, P, P, None, None) == 1
+    assert rc("lema_proj_codes", P, P, 128, 96, 128, 1, 1, 32, P, P, None, None) == 1
+    assert rc("lema_proj_codes", P, P, 100, 64, 64, 1, 1, 32, P, P, None, None) == 1
 
 
 def test_python_layer_refuses_cpu_tensors():
