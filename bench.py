@@ -338,6 +338,64 @@ def run_b200(args):
     print(json.dumps(line), flush=True)
 
 
+def run_proj(args):
+    """K1 alone at config 3's projection shapes: B=32 x T=16384 rows of dim 1024, d_qk 32,
+    hq = hk = H for H in --heads. One JSON line per H (TFLOP/s against the measured bf16 GEMM
+    peak), with the reference's own GPU recipe -- a bf16 GEMM to z in HBM, then pack_codes as
+    code/lema/attention.py:94-97 writes it -- timed beside it on the same inputs."""
+    import torch
+
+    from latest_exact_match_attention_b200 import proj_codes
+    dev = torch.device("cuda", int(os.environ.get("LOCAL_RANK", "0")))
+    torch.cuda.set_device(dev)
+    Bp, Tp, dim = args.proj_batch, 16384, 1024
+    g = torch.Generator(device=dev).manual_seed(0)
+    x = torch.randn((Bp, Tp, dim), generator=g, device=dev).to(torch.bfloat16)
+    pk = json.loads((ROOT / "MEASURED_PEAKS.json").read_text()) if (ROOT / "MEASURED_PEAKS.json").exists() else {}
+    peak, peak_src = (float(pk["bf16_tflops"]), "measured (burst)") if "bf16_tflops" in pk else (1590.0, "fallback")
+    stream = torch.cuda.current_stream(dev)
+
+    def timed(fn, steps):
+        for _ in range(max(3, args.warmup)):
+            fn()
+        torch.cuda.synchronize()
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a.record(stream)
+        for _ in range(steps):
+            fn()
+        b.record(stream)
+        torch.cuda.synchronize()
+        return a.elapsed_time(b) / steps
+
+    for H in args.heads:
+        w = (0.02 * torch.randn((2 * H * 32, dim), generator=g, device=dev)).to(torch.bfloat16)
+        status = torch.zeros(1, dtype=torch.int32, device=dev)
+        with ClockSampler(dev.index) as clk:
+            ms = timed(lambda: proj_codes(x, w, H, H, status=status), args.steps)
+        assert int(status.item()) == 0
+        pw = torch.ones((), dtype=torch.int64, device=dev) << torch.arange(32, device=dev)
+
+        def reference_recipe():
+            z = (x @ w.T).view(Bp, Tp, 2 * H, 32)
+            return ((z >= 0).to(torch.int64) * pw).sum(-1)
+        ref_ms = None if args.no_recipe else timed(reference_recipe, max(2, args.steps // 4))
+        flops = 2.0 * Bp * Tp * dim * (2 * H * 32)
+        tf = flops / (ms / 1e3) / 1e12
+        print(json.dumps({
+            "metric": "K1 code projection TFLOP/s", "value": round(tf, 1), "unit": "TFLOP/s",
+            "n_gpus": 1, "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms, 4),
+            "higher_is_better": True, "dtype": "bf16", "data": "synthetic N(0,1) x, N(0,0.02) w",
+            "config": {"workload": f"cfg3 K1: B={Bp} T={Tp} dim={dim} hq=hk={H} d_qk=32",
+                       "rows": Bp * Tp, "cols": 2 * H * 32, "l2": "x 1 GiB > L2"},
+            "roofline": {"bound": "tensor", "achieved": round(tf, 1), "peak": peak, "unit": "TFLOP/s",
+                         "frac": round(tf / peak, 4), "peak_source": peak_src},
+            "reference_recipe_ms": ref_ms and round(ref_ms, 4),
+            "speedup_vs_reference_recipe": ref_ms and round(ref_ms / ms, 2),
+            "gpu_launches": args.steps, "clocks": clk.summary(),
+        }), flush=True)
+        del w
+
+
 def main():
     ap = argparse.ArgumentParser(description=__doc__.split("\n")[0])
     ap.add_argument("--gpus", type=int, default=1)
@@ -348,10 +406,19 @@ def main():
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--streams", type=int, default=N_STREAMS,
                     help="streams per GPU (default: the workload's 512); smaller for profiling")
+    ap.add_argument("--workload", choices=["prefill", "proj"], default="prefill",
+                    help="prefill: the headline config-2 line; proj: K1 at config 3's shapes")
+    ap.add_argument("--heads", type=int, nargs="+", default=[8, 16, 32, 64],
+                    help="--workload proj: query (= key) heads per layer")
+    ap.add_argument("--proj-batch", type=int, default=32, help="--workload proj: sequences")
+    ap.add_argument("--no-recipe", action="store_true",
+                    help="--workload proj: skip timing the bf16 GEMM + pack recipe")
     args = ap.parse_args()
     if args.warmup < 3 and args.impl == "b200":
         args.warmup = 3
-    if args.impl == "reference":
+    if args.workload == "proj":
+        run_proj(args)
+    elif args.impl == "reference":
         run_reference(args)
     else:
         run_b200(args)
