@@ -14,5 +14,7 @@ The kernels live in liblema_b200.so (C ABI: include/lema_b200.h), built by `buil
 from .attention import (latest_prev_match, lema_hard, pack_codes, prefill_match,  # noqa: F401
                         proj_codes)
 from ._lib import LemaError  # noqa: F401
+from .model import ModelConfig, Transformer  # noqa: F401
+from .decode import LemaDecoder, decoder  # noqa: F401
 
 __version__ = "0.1.0"

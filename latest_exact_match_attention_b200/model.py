@@ -1,0 +1,251 @@
+"""The LEMA transformer, inference only, on the B200 kernels.
+
+Same architecture and parameter names as code/lema/model.py (pre-RMSNorm, SwiGLU MLP,
+untied head, no biases, no positional scheme), so a state dict trained by the reference
+loads unchanged. Only the exact ("hard") LEMA op is served: attention kinds other than
+"lema" and the training-time surrogate are outside this package.
+
+Where the time goes, and what replaced it:
+
+    Block.gpu_pre    norm1 -> K1 (lema_proj_codes: q/k GEMM + sign pack on the tensor
+                     cores, z never stored) + v_proj          code/lema/model.py:224-227
+    Attention        the exact op: K2 (lema_prefill_match: latest match + gather)
+                                                               code/lema/model.py:199-202
+    Block.forward    with a store: codes -> K3 (lema_store_exchange, the store in HBM)
+                                                               code/lema/model.py:249-253
+    Transformer.forward(idx, cache=)                           code/lema/model.py:337-363
+
+K1 serves d_qk = 32 with bf16 weights and dim % 64 == 0 (every benchmark configuration);
+other shapes project with torch and pack with lema_pack_codes.
+"""
+from __future__ import annotations
+
+import dataclasses
+import math
+from dataclasses import dataclass
+
+import torch
+import torch.nn.functional as F
+from torch import nn
+
+from .attention import pack_codes, prefill_match, proj_codes
+
+ATTN_KINDS = ("lema",)
+
+
+def _pad128(n) -> int:
+    return -(-int(n) // 128) * 128
+
+
+@dataclass
+class ModelConfig:
+    """Fields and defaults of code/lema/model.py:35-87 (`ModelConfig`): d_qk and d_v default
+    to dim // num_heads, dim_ff to 8 * dim / 3, and vocab_size and dim_ff are rounded up to a
+    multiple of 128."""
+    vocab_size: int
+    depth: int
+    dim: int
+    num_heads: int
+    d_qk: int = 0
+    d_v: int = 0
+    dim_ff: int = 0
+    num_kv_heads: int = 0
+    attn: str = "lema"
+    pos: str = "nope"
+    rope_base: float = 10000.0
+    gdn_expand_v: int = 2
+    norm_eps: float = 1e-5
+
+    def __post_init__(self):
+        if self.attn not in ATTN_KINDS:
+            raise ValueError(f"this build serves attn='lema' only (the exact op); got "
+                             f"{self.attn!r}")
+        if self.pos != "nope":
+            raise ValueError(f"a LEMA model has no positional scheme; pos={self.pos!r}")
+        if (not self.d_qk or not self.d_v) and self.dim % self.num_heads:
+            raise ValueError(f"dim {self.dim} is not divisible by num_heads {self.num_heads}")
+        head = self.dim // self.num_heads
+        self.d_qk = self.d_qk or head
+        self.d_v = self.d_v or head
+        self.dim_ff = _pad128(self.dim_ff or 8 * self.dim / 3)
+        self.vocab_size = _pad128(self.vocab_size)
+        self.num_kv_heads = self.num_kv_heads or self.num_heads
+        if self.num_kv_heads != self.num_heads:
+            raise ValueError("grouped-query attention is not defined for LEMA "
+                             "(num_kv_heads must equal num_heads)")
+        if self.d_qk > 64:
+            raise ValueError(f"d_qk {self.d_qk} > 64: codes must pack into one uint64")
+
+    @classmethod
+    def from_dict(cls, d: dict) -> "ModelConfig":
+        names = {f.name for f in dataclasses.fields(cls)}
+        return cls(**{k: v for k, v in d.items() if k in names})
+
+    def summary(self) -> str:
+        return (f"{self.depth}L d{self.dim} h{self.num_heads} d_qk {self.d_qk} d_v {self.d_v} "
+                f"dim_ff {self.dim_ff} attn {self.attn}")
+
+
+class SwiGLU(nn.Module):
+    def __init__(self, dim: int, dim_ff: int):
+        super().__init__()
+        self.gate = nn.Linear(dim, dim_ff, bias=False)
+        self.up = nn.Linear(dim, dim_ff, bias=False)
+        self.down = nn.Linear(dim_ff, dim, bias=False)
+
+    def forward(self, x):
+        return self.down(F.silu(self.gate(x)) * self.up(x))
+
+
+class Attention(nn.Module):
+    """A LEMA head group: projections named as code/lema/model.py:160-163; the op is always
+    the exact one (`hard`), computed from codes."""
+
+    def __init__(self, cfg: ModelConfig):
+        super().__init__()
+        self.cfg = cfg
+        self.kind = "lema"
+        H = cfg.num_heads
+        self.q_proj = nn.Linear(cfg.dim, H * cfg.d_qk, bias=False)
+        self.k_proj = nn.Linear(cfg.dim, H * cfg.d_qk, bias=False)
+        self.v_proj = nn.Linear(cfg.dim, H * cfg.d_v, bias=False)
+        self.o_proj = nn.Linear(H * cfg.d_v, cfg.dim, bias=False)
+        self.hard = True
+        self._wqk = None        # (key, stacked [q_proj; k_proj] weight) for K1
+
+    def project(self, x):
+        """[B, T, dim] -> query and key pre-activations and values, [B, H, T, d]."""
+        B, T, _ = x.shape
+        c = self.cfg
+        zq = self.q_proj(x).view(B, T, c.num_heads, c.d_qk).transpose(1, 2)
+        zk = self.k_proj(x).view(B, T, c.num_heads, c.d_qk).transpose(1, 2)
+        v = self.v_proj(x).view(B, T, c.num_heads, c.d_v).transpose(1, 2)
+        return zq, zk, v
+
+    def merge(self, y):
+        B, _, T, _ = y.shape
+        return self.o_proj(y.transpose(1, 2).reshape(B, T, -1))
+
+    def _k1_ok(self, x) -> bool:
+        w = self.q_proj.weight
+        return (self.cfg.d_qk == 32 and x.is_cuda and x.dtype == torch.bfloat16
+                and w.dtype == torch.bfloat16 and self.cfg.dim % 64 == 0)
+
+    def stacked_qk(self) -> torch.Tensor:
+        """[q_proj.weight; k_proj.weight], rebuilt only when either weight changes."""
+        q, k = self.q_proj.weight, self.k_proj.weight
+        key = (q.data_ptr(), k.data_ptr(), q._version, k._version)
+        if self._wqk is None or self._wqk[0] != key:
+            self._wqk = (key, torch.cat([q.detach(), k.detach()], 0).contiguous())
+        return self._wqk[1]
+
+    def codes(self, x):
+        """[B, T, dim] (normalised) -> (qcodes [B, H, T], kcodes [B, H, T], v [B, H, T, d_v]).
+        Codes are int32 (uint32 bit patterns) for d_qk <= 32, else int64."""
+        B, T, _ = x.shape
+        c = self.cfg
+        if self._k1_ok(x):
+            qc, kc = proj_codes(x, self.stacked_qk(), c.num_heads, c.num_heads)
+            v = self.v_proj(x).view(B, T, c.num_heads, c.d_v).transpose(1, 2)
+            return qc, kc, v
+        zq, zk, v = self.project(x)
+        return pack_codes(zq, narrow=True), pack_codes(zk, narrow=True), v
+
+    def forward(self, x):
+        """The exact op over the whole sequence (no store): code/lema/attention.py:135-158."""
+        qc, kc, v = self.codes(x)
+        B, H, T = qc.shape
+        vv = v.reshape(B * H, T, -1) if v.is_contiguous() else v.contiguous().view(B * H, T, -1)
+        _, y = prefill_match(qc.reshape(B * H, T), kc.reshape(B * H, T), vv, want_src=False)
+        return self.merge(y.view(B, H, T, -1))
+
+
+class Block(nn.Module):
+    def __init__(self, cfg: ModelConfig):
+        super().__init__()
+        self.norm1 = nn.RMSNorm(cfg.dim, eps=cfg.norm_eps)
+        self.attn = Attention(cfg)
+        self.norm2 = nn.RMSNorm(cfg.dim, eps=cfg.norm_eps)
+        self.mlp = SwiGLU(cfg.dim, cfg.dim_ff)
+        self.seg = None
+
+    def gpu_pre(self, x):
+        """Normalise, project and pack: the codes the store needs and the values."""
+        return self.attn.codes(self.norm1(x))
+
+    def gpu_post(self, x, got):
+        """Merge the retrieved values and finish the layer."""
+        x = x + self.attn.merge(got)
+        return x + self.mlp(self.norm2(x))
+
+    def forward(self, x, store=None):
+        if store is not None:
+            pre, post = self.seg or (self.gpu_pre, self.gpu_post)
+            qc, kc, v = pre(x)
+            return post(x, store.exchange(qc, kc, v))
+        x = x + self.attn(self.norm1(x))
+        return x + self.mlp(self.norm2(x))
+
+
+class Transformer(nn.Module):
+    def __init__(self, cfg: ModelConfig):
+        super().__init__()
+        self.cfg = cfg
+        self.tok_emb = nn.Embedding(cfg.vocab_size, cfg.dim)
+        self.blocks = nn.ModuleList(Block(cfg) for _ in range(cfg.depth))
+        self.norm_f = nn.RMSNorm(cfg.dim, eps=cfg.norm_eps)
+        self.lm_head = nn.Linear(cfg.dim, cfg.vocab_size, bias=False)
+        self._init_weights()
+
+    def _init_weights(self):
+        """The reference's random init (code/lema/model.py:269-281): N(0, 1/fan_in) for every
+        Linear, N(0, 1/dim) for the embedding, and the two residual-branch outputs of each
+        block (o_proj, mlp.down) scaled by 1/sqrt(2 * depth)."""
+        for m in self.modules():
+            if isinstance(m, nn.Linear):
+                nn.init.normal_(m.weight, mean=0.0, std=1.0 / math.sqrt(m.weight.shape[1]))
+            elif isinstance(m, nn.Embedding):
+                nn.init.normal_(m.weight, mean=0.0, std=1.0 / math.sqrt(self.cfg.dim))
+        for b in self.blocks:
+            for lin in (b.attn.o_proj, b.mlp.down):
+                lin.weight.data.mul_(1.0 / math.sqrt(2 * self.cfg.depth))
+
+    def lema_layers(self):
+        return [b.attn for b in self.blocks]
+
+    def set_hard(self, hard: bool = True):
+        if not hard:
+            raise ValueError("this build serves the exact (hard) op only")
+
+    def new_cache(self, place: str = "hbm", **kw):
+        """The retrieval cache for this model, in device memory (the store is HBM-resident;
+        place "ram" is accepted for the reference's call sites and means the same).
+        Keywords as code/lema/cache.py:313-355: max_cache_len= or capacity=, max_load=,
+        batch=, dtype= (default: the model's), codes_hook=."""
+        from .cache import LemaCache
+        if place not in ("hbm", "vram", "ram"):
+            raise ValueError(f"place must be 'hbm' (or 'ram'/'vram', the same device store), "
+                             f"got {place!r}")
+        p = next(self.parameters())
+        kw.setdefault("dtype", p.dtype)
+        kw.setdefault("device", p.device)
+        kw.pop("pin", None)
+        return LemaCache(self.cfg, **kw)
+
+    @torch.no_grad()
+    def forward(self, idx, *, cache=None, return_logits=True):
+        """forward(x): the whole batch, no state. forward(x, cache=c): queries also match
+        every key already in `c`, and this call's keys are added to it (prefill in pieces,
+        or one decode step); `return_logits=False` skips the head."""
+        x = self.tok_emb(idx)
+        for li, blk in enumerate(self.blocks):
+            x = blk(x, store=(cache.layer(li) if cache is not None else None))
+        if cache is not None:
+            cache.t += idx.shape[-1]
+        return self.lm_head(self.norm_f(x)) if return_logits else None
+
+    def n_params(self, embedding: bool = True) -> int:
+        n = sum(p.numel() for p in self.parameters())
+        if not embedding:
+            n -= self.tok_emb.weight.numel() + self.lm_head.weight.numel()
+        return n

@@ -11,6 +11,8 @@ same. Outputs come from the reference:
     code/lema/attention.py:82-97    pack_codes
     code/lema/attention.py:100-132  latest_prev_match (CPU torch)
     code/lema/cache.py:129-201      HashStore.exchange (its C++ store, code/lema/csrc/store.cpp)
+    code/lema/model.py:257-363      Transformer: a tiny random-init LEMA model's weights, and
+                                    its hard-mode logits and store counts (fp32, CPU)
 Value rows are regenerated from their seed at test time; each fixture stores a SHA-256 of the
 values and of the reference outputs, so a regeneration that drifted is detected.
 """
@@ -172,6 +174,26 @@ def main(ref_root: str):
         cases[f"{name}__values_sha"] = np.array(sha(vals))
         print(f"store {name}: load {st.load():.2f}")
     np.savez_compressed(HERE / "store.npz", **cases)
+
+    # ---- a tiny LEMA model end to end: code/lema/model.py (Transformer, hard mode, fp32 CPU)
+    from lema.model import ModelConfig, Transformer
+    cfg = ModelConfig(vocab_size=128, depth=2, dim=64, num_heads=2, d_qk=32, d_v=32,
+                      dim_ff=128, attn="lema")
+    torch.manual_seed(0)
+    model = Transformer(cfg).eval()
+    model.set_hard(True)
+    r = np.random.default_rng(11)
+    idx = torch.from_numpy(r.integers(0, 24, size=(2, 96), dtype=np.int64))  # many repeats
+    with torch.no_grad():
+        dense = model(idx)
+        cache = model.new_cache("ram", max_cache_len=96, batch=2)
+        chunked = torch.cat([model(idx[:, s:s + 16], cache=cache) for s in range(0, 96, 16)], 1)
+    assert torch.equal(dense, chunked)
+    sd = {f"w__{k}": v.numpy() for k, v in model.state_dict().items()}
+    np.savez_compressed(HERE / "model_tiny.npz", idx=idx.numpy(), logits=dense.numpy(),
+                        counts=cache.counts().numpy(),
+                        cfg=np.array([128, 2, 64, 2, 32, 32, 128]), **sd)
+    print(f"model_tiny: {len(sd)} tensors, entries {int(cache.counts().sum())}")
 
 
 if __name__ == "__main__":

@@ -1,0 +1,107 @@
+"""The model mirror and the one-graph decoder on the GPU.
+
+Mirrors code/tests/test_gpu.py:68-141: the store reproduces the dense hard forward in any
+chunking (fp32), and a CUDA-graph decoder reproduces eager decoding token for token. Adds
+the reference's own logits for a tiny model (tests/golden/model_tiny.npz, written by its
+code/lema/model.py on the CPU) and checks the store's entry counts against its store's.
+"""
+from pathlib import Path
+
+import numpy as np
+import pytest
+import torch
+
+from latest_exact_match_attention_b200.decode import decoder
+from latest_exact_match_attention_b200.model import ModelConfig, Transformer
+
+pytestmark = pytest.mark.gpu
+
+GOLDEN = Path(__file__).resolve().parent / "golden" / "model_tiny.npz"
+
+
+def tiny_from_golden(dev):
+    g = np.load(GOLDEN)
+    vocab, depth, dim, H, dqk, dv, ff = (int(x) for x in g["cfg"])
+    m = Transformer(ModelConfig(vocab_size=vocab, depth=depth, dim=dim, num_heads=H,
+                                d_qk=dqk, d_v=dv, dim_ff=ff))
+    m.load_state_dict({k[3:]: torch.from_numpy(g[k]) for k in g.files if k.startswith("w__")})
+    return m.to(dev).eval(), g
+
+
+def test_tiny_model_matches_reference_logits(cuda):
+    m, g = tiny_from_golden(cuda)
+    idx = torch.from_numpy(g["idx"]).to(cuda)
+    ref = torch.from_numpy(g["logits"])
+    dense = m(idx).cpu()
+    assert torch.equal(dense.argmax(-1), ref.argmax(-1))
+    torch.testing.assert_close(dense, ref, rtol=1e-4, atol=1e-4)
+    cache = m.new_cache("hbm", max_cache_len=96, batch=2)
+    chunked = torch.cat([m(idx[:, s:s + 16], cache=cache) for s in range(0, 96, 16)], 1).cpu()
+    torch.testing.assert_close(chunked, ref, rtol=1e-4, atol=1e-4)
+    assert torch.equal(cache.counts(), torch.from_numpy(g["counts"]))
+    cache.check()
+
+
+@pytest.mark.parametrize("step", [96, 16, 1])
+def test_store_matches_dense_in_any_chunking_fp32(cuda, step):
+    torch.manual_seed(0)
+    m = Transformer(ModelConfig(vocab_size=256, depth=2, dim=128, num_heads=1, d_qk=64,
+                                d_v=64)).to(cuda).eval()
+    idx = torch.randint(0, 40, (2, 96), device=cuda)
+    dense = m(idx)
+    cache = m.new_cache("hbm", max_cache_len=96, batch=2)
+    chunked = torch.cat([m(idx[:, s:s + step], cache=cache) for s in range(0, 96, step)], 1)
+    assert torch.equal(dense.argmax(-1), chunked.argmax(-1))
+    assert cache.entries() == int(cache.counts().sum()) > 0
+    assert cache.t == 96
+
+
+def bf16_model(dev, depth=2, vocab=512, dim=256, H=8):
+    torch.manual_seed(1)
+    return Transformer(ModelConfig(vocab_size=vocab, depth=depth, dim=dim, num_heads=H,
+                                   d_qk=32, d_v=32)).to(dev).to(torch.bfloat16).eval()
+
+
+def test_bf16_block_store_equals_dense(cuda):
+    # the K1 path: one block, the whole sequence at once through the store and densely;
+    # the same GEMM shapes on both sides, so the outputs are bitwise equal
+    m = bf16_model(cuda)
+    idx = torch.randint(0, 60, (3, 200), device=cuda)
+    x = m.tok_emb(idx)
+    blk = m.blocks[0]
+    with torch.no_grad():
+        dense = blk(x)
+        cache = m.new_cache("hbm", max_cache_len=200, batch=3)
+        stored = blk(x, store=cache.layer(0))
+    assert torch.equal(dense, stored)
+    cache.check()
+
+
+@pytest.mark.parametrize("temperature", [0.0, 0.8])
+def test_graph_decoder_reproduces_eager(cuda, temperature):
+    m = bf16_model(cuda)
+    prompt = torch.randint(0, 60, (4, 16), device=cuda)
+    # eager
+    c = m.new_cache("hbm", max_cache_len=64, batch=4)
+    m(prompt[:, :-1], cache=c, return_logits=False)
+    t, eager = prompt[:, -1:], []
+    if temperature == 0:
+        for _ in range(40):
+            t = m(t, cache=c).argmax(-1)
+            eager.append(t.clone())
+    # graph
+    c2 = m.new_cache("hbm", max_cache_len=64, batch=4)
+    m(prompt[:, :-1], cache=c2, return_logits=False)
+    before = c2.counts().clone()
+    d = decoder(m, c2, tok=prompt[:, -1:], temperature=temperature)
+    assert torch.equal(c2.counts(), before), "capturing must leave the store untouched"
+    graph = [d.step().clone() for _ in range(40)]
+    c2.check()
+    assert c2.t == 15 + 40
+    if temperature == 0:
+        assert torch.equal(torch.cat(eager, 1), torch.cat(graph, 1))
+        assert torch.equal(c.counts(), c2.counts())
+    else:
+        toks = torch.cat(graph, 1)
+        assert toks.min() >= 0 and toks.max() < m.cfg.vocab_size
+        assert len(set(toks.flatten().tolist())) > 4      # fresh noise on every replay
