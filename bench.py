@@ -396,6 +396,122 @@ def run_proj(args):
         del w
 
 
+def _model_cfg(which: int, H: int = 64):
+    from latest_exact_match_attention_b200.model import ModelConfig
+    if which == 3:   # 309M-shaped: d_model 1024, 24 blocks, SwiGLU 4x, heads swept, 32-bit codes
+        return ModelConfig(vocab_size=50304, depth=24, dim=1024, num_heads=H, d_qk=32,
+                           d_v=1024 // H, dim_ff=4096)
+    # 834M-shaped: d_model 1536, 24 blocks, 64 heads, d_v 24, 32-bit codes
+    return ModelConfig(vocab_size=50304, depth=24, dim=1536, num_heads=64, d_qk=32, d_v=24)
+
+
+def run_model_prefill(args):
+    """Config 3: full prefill of a random-init 309M-shaped LEMA LM (bf16), B=32 x T=16384
+    synthetic tokens, heads swept; every layer runs K1 (codes) and K2 (exact op). One JSON
+    line per head count, in tokens (= positions) per second."""
+    import torch
+
+    from latest_exact_match_attention_b200 import synth
+    from latest_exact_match_attention_b200.model import Transformer
+    dev = torch.device("cuda", int(os.environ.get("LOCAL_RANK", "0")))
+    torch.cuda.set_device(dev)
+    Bm, Tm = args.proj_batch, 16384
+    idx = torch.from_numpy(synth.token_stream(Bm, Tm, 50304, seed=0, config_id=3)).to(dev)
+    stream = torch.cuda.current_stream(dev)
+    for H in args.heads:
+        torch.manual_seed(0)
+        cfg = _model_cfg(3, H)
+        model = Transformer(cfg).to(dev).to(torch.bfloat16).eval()
+        for _ in range(max(3, args.warmup)):
+            model(idx, return_logits=False)
+        torch.cuda.synchronize()
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        with ClockSampler(dev.index) as clk:
+            a.record(stream)
+            for _ in range(args.steps):
+                model(idx, return_logits=False)
+            b.record(stream)
+            torch.cuda.synchronize()
+        ms = a.elapsed_time(b) / args.steps
+        print(json.dumps({
+            "metric": "LEMA full prefill tokens/s (config 3)", "value": round(Bm * Tm / ms / 1e3, 3),
+            "unit": "Mtok/s", "n_gpus": 1, "steps": args.steps, "warmup": args.warmup,
+            "ms_per_step": round(ms, 3), "higher_is_better": True, "dtype": "bf16",
+            "data": "synthetic Zipf(1.1) tokens, 20% bigram copies; random-init weights",
+            "config": {"workload": f"cfg3: {cfg.summary()}, B={Bm} T={Tm}", "params": model.n_params()},
+            "clocks": clk.summary(),
+        }), flush=True)
+        del model
+        torch.cuda.empty_cache()
+
+
+def run_decode(args):
+    """Config 4: batched greedy decode of a random-init 834M-shaped LEMA LM (bf16). Each
+    sequence's store is pre-filled from a --prefix-token bigram-structured prefix (chunked
+    prefill through the store), then every step is one CUDA-graph replay (all 24 layers'
+    store exchanges inside). Value: tokens/s = batch x steps / time."""
+    import math
+
+    import torch
+
+    from latest_exact_match_attention_b200 import synth
+    from latest_exact_match_attention_b200.decode import decoder
+    from latest_exact_match_attention_b200.model import Transformer
+    dev = torch.device("cuda", int(os.environ.get("LOCAL_RANK", "0")))
+    torch.cuda.set_device(dev)
+    cfg = _model_cfg(4)
+    Bd, prefix = args.decode_batch, args.prefix
+    torch.manual_seed(0)
+    model = Transformer(cfg).to(dev).to(torch.bfloat16).eval()
+    idx = torch.from_numpy(synth.token_stream(Bd, prefix + 1, 50304, seed=0, config_id=4)).to(dev)
+    P = Bd * cfg.num_heads
+    per_part = args.entries_per_partition or (prefix + args.steps + args.warmup + 8)
+    cap = math.ceil(cfg.depth * P * per_part / args.max_load)
+    cache = model.new_cache("hbm", capacity=cap, batch=Bd)
+    stream = torch.cuda.current_stream(dev)
+    a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    a.record(stream)
+    for s in range(0, prefix, args.chunk):
+        model(idx[:, s:min(prefix, s + args.chunk)], cache=cache, return_logits=False)
+    b.record(stream)
+    torch.cuda.synchronize()
+    prefill_ms = a.elapsed_time(b)
+    cache.check()
+    counts = cache.counts().float()            # [depth, batch, heads]
+    d = decoder(model, cache, tok=idx[:, prefix:prefix + 1])
+    for _ in range(max(3, args.warmup)):
+        d.step()
+    torch.cuda.synchronize()
+    with ClockSampler(dev.index) as clk:
+        a.record(stream)
+        for _ in range(args.steps):
+            d.step()
+        b.record(stream)
+        torch.cuda.synchronize()
+    cache.check()
+    ms = a.elapsed_time(b) / args.steps
+    weights = sum(p.numel() * p.element_size() for p in model.parameters())
+    store_bytes = cfg.depth * P * 216          # per (layer, seq, head) op: codes, row, slots
+    print(json.dumps({
+        "metric": "LEMA batched decode tok/s (config 4)", "value": round(Bd * 1e3 / ms, 1),
+        "unit": "tok/s", "n_gpus": 1, "steps": args.steps, "warmup": args.warmup,
+        "ms_per_step": round(ms, 4), "higher_is_better": True, "dtype": "bf16",
+        "data": "synthetic Zipf(1.1) tokens, 20% bigram copies; random-init weights",
+        "config": {"workload": f"cfg4: {cfg.summary()}, B={Bd}, prefix {prefix}",
+                   "store_slots": cap, "store_gb": round(cache.nbytes() / 1e9, 2),
+                   "store_load": round(cache.load(), 4),
+                   "entries_per_partition_by_layer": [round(float(x), 1) for x in counts.mean((1, 2))],
+                   "entries_per_partition_max": int(counts.max())},
+        "roofline": {"bound": "hbm", "bytes_per_step": weights + store_bytes,
+                     "achieved": round((weights + store_bytes) / (ms / 1e3) / 1e9, 1),
+                     "peak": peaks()[0], "unit": "GB/s",
+                     "frac": round((weights + store_bytes) / (ms / 1e3) / 1e9 / peaks()[0], 4)},
+        "prefill": {"tokens": Bd * prefix, "ms": round(prefill_ms, 1),
+                    "tok_s": round(Bd * prefix / prefill_ms * 1e3, 1), "chunk": args.chunk},
+        "gpu_launches": None, "clocks": clk.summary(),
+    }), flush=True)
+
+
 def main():
     ap = argparse.ArgumentParser(description=__doc__.split("\n")[0])
     ap.add_argument("--gpus", type=int, default=1)
@@ -406,8 +522,16 @@ def main():
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--streams", type=int, default=N_STREAMS,
                     help="streams per GPU (default: the workload's 512); smaller for profiling")
-    ap.add_argument("--workload", choices=["prefill", "proj"], default="prefill",
-                    help="prefill: the headline config-2 line; proj: K1 at config 3's shapes")
+    ap.add_argument("--workload", choices=["prefill", "proj", "model-prefill", "decode"],
+                    default="prefill",
+                    help="prefill: the headline config-2 line; proj: K1 at config 3's shapes; "
+                         "model-prefill: config 3; decode: config 4")
+    ap.add_argument("--decode-batch", type=int, default=256, help="--workload decode: batch")
+    ap.add_argument("--prefix", type=int, default=16384, help="--workload decode: prefix tokens")
+    ap.add_argument("--chunk", type=int, default=1024, help="--workload decode: prefill chunk")
+    ap.add_argument("--entries-per-partition", type=int, default=0,
+                    help="--workload decode: store sizing (0 = worst case, one entry per token)")
+    ap.add_argument("--max-load", type=float, default=0.8, help="--workload decode: table load")
     ap.add_argument("--heads", type=int, nargs="+", default=[8, 16, 32, 64],
                     help="--workload proj: query (= key) heads per layer")
     ap.add_argument("--proj-batch", type=int, default=32, help="--workload proj: sequences")
@@ -418,6 +542,10 @@ def main():
         args.warmup = 3
     if args.workload == "proj":
         run_proj(args)
+    elif args.workload == "model-prefill":
+        run_model_prefill(args)
+    elif args.workload == "decode":
+        run_decode(args)
     elif args.impl == "reference":
         run_reference(args)
     else:

@@ -108,3 +108,29 @@ def values_torch(n_streams: int, T: int, d_v: int, dtype, device, seed: int = 0,
     g = torch.Generator(device=device)
     g.manual_seed(int(seed) * 1000003 + int(config_id))
     return torch.randn((n_streams, T, d_v), generator=g, device=device, dtype=torch.float32).to(dtype)
+
+
+def token_stream(batch: int, T: int, vocab: int, seed: int = 0, config_id: int = 3,
+                 alpha: float = 1.1, copy: float = 0.2) -> np.ndarray:
+    """Token ids [batch, T] (int64) for the model configurations: Zipf(alpha) unigrams over
+    the vocabulary (rank -> token through a random permutation), where a fraction `copy` of
+    the positions start a copy of a bigram from earlier in the same sequence (the two tokens
+    at a uniformly drawn earlier position j, j + 1 are written at t, t + 1). Seeded with
+    numpy's default_rng([seed, config_id])."""
+    rng = np.random.default_rng([seed, config_id])
+    perm = rng.permutation(vocab)
+    cdf = zipf_cdf(vocab, alpha)
+    out = perm[np.minimum(np.searchsorted(cdf, rng.random((batch, T))), vocab - 1)]
+    start = rng.random((batch, T)) < copy
+    pick = rng.random((batch, T))
+    rows = np.arange(batch)
+    busy = np.zeros(batch, dtype=bool)     # position t is the second token of a copy
+    for t in range(2, T - 1):
+        go = start[:, t] & ~busy
+        if go.any():
+            j = np.minimum((pick[:, t] * (t - 1)).astype(np.int64), t - 2)  # j + 1 < t
+            r = rows[go]
+            out[r, t] = out[r, j[go]]
+            out[r, t + 1] = out[r, j[go] + 1]
+        busy = go
+    return out.astype(np.int64)
