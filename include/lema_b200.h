@@ -191,6 +191,71 @@ int lema_store_exchange(void* table, int64_t cap, int64_t vbytes,
                         int64_t g0, int64_t* counts, uint32_t* status,
                         void* workspace, size_t workspace_bytes, void* stream);
 
+/* ----------------------------------- (d) sequence-sharded prefill (config 5) */
+/*
+ * One sequence too long for one pass (or one GPU) is cut into contiguous shards of L
+ * positions per head; a rank owns positions [base, base + L) of all n_heads heads,
+ * laid out [n_heads][L]. Together the calls below give, bit for bit, what one
+ * lema_prefill_match over the whole sequence gives, with src as global positions:
+ *   lema_segment_match   K2 per segment of seg_len positions, with each segment's
+ *                        last-occurrence table (LT: distinct key codes, last position)
+ *   lema_shard_sweep     segments in order against an empty table: misses look up the
+ *                        earlier segments; the table ends up holding the shard's LT
+ *   lema_lt_extract      that LT, for the other ranks (all-gathered by the caller)
+ *   lema_lt_insert       + lema_lt_resolve: queries still unmatched look up the LTs of
+ *                        the earlier ranks
+ *   lema_shard_gather    rows from this shard or from rows fetched from earlier shards
+ * Hash tables: n_heads x slots uint64 words (slots a power of two, see
+ * lema_lt_table_slots), ZERO-FILLED by the caller; an insert keeps the larger position.
+ * Codes are 32-bit; global positions stay below 2^31 - 1.
+ *
+ * Replaces: code/lema/attention.py:100-132 (`latest_prev_match`) over the whole
+ * sequence and the gather of code/lema/attention.py:150-158, for a sharded sequence.
+ */
+size_t lema_segment_workspace_bytes(int64_t n_streams, int64_t T, int code_bytes);
+
+/* lema_prefill_match with src required and the per-stream last-occurrence tables:
+ * lt_code[n * T + e] (code_bytes wide), lt_pos[n * T + e] (position in the stream),
+ * e < lt_count[n], in no particular order. */
+int lema_segment_match(const void* qcodes, const void* kcodes, int code_bytes,
+                       int64_t n_streams, int64_t T, int32_t* src, void* lt_code,
+                       int32_t* lt_pos, int32_t* lt_count, void* workspace,
+                       size_t workspace_bytes, uint32_t* status, void* stream);
+
+/* Slots per head for a table that may hold max_entries codes (load <= 0.5). */
+int64_t lema_lt_table_slots(int64_t max_entries);
+
+/* Insert n entries (heads[i], codes[i]) -> pos[i] (global positions). */
+int lema_lt_insert(uint64_t* table, int64_t n_heads, int64_t slots, const int32_t* heads,
+                   const uint32_t* codes, const int32_t* pos, int64_t n,
+                   uint32_t* status, void* stream);
+
+/* src[h][i] == -1 only: the latest position of qcodes[h][i] in the table, or -1. */
+int lema_lt_resolve(const uint64_t* table, int64_t n_heads, int64_t slots,
+                    const uint32_t* qcodes, int32_t* src, int64_t L, void* stream);
+
+/* Entries with position >= lo, per head h into out_codes/out_pos[h * cap + k],
+ * k < out_count[h] (in no particular order); more than cap sets TABLE_FULL. */
+int lema_lt_extract(const uint64_t* table, int64_t n_heads, int64_t slots, int32_t lo,
+                    uint32_t* out_codes, int32_t* out_pos, int32_t* out_count, int64_t cap,
+                    uint32_t* status, void* stream);
+
+/* One CTA per head walks the L / seg_len segments in order: src (in: index within
+ * the segment or -1, from lema_segment_match) becomes the global position of the
+ * latest earlier key of the shard with the query's code, or -1; then the segment's
+ * LT goes into the table (zero-filled before the call; slots for the shard's
+ * distinct key codes). */
+int lema_shard_sweep(uint64_t* table, int64_t n_heads, int64_t slots, const uint32_t* qcodes,
+                     int32_t* src, int64_t L, int64_t seg_len, const uint32_t* lt_code,
+                     const int32_t* lt_pos, const int32_t* lt_count, int64_t base,
+                     uint32_t* status, void* stream);
+
+/* out[h][i] = values[h][src - base] for src >= base, remote_rows[remote_idx[h][i]]
+ * for 0 <= src < base, zeros for -1. */
+int lema_shard_gather(const int32_t* src, int64_t base, const void* values,
+                      const void* remote_rows, const int32_t* remote_idx, int64_t vbytes,
+                      void* out, int64_t n_heads, int64_t L, uint32_t* status, void* stream);
+
 #ifdef __cplusplus
 }
 #endif

@@ -27,7 +27,8 @@ struct MatchLaunch {
   cudaStream_t stream = nullptr;
 };
 
-size_t match_workspace_bytes(int64_t N, int64_t T, int code_bytes);
+// need_src = false: the caller passes src, so no index scratch is counted.
+size_t match_workspace_bytes(int64_t N, int64_t T, int code_bytes, bool need_src = true);
 int launch_match(const MatchLaunch& a);
 
 }  // namespace lema

@@ -602,12 +602,14 @@ struct Plan {
   size_t off_list = 0, off_tables = 0, total = 0;
 };
 
-Plan make_plan(int64_t N, int64_t T, int code_bytes) {
+// need_src: the caller passes no index output, so the indices live in the workspace.
+Plan make_plan(int64_t N, int64_t T, int code_bytes, bool need_src = true) {
   Plan pl;
   if (N <= 0 || T <= 0) return pl;
   const uint32_t limit = code_bytes == 4 ? overflow_limit<uint32_t>() : overflow_limit<uint64_t>();
   pl.fast = true;  // any T: a stream with too many distinct keys moves to the global path
-  const size_t src_bytes = round_up(4 * static_cast<size_t>(N) * static_cast<size_t>(T), 256);
+  const size_t src_bytes =
+      need_src ? round_up(4 * static_cast<size_t>(N) * static_cast<size_t>(T), 256) : 0;
   pl.total = src_bytes;
   const bool may_overflow = T > static_cast<int64_t>(limit);
   if (!may_overflow) return pl;
@@ -671,8 +673,8 @@ int run(const MatchLaunch& a, const Plan& pl, const DeviceInfo& dev) {
 
 }  // namespace k2
 
-size_t match_workspace_bytes(int64_t N, int64_t T, int code_bytes) {
-  return k2::make_plan(N, T, code_bytes).total;
+size_t match_workspace_bytes(int64_t N, int64_t T, int code_bytes, bool need_src) {
+  return k2::make_plan(N, T, code_bytes, need_src).total;
 }
 
 int launch_match(const MatchLaunch& a) {
@@ -690,7 +692,7 @@ int launch_match(const MatchLaunch& a) {
   }
   const bool lt_any = a.lt_code || a.lt_pos || a.lt_count;
   if (lt_any && !(a.lt_code && a.lt_pos && a.lt_count)) return fail(LEMA_ERR_INVALID_ARGUMENT, "last-occurrence outputs: all three or none");
-  const k2::Plan pl = k2::make_plan(a.N, a.T, a.code_bytes);
+  const k2::Plan pl = k2::make_plan(a.N, a.T, a.code_bytes, a.src == nullptr);
   if (a.ws_bytes < pl.total || (pl.total > 0 && a.ws == nullptr)) {
     return fail(LEMA_ERR_WORKSPACE, "workspace of %zu bytes, %zu needed", a.ws_bytes, pl.total);
   }

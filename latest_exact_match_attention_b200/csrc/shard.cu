@@ -1,0 +1,409 @@
+// Sequence-sharded prefill: the latest exact match over sequences too long for one pass or
+// one GPU (config 5: one sequence of 2^26 positions, 16 heads, sharded over 2-8 GPUs).
+//
+// Replaces, for one sequence cut into contiguous shards, what code/lema/attention.py:100-132
+// (`latest_prev_match`) computes in one pass over the whole sequence. Each rank owns positions
+// [base, base + L) of every head and runs:
+//   1. segment match (K2): the shard is cut into segments of seg_len positions, each matched
+//      on its own by the shared-memory matcher, which also emits the segment's
+//      last-occurrence table (LT): its distinct key codes and their last positions;
+//   2. sweep (lema_shard_sweep): one CTA per head walks the segments in order against a hash
+//      of {code -> latest position so far}, starting empty: the queries a segment could not
+//      resolve on its own look the hash up, then the segment's LT is inserted. Indices become
+//      global positions. Afterwards the hash holds the shard's LT (lema_lt_extract), which the
+//      ranks all-gather: no rank waits for another before this point;
+//   3. resolve (lema_lt_resolve): the queries still without a match look up a hash of the
+//      earlier ranks' LTs (lema_lt_insert), all in parallel;
+//   4. gather (lema_shard_gather): rows of this shard's own positions from its values, rows of
+//      earlier shards' positions from a buffer the caller fetched from their owners.
+// The result is bit-identical to one pass over the whole sequence: the latest earlier key of a
+// query is in its own segment (1), else it is the last occurrence of the code in the latest
+// earlier segment of the shard holding it (2), else in the latest earlier shard holding it (3).
+//
+// Hash tables: per head, `slots` (a power of two) 64-bit words, zero = empty, else
+// (code << 32) | (position + 1); linear probing from fmix32(code). An insert keeps the larger
+// position. Slots are never freed, so a probe that meets an empty slot has seen every slot
+// its code could occupy. Codes are 32-bit (d_qk <= 32).
+#include <cuda_runtime.h>
+
+#include <algorithm>
+
+#include "common.cuh"
+#include "match.cuh"
+
+namespace lema {
+namespace k5 {
+
+__device__ __forceinline__ uint64_t lt_word(uint32_t code, int32_t pos) {
+  return (static_cast<uint64_t>(code) << 32) | static_cast<uint32_t>(pos + 1);
+}
+
+// Inserts code -> pos keeping the larger position. False when every slot was probed.
+__device__ bool lt_insert_max(uint64_t* tab, uint32_t mask, uint32_t code, int32_t pos) {
+  const unsigned long long want = lt_word(code, pos);
+  uint32_t i = fmix32(code) & mask;
+  for (uint32_t probe = 0; probe <= mask; ++probe, i = (i + 1) & mask) {
+    unsigned long long* slot = reinterpret_cast<unsigned long long*>(tab + i);
+    unsigned long long cur = __ldcg(slot);
+    for (;;) {
+      if (cur == 0) {
+        const unsigned long long prev = atomicCAS(slot, 0ull, want);
+        if (prev == 0) return true;
+        cur = prev;
+        continue;
+      }
+      if (static_cast<uint32_t>(cur >> 32) != code) break;
+      if (static_cast<uint32_t>(cur) >= static_cast<uint32_t>(want)) return true;
+      const unsigned long long prev = atomicCAS(slot, cur, want);
+      if (prev == cur) return true;
+      cur = prev;
+    }
+  }
+  return false;
+}
+
+// Latest position stored for code, or -1.
+__device__ __forceinline__ int32_t lt_find(const uint64_t* tab, uint32_t mask, uint32_t code) {
+  uint32_t i = fmix32(code) & mask;
+  for (uint32_t probe = 0; probe <= mask; ++probe, i = (i + 1) & mask) {
+    const uint64_t cur = __ldcg(reinterpret_cast<const unsigned long long*>(tab + i));
+    if (cur == 0) return -1;
+    if (static_cast<uint32_t>(cur >> 32) == code) return static_cast<int32_t>(static_cast<uint32_t>(cur)) - 1;
+  }
+  return -1;
+}
+
+// ------------------------------------------------------------------ inserts
+struct InsertParams {
+  uint64_t* table;
+  int64_t slots;
+  int64_t n_heads;
+  const int32_t* heads;
+  const uint32_t* codes;
+  const int32_t* pos;
+  int64_t n;
+  uint32_t* status;
+};
+
+__global__ void insert_entries_kernel(const InsertParams p) {
+  const uint32_t mask = static_cast<uint32_t>(p.slots - 1);
+  for (int64_t i = blockIdx.x * int64_t(blockDim.x) + threadIdx.x; i < p.n; i += int64_t(gridDim.x) * blockDim.x) {
+    const int32_t h = p.heads[i];
+    if (h < 0 || h >= p.n_heads) {
+      raise_status(p.status, LEMA_STATUS_PROBE_LIMIT);
+      continue;
+    }
+    if (!lt_insert_max(p.table + h * p.slots, mask, p.codes[i], p.pos[i]))
+      raise_status(p.status, LEMA_STATUS_TABLE_FULL);
+  }
+}
+
+// Entries with position >= lo, per head, into out_*[h * cap + k], k < out_count[h].
+struct ExtractParams {
+  const uint64_t* table;
+  int64_t slots, n_heads;
+  int32_t lo;
+  uint32_t* out_codes;
+  int32_t* out_pos;
+  int32_t* out_count;
+  int64_t cap;
+  uint32_t* status;
+};
+
+__global__ void extract_kernel(const ExtractParams p) {
+  const int64_t total = p.n_heads * p.slots;
+  for (int64_t i = blockIdx.x * int64_t(blockDim.x) + threadIdx.x; i < total; i += int64_t(gridDim.x) * blockDim.x) {
+    const uint64_t w = p.table[i];
+    if (w == 0) continue;
+    const int32_t pos = static_cast<int32_t>(static_cast<uint32_t>(w)) - 1;
+    if (pos < p.lo) continue;
+    const int64_t h = i / p.slots;
+    const int32_t k = atomicAdd(p.out_count + h, 1);
+    if (k >= p.cap) {
+      raise_status(p.status, LEMA_STATUS_TABLE_FULL);
+      continue;
+    }
+    p.out_codes[h * p.cap + k] = static_cast<uint32_t>(w >> 32);
+    p.out_pos[h * p.cap + k] = pos;
+  }
+}
+
+// ------------------------------------------------------------------ resolve
+// src[h][i] == -1: the latest position of qc[h][i] in the table (earlier shards), or -1.
+struct ResolveParams {
+  const uint64_t* table;
+  int64_t slots, n_heads, L;
+  const uint32_t* qc;
+  int32_t* src;
+};
+
+__global__ void resolve_kernel(const ResolveParams p) {
+  const uint32_t mask = static_cast<uint32_t>(p.slots - 1);
+  const int64_t total = p.n_heads * p.L;
+  for (int64_t i = blockIdx.x * int64_t(blockDim.x) + threadIdx.x; i < total; i += int64_t(gridDim.x) * blockDim.x) {
+    if (p.src[i] >= 0) continue;
+    const int64_t h = i / p.L;
+    p.src[i] = lt_find(p.table + h * p.slots, mask, p.qc[i]);
+  }
+}
+
+// ------------------------------------------------------------------ sweep
+constexpr int kSweepThreads = 1024;
+constexpr int kSweepPer = 4;  // positions per thread per pass, looked up together
+
+struct SweepParams {
+  uint64_t* table;
+  int64_t slots;
+  const uint32_t* qc;  // [H][L]
+  int32_t* src;        // [H][L]: in, segment-relative index or -1; out, global position or -1
+  int64_t L, seg_len, n_seg, base;
+  const uint32_t* lt_code;
+  const int32_t* lt_pos;
+  const int32_t* lt_count;
+  uint32_t* status;
+};
+
+__global__ void __launch_bounds__(kSweepThreads) sweep_kernel(const SweepParams p) {
+  const int64_t h = blockIdx.x;
+  uint64_t* tab = p.table + h * p.slots;
+  const uint32_t mask = static_cast<uint32_t>(p.slots - 1);
+  const uint32_t* qc = p.qc + h * p.L;
+  int32_t* src = p.src + h * p.L;
+  for (int64_t seg = 0; seg < p.n_seg; ++seg) {
+    const int64_t s0 = seg * p.seg_len;
+    const int64_t g0 = p.base + s0;
+    // queries: in-segment hits become global; misses look up the earlier segments and shards
+    for (int64_t c = 0; c < p.seg_len; c += int64_t(kSweepThreads) * kSweepPer) {
+      int32_t s[kSweepPer];
+      uint32_t q[kSweepPer];
+#pragma unroll
+      for (int k = 0; k < kSweepPer; ++k) {
+        const int64_t i = c + k * kSweepThreads + threadIdx.x;
+        s[k] = i < p.seg_len ? src[s0 + i] : 0;
+        q[k] = (i < p.seg_len && s[k] < 0) ? qc[s0 + i] : 0;
+      }
+#pragma unroll
+      for (int k = 0; k < kSweepPer; ++k) {
+        const int64_t i = c + k * kSweepThreads + threadIdx.x;
+        if (i >= p.seg_len) continue;
+        src[s0 + i] = s[k] >= 0 ? static_cast<int32_t>(g0 + s[k]) : lt_find(tab, mask, q[k]);
+      }
+    }
+    __syncthreads();
+    // the segment's keys: each distinct code once, at its last position in the segment
+    const int64_t st = h * p.n_seg + seg;
+    const int32_t cnt = p.lt_count[st];
+    const uint32_t* lc = p.lt_code + st * p.seg_len;
+    const int32_t* lp = p.lt_pos + st * p.seg_len;
+    for (int e = threadIdx.x; e < cnt; e += kSweepThreads)
+      if (!lt_insert_max(tab, mask, lc[e], static_cast<int32_t>(g0 + lp[e])))
+        raise_status(p.status, LEMA_STATUS_TABLE_FULL);
+    __syncthreads();
+  }
+}
+
+// ------------------------------------------------------------------ gather
+struct GatherParams {
+  const int32_t* src;  // [H][L] global positions or -1
+  int64_t base, L, rows;
+  const unsigned char* v;       // [H][L] rows of this shard
+  const unsigned char* remote;  // rows fetched from earlier shards
+  const int32_t* remote_idx;    // [H][L] row of `remote` for a position before base
+  unsigned char* out;
+  int64_t vbytes;
+  uint32_t* status;
+};
+
+// One thread per output row; a row is vbytes / sizeof(Vec) words, all loads issued first.
+template <typename Vec>
+__global__ void __launch_bounds__(256) shard_gather_kernel(const GatherParams g) {
+  const int64_t W = g.vbytes / static_cast<int64_t>(sizeof(Vec));
+  for (int64_t r = blockIdx.x * int64_t(blockDim.x) + threadIdx.x; r < g.rows; r += int64_t(gridDim.x) * blockDim.x) {
+    const int32_t s = g.src[r];
+    Vec* dst = reinterpret_cast<Vec*>(g.out + r * g.vbytes);
+    const Vec* from = nullptr;
+    if (s >= g.base) {
+      const int64_t h = r / g.L;
+      from = reinterpret_cast<const Vec*>(g.v + (h * g.L + (s - g.base)) * g.vbytes);
+    } else if (s >= 0) {
+      const int32_t ri = g.remote_idx[r];
+      if (ri < 0) {
+        raise_status(g.status, LEMA_STATUS_PROBE_LIMIT);  // a remote row nobody fetched
+      } else {
+        from = reinterpret_cast<const Vec*>(g.remote + static_cast<int64_t>(ri) * g.vbytes);
+      }
+    }
+    constexpr int kBatch = 8;
+    for (int64_t w0 = 0; w0 < W; w0 += kBatch) {
+      Vec buf[kBatch];
+#pragma unroll
+      for (int k = 0; k < kBatch; ++k)
+        if (w0 + k < W) buf[k] = from ? from[w0 + k] : zero_vec<Vec>();
+#pragma unroll
+      for (int k = 0; k < kBatch; ++k)
+        if (w0 + k < W) store_stream(dst + w0 + k, buf[k]);
+    }
+  }
+}
+
+int grid_for(int64_t work, int threads, const DeviceInfo& dev, int per_sm = 8) {
+  const int64_t want = (work + threads - 1) / threads;
+  return static_cast<int>(std::max<int64_t>(1, std::min<int64_t>(want, int64_t(dev.sms) * per_sm)));
+}
+
+const DeviceInfo* sm100() {
+  const DeviceInfo* dev = current_device_info();
+  if (dev == nullptr) return nullptr;
+  if (dev->cc_major != 10) {
+    fail(LEMA_ERR_UNSUPPORTED, "built for sm_100a; device is sm_%d%d", dev->cc_major, dev->cc_minor);
+    return nullptr;
+  }
+  return dev;
+}
+
+bool pow2(int64_t x) { return x > 0 && (x & (x - 1)) == 0; }
+
+}  // namespace k5
+}  // namespace lema
+
+using namespace lema;
+
+extern "C" size_t lema_segment_workspace_bytes(int64_t n_streams, int64_t T, int code_bytes) {
+  return match_workspace_bytes(n_streams, T, code_bytes, false);
+}
+
+extern "C" int lema_segment_match(const void* qcodes, const void* kcodes, int code_bytes, int64_t n_streams,
+                                  int64_t T, int32_t* src, void* lt_code, int32_t* lt_pos, int32_t* lt_count,
+                                  void* workspace, size_t workspace_bytes, uint32_t* status, void* stream) {
+  clear_error();
+  if (src == nullptr || lt_code == nullptr || lt_pos == nullptr || lt_count == nullptr)
+    return fail(LEMA_ERR_INVALID_ARGUMENT, "src and the three last-occurrence outputs are required");
+  MatchLaunch m;
+  m.qc = qcodes;
+  m.kc = kcodes;
+  m.code_bytes = code_bytes;
+  m.N = n_streams;
+  m.T = T;
+  m.src = src;
+  m.lt_code = lt_code;
+  m.lt_pos = lt_pos;
+  m.lt_count = lt_count;
+  m.ws = workspace;
+  m.ws_bytes = workspace_bytes;
+  m.status = status;
+  m.stream = static_cast<cudaStream_t>(stream);
+  return launch_match(m);
+}
+
+extern "C" int64_t lema_lt_table_slots(int64_t max_entries) {
+  return static_cast<int64_t>(next_pow2(static_cast<uint64_t>(std::max<int64_t>(64, 2 * max_entries))));
+}
+
+extern "C" int lema_lt_insert(uint64_t* table, int64_t n_heads, int64_t slots, const int32_t* heads,
+                              const uint32_t* codes, const int32_t* pos, int64_t n, uint32_t* status,
+                              void* stream) {
+  clear_error();
+  if (n_heads <= 0 || !k5::pow2(slots) || slots > (int64_t(1) << 31) || n < 0)
+    return fail(LEMA_ERR_INVALID_ARGUMENT, "bad table shape (heads %lld, slots %lld) or count", (long long)n_heads, (long long)slots);
+  if (n == 0) return LEMA_OK;
+  if (table == nullptr || heads == nullptr || codes == nullptr || pos == nullptr)
+    return fail(LEMA_ERR_INVALID_ARGUMENT, "null pointer argument");
+  const DeviceInfo* dev = k5::sm100();
+  if (dev == nullptr) return LEMA_ERR_UNSUPPORTED;
+  k5::InsertParams p{};
+  p.table = table;
+  p.slots = slots;
+  p.n_heads = n_heads;
+  p.heads = heads;
+  p.codes = codes;
+  p.pos = pos;
+  p.n = n;
+  p.status = status;
+  k5::insert_entries_kernel<<<k5::grid_for(n, 256, *dev), 256, 0, static_cast<cudaStream_t>(stream)>>>(p);
+  LEMA_CUDA_TRY(cudaGetLastError());
+  return LEMA_OK;
+}
+
+extern "C" int lema_lt_resolve(const uint64_t* table, int64_t n_heads, int64_t slots, const uint32_t* qcodes,
+                               int32_t* src, int64_t L, void* stream) {
+  clear_error();
+  if (n_heads <= 0 || !k5::pow2(slots) || slots > (int64_t(1) << 31) || L < 0)
+    return fail(LEMA_ERR_INVALID_ARGUMENT, "bad shape (heads %lld, slots %lld, L %lld)", (long long)n_heads,
+                (long long)slots, (long long)L);
+  if (L == 0) return LEMA_OK;
+  if (table == nullptr || qcodes == nullptr || src == nullptr) return fail(LEMA_ERR_INVALID_ARGUMENT, "null pointer argument");
+  const DeviceInfo* dev = k5::sm100();
+  if (dev == nullptr) return LEMA_ERR_UNSUPPORTED;
+  k5::ResolveParams p{table, slots, n_heads, L, qcodes, src};
+  k5::resolve_kernel<<<k5::grid_for(n_heads * L, 256, *dev), 256, 0, static_cast<cudaStream_t>(stream)>>>(p);
+  LEMA_CUDA_TRY(cudaGetLastError());
+  return LEMA_OK;
+}
+
+extern "C" int lema_lt_extract(const uint64_t* table, int64_t n_heads, int64_t slots, int32_t lo,
+                               uint32_t* out_codes, int32_t* out_pos, int32_t* out_count, int64_t cap,
+                               uint32_t* status, void* stream) {
+  clear_error();
+  if (n_heads <= 0 || !k5::pow2(slots) || cap < 0)
+    return fail(LEMA_ERR_INVALID_ARGUMENT, "bad table shape or capacity");
+  if (table == nullptr || out_codes == nullptr || out_pos == nullptr || out_count == nullptr)
+    return fail(LEMA_ERR_INVALID_ARGUMENT, "null pointer argument");
+  const DeviceInfo* dev = k5::sm100();
+  if (dev == nullptr) return LEMA_ERR_UNSUPPORTED;
+  k5::ExtractParams p{table, slots, n_heads, lo, out_codes, out_pos, out_count, cap, status};
+  LEMA_CUDA_TRY(cudaMemsetAsync(out_count, 0, sizeof(int32_t) * n_heads, static_cast<cudaStream_t>(stream)));
+  k5::extract_kernel<<<k5::grid_for(n_heads * slots, 256, *dev), 256, 0, static_cast<cudaStream_t>(stream)>>>(p);
+  LEMA_CUDA_TRY(cudaGetLastError());
+  return LEMA_OK;
+}
+
+extern "C" int lema_shard_sweep(uint64_t* table, int64_t n_heads, int64_t slots, const uint32_t* qcodes,
+                                int32_t* src, int64_t L, int64_t seg_len, const uint32_t* lt_code,
+                                const int32_t* lt_pos, const int32_t* lt_count, int64_t base, uint32_t* status,
+                                void* stream) {
+  clear_error();
+  if (n_heads <= 0 || !k5::pow2(slots) || slots > (int64_t(1) << 31) || L < 0 || seg_len <= 0 || base < 0)
+    return fail(LEMA_ERR_INVALID_ARGUMENT, "bad shape (heads %lld, slots %lld, L %lld, segment %lld)",
+                (long long)n_heads, (long long)slots, (long long)L, (long long)seg_len);
+  if (L % seg_len != 0) return fail(LEMA_ERR_INVALID_ARGUMENT, "L = %lld is not whole segments of %lld", (long long)L, (long long)seg_len);
+  if (base + L >= (int64_t(1) << 31) - 1) return fail(LEMA_ERR_INVALID_ARGUMENT, "positions must stay below 2^31 - 1");
+  if (L == 0) return LEMA_OK;
+  if (table == nullptr || qcodes == nullptr || src == nullptr || lt_code == nullptr || lt_pos == nullptr || lt_count == nullptr)
+    return fail(LEMA_ERR_INVALID_ARGUMENT, "null pointer argument");
+  const DeviceInfo* dev = k5::sm100();
+  if (dev == nullptr) return LEMA_ERR_UNSUPPORTED;
+  k5::SweepParams p{table, slots, qcodes, src, L, seg_len, L / seg_len, base, lt_code, lt_pos, lt_count, status};
+  k5::sweep_kernel<<<static_cast<unsigned>(n_heads), k5::kSweepThreads, 0, static_cast<cudaStream_t>(stream)>>>(p);
+  LEMA_CUDA_TRY(cudaGetLastError());
+  return LEMA_OK;
+}
+
+extern "C" int lema_shard_gather(const int32_t* src, int64_t base, const void* values, const void* remote_rows,
+                                 const int32_t* remote_idx, int64_t vbytes, void* out, int64_t n_heads, int64_t L,
+                                 uint32_t* status, void* stream) {
+  clear_error();
+  if (n_heads < 0 || L < 0 || base < 0 || vbytes <= 0 || vbytes % 2 != 0)
+    return fail(LEMA_ERR_INVALID_ARGUMENT, "bad shape or value row of %lld bytes (positive, even)", (long long)vbytes);
+  if (n_heads == 0 || L == 0) return LEMA_OK;
+  if (src == nullptr || values == nullptr || out == nullptr || (base > 0 && (remote_idx == nullptr)))
+    return fail(LEMA_ERR_INVALID_ARGUMENT, "null pointer argument");
+  const DeviceInfo* dev = k5::sm100();
+  if (dev == nullptr) return LEMA_ERR_UNSUPPORTED;
+  k5::GatherParams g{src, base, L, n_heads * L, static_cast<const unsigned char*>(values),
+                     static_cast<const unsigned char*>(remote_rows), remote_idx, static_cast<unsigned char*>(out),
+                     vbytes, status};
+  const cudaStream_t s = static_cast<cudaStream_t>(stream);
+  const int grid = k5::grid_for(g.rows, 256, *dev);
+  const uintptr_t a = reinterpret_cast<uintptr_t>(values) | reinterpret_cast<uintptr_t>(out) |
+                      reinterpret_cast<uintptr_t>(remote_rows) | static_cast<uintptr_t>(vbytes);
+  if (a % 16 == 0)
+    k5::shard_gather_kernel<uint4><<<grid, 256, 0, s>>>(g);
+  else if (a % 8 == 0)
+    k5::shard_gather_kernel<uint2><<<grid, 256, 0, s>>>(g);
+  else if (a % 4 == 0)
+    k5::shard_gather_kernel<unsigned int><<<grid, 256, 0, s>>>(g);
+  else
+    k5::shard_gather_kernel<unsigned short><<<grid, 256, 0, s>>>(g);
+  LEMA_CUDA_TRY(cudaGetLastError());
+  return LEMA_OK;
+}

@@ -1,0 +1,306 @@
+"""The exact op over one sequence too long for one pass or one GPU, sharded by sequence.
+
+Config 5 of the benchmark: one sequence of 2^26 positions, 16 heads, 32-bit codes, 128-byte
+value rows -- about 287 GB resident, so at least two B200s. Rank r of W owns positions
+[r * L, (r + 1) * L) of every head ([H, L] codes, [H, L, d_v] values) and computes, for
+those positions, exactly what one `latest_prev_match` + gather over the whole sequence gives
+(code/lema/attention.py:100-158): src as global positions, and the value rows.
+
+Per rank (kernels in csrc/shard.cu, K2 in csrc/prefill_match.cu):
+
+    1. segment match     K2 on segments of `seg_len` positions, each with its last-occurrence
+                         table (LT: distinct key codes and their last positions)
+    2. sweep             per head, segments in order against a device hash: in-segment
+                         misses look up earlier segments; the hash ends as the shard's LT
+    3. exchange          all-gather of the shards' LTs (code, position; 12 bytes per entry)
+    4. resolve           queries still unmatched look up the earlier shards' LTs
+    5. fetch             rows at earlier shards' positions: requests (deduplicated) and rows
+                         by all-to-all, landing in this GPU's memory before any kernel reads
+    6. gather            one kernel: own rows, fetched rows, or zeros
+
+Only step 3 and 5 talk to other ranks, and nothing waits for another rank before step 3.
+The collectives go through a `Comm`: `TorchComm` (torch.distributed: NCCL on the GPU, gloo
+in the CPU tests), `ThreadComm` (ranks as threads of one process, for running the same code
+over virtual shards on one GPU), `SingleComm`. The per-rank device work goes through an ops
+object (`CudaOps` here; the CPU tests plug in a restatement).
+"""
+from __future__ import annotations
+
+import threading
+
+import torch
+
+from . import _lib
+from ._lib import LEMA_STATUS_PROBE_LIMIT, LEMA_STATUS_TABLE_FULL, LemaError, call, ptr, require_cuda
+
+__all__ = ["sharded_prefill", "emulated_sharded_prefill", "CudaOps", "TorchComm", "ThreadComm",
+           "SingleComm"]
+
+
+# ---------------------------------------------------------------------------- comms
+class SingleComm:
+    rank, world = 0, 1
+
+    def all_gather(self, t):
+        return [t]
+
+    def all_to_all(self, parts):
+        return list(parts)
+
+
+class TorchComm:
+    """Collectives over a torch.distributed process group (every rank calls every method in
+    the same order). Variable-length data: counts first, then padded / split transfers."""
+
+    def __init__(self, group=None):
+        import torch.distributed as dist
+        self.dist, self.group = dist, group
+        self.rank = dist.get_rank(group)
+        self.world = dist.get_world_size(group)
+
+    def _counts(self, n: int, device) -> list[int]:
+        c = torch.tensor([n], dtype=torch.int64, device=device)
+        out = torch.empty(self.world, dtype=torch.int64, device=device)
+        self.dist.all_gather_into_tensor(out, c, group=self.group)
+        return [int(x) for x in out.cpu()]
+
+    def all_gather(self, t: torch.Tensor) -> list[torch.Tensor]:
+        """t [n, ...] -> the tensors of every rank, in rank order."""
+        counts = self._counts(t.shape[0], t.device)
+        m = max(counts)
+        pad = torch.zeros((m,) + tuple(t.shape[1:]), dtype=t.dtype, device=t.device)
+        pad[: t.shape[0]] = t
+        out = torch.empty((self.world * m,) + tuple(t.shape[1:]), dtype=t.dtype, device=t.device)
+        self.dist.all_gather_into_tensor(out, pad, group=self.group)
+        return [out[r * m: r * m + counts[r]] for r in range(self.world)]
+
+    def all_to_all(self, parts: list[torch.Tensor]) -> list[torch.Tensor]:
+        """parts[d] goes to rank d; returns what every rank sent here, in rank order."""
+        dev = parts[0].device
+        send_n = torch.tensor([p.shape[0] for p in parts], dtype=torch.int64, device=dev)
+        recv_n = torch.empty_like(send_n)
+        self.dist.all_to_all_single(recv_n, send_n, group=self.group)
+        rn = [int(x) for x in recv_n.cpu()]
+        tail = tuple(parts[0].shape[1:])
+        send = torch.cat(parts) if parts else torch.empty((0,) + tail, dtype=parts[0].dtype, device=dev)
+        recv = torch.empty((sum(rn),) + tail, dtype=send.dtype, device=dev)
+        self.dist.all_to_all_single(recv, send, output_split_sizes=rn,
+                                    input_split_sizes=[p.shape[0] for p in parts], group=self.group)
+        return list(recv.split(rn))
+
+
+class _Board:
+    def __init__(self, world):
+        self.world = world
+        self.slots = [None] * world
+        self.barrier = threading.Barrier(world)
+
+
+class ThreadComm:
+    """Ranks as threads of one process sharing one board; for emulating W shards on one GPU
+    with the code path the distributed run takes."""
+
+    def __init__(self, board: _Board, rank: int):
+        self.board, self.rank, self.world = board, rank, board.world
+
+    def _swap(self, obj):
+        b = self.board
+        b.barrier.wait()
+        b.slots[self.rank] = obj
+        b.barrier.wait()
+        got = list(b.slots)
+        b.barrier.wait()
+        return got
+
+    def all_gather(self, t):
+        return self._swap(t)
+
+    def all_to_all(self, parts):
+        got = self._swap(list(parts))
+        return [got[r][self.rank] for r in range(self.world)]
+
+
+# ---------------------------------------------------------------------------- device ops
+class CudaOps:
+    """The per-rank device work, on this library's kernels."""
+
+    def __init__(self, device):
+        self.device = device
+        self.status = torch.zeros(1, dtype=torch.int32, device=device)
+
+    def _stream(self):
+        return torch.cuda.current_stream(self.device).cuda_stream
+
+    def segment_match(self, qc, kc, seg_len):
+        """-> src [H, L] (index within the segment or -1), lt_code/lt_pos [H * n_seg, seg_len],
+        lt_count [H * n_seg]."""
+        H, L = qc.shape
+        n = H * (L // seg_len)
+        src = torch.empty((H, L), dtype=torch.int32, device=self.device)
+        ltc = torch.empty((n, seg_len), dtype=torch.int32, device=self.device)
+        ltp = torch.empty((n, seg_len), dtype=torch.int32, device=self.device)
+        ltn = torch.empty(n, dtype=torch.int32, device=self.device)
+        wsb = int(_lib.lib().lema_segment_workspace_bytes(n, seg_len, 4))
+        ws = torch.empty(wsb, dtype=torch.uint8, device=self.device) if wsb else None
+        call("lema_segment_match", ptr(qc), ptr(kc), 4, n, seg_len, ptr(src), ptr(ltc), ptr(ltp),
+             ptr(ltn), ptr(ws), wsb, ptr(self.status), self._stream())
+        return src, ltc, ltp, ltn
+
+    def sweep(self, qc, src, lt, seg_len, base):
+        """Segments in order; returns the shard's LT as entries [m, 3] int32 (head, code, pos)."""
+        ltc, ltp, ltn = lt
+        H, L = qc.shape
+        n_seg = L // seg_len
+        # distinct codes per head <= the sum of its segments' distinct codes, and <= L
+        bound = int(torch.minimum(ltn.view(H, n_seg).sum(1, dtype=torch.int64),
+                                  torch.tensor(L, device=self.device)).max())
+        slots = int(_lib.lib().lema_lt_table_slots(bound))
+        table = torch.zeros((H, slots), dtype=torch.int64, device=self.device)
+        call("lema_shard_sweep", ptr(table), H, slots, ptr(qc), ptr(src), L, seg_len, ptr(ltc),
+             ptr(ltp), ptr(ltn), base, ptr(self.status), self._stream())
+        cap = int((table != 0).sum(1).max())              # the shard's distinct codes per head
+        codes = torch.empty((H, cap), dtype=torch.int32, device=self.device)
+        pos = torch.empty((H, cap), dtype=torch.int32, device=self.device)
+        cnt = torch.empty(H, dtype=torch.int32, device=self.device)
+        call("lema_lt_extract", ptr(table), H, slots, base, ptr(codes), ptr(pos), ptr(cnt), cap,
+             ptr(self.status), self._stream())
+        del table
+        keep = torch.arange(cap, device=self.device)[None, :] < cnt[:, None]
+        heads = torch.arange(H, dtype=torch.int32, device=self.device)[:, None].expand(H, cap)
+        return torch.stack([heads[keep], codes[keep], pos[keep]], 1)
+
+    def resolve(self, qc, src, earlier):
+        """Queries with src == -1 look up the earlier shards' entries [m, 3]."""
+        if earlier.shape[0] == 0:
+            return
+        H, L = qc.shape
+        per_head = torch.bincount(earlier[:, 0].long(), minlength=H)
+        slots = int(_lib.lib().lema_lt_table_slots(int(per_head.max())))
+        table = torch.zeros((H, slots), dtype=torch.int64, device=self.device)
+        e = earlier.contiguous()
+        heads, codes, pos = (e[:, i].contiguous() for i in range(3))
+        call("lema_lt_insert", ptr(table), H, slots, ptr(heads), ptr(codes), ptr(pos), e.shape[0],
+             ptr(self.status), self._stream())
+        call("lema_lt_resolve", ptr(table), H, slots, ptr(qc), ptr(src), L, self._stream())
+
+    @staticmethod
+    def rows(vflat, idx):
+        return vflat.index_select(0, idx)
+
+    def gather(self, src, base, v, remote_rows, remote_idx):
+        H, L = src.shape
+        vb = v[0, 0].numel() * v.element_size()
+        out = torch.empty_like(v)
+        call("lema_shard_gather", ptr(src), base, ptr(v), ptr(remote_rows), ptr(remote_idx), vb,
+             ptr(out), H, L, ptr(self.status), self._stream())
+        return out
+
+    def check(self):
+        s = int(self.status.item())
+        if s:
+            self.status.zero_()
+            what = "a hash table filled up" if s & LEMA_STATUS_TABLE_FULL else (
+                "an internal bound ran out" if s & LEMA_STATUS_PROBE_LIMIT else f"status {s:#x}")
+            raise LemaError(f"sharded prefill: {what}")
+
+
+# ---------------------------------------------------------------------------- the protocol
+def sharded_prefill(qc: torch.Tensor, kc: torch.Tensor, v: torch.Tensor, comm=None, ops=None,
+                    seg_len: int = 4096):
+    """This rank's part of the exact op over one sharded sequence.
+
+    qc, kc: [H, L] int32 (uint32 codes) of positions [rank * L, (rank + 1) * L); v: [H, L, d_v].
+    Every rank passes the same H, L and seg_len (L a multiple of seg_len). Returns
+    (src [H, L] int32 global positions or -1, out [H, L, d_v])."""
+    comm = comm or SingleComm()
+    if ops is None:
+        ops = CudaOps(require_cuda(qc, kc, v))
+    H, L = qc.shape
+    if kc.shape != (H, L) or v.shape[:2] != (H, L):
+        raise ValueError(f"shapes qc {tuple(qc.shape)}, kc {tuple(kc.shape)}, v {tuple(v.shape)}")
+    if qc.dtype != torch.int32 or kc.dtype != torch.int32:
+        raise ValueError("codes must be int32 (uint32 bit patterns)")
+    if L % seg_len:
+        raise ValueError(f"L = {L} is not a multiple of seg_len = {seg_len}")
+    if comm.world * L >= 2 ** 31 - 1:
+        raise ValueError("the sequence must stay below 2^31 - 1 positions")
+    qc, kc, v = qc.contiguous(), kc.contiguous(), v.contiguous()
+    base = comm.rank * L
+
+    # 1-2: local work, no rank waits for another
+    src, ltc, ltp, ltn = ops.segment_match(qc, kc, seg_len)
+    mine = ops.sweep(qc, src, (ltc, ltp, ltn), seg_len, base)
+    del ltc, ltp, ltn
+    # 3-4: the shards' last-occurrence tables
+    tables = comm.all_gather(mine)
+    earlier = torch.cat(tables[: comm.rank]) if comm.rank else mine[:0]
+    ops.resolve(qc, src, earlier)
+    del tables, earlier
+
+    # 5: rows at earlier shards' positions, requested once each, head by head
+    vflat = v.view(H * L, -1).view(torch.uint8)           # rows as bytes, for transport
+    remote_idx = torch.full((H, L), -1, dtype=torch.int32, device=src.device)
+    want, where = [], []
+    n_before = 0
+    for h in range(H):
+        s = src[h]
+        q = ((s >= 0) & (s < base)).nonzero().squeeze(1)
+        p = s[q].long()
+        owner = p // L
+        key = owner * (H * L) + h * L + (p - owner * L)   # owner-major, then the owner's flat row
+        uniq, inv = torch.unique(key, return_inverse=True)
+        want.append(uniq)
+        where.append((h, q, inv + n_before))
+        n_before += uniq.numel()
+    uniq = torch.cat(want) if want else torch.empty(0, dtype=torch.int64, device=src.device)
+    order = torch.sort(uniq // (H * L), stable=True)                # group by owner
+    pos_of = torch.empty_like(order.indices)
+    pos_of[order.indices] = torch.arange(order.indices.numel(), device=src.device)
+    for h, q, j in where:
+        remote_idx[h, q] = pos_of[j].to(torch.int32)
+    req = uniq[order.indices]
+    counts = torch.bincount(order.values, minlength=comm.world).tolist()
+    send = list((req % (H * L)).split(counts))
+    asked = comm.all_to_all(send)                          # rows the other ranks want from me
+    reply = [ops.rows(vflat, a) for a in asked]
+    got = comm.all_to_all(reply)
+    remote_rows = torch.cat(got) if got else vflat[:0]
+
+    # 6
+    out = ops.gather(src, base, v, remote_rows, remote_idx)
+    ops.check()
+    return src, out
+
+
+def emulated_sharded_prefill(qc: torch.Tensor, kc: torch.Tensor, v: torch.Tensor, n_shards: int,
+                             seg_len: int = 4096):
+    """The sharded computation over [H, T] inputs on ONE device: n_shards ranks as threads,
+    each with its slice, through the same protocol a multi-GPU run takes. Returns the shards'
+    (src, out) concatenated along the sequence."""
+    H, T = qc.shape
+    if T % n_shards:
+        raise ValueError(f"T = {T} does not split into {n_shards} shards")
+    L = T // n_shards
+    board = _Board(n_shards)
+    results: list = [None] * n_shards
+    errors: list = []
+    dev = qc.device
+
+    def run(r):
+        try:
+            with torch.cuda.device(dev):
+                sl = slice(r * L, (r + 1) * L)
+                results[r] = sharded_prefill(qc[:, sl], kc[:, sl], v[:, sl], ThreadComm(board, r),
+                                             CudaOps(dev), seg_len)
+        except BaseException as e:  # noqa: BLE001 -- re-raised in the caller
+            errors.append(e)
+            board.barrier.abort()
+
+    threads = [threading.Thread(target=run, args=(r,)) for r in range(n_shards)]
+    for t in threads:
+        t.start()
+    for t in threads:
+        t.join()
+    if errors:
+        raise errors[0]
+    return (torch.cat([s for s, _ in results], 1), torch.cat([o for _, o in results], 1))
