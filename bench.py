@@ -512,6 +512,81 @@ def run_decode(args):
     }), flush=True)
 
 
+def run_longctx(args):
+    """Config 5: the exact op over ONE sequence of --long-t positions (default 2^26), 16 heads,
+    32-bit codes (pool 2^20, Zipf 1.05, 5% fresh), 128-byte bf16 value rows, sharded by
+    sequence over the torchrun ranks (one per GPU): each rank owns a contiguous slice of every
+    head and the ranks exchange last-occurrence tables and value rows over NCCL
+    (latest_exact_match_attention_b200.longctx). Value: positions per second of the whole
+    sequence; time = max over ranks of CUDA-event time."""
+    import torch
+
+    from latest_exact_match_attention_b200 import synth
+    from latest_exact_match_attention_b200.longctx import SingleComm, TorchComm, sharded_prefill
+    rank, world = dist_setup(args.gpus)
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    H, T = 16, args.long_t
+    L = T // world
+    qc, kc, v = synth.long_code_shard(H, rank * L, L, synth.CONFIG5, seed=0, device=dev)
+    comm = TorchComm() if world > 1 else SingleComm()
+    stream = torch.cuda.current_stream(dev)
+
+    def barrier():
+        if world > 1:
+            torch.distributed.barrier()
+
+    for _ in range(max(1, args.warmup)):
+        src, out = sharded_prefill(qc, kc, v, comm, seg_len=args.seg_len)
+        del src, out
+    torch.cuda.synchronize()
+    hit = 0.0
+    times, phases = [], {}
+    with ClockSampler(local) as clk:
+        for _ in range(args.steps):
+            barrier()
+            torch.cuda.synchronize()
+            marks = []
+            a = torch.cuda.Event(enable_timing=True)
+            a.record(stream)
+            src, out = sharded_prefill(qc, kc, v, comm, seg_len=args.seg_len, marks=marks)
+            torch.cuda.synchronize()
+            times.append(a.elapsed_time(marks[-1][1]))
+            prev = a
+            for name, e in marks:
+                phases[name] = phases.get(name, 0.0) + prev.elapsed_time(e) / args.steps
+                prev = e
+            hit = float((src >= 0).float().mean())
+            del src, out
+    barrier()
+    ms = statistics.mean(times)
+    if world > 1:
+        t = torch.tensor([ms], device=dev)
+        torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
+        ms = float(t.item())
+    if world > 1:
+        torch.distributed.destroy_process_group()
+    if rank != 0:
+        return
+    n = H * T
+    alg = n * (4 + 4 + 128 + 4)            # codes, index, row out per position (+ rows read)
+    print(json.dumps({
+        "metric": "LEMA sequence-sharded prefill Mpos/s (config 5)", "value": round(n / ms / 1e3, 2),
+        "unit": "Mpos/s", "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
+        "ms_per_step": round(ms, 3), "higher_is_better": True, "scaling": "strong",
+        "dtype": "u32", "data": "synthetic (device-generated, chunk-seeded)",
+        "config": {"workload": f"cfg5: T={T} H={H} 32-bit codes pool 2^20 Zipf 1.05 5% fresh, d_v 64 bf16",
+                   "positions_per_gpu": n // world, "seg_len": args.seg_len, "hit_rate": round(hit, 4),
+                   "parallelism": f"sequence x{world}, NCCL all-gather + all-to-all"},
+        "phases_ms_rank0": {k: round(x, 3) for k, x in phases.items()},
+        "roofline": {"bound": "hbm", "alg_bytes_per_gpu_lower": alg // world,
+                     "achieved": round(alg / world / (ms / 1e3) / 1e9, 1), "peak": peaks()[0],
+                     "unit": "GB/s", "frac": round(alg / world / (ms / 1e3) / 1e9 / peaks()[0], 4)},
+        "clocks": clk.summary(),
+    }), flush=True)
+
+
 def main():
     ap = argparse.ArgumentParser(description=__doc__.split("\n")[0])
     ap.add_argument("--gpus", type=int, default=1)
@@ -522,7 +597,9 @@ def main():
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--streams", type=int, default=N_STREAMS,
                     help="streams per GPU (default: the workload's 512); smaller for profiling")
-    ap.add_argument("--workload", choices=["prefill", "proj", "model-prefill", "decode"],
+    ap.add_argument("--long-t", type=int, default=1 << 26, help="--workload longctx: positions")
+    ap.add_argument("--seg-len", type=int, default=4096, help="--workload longctx: segment")
+    ap.add_argument("--workload", choices=["prefill", "proj", "model-prefill", "decode", "longctx"],
                     default="prefill",
                     help="prefill: the headline config-2 line; proj: K1 at config 3's shapes; "
                          "model-prefill: config 3; decode: config 4")
@@ -546,6 +623,8 @@ def main():
         run_model_prefill(args)
     elif args.workload == "decode":
         run_decode(args)
+    elif args.workload == "longctx":
+        run_longctx(args)
     elif args.impl == "reference":
         run_reference(args)
     else:

@@ -206,12 +206,13 @@ class CudaOps:
 
 # ---------------------------------------------------------------------------- the protocol
 def sharded_prefill(qc: torch.Tensor, kc: torch.Tensor, v: torch.Tensor, comm=None, ops=None,
-                    seg_len: int = 4096):
+                    seg_len: int = 4096, marks: list | None = None):
     """This rank's part of the exact op over one sharded sequence.
 
     qc, kc: [H, L] int32 (uint32 codes) of positions [rank * L, (rank + 1) * L); v: [H, L, d_v].
     Every rank passes the same H, L and seg_len (L a multiple of seg_len). Returns
-    (src [H, L] int32 global positions or -1, out [H, L, d_v])."""
+    (src [H, L] int32 global positions or -1, out [H, L, d_v]). `marks`, if a list, receives
+    (phase name, CUDA event recorded after it) for timing the phases."""
     comm = comm or SingleComm()
     if ops is None:
         ops = CudaOps(require_cuda(qc, kc, v))
@@ -229,13 +230,17 @@ def sharded_prefill(qc: torch.Tensor, kc: torch.Tensor, v: torch.Tensor, comm=No
 
     # 1-2: local work, no rank waits for another
     src, ltc, ltp, ltn = ops.segment_match(qc, kc, seg_len)
+    _mark(marks, "segment_match")
     mine = ops.sweep(qc, src, (ltc, ltp, ltn), seg_len, base)
     del ltc, ltp, ltn
+    _mark(marks, "sweep")
     # 3-4: the shards' last-occurrence tables
     tables = comm.all_gather(mine)
+    _mark(marks, "lt_all_gather")
     earlier = torch.cat(tables[: comm.rank]) if comm.rank else mine[:0]
     ops.resolve(qc, src, earlier)
     del tables, earlier
+    _mark(marks, "resolve")
 
     # 5: rows at earlier shards' positions, requested once each, head by head
     vflat = v.view(H * L, -1).view(torch.uint8)           # rows as bytes, for transport
@@ -261,15 +266,25 @@ def sharded_prefill(qc: torch.Tensor, kc: torch.Tensor, v: torch.Tensor, comm=No
     req = uniq[order.indices]
     counts = torch.bincount(order.values, minlength=comm.world).tolist()
     send = list((req % (H * L)).split(counts))
+    _mark(marks, "requests")
     asked = comm.all_to_all(send)                          # rows the other ranks want from me
     reply = [ops.rows(vflat, a) for a in asked]
     got = comm.all_to_all(reply)
     remote_rows = torch.cat(got) if got else vflat[:0]
+    _mark(marks, "row_all_to_all")
 
     # 6
     out = ops.gather(src, base, v, remote_rows, remote_idx)
+    _mark(marks, "gather")
     ops.check()
     return src, out
+
+
+def _mark(marks, name):
+    if marks is not None:
+        e = torch.cuda.Event(enable_timing=True)
+        e.record()
+        marks.append((name, e))
 
 
 def emulated_sharded_prefill(qc: torch.Tensor, kc: torch.Tensor, v: torch.Tensor, n_shards: int,

@@ -134,3 +134,56 @@ def token_stream(batch: int, T: int, vocab: int, seed: int = 0, config_id: int =
             out[r, t + 1] = out[r, j[go] + 1]
         busy = go
     return out.astype(np.int64)
+
+
+def _mix32_torch(x):
+    """MurmurHash3's 32-bit finalizer on an int64 tensor of values < 2^32 (a bijection of the
+    32-bit integers), computed in int64 with explicit wrap-around."""
+    m = (1 << 32) - 1
+    x = x & m
+    x = x ^ (x >> 16)
+    x = (x * 0x85EBCA6B) & m
+    x = x ^ (x >> 13)
+    x = (x * 0xC2B2AE35) & m
+    return x ^ (x >> 16)
+
+
+def long_code_shard(H: int, start: int, length: int, spec: CodeSpec = CONFIG5, seed: int = 0,
+                    device="cuda", chunk: int = 1 << 20, d_v: int = 64):
+    """Positions [start, start + length) of config 5's single long sequence, generated on the
+    device: (qcodes [H, length] int32, kcodes [H, length] int32, values [H, length, d_v] bf16).
+
+    Built in fixed chunks of `chunk` positions, each from its own seeded torch generator, so a
+    shard is the same slice of the same sequence whatever the number of shards. Codes are the
+    image of a 32-bit bijection (MurmurHash3's finalizer) of disjoint input ranges: per head a
+    pool of `spec.pool` codes (inputs h * 2^20 + rank, below 2^30), key-fresh codes (inputs in
+    [2^31, 3 * 2^30)) and query-fresh codes (inputs in [3 * 2^30, 2^32)) -- so query-fresh codes
+    match no key. Ranks
+    are drawn Zipf(spec.alpha) over the pool; a fraction spec.fresh of queries and of keys is
+    fresh. start and length must be multiples of `chunk`."""
+    import torch
+    if start % chunk or length % chunk:
+        raise ValueError("start and length must be whole chunks")
+    if spec.pool > 1 << 20 or H > 1 << 10:
+        raise ValueError("pool <= 2^20 codes per head and H <= 1024")
+    dev = torch.device(device)
+    cdf = torch.from_numpy(zipf_cdf(spec.pool, spec.alpha)).to(dev)
+    qc = torch.empty((H, length), dtype=torch.int32, device=dev)
+    kc = torch.empty((H, length), dtype=torch.int32, device=dev)
+    v = torch.empty((H, length, d_v), dtype=torch.bfloat16, device=dev)
+    g = torch.Generator(device=dev)
+    for h in range(H):
+        for c0 in range(0, length, chunk):
+            c = (start + c0) // chunk
+            g.manual_seed(((seed * 1009 + h) * 1_000_003 + c) & ((1 << 62) - 1))
+            for which, out in ((0, kc), (1, qc)):
+                u = torch.rand(chunk, generator=g, device=dev, dtype=torch.float64)
+                rank = torch.searchsorted(cdf, u, right=True).clamp_(max=spec.pool - 1)
+                x = h * (1 << 20) + rank
+                fresh = torch.rand(chunk, generator=g, device=dev) < spec.fresh
+                fx = torch.randint(0, 1 << 30, (chunk,), generator=g, device=dev) + ((2 + which) << 30)
+                x = torch.where(fresh, fx, x)
+                code = _mix32_torch(x)
+                out[h, c0:c0 + chunk] = (code - ((code >> 31) << 32)).to(torch.int32)
+            v[h, c0:c0 + chunk] = torch.randn((chunk, d_v), generator=g, device=dev).to(torch.bfloat16)
+    return qc, kc, v
