@@ -240,7 +240,7 @@ int lema_lt_extract(const uint64_t* table, int64_t n_heads, int64_t slots, int32
                     uint32_t* out_codes, int32_t* out_pos, int32_t* out_count, int64_t cap,
                     uint32_t* status, void* stream);
 
-/* One CTA per head walks the L / seg_len segments in order: src (in: index within
+/* One 8-CTA cluster per head walks the L / seg_len segments in order: src (in: index within
  * the segment or -1, from lema_segment_match) becomes the global position of the
  * latest earlier key of the shard with the query's code, or -1; then the segment's
  * LT goes into the table (zero-filled before the call; slots for the shard's

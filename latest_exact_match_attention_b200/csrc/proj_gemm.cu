@@ -31,22 +31,28 @@
 namespace lema {
 namespace k1 {
 
-constexpr int kBM = 128, kBN = 256, kBK = 64;  // tile rows, columns (8 heads), K per stage
-constexpr int kStages = 4;
-constexpr int kHeadsPerTile = kBN / 32;
+constexpr int kBM = 128, kBK = 64;  // tile rows, K per stage
 constexpr int kABytes = kBM * kBK * 2;  // 16 KiB
-constexpr int kBBytes = kBN * kBK * 2;  // 32 KiB
-constexpr int kStageBytes = kABytes + kBBytes;
-constexpr int kThreads = 192;             // 6 warps: producer, MMA, 4 x epilogue
-constexpr uint32_t kTmemCols = 2 * kBN;   // two fp32 accumulators of 256 columns
-constexpr size_t kSmemBytes = size_t(kStages) * kStageBytes + 1024 /* alignment */ + 256 /* barriers */;
+constexpr int kThreads = 192;           // 6 warps: producer, MMA, 4 x epilogue
 constexpr uint64_t kWaitNs = 4000000000ull;  // a pipeline wait gives up after 4 s
 
-// Instruction descriptor of tcgen05.mma kind::f16 (32-bit form): fp32 accumulator (bits 4-5 =
-// 1), A and B bf16 (bits 7-9 = 1, bits 10-12 = 1), both K-major (bits 15, 16 = 0), N >> 3 at
-// bits 17-22, M >> 4 at bits 24-28.
-constexpr uint32_t kInstrDesc = (1u << 4) | (1u << 7) | (1u << 10) | (uint32_t(kBN >> 3) << 17) |
-                                (uint32_t(kBM >> 4) << 24);
+// A tile is 128 rows x BN columns (BN / 32 heads). Per width: as many stages as fit in about
+// 192 KiB of shared memory (at most 8), two BN-column fp32 TMEM accumulators, and the
+// instruction descriptor of tcgen05.mma kind::f16 (32-bit form): fp32 accumulator (bits 4-5
+// = 1), A and B bf16 (bits 7-9 = 1, bits 10-12 = 1), both K-major (bits 15, 16 = 0), N >> 3
+// at bits 17-22, M >> 4 at bits 24-28. The widest tile (256) is for large M; narrower ones
+// give small M (decode: a few hundred rows) enough tiles to occupy the SMs.
+template <int BN>
+struct Tile {
+  static constexpr int kBBytes = BN * kBK * 2;
+  static constexpr int kStageBytes = kABytes + kBBytes;
+  static constexpr int kStages = (192 * 1024) / kStageBytes < 8 ? (192 * 1024) / kStageBytes : 8;
+  static constexpr int kHeads = BN / 32;
+  static constexpr uint32_t kTmemCols = 2 * BN;
+  static constexpr size_t kSmemBytes = size_t(kStages) * kStageBytes + 1024 /* alignment */ + 256 /* barriers */;
+  static constexpr uint32_t kInstrDesc = (1u << 4) | (1u << 7) | (1u << 10) | (uint32_t(BN >> 3) << 17) |
+                                         (uint32_t(kBM >> 4) << 24);
+};
 
 struct Params {
   uint32_t* qcodes;
@@ -100,12 +106,13 @@ __device__ __forceinline__ void tc_fence_before() {
 __device__ __forceinline__ void tc_fence_after() {
   asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
 }
-__device__ __forceinline__ void mma_bf16(uint32_t d_tmem, uint64_t a_desc, uint64_t b_desc, uint32_t accumulate) {
+__device__ __forceinline__ void mma_bf16(uint32_t d_tmem, uint64_t a_desc, uint64_t b_desc, uint32_t idesc,
+                                         uint32_t accumulate) {
   asm volatile(
       "{\n\t.reg .pred p;\n\t"
       "setp.ne.b32 p, %4, 0;\n\t"
       "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}"
-      ::"r"(d_tmem), "l"(a_desc), "l"(b_desc), "r"(kInstrDesc), "r"(accumulate)
+      ::"r"(d_tmem), "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(accumulate)
       : "memory");
 }
 // Arrives on `bar` once every tcgen05 operation this thread issued before has completed.
@@ -184,9 +191,12 @@ __device__ __forceinline__ uint32_t pack_signs(const uint32_t (&r)[32]) {
   return code;
 }
 
+template <int BN>
 __global__ void __launch_bounds__(kThreads, 1)
     proj_codes_kernel(const __grid_constant__ CUtensorMap map_x, const __grid_constant__ CUtensorMap map_w,
                       const Params p) {
+  using TL = Tile<BN>;
+  constexpr int kStages = TL::kStages, kStageBytes = TL::kStageBytes;
   extern __shared__ unsigned char smem_raw[];
   // 1024-byte alignment of the stage buffers (the swizzle atom), done on the shared address
   const uint32_t raw = smem_addr(smem_raw);
@@ -222,7 +232,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   }
   if (warp == 0) {  // TMEM: 512 columns, written to s_tmem; the same warp frees it at exit
     asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_addr(s_tmem)),
-                 "r"(kTmemCols)
+                 "r"(TL::kTmemCols)
                  : "memory");
     asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
   }
@@ -239,7 +249,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       bool ok = true;
       for (int64_t tile = blockIdx.x; ok && tile < p.n_tiles; tile += gridDim.x) {
         const int m0 = static_cast<int>(tile / p.n_blocks) * kBM;
-        const int n0 = static_cast<int>(tile % p.n_blocks) * kBN;
+        const int n0 = static_cast<int>(tile % p.n_blocks) * BN;
         for (int kb = 0; kb < p.k_blocks; ++kb) {
           if (!wait_phase(empty_bar(s), ph ^ 1u, s_abort, p.status)) {
             ok = false;
@@ -271,7 +281,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       for (int64_t tile = blockIdx.x; ok && tile < p.n_tiles; tile += gridDim.x) {
         if (!wait_phase(acce_bar(acc), aph ^ 1u, s_abort, p.status)) break;
         tc_fence_after();
-        const uint32_t d_tmem = tmem_base + static_cast<uint32_t>(acc * kBN);
+        const uint32_t d_tmem = tmem_base + static_cast<uint32_t>(acc * BN);
         for (int kb = 0; kb < p.k_blocks; ++kb) {
           if (!wait_phase(full_bar(s), ph, s_abort, p.status)) {
             ok = false;
@@ -282,7 +292,7 @@ __global__ void __launch_bounds__(kThreads, 1)
           const uint64_t a_desc = sw128_desc(a_addr), b_desc = sw128_desc(a_addr + kABytes);
 #pragma unroll
           for (int kk = 0; kk < kBK / 16; ++kk)
-            mma_bf16(d_tmem, a_desc + 2u * kk, b_desc + 2u * kk, (kb | kk) != 0 ? 1u : 0u);
+            mma_bf16(d_tmem, a_desc + 2u * kk, b_desc + 2u * kk, TL::kInstrDesc, (kb | kk) != 0 ? 1u : 0u);
           mma_commit(empty_bar(s));  // the stage is free once these MMAs have read it
           if (++s == kStages) {
             s = 0;
@@ -311,15 +321,15 @@ __global__ void __launch_bounds__(kThreads, 1)
       if (!wait_phase(accf_bar(acc), aph, s_abort, p.status)) break;
       tc_fence_after();
       const int64_t m = (tile / p.n_blocks) * kBM + quarter * 32 + lane;
-      const int h0 = static_cast<int>(tile % p.n_blocks) * kHeadsPerTile;
+      const int h0 = static_cast<int>(tile % p.n_blocks) * TL::kHeads;
       const bool live = m < p.M;
       const int64_t b = live ? m / p.T : 0;
       const int64_t t = live ? m - b * p.T : 0;
-      for (int j = 0; j < kHeadsPerTile; ++j) {
+      for (int j = 0; j < TL::kHeads; ++j) {
         const int h = h0 + j;
         if (h >= n_heads) break;  // warp-uniform
         uint32_t r[32];
-        tmem_load32(tmem_base + lane_base + static_cast<uint32_t>(acc * kBN + j * 32), r);
+        tmem_load32(tmem_base + lane_base + static_cast<uint32_t>(acc * BN + j * 32), r);
         const uint32_t code = pack_signs(r);
         if (live) {
           if (h < p.hq)
@@ -342,7 +352,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   __syncthreads();
   if (warp == 0) {
     tc_fence_after();
-    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem_base), "r"(kTmemCols)
+    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem_base), "r"(TL::kTmemCols)
                  : "memory");
   }
 }
@@ -378,6 +388,15 @@ bool encode_kmajor(EncodeTiledFn enc, CUtensorMap* map, const void* base, int64_
              CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
 
+template <int BN>
+int launch(const CUtensorMap& map_x, const CUtensorMap& map_w, const Params& prm, int64_t grid, cudaStream_t stream) {
+  LEMA_CUDA_TRY(cudaFuncSetAttribute(proj_codes_kernel<BN>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                     static_cast<int>(Tile<BN>::kSmemBytes)));
+  proj_codes_kernel<BN><<<static_cast<unsigned>(grid), kThreads, Tile<BN>::kSmemBytes, stream>>>(map_x, map_w, prm);
+  LEMA_CUDA_TRY(cudaGetLastError());
+  return LEMA_OK;
+}
+
 }  // namespace k1
 
 int proj_codes(const void* x, const void* w_qk, int64_t M, int64_t K, int64_t T, int hq, int hk, int d_qk,
@@ -406,8 +425,12 @@ int proj_codes(const void* x, const void* w_qk, int64_t M, int64_t K, int64_t T,
   if (enc == nullptr) return fail(LEMA_ERR_CUDA, "cuTensorMapEncodeTiled is not available from the driver");
 
   const int64_t n_cols = static_cast<int64_t>(hq + hk) * 32;
+  // the widest tile that still gives every SM a tile; narrower tiles only for small M
+  const int64_t m_blocks = (M + kBM - 1) / kBM;
+  int bn = 256;
+  while (bn > 64 && m_blocks * ((n_cols + bn - 1) / bn) < dev->sms) bn /= 2;
   CUtensorMap map_x, map_w;
-  if (!encode_kmajor(enc, &map_x, x, M, K, kBM) || !encode_kmajor(enc, &map_w, w_qk, n_cols, K, kBN))
+  if (!encode_kmajor(enc, &map_x, x, M, K, kBM) || !encode_kmajor(enc, &map_w, w_qk, n_cols, K, bn))
     return fail(LEMA_ERR_INVALID_ARGUMENT, "tensor map encoding failed (M=%lld K=%lld N=%lld)", (long long)M,
                 (long long)K, (long long)n_cols);
 
@@ -420,15 +443,14 @@ int proj_codes(const void* x, const void* w_qk, int64_t M, int64_t K, int64_t T,
   prm.hq = hq;
   prm.hk = hk;
   prm.k_blocks = static_cast<int>(K / kBK);
-  prm.n_blocks = static_cast<int>((n_cols + kBN - 1) / kBN);
-  prm.n_tiles = ((M + kBM - 1) / kBM) * prm.n_blocks;
-
-  LEMA_CUDA_TRY(cudaFuncSetAttribute(proj_codes_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                     static_cast<int>(kSmemBytes)));
+  prm.n_blocks = static_cast<int>((n_cols + bn - 1) / bn);
+  prm.n_tiles = m_blocks * prm.n_blocks;
   const int64_t grid = std::min<int64_t>(prm.n_tiles, dev->sms);
-  proj_codes_kernel<<<static_cast<unsigned>(grid), kThreads, kSmemBytes, stream>>>(map_x, map_w, prm);
-  LEMA_CUDA_TRY(cudaGetLastError());
-  return LEMA_OK;
+  switch (bn) {
+    case 256: return launch<256>(map_x, map_w, prm, grid, stream);
+    case 128: return launch<128>(map_x, map_w, prm, grid, stream);
+    default: return launch<64>(map_x, map_w, prm, grid, stream);
+  }
 }
 
 }  // namespace lema

@@ -7,7 +7,7 @@
 //   1. segment match (K2): the shard is cut into segments of seg_len positions, each matched
 //      on its own by the shared-memory matcher, which also emits the segment's
 //      last-occurrence table (LT): its distinct key codes and their last positions;
-//   2. sweep (lema_shard_sweep): one CTA per head walks the segments in order against a hash
+//   2. sweep (lema_shard_sweep): one CTA cluster per head walks the segments in order against a hash
 //      of {code -> latest position so far}, starting empty: the queries a segment could not
 //      resolve on its own look the hash up, then the segment's LT is inserted. Indices become
 //      global positions. Afterwards the hash holds the shard's LT (lema_lt_extract), which the
@@ -148,8 +148,12 @@ __global__ void resolve_kernel(const ResolveParams p) {
 }
 
 // ------------------------------------------------------------------ sweep
-constexpr int kSweepThreads = 1024;
-constexpr int kSweepPer = 4;  // positions per thread per pass, looked up together
+// One 8-CTA cluster per head: the segment's lookups and inserts are spread over the cluster's
+// 4096 threads, and cluster barriers (release / acquire at cluster scope) separate the two
+// phases of a segment and the segments from one another. The barrier is the hardware's own
+// (every CTA of a cluster is resident at once and every CTA takes the same number of steps).
+constexpr int kClusterCtas = 8;
+constexpr int kSweepThreads = 512;
 
 struct SweepParams {
   uint64_t* table;
@@ -163,42 +167,94 @@ struct SweepParams {
   uint32_t* status;
 };
 
-__global__ void __launch_bounds__(kSweepThreads) sweep_kernel(const SweepParams p) {
-  const int64_t h = blockIdx.x;
+__device__ __forceinline__ void cluster_sync() {
+  asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::: "memory");
+}
+
+__device__ __forceinline__ uint32_t cluster_rank() {
+  uint32_t r;
+  asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
+  return r;
+}
+
+// Insert for the sweep: a blind claim of the probed slot first (one round trip for a new code);
+// where the slot already holds the code, the larger position is kept by a 64-bit atomicMax
+// (both words carry the same code in their high half), which nothing waits for.
+__device__ __forceinline__ bool lt_put(uint64_t* tab, uint32_t mask, uint32_t code, int32_t pos) {
+  const unsigned long long want = lt_word(code, pos);
+  uint32_t i = fmix32(code) & mask;
+  for (uint32_t probe = 0; probe <= mask; ++probe, i = (i + 1) & mask) {
+    unsigned long long* slot = reinterpret_cast<unsigned long long*>(tab + i);
+    const unsigned long long old = atomicCAS(slot, 0ull, want);
+    if (old == 0) return true;
+    if (static_cast<uint32_t>(old >> 32) == code) {
+      atomicMax(slot, want);
+      return true;
+    }
+  }
+  return false;
+}
+
+constexpr int kSweepPer = 2;  // positions (and LT entries) per thread per segment: seg_len <= 8192
+
+__global__ void __cluster_dims__(kClusterCtas, 1, 1) __launch_bounds__(kSweepThreads)
+    sweep_kernel(const SweepParams p) {
+  const int64_t h = blockIdx.x / kClusterCtas;
+  const int t = static_cast<int>(cluster_rank()) * kSweepThreads + threadIdx.x;
+  constexpr int kStride = kClusterCtas * kSweepThreads;
   uint64_t* tab = p.table + h * p.slots;
   const uint32_t mask = static_cast<uint32_t>(p.slots - 1);
   const uint32_t* qc = p.qc + h * p.L;
   int32_t* src = p.src + h * p.L;
+  // the next segment's inputs, loaded one segment ahead: query index and code, the LT count
+  // and this thread's LT entries (entries past the count are read but never used)
+  int32_t ns[kSweepPer], np_[kSweepPer], ncnt = 0;
+  uint32_t nq[kSweepPer], nc[kSweepPer];
+  auto load = [&](int64_t seg) {
+    const int64_t s0 = seg * p.seg_len;
+    const int64_t st = h * p.n_seg + seg;
+    ncnt = p.lt_count[st];
+#pragma unroll
+    for (int k = 0; k < kSweepPer; ++k) {
+      const int64_t i = t + int64_t(k) * kStride;
+      const bool in = i < p.seg_len;
+      ns[k] = in ? src[s0 + i] : 0;
+      nq[k] = in ? qc[s0 + i] : 0;
+      nc[k] = in ? p.lt_code[st * p.seg_len + i] : 0;
+      np_[k] = in ? p.lt_pos[st * p.seg_len + i] : 0;
+    }
+  };
+  if (p.n_seg > 0) load(0);
   for (int64_t seg = 0; seg < p.n_seg; ++seg) {
     const int64_t s0 = seg * p.seg_len;
     const int64_t g0 = p.base + s0;
-    // queries: in-segment hits become global; misses look up the earlier segments and shards
-    for (int64_t c = 0; c < p.seg_len; c += int64_t(kSweepThreads) * kSweepPer) {
-      int32_t s[kSweepPer];
-      uint32_t q[kSweepPer];
+    int32_t cs[kSweepPer], cp[kSweepPer];
+    uint32_t cq[kSweepPer], cc[kSweepPer];
+    const int32_t cnt = ncnt;
 #pragma unroll
-      for (int k = 0; k < kSweepPer; ++k) {
-        const int64_t i = c + k * kSweepThreads + threadIdx.x;
-        s[k] = i < p.seg_len ? src[s0 + i] : 0;
-        q[k] = (i < p.seg_len && s[k] < 0) ? qc[s0 + i] : 0;
-      }
-#pragma unroll
-      for (int k = 0; k < kSweepPer; ++k) {
-        const int64_t i = c + k * kSweepThreads + threadIdx.x;
-        if (i >= p.seg_len) continue;
-        src[s0 + i] = s[k] >= 0 ? static_cast<int32_t>(g0 + s[k]) : lt_find(tab, mask, q[k]);
-      }
+    for (int k = 0; k < kSweepPer; ++k) {
+      cs[k] = ns[k];
+      cq[k] = nq[k];
+      cc[k] = nc[k];
+      cp[k] = np_[k];
     }
-    __syncthreads();
+    if (seg + 1 < p.n_seg) load(seg + 1);
+    // queries: in-segment hits become global; misses look up the earlier segments
+#pragma unroll
+    for (int k = 0; k < kSweepPer; ++k) {
+      const int64_t i = t + int64_t(k) * kStride;
+      if (i < p.seg_len)
+        src[s0 + i] = cs[k] >= 0 ? static_cast<int32_t>(g0 + cs[k]) : lt_find(tab, mask, cq[k]);
+    }
+    cluster_sync();
     // the segment's keys: each distinct code once, at its last position in the segment
-    const int64_t st = h * p.n_seg + seg;
-    const int32_t cnt = p.lt_count[st];
-    const uint32_t* lc = p.lt_code + st * p.seg_len;
-    const int32_t* lp = p.lt_pos + st * p.seg_len;
-    for (int e = threadIdx.x; e < cnt; e += kSweepThreads)
-      if (!lt_insert_max(tab, mask, lc[e], static_cast<int32_t>(g0 + lp[e])))
+#pragma unroll
+    for (int k = 0; k < kSweepPer; ++k) {
+      const int e = t + k * kStride;
+      if (e < cnt && !lt_put(tab, mask, cc[k], static_cast<int32_t>(g0 + cp[k])))
         raise_status(p.status, LEMA_STATUS_TABLE_FULL);
-    __syncthreads();
+    }
+    cluster_sync();
   }
 }
 
@@ -366,6 +422,9 @@ extern "C" int lema_shard_sweep(uint64_t* table, int64_t n_heads, int64_t slots,
     return fail(LEMA_ERR_INVALID_ARGUMENT, "bad shape (heads %lld, slots %lld, L %lld, segment %lld)",
                 (long long)n_heads, (long long)slots, (long long)L, (long long)seg_len);
   if (L % seg_len != 0) return fail(LEMA_ERR_INVALID_ARGUMENT, "L = %lld is not whole segments of %lld", (long long)L, (long long)seg_len);
+  if (seg_len > int64_t(k5::kClusterCtas) * k5::kSweepThreads * k5::kSweepPer)
+    return fail(LEMA_ERR_INVALID_ARGUMENT, "seg_len = %lld: at most %d positions per segment", (long long)seg_len,
+                k5::kClusterCtas * k5::kSweepThreads * k5::kSweepPer);
   if (base + L >= (int64_t(1) << 31) - 1) return fail(LEMA_ERR_INVALID_ARGUMENT, "positions must stay below 2^31 - 1");
   if (L == 0) return LEMA_OK;
   if (table == nullptr || qcodes == nullptr || src == nullptr || lt_code == nullptr || lt_pos == nullptr || lt_count == nullptr)
@@ -373,7 +432,8 @@ extern "C" int lema_shard_sweep(uint64_t* table, int64_t n_heads, int64_t slots,
   const DeviceInfo* dev = k5::sm100();
   if (dev == nullptr) return LEMA_ERR_UNSUPPORTED;
   k5::SweepParams p{table, slots, qcodes, src, L, seg_len, L / seg_len, base, lt_code, lt_pos, lt_count, status};
-  k5::sweep_kernel<<<static_cast<unsigned>(n_heads), k5::kSweepThreads, 0, static_cast<cudaStream_t>(stream)>>>(p);
+  k5::sweep_kernel<<<static_cast<unsigned>(n_heads * k5::kClusterCtas), k5::kSweepThreads, 0,
+                     static_cast<cudaStream_t>(stream)>>>(p);
   LEMA_CUDA_TRY(cudaGetLastError());
   return LEMA_OK;
 }

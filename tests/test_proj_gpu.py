@@ -56,6 +56,8 @@ CASES = [
     (4, 1024, 1024, 8, 8),
     (2, 1000, 512, 4, 2),
     (2, 2048, 1024, 64, 64),
+    (5, 2048, 256, 4, 4),      # picks the 128-column tile (64 and 256 are picked above)
+    (256, 1, 1536, 64, 64),    # a decode step: 256 rows, the 64-column tile
 ]
 
 
