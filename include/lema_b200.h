@@ -234,11 +234,12 @@ int lema_lt_insert(uint64_t* table, int64_t n_heads, int64_t slots, const int32_
 int lema_lt_resolve(const uint64_t* table, int64_t n_heads, int64_t slots,
                     const uint32_t* qcodes, int32_t* src, int64_t L, void* stream);
 
-/* Entries with position >= lo, per head h into out_codes/out_pos[h * cap + k],
- * k < out_count[h] (in no particular order); more than cap sets TABLE_FULL. */
+/* Entries with position >= lo as one flat list: out_heads/out_codes/out_pos[k],
+ * k < *out_count (a single int32), in no particular order; more than cap entries sets
+ * LEMA_STATUS_TABLE_FULL (the first cap are written). */
 int lema_lt_extract(const uint64_t* table, int64_t n_heads, int64_t slots, int32_t lo,
-                    uint32_t* out_codes, int32_t* out_pos, int32_t* out_count, int64_t cap,
-                    uint32_t* status, void* stream);
+                    int32_t* out_heads, uint32_t* out_codes, int32_t* out_pos,
+                    int32_t* out_count, int64_t cap, uint32_t* status, void* stream);
 
 /* One 8-CTA cluster per head walks the L / seg_len segments in order: src (in: index within
  * the segment or -1, from lema_segment_match) becomes the global position of the

@@ -98,11 +98,12 @@ __global__ void insert_entries_kernel(const InsertParams p) {
   }
 }
 
-// Entries with position >= lo, per head, into out_*[h * cap + k], k < out_count[h].
+// Entries with position >= lo as one flat list (head, code, position), in no particular order.
 struct ExtractParams {
   const uint64_t* table;
   int64_t slots, n_heads;
   int32_t lo;
+  int32_t* out_heads;
   uint32_t* out_codes;
   int32_t* out_pos;
   int32_t* out_count;
@@ -117,14 +118,14 @@ __global__ void extract_kernel(const ExtractParams p) {
     if (w == 0) continue;
     const int32_t pos = static_cast<int32_t>(static_cast<uint32_t>(w)) - 1;
     if (pos < p.lo) continue;
-    const int64_t h = i / p.slots;
-    const int32_t k = atomicAdd(p.out_count + h, 1);
+    const int32_t k = atomicAdd(p.out_count, 1);
     if (k >= p.cap) {
       raise_status(p.status, LEMA_STATUS_TABLE_FULL);
       continue;
     }
-    p.out_codes[h * p.cap + k] = static_cast<uint32_t>(w >> 32);
-    p.out_pos[h * p.cap + k] = pos;
+    p.out_heads[k] = static_cast<int32_t>(i / p.slots);
+    p.out_codes[k] = static_cast<uint32_t>(w >> 32);
+    p.out_pos[k] = pos;
   }
 }
 
@@ -167,8 +168,14 @@ struct SweepParams {
   uint32_t* status;
 };
 
+// After the inserts: release, so every insert is visible to the next segment's lookups.
 __device__ __forceinline__ void cluster_sync() {
   asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::: "memory");
+}
+// After the lookups: they have all returned (their values are in registers), so the barrier
+// need not wait for this thread's stores; it only keeps the inserts behind every lookup.
+__device__ __forceinline__ void cluster_sync_relaxed() {
+  asm volatile("barrier.cluster.arrive.relaxed.aligned;\n\tbarrier.cluster.wait.aligned;" ::: "memory");
 }
 
 __device__ __forceinline__ uint32_t cluster_rank() {
@@ -239,14 +246,15 @@ __global__ void __cluster_dims__(kClusterCtas, 1, 1) __launch_bounds__(kSweepThr
       cp[k] = np_[k];
     }
     if (seg + 1 < p.n_seg) load(seg + 1);
-    // queries: in-segment hits become global; misses look up the earlier segments
+    // queries: in-segment hits become global; misses look up the earlier segments. The
+    // results are stored after this segment's inserts, so no barrier waits for the stores.
+    int32_t res[kSweepPer];
 #pragma unroll
     for (int k = 0; k < kSweepPer; ++k) {
       const int64_t i = t + int64_t(k) * kStride;
-      if (i < p.seg_len)
-        src[s0 + i] = cs[k] >= 0 ? static_cast<int32_t>(g0 + cs[k]) : lt_find(tab, mask, cq[k]);
+      res[k] = (i < p.seg_len && cs[k] < 0) ? lt_find(tab, mask, cq[k]) : static_cast<int32_t>(g0 + cs[k]);
     }
-    cluster_sync();
+    cluster_sync_relaxed();
     // the segment's keys: each distinct code once, at its last position in the segment
 #pragma unroll
     for (int k = 0; k < kSweepPer; ++k) {
@@ -255,6 +263,11 @@ __global__ void __cluster_dims__(kClusterCtas, 1, 1) __launch_bounds__(kSweepThr
         raise_status(p.status, LEMA_STATUS_TABLE_FULL);
     }
     cluster_sync();
+#pragma unroll
+    for (int k = 0; k < kSweepPer; ++k) {
+      const int64_t i = t + int64_t(k) * kStride;
+      if (i < p.seg_len) src[s0 + i] = res[k];
+    }
   }
 }
 
@@ -397,17 +410,17 @@ extern "C" int lema_lt_resolve(const uint64_t* table, int64_t n_heads, int64_t s
 }
 
 extern "C" int lema_lt_extract(const uint64_t* table, int64_t n_heads, int64_t slots, int32_t lo,
-                               uint32_t* out_codes, int32_t* out_pos, int32_t* out_count, int64_t cap,
-                               uint32_t* status, void* stream) {
+                               int32_t* out_heads, uint32_t* out_codes, int32_t* out_pos, int32_t* out_count,
+                               int64_t cap, uint32_t* status, void* stream) {
   clear_error();
-  if (n_heads <= 0 || !k5::pow2(slots) || cap < 0)
+  if (n_heads <= 0 || !k5::pow2(slots) || cap < 0 || cap >= (int64_t(1) << 31))
     return fail(LEMA_ERR_INVALID_ARGUMENT, "bad table shape or capacity");
-  if (table == nullptr || out_codes == nullptr || out_pos == nullptr || out_count == nullptr)
+  if (table == nullptr || out_heads == nullptr || out_codes == nullptr || out_pos == nullptr || out_count == nullptr)
     return fail(LEMA_ERR_INVALID_ARGUMENT, "null pointer argument");
   const DeviceInfo* dev = k5::sm100();
   if (dev == nullptr) return LEMA_ERR_UNSUPPORTED;
-  k5::ExtractParams p{table, slots, n_heads, lo, out_codes, out_pos, out_count, cap, status};
-  LEMA_CUDA_TRY(cudaMemsetAsync(out_count, 0, sizeof(int32_t) * n_heads, static_cast<cudaStream_t>(stream)));
+  k5::ExtractParams p{table, slots, n_heads, lo, out_heads, out_codes, out_pos, out_count, cap, status};
+  LEMA_CUDA_TRY(cudaMemsetAsync(out_count, 0, sizeof(int32_t), static_cast<cudaStream_t>(stream)));
   k5::extract_kernel<<<k5::grid_for(n_heads * slots, 256, *dev), 256, 0, static_cast<cudaStream_t>(stream)>>>(p);
   LEMA_CUDA_TRY(cudaGetLastError());
   return LEMA_OK;

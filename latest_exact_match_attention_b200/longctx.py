@@ -152,22 +152,20 @@ class CudaOps:
         H, L = qc.shape
         n_seg = L // seg_len
         # distinct codes per head <= the sum of its segments' distinct codes, and <= L
-        bound = int(torch.minimum(ltn.view(H, n_seg).sum(1, dtype=torch.int64),
-                                  torch.tensor(L, device=self.device)).max())
-        slots = int(_lib.lib().lema_lt_table_slots(bound))
+        per_head = torch.minimum(ltn.view(H, n_seg).sum(1, dtype=torch.int64),
+                                 torch.tensor(L, device=self.device))
+        bounds = per_head.tolist()
+        slots = int(_lib.lib().lema_lt_table_slots(max(bounds)))
         table = torch.zeros((H, slots), dtype=torch.int64, device=self.device)
         call("lema_shard_sweep", ptr(table), H, slots, ptr(qc), ptr(src), L, seg_len, ptr(ltc),
              ptr(ltp), ptr(ltn), base, ptr(self.status), self._stream())
-        cap = int((table != 0).sum(1).max())              # the shard's distinct codes per head
-        codes = torch.empty((H, cap), dtype=torch.int32, device=self.device)
-        pos = torch.empty((H, cap), dtype=torch.int32, device=self.device)
-        cnt = torch.empty(H, dtype=torch.int32, device=self.device)
-        call("lema_lt_extract", ptr(table), H, slots, base, ptr(codes), ptr(pos), ptr(cnt), cap,
-             ptr(self.status), self._stream())
+        cap = sum(bounds)
+        ent = torch.empty((3, cap), dtype=torch.int32, device=self.device)
+        cnt = torch.empty(1, dtype=torch.int32, device=self.device)
+        call("lema_lt_extract", ptr(table), H, slots, base, ptr(ent[0]), ptr(ent[1]), ptr(ent[2]),
+             ptr(cnt), cap, ptr(self.status), self._stream())
         del table
-        keep = torch.arange(cap, device=self.device)[None, :] < cnt[:, None]
-        heads = torch.arange(H, dtype=torch.int32, device=self.device)[:, None].expand(H, cap)
-        return torch.stack([heads[keep], codes[keep], pos[keep]], 1)
+        return ent[:, : int(cnt.item())].t()
 
     def resolve(self, qc, src, earlier):
         """Queries with src == -1 look up the earlier shards' entries [m, 3]."""
