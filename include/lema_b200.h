@@ -163,7 +163,10 @@ int lema_prefill_match_noalloc(const void* qcodes, const void* kcodes, int code_
  * no free slot sets LEMA_STATUS_TABLE_FULL.
  *
  * Replaces: the host table of code/lema/cache.py:129-201 (`HashStore`), whose
- * slots are [code | state | value] at code/lema/csrc/store.cpp:3-16.
+ * slots are [code | state | value] at code/lema/csrc/store.cpp:3-16. The size per
+ * slot is the reference's (16 + the row); inside, the bytes are a dense array of
+ * 16-byte slot headers (code, state) followed by the rows, so probing at high
+ * load walks few cache lines.
  */
 int64_t lema_store_slot_bytes(int64_t vbytes);
 
@@ -190,6 +193,23 @@ int lema_store_exchange(void* table, int64_t cap, int64_t vbytes,
                         const void* values, void* out, int64_t n, int64_t T,
                         int64_t g0, int64_t* counts, uint32_t* status,
                         void* workspace, size_t workspace_bytes, void* stream);
+
+/*
+ * lema_store_exchange on a SEGMENTED table: the home slot of a group g lies in segment
+ * g / seg_groups, slots [seg * seg_slots, (seg + 1) * seg_slots); probing continues past
+ * the segment and wraps at cap as before, so capacity and "full" are still those of one
+ * shared table. With one segment per layer (seg_groups = the partitions of a layer), a
+ * layer's exchange touches 1/depth of a large table instead of all of it. A table must be
+ * used with one segmentation throughout. (0, 0) = lema_store_exchange.
+ * Replaces: code/lema/csrc/store.cpp:127-162 like lema_store_exchange; the segmentation
+ * is a placement choice of this build, invisible in results.
+ */
+int lema_store_exchange_seg(void* table, int64_t cap, int64_t vbytes,
+                            const void* qcodes, const void* kcodes, int code_bytes,
+                            const void* values, void* out, int64_t n, int64_t T,
+                            int64_t g0, int64_t* counts, uint32_t* status,
+                            void* workspace, size_t workspace_bytes, int64_t seg_groups,
+                            int64_t seg_slots, void* stream);
 
 /* ----------------------------------- (d) sequence-sharded prefill (config 5) */
 /*

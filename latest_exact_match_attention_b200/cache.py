@@ -71,7 +71,7 @@ class HashStore:
     """
 
     def __init__(self, d_v: int, groups: int, dtype=torch.bfloat16, capacity: int = 256,
-                 device=None):
+                 device=None, segments: int = 1):
         self.dtype = _as_torch_dtype(dtype)
         self.d_v, self.groups = d_v, groups
         self.vbytes = d_v * torch.empty((), dtype=self.dtype).element_size()
@@ -88,6 +88,11 @@ class HashStore:
         self.counts = torch.zeros(groups, dtype=torch.int64, device=self.device)
         self.status = torch.zeros(1, dtype=torch.int32, device=self.device)
         self._ws = None
+        # segments > 1: each run of groups/segments groups (a layer, for LemaCache) has its
+        # home slots in its own 1/segments of the table; results are the same either way
+        segments = max(1, min(int(segments), groups, self.cap))
+        self.seg_groups = -(-groups // segments) if segments > 1 else 0
+        self.seg_slots = self.cap // segments if segments > 1 else 0
 
     def __len__(self):
         return int(self.counts.sum())
@@ -139,10 +144,10 @@ class HashStore:
             raise ValueError("out must be contiguous")
         ws = self._workspace(n, T, cb)
         qcodes, kcodes, values = qcodes.contiguous(), kcodes.contiguous(), values.contiguous()
-        call("lema_store_exchange", ptr(self.table), self.cap, self.vbytes, ptr(qcodes),
+        call("lema_store_exchange_seg", ptr(self.table), self.cap, self.vbytes, ptr(qcodes),
              ptr(kcodes), cb, ptr(values), ptr(out), n, T, g0,
              ptr(self.counts) + 8 * g0, ptr(self.status), ptr(ws), 0 if ws is None else ws.numel(),
-             stream_handle(self.device))
+             self.seg_groups, self.seg_slots, stream_handle(self.device))
         if check:
             self.check()
 
@@ -252,7 +257,7 @@ class LemaCache:
         slots = int(capacity) if capacity else math.ceil(cfg.depth * P * max_cache_len / max_load)
         self.cfg, self.batch = cfg, batch
         self.store = HashStore(cfg.d_v, groups=cfg.depth * P, dtype=dtype, capacity=slots,
-                               device=device)
+                               device=device, segments=cfg.depth)
         self.t = 0
         self.buffers = Buffers(dtype, codes_hook)
         self._views = [LayerStore(self.store, self.buffers, i * P, P) for i in range(cfg.depth)]

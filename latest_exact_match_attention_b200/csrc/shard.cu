@@ -274,45 +274,80 @@ __global__ void __cluster_dims__(kClusterCtas, 1, 1) __launch_bounds__(kSweepThr
 // ------------------------------------------------------------------ gather
 struct GatherParams {
   const int32_t* src;  // [H][L] global positions or -1
-  int64_t base, L, rows;
+  int64_t base, L, H;
   const unsigned char* v;       // [H][L] rows of this shard
   const unsigned char* remote;  // rows fetched from earlier shards
   const int32_t* remote_idx;    // [H][L] row of `remote` for a position before base
   unsigned char* out;
-  int64_t vbytes;
+  uint32_t wpr;        // vector words per row
+  uint32_t words;      // words per head = L * wpr (< 2^32)
+  int div_shift;       // log2(wpr) when a power of two, else -1
+  uint32_t div_magic;  // floor(2^32 / wpr) + 1 when exact for every word index, else 0
   uint32_t* status;
 };
 
-// One thread per output row; a row is vbytes / sizeof(Vec) words, all loads issued first.
+constexpr int kGThreads = 256, kGUnroll = 8;
+
+// Word-parallel, like the prefill gather: each CTA owns a run of output words of one head
+// (blockIdx.y), kGUnroll loads in flight per thread, consecutive lanes on consecutive words
+// of a row, streaming stores.
 template <typename Vec>
-__global__ void __launch_bounds__(256) shard_gather_kernel(const GatherParams g) {
-  const int64_t W = g.vbytes / static_cast<int64_t>(sizeof(Vec));
-  for (int64_t r = blockIdx.x * int64_t(blockDim.x) + threadIdx.x; r < g.rows; r += int64_t(gridDim.x) * blockDim.x) {
-    const int32_t s = g.src[r];
-    Vec* dst = reinterpret_cast<Vec*>(g.out + r * g.vbytes);
-    const Vec* from = nullptr;
-    if (s >= g.base) {
-      const int64_t h = r / g.L;
-      from = reinterpret_cast<const Vec*>(g.v + (h * g.L + (s - g.base)) * g.vbytes);
-    } else if (s >= 0) {
-      const int32_t ri = g.remote_idx[r];
-      if (ri < 0) {
-        raise_status(g.status, LEMA_STATUS_PROBE_LIMIT);  // a remote row nobody fetched
-      } else {
-        from = reinterpret_cast<const Vec*>(g.remote + static_cast<int64_t>(ri) * g.vbytes);
+__global__ void __launch_bounds__(kGThreads) shard_gather_kernel(const GatherParams g) {
+  const uint32_t w0 = blockIdx.x * (kGThreads * kGUnroll) + threadIdx.x;
+  for (int64_t h = blockIdx.y; h < g.H; h += gridDim.y) {
+    const int32_t* src = g.src + h * g.L;
+    const int32_t* ridx = g.remote_idx ? g.remote_idx + h * g.L : nullptr;
+    const Vec* v = reinterpret_cast<const Vec*>(g.v) + h * static_cast<int64_t>(g.words);
+    const Vec* rem = reinterpret_cast<const Vec*>(g.remote);
+    Vec* o = reinterpret_cast<Vec*>(g.out) + h * static_cast<int64_t>(g.words);
+    Vec val[kGUnroll];
+#pragma unroll
+    for (int u = 0; u < kGUnroll; ++u) {
+      const uint32_t w = w0 + u * kGThreads;
+      val[u] = zero_vec<Vec>();
+      if (w < g.words) {
+        const uint32_t r = g.div_shift >= 0 ? (w >> g.div_shift)
+                                            : (g.div_magic ? __umulhi(w, g.div_magic) : w / g.wpr);
+        const uint32_t col = w - r * g.wpr;
+        const int32_t s = __ldg(src + r);
+        if (s >= g.base) {
+          val[u] = __ldg(v + (static_cast<int64_t>(s) - g.base) * g.wpr + col);
+        } else if (s >= 0) {
+          const int32_t ri = ridx ? __ldg(ridx + r) : -1;
+          if (ri >= 0)
+            val[u] = __ldg(rem + static_cast<int64_t>(ri) * g.wpr + col);
+          else if (col == 0)
+            raise_status(g.status, LEMA_STATUS_PROBE_LIMIT);  // a remote row nobody fetched
+        }
       }
     }
-    constexpr int kBatch = 8;
-    for (int64_t w0 = 0; w0 < W; w0 += kBatch) {
-      Vec buf[kBatch];
 #pragma unroll
-      for (int k = 0; k < kBatch; ++k)
-        if (w0 + k < W) buf[k] = from ? from[w0 + k] : zero_vec<Vec>();
-#pragma unroll
-      for (int k = 0; k < kBatch; ++k)
-        if (w0 + k < W) store_stream(dst + w0 + k, buf[k]);
+    for (int u = 0; u < kGUnroll; ++u) {
+      const uint32_t w = w0 + u * kGThreads;
+      if (w < g.words) store_stream(o + w, val[u]);
     }
   }
+}
+
+template <typename Vec>
+int launch_shard_gather(GatherParams g, int64_t vbytes, cudaStream_t stream) {
+  const uint64_t wpr = static_cast<uint64_t>(vbytes) / sizeof(Vec);
+  const uint64_t words = static_cast<uint64_t>(g.L) * wpr;
+  if (words >= (uint64_t(1) << 32)) return fail(LEMA_ERR_INVALID_ARGUMENT, "L * row words = %llu exceeds 2^32", (unsigned long long)words);
+  g.wpr = static_cast<uint32_t>(wpr);
+  g.words = static_cast<uint32_t>(words);
+  g.div_shift = -1;
+  g.div_magic = 0;
+  if ((wpr & (wpr - 1)) == 0) {
+    g.div_shift = log2_exact(wpr);
+  } else if (words * wpr < (uint64_t(1) << 32)) {  // multiply-high is exact for w * wpr < 2^32
+    g.div_magic = static_cast<uint32_t>(0xFFFFFFFFull / wpr + 1);
+  }
+  const uint64_t per_cta = kGThreads * kGUnroll;
+  const dim3 grid(static_cast<unsigned>((words + per_cta - 1) / per_cta), static_cast<unsigned>(std::min<int64_t>(g.H, 65535)));
+  shard_gather_kernel<Vec><<<grid, kGThreads, 0, stream>>>(g);
+  LEMA_CUDA_TRY(cudaGetLastError());
+  return LEMA_OK;
 }
 
 int grid_for(int64_t work, int threads, const DeviceInfo& dev, int per_sm = 8) {
@@ -462,21 +497,21 @@ extern "C" int lema_shard_gather(const int32_t* src, int64_t base, const void* v
     return fail(LEMA_ERR_INVALID_ARGUMENT, "null pointer argument");
   const DeviceInfo* dev = k5::sm100();
   if (dev == nullptr) return LEMA_ERR_UNSUPPORTED;
-  k5::GatherParams g{src, base, L, n_heads * L, static_cast<const unsigned char*>(values),
-                     static_cast<const unsigned char*>(remote_rows), remote_idx, static_cast<unsigned char*>(out),
-                     vbytes, status};
+  k5::GatherParams g{};
+  g.src = src;
+  g.base = base;
+  g.L = L;
+  g.H = n_heads;
+  g.v = static_cast<const unsigned char*>(values);
+  g.remote = static_cast<const unsigned char*>(remote_rows);
+  g.remote_idx = remote_idx;
+  g.out = static_cast<unsigned char*>(out);
+  g.status = status;
   const cudaStream_t s = static_cast<cudaStream_t>(stream);
-  const int grid = k5::grid_for(g.rows, 256, *dev);
   const uintptr_t a = reinterpret_cast<uintptr_t>(values) | reinterpret_cast<uintptr_t>(out) |
                       reinterpret_cast<uintptr_t>(remote_rows) | static_cast<uintptr_t>(vbytes);
-  if (a % 16 == 0)
-    k5::shard_gather_kernel<uint4><<<grid, 256, 0, s>>>(g);
-  else if (a % 8 == 0)
-    k5::shard_gather_kernel<uint2><<<grid, 256, 0, s>>>(g);
-  else if (a % 4 == 0)
-    k5::shard_gather_kernel<unsigned int><<<grid, 256, 0, s>>>(g);
-  else
-    k5::shard_gather_kernel<unsigned short><<<grid, 256, 0, s>>>(g);
-  LEMA_CUDA_TRY(cudaGetLastError());
-  return LEMA_OK;
+  if (a % 16 == 0) return k5::launch_shard_gather<uint4>(g, vbytes, s);
+  if (a % 8 == 0) return k5::launch_shard_gather<uint2>(g, vbytes, s);
+  if (a % 4 == 0) return k5::launch_shard_gather<unsigned int>(g, vbytes, s);
+  return k5::launch_shard_gather<unsigned short>(g, vbytes, s);
 }

@@ -6,11 +6,13 @@
 // wins); counts[p] grows by the slots partition p newly claims; a table with no free slot
 // left reports "full" instead of growing.
 //
-// Slot layout (stride = 16 + vbytes rounded up to 16, so value rows are 16-byte aligned):
-//   [0, 8)    code (zero-extended to 64 bits)
-//   [8, 16)   state: 0 = EMPTY, 1 = LOCKED (being claimed), group + 2 = published
-//   [16, ..)  value row, opaque bytes
-// A zero-filled allocation is an empty table. Claims are a compare-and-swap EMPTY -> LOCKED,
+// Table layout: cap slots in cap * (16 + row) bytes, row = vbytes rounded up to 16 -- the
+// reference's size for the same capacity -- arranged as two arrays:
+//   headers  [0, 16 * cap):       per slot code (8 bytes, zero-extended) and state (8 bytes):
+//                                 0 = EMPTY, 1 = LOCKED (being claimed), group + 2 = published
+//   rows     [16 * cap, ...):     per slot one value row of `row` bytes, opaque
+// Headers are dense (eight per 128-byte line), so a probe chain at high load costs a few lines
+// instead of one 64-byte round trip per slot. A zero-filled allocation is an empty table. Claims are a compare-and-swap EMPTY -> LOCKED,
 // then the code and value are written and the state is published with a release store;
 // probers read the state with acquire loads, so a published slot's code and value are
 // complete when seen. The home slot is a 64-bit mix of (group, code) mapped onto [0, cap)
@@ -43,9 +45,10 @@ constexpr uint64_t kEmpty = 0, kLocked = 1;
 constexpr int kThreads = 256;
 
 struct Args {
-  unsigned char* table;
+  unsigned char* table;  // the header array
+  unsigned char* rows;   // the row array, table + 16 * cap
   uint64_t cap;
-  int64_t stride;
+  int64_t stride;        // bytes per row in the row array
   int64_t vbytes;
   const void* qc;
   const void* kc;
@@ -59,11 +62,18 @@ struct Args {
   const void* lt_code;
   const int32_t* lt_pos;
   const int32_t* lt_count;
+  uint64_t seg_groups;  // > 0: groups [k * seg_groups, (k + 1) * seg_groups) have their home
+  uint64_t seg_slots;   //   slots in [k * seg_slots, (k + 1) * seg_slots); probing still wraps cap
 };
 
-__device__ __forceinline__ uint64_t home(uint64_t code, uint64_t group, uint64_t cap) {
+// Home slot of (group, code): a 64-bit mix mapped by multiply-high onto the whole table, or,
+// when the table is segmented, onto the group's segment. Probing continues across segment
+// ends and wraps at cap either way, so capacity and fullness are those of one shared table;
+// segmenting only keeps one layer's exchange (its groups) inside a slice of the table.
+__device__ __forceinline__ uint64_t home(uint64_t code, uint64_t group, const Args& a) {
   const uint64_t h = fmix64(code ^ fmix64(group ^ 0x5851F42D4C957F2Dull));
-  return __umul64hi(h, cap);
+  if (a.seg_groups == 0) return __umul64hi(h, a.cap);
+  return (group / a.seg_groups) * a.seg_slots + __umul64hi(h, a.seg_slots);
 }
 
 __device__ __forceinline__ uint64_t ld_acquire(const uint64_t* p) {
@@ -87,18 +97,54 @@ __device__ __forceinline__ void zero_row(Vec* dst, int wpr) {
   for (int k = 0; k < wpr; ++k) dst[k] = z;
 }
 
+constexpr int kSpecWords = 8;  // rows of up to 8 vector words are read with the home header
+
+__device__ __forceinline__ uint64_t* header(const Args& a, uint64_t s) {
+  return reinterpret_cast<uint64_t*>(a.table) + 2 * s;
+}
+template <typename Vec>
+__device__ __forceinline__ Vec* row_of(const Args& a, uint64_t s) {
+  return reinterpret_cast<Vec*>(a.rows + s * a.stride);
+}
+
 // Copies the value stored under (group, code) into dst, or zeros. Returns whether it hit.
+// The home slot's header and (for rows of up to kSpecWords words) its row are read together,
+// with plain loads; further probes walk the dense header array. Plain loads are safe because a
+// lookup only runs where nothing else can be writing a slot of its group: in a decode step the
+// item's own insert comes after its lookup and every other item has another group; a prefill
+// chunk's lookups are a kernel of their own. A slot seen empty ends the probe: slots are never
+// freed, so every slot between an entry's home and the entry was occupied before this call.
 template <typename Vec>
 __device__ bool lookup(const Args& a, uint64_t code, uint64_t group, Vec* dst) {
   const int wpr = static_cast<int>(a.vbytes / static_cast<int64_t>(sizeof(Vec)));
   const uint64_t tag = group + 2;
-  uint64_t s = home(code, group, a.cap);
+  uint64_t s = home(code, group, a);
+  if (wpr <= kSpecWords) {
+    Vec row[kSpecWords];
+    const uint64_t* h = header(a, s);
+    const uint64_t cd = h[0], st = h[1];
+    const Vec* src = row_of<const Vec>(a, s);
+#pragma unroll
+    for (int k = 0; k < kSpecWords; ++k)
+      if (k < wpr) row[k] = src[k];
+    if (st == kEmpty) {
+      zero_row(dst, wpr);
+      return false;
+    }
+    if (st == tag && cd == code) {
+#pragma unroll
+      for (int k = 0; k < kSpecWords; ++k)
+        if (k < wpr) dst[k] = row[k];
+      return true;
+    }
+    s = (s + 1 == a.cap) ? 0 : s + 1;
+  }
   for (uint64_t t = 0; t < a.cap; ++t) {
-    uint64_t* hdr = reinterpret_cast<uint64_t*>(a.table + s * a.stride);
-    const uint64_t st = ld_acquire(hdr + 1);
+    const uint64_t* h = header(a, s);
+    const uint64_t st = h[1];
     if (st == kEmpty) break;
-    if (st == tag && hdr[0] == code) {
-      copy_row(dst, reinterpret_cast<const Vec*>(hdr + 2), wpr);
+    if (st == tag && h[0] == code) {
+      copy_row(dst, row_of<const Vec>(a, s), wpr);
       return true;
     }
     s = (s + 1 == a.cap) ? 0 : s + 1;
@@ -108,26 +154,27 @@ __device__ bool lookup(const Args& a, uint64_t code, uint64_t group, Vec* dst) {
 }
 
 // (group, code) -> row, latest write wins. Returns 1 for a newly claimed slot, 0 for an
-// overwrite, -1 when every slot was probed (the table is full).
+// overwrite, -1 when every slot was probed (the table is full). `first` is the state of the
+// home slot if the caller already read it (a stale read only costs a failed claim), else ~0.
 template <typename Vec>
-__device__ int insert(const Args& a, uint64_t code, uint64_t group, const Vec* row) {
+__device__ int insert(const Args& a, uint64_t code, uint64_t group, const Vec* row, uint64_t first = ~0ull) {
   const int wpr = static_cast<int>(a.vbytes / static_cast<int64_t>(sizeof(Vec)));
   const uint64_t tag = group + 2;
-  uint64_t s = home(code, group, a.cap);
+  uint64_t s = home(code, group, a);
   for (uint64_t t = 0; t < a.cap; ++t) {
-    uint64_t* hdr = reinterpret_cast<uint64_t*>(a.table + s * a.stride);
-    uint64_t st = ld_acquire(hdr + 1);
+    uint64_t* hdr = header(a, s);
+    uint64_t st = (t == 0 && first != ~0ull) ? first : ld_acquire(hdr + 1);
     if (st == kEmpty) {
       st = atomicCAS(reinterpret_cast<unsigned long long*>(hdr + 1), kEmpty, kLocked);
       if (st == kEmpty) {
         hdr[0] = code;
-        copy_row(reinterpret_cast<Vec*>(hdr + 2), row, wpr);
+        copy_row(row_of<Vec>(a, s), row, wpr);
         st_release(hdr + 1, tag);
         return 1;
       }
     }
     if (st == tag && hdr[0] == code) {
-      copy_row(reinterpret_cast<Vec*>(hdr + 2), row, wpr);
+      copy_row(row_of<Vec>(a, s), row, wpr);
       return 0;
     }
     s = (s + 1 == a.cap) ? 0 : s + 1;
@@ -147,8 +194,11 @@ __global__ void __launch_bounds__(kThreads) exchange_step(const Args a) {
   if (i >= a.n) return;
   const int64_t wpr = a.vbytes / static_cast<int64_t>(sizeof(Vec));
   const uint64_t g = a.g0 + static_cast<uint64_t>(i);
+  const uint64_t kcode = load_code<CodeT>(a.kc, i);
+  // the insert's home slot state is read alongside the lookup (an independent load)
+  const uint64_t first = header(a, home(kcode, g, a))[1];
   lookup<Vec>(a, load_code<CodeT>(a.qc, i), g, reinterpret_cast<Vec*>(a.out) + i * wpr);
-  const int r = insert<Vec>(a, load_code<CodeT>(a.kc, i), g, reinterpret_cast<const Vec*>(a.v) + i * wpr);
+  const int r = insert<Vec>(a, kcode, g, reinterpret_cast<const Vec*>(a.v) + i * wpr, first);
   if (r < 0) {
     raise_status(a.status, LEMA_STATUS_TABLE_FULL);
   } else if (r > 0) {
@@ -264,12 +314,17 @@ size_t store_workspace_bytes(int64_t n, int64_t T, int code_bytes) {
 int store_exchange(void* table, int64_t cap, int64_t vbytes, const void* qc, const void* kc,
                    int code_bytes, const void* values, void* out, int64_t n, int64_t T, int64_t g0,
                    int64_t* counts, uint32_t* status, void* ws, size_t ws_bytes,
-                   cudaStream_t stream) {
+                   cudaStream_t stream, int64_t seg_groups, int64_t seg_slots) {
   if (code_bytes != 4 && code_bytes != 8) return fail(LEMA_ERR_INVALID_ARGUMENT, "code_bytes must be 4 or 8, got %d", code_bytes);
   if (vbytes <= 0 || vbytes % 8 != 0) return fail(LEMA_ERR_INVALID_ARGUMENT, "value row of %lld bytes: vbytes must be a positive multiple of 8", (long long)vbytes);
   if (cap < 1) return fail(LEMA_ERR_INVALID_ARGUMENT, "capacity must be >= 1 slot, got %lld", (long long)cap);
   if (n < 0 || T <= 0 || n % T != 0) return fail(LEMA_ERR_INVALID_ARGUMENT, "items must be partitions x T (n = %lld, T = %lld)", (long long)n, (long long)T);
   if (g0 < 0) return fail(LEMA_ERR_INVALID_ARGUMENT, "negative group offset");
+  if (seg_groups < 0 || seg_slots < 0 || (seg_groups > 0) != (seg_slots > 0))
+    return fail(LEMA_ERR_INVALID_ARGUMENT, "segments: groups and slots per segment both positive or both 0");
+  if (seg_groups > 0 && n > 0 && ((g0 + n / T - 1) / seg_groups + 1) * seg_slots > cap)
+    return fail(LEMA_ERR_INVALID_ARGUMENT, "group %lld's segment lies past the table's %lld slots",
+                (long long)(g0 + n / T - 1), (long long)cap);
   if (n == 0) return LEMA_OK;
   if (table == nullptr || !aligned(table, 16)) return fail(LEMA_ERR_INVALID_ARGUMENT, "table must be a 16-byte aligned device pointer");
   if (qc == nullptr || kc == nullptr || values == nullptr || out == nullptr || counts == nullptr) return fail(LEMA_ERR_INVALID_ARGUMENT, "null pointer argument");
@@ -285,7 +340,8 @@ int store_exchange(void* table, int64_t cap, int64_t vbytes, const void* qc, con
   k3::Args a{};
   a.table = static_cast<unsigned char*>(table);
   a.cap = static_cast<uint64_t>(cap);
-  a.stride = store_slot_bytes(vbytes);
+  a.rows = a.table + 16 * a.cap;
+  a.stride = store_slot_bytes(vbytes) - 16;
   a.vbytes = vbytes;
   a.qc = qc;
   a.kc = kc;
@@ -296,6 +352,8 @@ int store_exchange(void* table, int64_t cap, int64_t vbytes, const void* qc, con
   a.g0 = static_cast<uint64_t>(g0);
   a.counts = counts;
   a.status = status;
+  a.seg_groups = static_cast<uint64_t>(seg_groups);
+  a.seg_slots = static_cast<uint64_t>(seg_slots);
   const bool v16 = vbytes % 16 == 0 && aligned(values, 16) && aligned(out, 16);
   if (code_bytes == 4) {
     return v16 ? k3::run<uint32_t, uint4>(a, T, ws, ws_bytes, code_bytes, stream)

@@ -69,7 +69,8 @@ class LemaDecoder:
         # warm up on a scratch store (same row size and groups, room for the warm-up's keys)
         real = cache.store
         scratch = HashStore(cfg.d_v, groups=real.groups, dtype=real.dtype,
-                            capacity=4 * cfg.depth * B * cfg.num_heads + 64, device=dev)
+                            capacity=4 * cfg.depth * B * cfg.num_heads + 64, device=dev,
+                            segments=cfg.depth)
         tok0 = self.tok.clone()
         cb = 4 if cfg.d_qk <= 32 else 8          # the codes' width (int32 or int64)
         real.reserve(B * cfg.num_heads, 1, cb)

@@ -20,12 +20,16 @@ def dev_codes(a, dev):
     return torch.from_numpy(a.astype(np.int64)).to(dev)
 
 
+@pytest.mark.parametrize("segments", [1, 7])
 @pytest.mark.parametrize("name", sorted(G.store_cases()))
-def test_reference_store_cases(cuda, name):
+def test_reference_store_cases(cuda, name, segments):
+    # segments: home slots of each run of groups in its own slice of the table (probing still
+    # spans the table), which must change nothing in the results
     c = G.store_cases()[name]
     P, T, chunk = c["P"], c["T"], c["chunk"]
     vals = G.store_case_values(P, T, 8, c["seed"])
-    st = HashStore(8, groups=P, dtype=torch.float16, capacity=c["cap"], device=cuda)
+    st = HashStore(8, groups=P, dtype=torch.float16, capacity=c["cap"], device=cuda,
+                   segments=segments)
     v16 = torch.from_numpy(vals.view(np.float16))
     outs = np.empty_like(vals)
     for lo in range(0, T, chunk):
@@ -108,13 +112,15 @@ def test_chunking_invariance(cuda, chunk):
     assert st.counts[:5].sum().item() == 0
 
 
-def test_store_vs_oracle_store_random(cuda):
+@pytest.mark.parametrize("segments", [1, 12])
+def test_store_vs_oracle_store_random(cuda, segments):
     """Many partitions sharing a small code space, capacity tight: the GPU store and the
-    oracle store agree call by call, including the counts."""
+    oracle store agree call by call, including the counts (also with a segmented table,
+    where full segments spill into their neighbours)."""
     rng = np.random.default_rng(17)
     P, T, cap = 300, 40, 20000
     tab = oracle.new_table(cap, 16)
-    st = HashStore(8, groups=P, dtype=torch.float16, capacity=cap, device=cuda)
+    st = HashStore(8, groups=P, dtype=torch.float16, capacity=cap, device=cuda, segments=segments)
     for step in range(6):
         qc = rng.integers(0, 50, size=(P, T)).astype(np.int64)
         kc = rng.integers(0, 50, size=(P, T)).astype(np.int64)
