@@ -304,10 +304,14 @@ def run_b200(args):
 
     peak, peak_src = peaks()
     achieved = alg_bytes / (per_launch_ms / 1e3) / 1e9
+    # DRAM bytes per call of the three kernels, from the full-size ncu capture summarised in
+    # profiles/ (only meaningful for the default 512-stream workload)
     traffic = None
-    tf = ROOT / "profiles" / "prefill_match_cfg2_traffic.json"
-    if tf.exists():
-        traffic = json.loads(tf.read_text()).get("dram_bytes_per_launch")
+    tf = ROOT / "profiles" / "prefill_match_cfg2.md"
+    if tf.exists() and N_STREAMS == 512:
+        import re
+        m = re.search(r"traffic_bytes_per_call:\s*(\d+)", tf.read_text())
+        traffic = int(m.group(1)) if m else None
     if world > 1:
         import torch.distributed as dist
         dist.destroy_process_group()
