@@ -274,6 +274,12 @@ def run_b200(args):
     hs = torch.empty((N_STREAMS, T), dtype=torch.int32).pin_memory()
     h2d = hq.numel() * 4 + hk.numel() * 4 + hv.numel() * 2
     d2h = ho.numel() * 2 + hs.numel() * 4
+    # the public host-buffer call: batches of 64 streams, copies both ways overlapped with the
+    # kernels (attention.HostPrefill); one untimed call first
+    from latest_exact_match_attention_b200.attention import HostPrefill
+    hp = HostPrefill(dev, T, torch.int32, (D_V,), torch.bfloat16, batch=64)
+    if e2e_steps:
+        hp(hq, hk, hv, hs, ho)
     barrier()
     torch.cuda.synchronize()
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
@@ -281,12 +287,7 @@ def run_b200(args):
     if e2e_steps == 0:
         step()
     for _ in range(e2e_steps):
-        q.copy_(hq, non_blocking=True)
-        k.copy_(hk, non_blocking=True)
-        v.copy_(hv, non_blocking=True)
-        step()
-        ho.copy_(out, non_blocking=True)
-        hs.copy_(src, non_blocking=True)
+        hp(hq, hk, hv, hs, ho)
     e1.record(stream)
     torch.cuda.synchronize()
     e2e_ms = e0.elapsed_time(e1)

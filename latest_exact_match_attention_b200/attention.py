@@ -26,7 +26,7 @@ from . import _lib
 from ._lib import DTYPE_TAG, LemaError, call, ptr, require_cuda, stream_handle
 
 __all__ = ["pack_codes", "proj_codes", "latest_prev_match", "lema_hard", "prefill_match",
-           "code_bytes_of"]
+           "prefill_match_host", "HostPrefill", "code_bytes_of"]
 
 
 def code_bytes_of(codes: torch.Tensor) -> int:
@@ -157,3 +157,88 @@ def lema_hard(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, store=None) -> 
     _, out = prefill_match(qc.view(B * H, T), kc.view(B * H, T),
                            v.reshape(B * H, T, d_v), want_src=False)
     return out.view(B, H, T, d_v)
+
+
+class HostPrefill:
+    """`prefill_match` for inputs and outputs in HOST memory (pinned for overlap), streamed
+    through the device in batches of `batch` streams. The host->device copies of batch b+1,
+    the kernels of batch b and the device->host copies of batch b-1 run at once on three CUDA
+    streams, so the call costs about the slower copy direction instead of the sum of both.
+    Device buffers (two batches in flight) and the three streams are allocated once; one
+    instance serves calls of its shape. The call returns once the work is queued; the host
+    outputs are complete when the caller's current stream reaches that point."""
+
+    def __init__(self, device, T: int, code_dtype=torch.int32, row_shape=(), row_dtype=None,
+                 batch: int = 64, want_src: bool = True):
+        self.device = torch.device(device)
+        self.T, self.batch, self.want_src = T, batch, want_src
+        self.code_dtype = code_dtype
+        self.cb = torch.empty((), dtype=code_dtype).element_size()
+        mk = lambda shape, dt: [torch.empty(shape, dtype=dt, device=self.device) for _ in range(2)]
+        self.dq = mk((batch, T), code_dtype)
+        self.dk = mk((batch, T), code_dtype)
+        self.dsrc = mk((batch, T), torch.int32) if want_src else [None, None]
+        self.has_v = row_dtype is not None
+        self.dv = mk((batch, T) + tuple(row_shape), row_dtype) if self.has_v else [None, None]
+        self.dout = mk((batch, T) + tuple(row_shape), row_dtype) if self.has_v else [None, None]
+        self.vbytes = (self.dv[0][0, 0].numel() * self.dv[0].element_size()) if self.has_v else 0
+        nb = int(_lib.lib().lema_prefill_workspace_bytes(batch, T, self.cb))
+        self.ws = _workspace(nb, self.device)
+        self.streams = [torch.cuda.Stream(self.device) for _ in range(3)]
+
+    def __call__(self, qc, kc, v=None, src_out=None, out=None, status=None):
+        s_in, s_cp, s_out = self.streams
+        cur = torch.cuda.current_stream(self.device)
+        N = qc.shape[0]
+        for s in self.streams:
+            s.wait_stream(cur)
+        ev_cp, ev_out = [], []
+        for b, n0 in enumerate(range(0, N, self.batch)):
+            n, j = min(self.batch, N - n0), b % 2
+            with torch.cuda.stream(s_in):
+                if b >= 2:
+                    s_in.wait_event(ev_cp[b - 2])        # slot j's inputs were read
+                self.dq[j][:n].copy_(qc[n0:n0 + n], non_blocking=True)
+                self.dk[j][:n].copy_(kc[n0:n0 + n], non_blocking=True)
+                if self.has_v:
+                    self.dv[j][:n].copy_(v[n0:n0 + n], non_blocking=True)
+                e_in = torch.cuda.Event()
+                e_in.record(s_in)
+            with torch.cuda.stream(s_cp):
+                s_cp.wait_event(e_in)
+                if b >= 2:
+                    s_cp.wait_event(ev_out[b - 2])       # slot j's outputs were copied out
+                call("lema_prefill_match", ptr(self.dq[j]), ptr(self.dk[j]), self.cb, n, self.T,
+                     ptr(self.dsrc[j]), ptr(self.dv[j]), self.vbytes, ptr(self.dout[j]),
+                     ptr(self.ws), 0 if self.ws is None else self.ws.numel(), ptr(status),
+                     s_cp.cuda_stream)
+                e = torch.cuda.Event()
+                e.record(s_cp)
+                ev_cp.append(e)
+            with torch.cuda.stream(s_out):
+                s_out.wait_event(e)
+                if self.want_src and src_out is not None:
+                    src_out[n0:n0 + n].copy_(self.dsrc[j][:n], non_blocking=True)
+                if self.has_v and out is not None:
+                    out[n0:n0 + n].copy_(self.dout[j][:n], non_blocking=True)
+                e = torch.cuda.Event()
+                e.record(s_out)
+                ev_out.append(e)
+        for s in self.streams:
+            cur.wait_stream(s)
+
+
+def prefill_match_host(qc: torch.Tensor, kc: torch.Tensor, v: torch.Tensor | None = None, *,
+                       device=None, batch: int = 64, want_src: bool = True):
+    """`prefill_match` on host tensors: returns (src, out) as pinned host tensors, filled once
+    the current stream of `device` (default: the current CUDA device) has run the queued work
+    (synchronise before reading them)."""
+    dev = torch.device(device) if device is not None else torch.device("cuda", torch.cuda.current_device())
+    N, T = qc.shape
+    run = HostPrefill(dev, T, qc.dtype, tuple(v.shape[2:]) if v is not None else (),
+                      v.dtype if v is not None else None, batch=min(batch, max(N, 1)),
+                      want_src=want_src)
+    src = torch.empty((N, T), dtype=torch.int32).pin_memory() if want_src else None
+    out = torch.empty(v.shape, dtype=v.dtype).pin_memory() if v is not None else None
+    run(qc, kc, v, src, out)
+    return src, out
