@@ -566,10 +566,15 @@ def run_longctx(args):
             del src, out
     barrier()
     ms = statistics.mean(times)
+    names = list(phases)
+    pmax = dict(phases)
     if world > 1:
         t = torch.tensor([ms], device=dev)
         torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
         ms = float(t.item())
+        pt = torch.tensor([phases[k] for k in names], device=dev)
+        torch.distributed.all_reduce(pt, op=torch.distributed.ReduceOp.MAX)
+        pmax = dict(zip(names, pt.tolist()))
     if world > 1:
         torch.distributed.destroy_process_group()
     if rank != 0:
@@ -585,6 +590,7 @@ def run_longctx(args):
                    "positions_per_gpu": n // world, "seg_len": args.seg_len, "hit_rate": round(hit, 4),
                    "parallelism": f"sequence x{world}, NCCL all-gather + all-to-all"},
         "phases_ms_rank0": {k: round(x, 3) for k, x in phases.items()},
+        "phases_ms_max_over_ranks": {k: round(x, 3) for k, x in pmax.items()},
         "roofline": {"bound": "hbm", "alg_bytes_per_gpu_lower": alg // world,
                      "achieved": round(alg / world / (ms / 1e3) / 1e9, 1), "peak": peaks()[0],
                      "unit": "GB/s", "frac": round(alg / world / (ms / 1e3) / 1e9 / peaks()[0], 4)},

@@ -250,6 +250,14 @@ int lema_lt_insert(uint64_t* table, int64_t n_heads, int64_t slots, const int32_
                    const uint32_t* codes, const int32_t* pos, int64_t n,
                    uint32_t* status, void* stream);
 
+/* src[h][i] == -1 only: probe the tables of earlier shards, newest (index n_tables - 1)
+ * first; the first holding qcodes[h][i] gives its latest position, else -1. `tables`
+ * and `slots` are DEVICE arrays of n_tables table pointers (each n_heads x slots[t]
+ * words, slots a power of two) and slot counts. */
+int lema_lt_resolve_tables(const uint64_t* const* tables, const int64_t* slots, int n_tables,
+                           int64_t n_heads, const uint32_t* qcodes, int32_t* src, int64_t L,
+                           void* stream);
+
 /* src[h][i] == -1 only: the latest position of qcodes[h][i] in the table, or -1. */
 int lema_lt_resolve(const uint64_t* table, int64_t n_heads, int64_t slots,
                     const uint32_t* qcodes, int32_t* src, int64_t L, void* stream);

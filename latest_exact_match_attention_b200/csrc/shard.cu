@@ -148,6 +148,32 @@ __global__ void resolve_kernel(const ResolveParams p) {
   }
 }
 
+// Queries with src == -1 probe the earlier shards' tables, newest shard first; the first
+// shard holding the code has its latest occurrence. tables[t] holds n_heads x slots[t] words.
+struct ResolveTablesParams {
+  const uint64_t* const* tables;
+  const int64_t* slots;
+  int n_tables;
+  int64_t n_heads, L;
+  const uint32_t* qc;
+  int32_t* src;
+};
+
+__global__ void resolve_tables_kernel(const ResolveTablesParams p) {
+  const int64_t total = p.n_heads * p.L;
+  for (int64_t i = blockIdx.x * int64_t(blockDim.x) + threadIdx.x; i < total; i += int64_t(gridDim.x) * blockDim.x) {
+    if (p.src[i] >= 0) continue;
+    const int64_t h = i / p.L;
+    const uint32_t q = p.qc[i];
+    int32_t r = -1;
+    for (int t = p.n_tables - 1; t >= 0 && r < 0; --t) {
+      const int64_t sl = p.slots[t];
+      r = lt_find(p.tables[t] + h * sl, static_cast<uint32_t>(sl - 1), q);
+    }
+    p.src[i] = r;
+  }
+}
+
 // ------------------------------------------------------------------ sweep
 // One 8-CTA cluster per head: the segment's lookups and inserts are spread over the cluster's
 // 4096 threads, and cluster barriers (release / acquire at cluster scope) separate the two
@@ -440,6 +466,22 @@ extern "C" int lema_lt_resolve(const uint64_t* table, int64_t n_heads, int64_t s
   if (dev == nullptr) return LEMA_ERR_UNSUPPORTED;
   k5::ResolveParams p{table, slots, n_heads, L, qcodes, src};
   k5::resolve_kernel<<<k5::grid_for(n_heads * L, 256, *dev), 256, 0, static_cast<cudaStream_t>(stream)>>>(p);
+  LEMA_CUDA_TRY(cudaGetLastError());
+  return LEMA_OK;
+}
+
+extern "C" int lema_lt_resolve_tables(const uint64_t* const* tables, const int64_t* slots, int n_tables,
+                                      int64_t n_heads, const uint32_t* qcodes, int32_t* src, int64_t L,
+                                      void* stream) {
+  clear_error();
+  if (n_tables < 0 || n_heads <= 0 || L < 0) return fail(LEMA_ERR_INVALID_ARGUMENT, "bad shape");
+  if (n_tables == 0 || L == 0) return LEMA_OK;
+  if (tables == nullptr || slots == nullptr || qcodes == nullptr || src == nullptr)
+    return fail(LEMA_ERR_INVALID_ARGUMENT, "null pointer argument");
+  const DeviceInfo* dev = k5::sm100();
+  if (dev == nullptr) return LEMA_ERR_UNSUPPORTED;
+  k5::ResolveTablesParams p{tables, slots, n_tables, n_heads, L, qcodes, src};
+  k5::resolve_tables_kernel<<<k5::grid_for(n_heads * L, 256, *dev), 256, 0, static_cast<cudaStream_t>(stream)>>>(p);
   LEMA_CUDA_TRY(cudaGetLastError());
   return LEMA_OK;
 }

@@ -12,8 +12,10 @@ Per rank (kernels in csrc/shard.cu, K2 in csrc/prefill_match.cu):
                          table (LT: distinct key codes and their last positions)
     2. sweep             per head, segments in order against a device hash: in-segment
                          misses look up earlier segments; the hash ends as the shard's LT
-    3. exchange          all-gather of the shards' LTs (code, position; 12 bytes per entry)
-    4. resolve           queries still unmatched look up the earlier shards' LTs
+    3. exchange          all-gather of the shards' LTs, each re-hashed by its owner into a
+                         table sized for it (8 bytes per slot, load <= 0.5)
+    4. resolve           queries still unmatched probe the earlier shards' tables, newest
+                         first (reads only: no rank re-inserts the others' entries)
     5. fetch             rows at earlier shards' positions: requests (deduplicated) and rows
                          by all-to-all, landing in this GPU's memory before any kernel reads
     6. gather            one kernel: own rows, fetched rows, or zeros
@@ -165,21 +167,26 @@ class CudaOps:
         call("lema_lt_extract", ptr(table), H, slots, base, ptr(ent[0]), ptr(ent[1]), ptr(ent[2]),
              ptr(cnt), cap, ptr(self.status), self._stream())
         del table
-        return ent[:, : int(cnt.item())].t()
+        # the shard's LT re-hashed into a table sized for it (what the other ranks receive)
+        m = int(cnt.item())
+        per_head = torch.bincount(ent[0, :m].long(), minlength=H)
+        cslots = int(_lib.lib().lema_lt_table_slots(int(per_head.max()) if m else 1))
+        compact = torch.zeros((H, cslots), dtype=torch.int64, device=self.device)
+        call("lema_lt_insert", ptr(compact), H, cslots, ptr(ent[0]), ptr(ent[1]), ptr(ent[2]), m,
+             ptr(self.status), self._stream())
+        return compact.view(-1)
 
     def resolve(self, qc, src, earlier):
-        """Queries with src == -1 look up the earlier shards' entries [m, 3]."""
-        if earlier.shape[0] == 0:
+        """Queries with src == -1 probe the earlier shards' tables (a list, rank order; each
+        [H * slots] int64), newest first."""
+        if not earlier:
             return
         H, L = qc.shape
-        per_head = torch.bincount(earlier[:, 0].long(), minlength=H)
-        slots = int(_lib.lib().lema_lt_table_slots(int(per_head.max())))
-        table = torch.zeros((H, slots), dtype=torch.int64, device=self.device)
-        e = earlier.contiguous()
-        heads, codes, pos = (e[:, i].contiguous() for i in range(3))
-        call("lema_lt_insert", ptr(table), H, slots, ptr(heads), ptr(codes), ptr(pos), e.shape[0],
-             ptr(self.status), self._stream())
-        call("lema_lt_resolve", ptr(table), H, slots, ptr(qc), ptr(src), L, self._stream())
+        tabs = [t.contiguous() for t in earlier]
+        ptrs = torch.tensor([t.data_ptr() for t in tabs], dtype=torch.int64, device=self.device)
+        slots = torch.tensor([t.numel() // H for t in tabs], dtype=torch.int64, device=self.device)
+        call("lema_lt_resolve_tables", ptr(ptrs), ptr(slots), len(tabs), H, ptr(qc), ptr(src), L,
+             self._stream())
 
     @staticmethod
     def rows(vflat, idx):
@@ -235,32 +242,34 @@ def sharded_prefill(qc: torch.Tensor, kc: torch.Tensor, v: torch.Tensor, comm=No
     # 3-4: the shards' last-occurrence tables
     tables = comm.all_gather(mine)
     _mark(marks, "lt_all_gather")
-    earlier = torch.cat(tables[: comm.rank]) if comm.rank else mine[:0]
+    earlier = list(tables[: comm.rank])
     ops.resolve(qc, src, earlier)
     del tables, earlier
     _mark(marks, "resolve")
 
-    # 5: rows at earlier shards' positions, requested once each, head by head
+    # 5: rows at earlier shards' positions, requested once each, in groups of heads
     vflat = v.view(H * L, -1).view(torch.uint8)           # rows as bytes, for transport
     remote_idx = torch.full((H, L), -1, dtype=torch.int32, device=src.device)
     want, where = [], []
     n_before = 0
-    for h in range(H):
-        s = src[h]
-        q = ((s >= 0) & (s < base)).nonzero().squeeze(1)
+    hg = max(1, min(H, (1 << 26) // max(L, 1)))           # heads per group: <= 64 M positions
+    for h0 in range(0, H, hg):
+        h1 = min(H, h0 + hg)
+        s = src[h0:h1].reshape(-1)
+        q = ((s >= 0) & (s < base)).nonzero().squeeze(1)   # flat index within the group
         p = s[q].long()
         owner = p // L
-        key = owner * (H * L) + h * L + (p - owner * L)   # owner-major, then the owner's flat row
+        key = owner * (H * L) + (q // L + h0) * L + (p - owner * L)  # owner-major, owner's row
         uniq, inv = torch.unique(key, return_inverse=True)
         want.append(uniq)
-        where.append((h, q, inv + n_before))
+        where.append((h0, h1, q, inv + n_before))
         n_before += uniq.numel()
     uniq = torch.cat(want) if want else torch.empty(0, dtype=torch.int64, device=src.device)
     order = torch.sort(uniq // (H * L), stable=True)                # group by owner
     pos_of = torch.empty_like(order.indices)
     pos_of[order.indices] = torch.arange(order.indices.numel(), device=src.device)
-    for h, q, j in where:
-        remote_idx[h, q] = pos_of[j].to(torch.int32)
+    for h0, h1, q, j in where:
+        remote_idx[h0:h1].view(-1)[q] = pos_of[j].to(torch.int32)
     req = uniq[order.indices]
     counts = torch.bincount(order.values, minlength=comm.world).tolist()
     send = list((req % (H * L)).split(counts))

@@ -64,7 +64,9 @@ class PlainOps:
     def resolve(qc, src, earlier):
         H, L = qc.shape
         best = {}
-        for h, c, p in earlier.tolist():
+        if not earlier:
+            return
+        for h, c, p in torch.cat(list(earlier)).tolist():
             key = (h, c)
             best[key] = max(best.get(key, -1), p)
         q, s = qc.numpy(), src.numpy()
