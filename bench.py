@@ -527,7 +527,7 @@ def run_longctx(args):
     import torch
 
     from latest_exact_match_attention_b200 import synth
-    from latest_exact_match_attention_b200.longctx import SingleComm, TorchComm, sharded_prefill
+    from latest_exact_match_attention_b200.longctx import CudaOps, SingleComm, TorchComm, sharded_prefill
     rank, world = dist_setup(args.gpus)
     local = int(os.environ.get("LOCAL_RANK", "0"))
     torch.cuda.set_device(local)
@@ -536,6 +536,7 @@ def run_longctx(args):
     L = T // world
     qc, kc, v = synth.long_code_shard(H, rank * L, L, synth.CONFIG5, seed=0, device=dev)
     comm = TorchComm() if world > 1 else SingleComm()
+    ops = CudaOps(dev, rows_per_head=args.sweep_rows or None)
     stream = torch.cuda.current_stream(dev)
 
     def barrier():
@@ -543,7 +544,7 @@ def run_longctx(args):
             torch.distributed.barrier()
 
     for _ in range(max(1, args.warmup)):
-        src, out = sharded_prefill(qc, kc, v, comm, seg_len=args.seg_len)
+        src, out = sharded_prefill(qc, kc, v, comm, ops, seg_len=args.seg_len)
         del src, out
     torch.cuda.synchronize()
     hit = 0.0
@@ -555,7 +556,7 @@ def run_longctx(args):
             marks = []
             a = torch.cuda.Event(enable_timing=True)
             a.record(stream)
-            src, out = sharded_prefill(qc, kc, v, comm, seg_len=args.seg_len, marks=marks)
+            src, out = sharded_prefill(qc, kc, v, comm, ops, seg_len=args.seg_len, marks=marks)
             torch.cuda.synchronize()
             times.append(a.elapsed_time(marks[-1][1]))
             prev = a
@@ -609,7 +610,9 @@ def main():
     ap.add_argument("--streams", type=int, default=N_STREAMS,
                     help="streams per GPU (default: the workload's 512); smaller for profiling")
     ap.add_argument("--long-t", type=int, default=1 << 26, help="--workload longctx: positions")
-    ap.add_argument("--seg-len", type=int, default=4096, help="--workload longctx: segment")
+    ap.add_argument("--seg-len", type=int, default=8192, help="--workload longctx: segment")
+    ap.add_argument("--sweep-rows", type=int, default=0,
+                    help="--workload longctx: sweep rows per head (0 = chosen automatically)")
     ap.add_argument("--workload", choices=["prefill", "proj", "model-prefill", "decode", "longctx"],
                     default="prefill",
                     help="prefill: the headline config-2 line; proj: K1 at config 3's shapes; "

@@ -277,7 +277,13 @@ int lema_lt_extract(const uint64_t* table, int64_t n_heads, int64_t slots, int32
 int lema_shard_sweep(uint64_t* table, int64_t n_heads, int64_t slots, const uint32_t* qcodes,
                      int32_t* src, int64_t L, int64_t seg_len, const uint32_t* lt_code,
                      const int32_t* lt_pos, const int32_t* lt_count, int64_t base,
-                     uint32_t* status, void* stream);
+                     int64_t vrows, uint32_t* status, void* stream);
+/* (vrows > 1: each head is swept as vrows independent rows of L positions -- "n_heads" then
+ * counts rows, row r starting at position base + (r % vrows) * L -- and
+ * lema_lt_resolve_rows then lets a row's remaining misses probe the earlier rows of its
+ * head, newest first.) */
+int lema_lt_resolve_rows(const uint64_t* table, int64_t n_rows, int64_t slots, int64_t vrows,
+                         const uint32_t* qcodes, int32_t* src, int64_t L, void* stream);
 
 /* out[h][i] = values[h][src - base] for src >= base, remote_rows[remote_idx[h][i]]
  * for 0 <= src < base, zeros for -1. */

@@ -45,7 +45,8 @@ _SIGNATURES = {
     "lema_lt_resolve": ([_P, _I64, _I64, _P, _P, _I64, _P], _I),
     "lema_lt_resolve_tables": ([_P, _P, _I, _I64, _P, _P, _I64, _P], _I),
     "lema_lt_extract": ([_P, _I64, _I64, ctypes.c_int32, _P, _P, _P, _P, _I64, _P, _P], _I),
-    "lema_shard_sweep": ([_P, _I64, _I64, _P, _P, _I64, _I64, _P, _P, _P, _I64, _P, _P], _I),
+    "lema_shard_sweep": ([_P, _I64, _I64, _P, _P, _I64, _I64, _P, _P, _P, _I64, _I64, _P, _P], _I),
+    "lema_lt_resolve_rows": ([_P, _I64, _I64, _I64, _P, _P, _I64, _P], _I),
     "lema_shard_gather": ([_P, _I64, _P, _P, _P, _I64, _P, _I64, _I64, _P, _P], _I),
     "lema_store_slot_bytes": ([_I64], _I64),
     "lema_store_workspace_bytes": ([_I64, _I64, _I], _SZ),

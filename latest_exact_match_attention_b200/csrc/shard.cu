@@ -174,6 +174,30 @@ __global__ void resolve_tables_kernel(const ResolveTablesParams p) {
   }
 }
 
+// A head swept as vrows rows (sub-shards) of L positions: queries of row r (v = r % vrows)
+// still without a match probe the rows r - 1, ..., r - v of the same head in the sweep's table,
+// newest first.
+struct ResolveRowsParams {
+  const uint64_t* table;
+  int64_t slots, n_rows, vrows, L;
+  const uint32_t* qc;
+  int32_t* src;
+};
+
+__global__ void resolve_rows_kernel(const ResolveRowsParams p) {
+  const uint32_t mask = static_cast<uint32_t>(p.slots - 1);
+  const int64_t total = p.n_rows * p.L;
+  for (int64_t i = blockIdx.x * int64_t(blockDim.x) + threadIdx.x; i < total; i += int64_t(gridDim.x) * blockDim.x) {
+    const int64_t r = i / p.L;
+    const int64_t v = r % p.vrows;
+    if (v == 0 || p.src[i] >= 0) continue;
+    const uint32_t q = p.qc[i];
+    int32_t res = -1;
+    for (int64_t rr = r - 1; rr >= r - v && res < 0; --rr) res = lt_find(p.table + rr * p.slots, mask, q);
+    p.src[i] = res;
+  }
+}
+
 // ------------------------------------------------------------------ sweep
 // One 8-CTA cluster per head: the segment's lookups and inserts are spread over the cluster's
 // 4096 threads, and cluster barriers (release / acquire at cluster scope) separate the two
@@ -192,6 +216,7 @@ struct SweepParams {
   const int32_t* lt_pos;
   const int32_t* lt_count;
   uint32_t* status;
+  int64_t vrows;       // rows per head: row r's positions start at base + (r % vrows) * L
 };
 
 // After the inserts: release, so every insert is visible to the next segment's lookups.
@@ -260,7 +285,7 @@ __global__ void __cluster_dims__(kClusterCtas, 1, 1) __launch_bounds__(kSweepThr
   if (p.n_seg > 0) load(0);
   for (int64_t seg = 0; seg < p.n_seg; ++seg) {
     const int64_t s0 = seg * p.seg_len;
-    const int64_t g0 = p.base + s0;
+    const int64_t g0 = p.base + (h % p.vrows) * p.L + s0;
     int32_t cs[kSweepPer], cp[kSweepPer];
     uint32_t cq[kSweepPer], cc[kSweepPer];
     const int32_t cnt = ncnt;
@@ -470,6 +495,22 @@ extern "C" int lema_lt_resolve(const uint64_t* table, int64_t n_heads, int64_t s
   return LEMA_OK;
 }
 
+extern "C" int lema_lt_resolve_rows(const uint64_t* table, int64_t n_rows, int64_t slots, int64_t vrows,
+                                    const uint32_t* qcodes, int32_t* src, int64_t L, void* stream) {
+  clear_error();
+  if (n_rows <= 0 || !k5::pow2(slots) || slots > (int64_t(1) << 31) || L < 0 || vrows < 1 || n_rows % vrows)
+    return fail(LEMA_ERR_INVALID_ARGUMENT, "bad shape (rows %lld, slots %lld, rows per head %lld)", (long long)n_rows,
+                (long long)slots, (long long)vrows);
+  if (L == 0 || vrows == 1) return LEMA_OK;
+  if (table == nullptr || qcodes == nullptr || src == nullptr) return fail(LEMA_ERR_INVALID_ARGUMENT, "null pointer argument");
+  const DeviceInfo* dev = k5::sm100();
+  if (dev == nullptr) return LEMA_ERR_UNSUPPORTED;
+  k5::ResolveRowsParams p{table, slots, n_rows, vrows, L, qcodes, src};
+  k5::resolve_rows_kernel<<<k5::grid_for(n_rows * L, 256, *dev), 256, 0, static_cast<cudaStream_t>(stream)>>>(p);
+  LEMA_CUDA_TRY(cudaGetLastError());
+  return LEMA_OK;
+}
+
 extern "C" int lema_lt_resolve_tables(const uint64_t* const* tables, const int64_t* slots, int n_tables,
                                       int64_t n_heads, const uint32_t* qcodes, int32_t* src, int64_t L,
                                       void* stream) {
@@ -505,8 +546,8 @@ extern "C" int lema_lt_extract(const uint64_t* table, int64_t n_heads, int64_t s
 
 extern "C" int lema_shard_sweep(uint64_t* table, int64_t n_heads, int64_t slots, const uint32_t* qcodes,
                                 int32_t* src, int64_t L, int64_t seg_len, const uint32_t* lt_code,
-                                const int32_t* lt_pos, const int32_t* lt_count, int64_t base, uint32_t* status,
-                                void* stream) {
+                                const int32_t* lt_pos, const int32_t* lt_count, int64_t base, int64_t vrows,
+                                uint32_t* status, void* stream) {
   clear_error();
   if (n_heads <= 0 || !k5::pow2(slots) || slots > (int64_t(1) << 31) || L < 0 || seg_len <= 0 || base < 0)
     return fail(LEMA_ERR_INVALID_ARGUMENT, "bad shape (heads %lld, slots %lld, L %lld, segment %lld)",
@@ -515,13 +556,14 @@ extern "C" int lema_shard_sweep(uint64_t* table, int64_t n_heads, int64_t slots,
   if (seg_len > int64_t(k5::kClusterCtas) * k5::kSweepThreads * k5::kSweepPer)
     return fail(LEMA_ERR_INVALID_ARGUMENT, "seg_len = %lld: at most %d positions per segment", (long long)seg_len,
                 k5::kClusterCtas * k5::kSweepThreads * k5::kSweepPer);
-  if (base + L >= (int64_t(1) << 31) - 1) return fail(LEMA_ERR_INVALID_ARGUMENT, "positions must stay below 2^31 - 1");
+  if (vrows < 1 || n_heads % vrows != 0) return fail(LEMA_ERR_INVALID_ARGUMENT, "rows (%lld) must be whole heads of %lld rows", (long long)n_heads, (long long)vrows);
+  if (base + vrows * L >= (int64_t(1) << 31) - 1) return fail(LEMA_ERR_INVALID_ARGUMENT, "positions must stay below 2^31 - 1");
   if (L == 0) return LEMA_OK;
   if (table == nullptr || qcodes == nullptr || src == nullptr || lt_code == nullptr || lt_pos == nullptr || lt_count == nullptr)
     return fail(LEMA_ERR_INVALID_ARGUMENT, "null pointer argument");
   const DeviceInfo* dev = k5::sm100();
   if (dev == nullptr) return LEMA_ERR_UNSUPPORTED;
-  k5::SweepParams p{table, slots, qcodes, src, L, seg_len, L / seg_len, base, lt_code, lt_pos, lt_count, status};
+  k5::SweepParams p{table, slots, qcodes, src, L, seg_len, L / seg_len, base, lt_code, lt_pos, lt_count, status, vrows};
   k5::sweep_kernel<<<static_cast<unsigned>(n_heads * k5::kClusterCtas), k5::kSweepThreads, 0,
                      static_cast<cudaStream_t>(stream)>>>(p);
   LEMA_CUDA_TRY(cudaGetLastError());

@@ -126,8 +126,9 @@ class ThreadComm:
 class CudaOps:
     """The per-rank device work, on this library's kernels."""
 
-    def __init__(self, device):
+    def __init__(self, device, rows_per_head: int | None = None):
         self.device = device
+        self.vrows = rows_per_head
         self.status = torch.zeros(1, dtype=torch.int32, device=device)
 
     def _stream(self):
@@ -148,25 +149,42 @@ class CudaOps:
              ptr(ltn), ptr(ws), wsb, ptr(self.status), self._stream())
         return src, ltc, ltp, ltn
 
-    def sweep(self, qc, src, lt, seg_len, base):
-        """Segments in order; returns the shard's LT as entries [m, 3] int32 (head, code, pos)."""
+    def rows_per_head(self, H: int, n_seg: int) -> int:
+        """Independent sweep rows per head (rows_per_head, default 1). More rows sweep in
+        parallel, but merging their tables into the shard's table costs more than that saves
+        at config 5's sizes (measured at 2^25 x 16 positions: 1 row 45.7 ms, 2 rows 49.4 ms,
+        4 rows 58.0 ms for the whole sweep phase)."""
+        if self.vrows is not None:
+            return self.vrows
+        return 1
+
+    def sweep(self, qc, src, lt, seg_len, base, want_table=True):
+        """Segments in order, each head as V rows swept in parallel (a row's remaining misses then
+        probe its head's earlier rows); returns the shard's LT re-hashed into a compact table,
+        [H * slots] int64, for the other ranks."""
         ltc, ltp, ltn = lt
         H, L = qc.shape
         n_seg = L // seg_len
-        # distinct codes per head <= the sum of its segments' distinct codes, and <= L
-        per_head = torch.minimum(ltn.view(H, n_seg).sum(1, dtype=torch.int64),
-                                 torch.tensor(L, device=self.device))
-        bounds = per_head.tolist()
-        slots = int(_lib.lib().lema_lt_table_slots(max(bounds)))
-        table = torch.zeros((H, slots), dtype=torch.int64, device=self.device)
-        call("lema_shard_sweep", ptr(table), H, slots, ptr(qc), ptr(src), L, seg_len, ptr(ltc),
-             ptr(ltp), ptr(ltn), base, ptr(self.status), self._stream())
-        cap = sum(bounds)
+        V = self.rows_per_head(H, n_seg)
+        R, Lr = H * V, L // V
+        # distinct codes per row <= the sum of its segments' distinct codes, and <= its length
+        per_row = torch.minimum(ltn.view(R, n_seg // V).sum(1, dtype=torch.int64),
+                                torch.tensor(Lr, device=self.device)).tolist()
+        slots = int(_lib.lib().lema_lt_table_slots(max(per_row)))
+        table = torch.zeros((R, slots), dtype=torch.int64, device=self.device)
+        call("lema_shard_sweep", ptr(table), R, slots, ptr(qc), ptr(src), Lr, seg_len, ptr(ltc),
+             ptr(ltp), ptr(ltn), base, V, ptr(self.status), self._stream())
+        call("lema_lt_resolve_rows", ptr(table), R, slots, V, ptr(qc), ptr(src), Lr, self._stream())
+        if not want_table:                                   # a single rank: nobody asks
+            return None
+        cap = sum(per_row)
         ent = torch.empty((3, cap), dtype=torch.int32, device=self.device)
         cnt = torch.empty(1, dtype=torch.int32, device=self.device)
-        call("lema_lt_extract", ptr(table), H, slots, base, ptr(ent[0]), ptr(ent[1]), ptr(ent[2]),
+        call("lema_lt_extract", ptr(table), R, slots, base, ptr(ent[0]), ptr(ent[1]), ptr(ent[2]),
              ptr(cnt), cap, ptr(self.status), self._stream())
         del table
+        if V > 1:
+            ent[0].div_(V, rounding_mode="floor")            # row -> head
         # the shard's LT re-hashed into a table sized for it (what the other ranks receive)
         m = int(cnt.item())
         per_head = torch.bincount(ent[0, :m].long(), minlength=H)
@@ -236,11 +254,11 @@ def sharded_prefill(qc: torch.Tensor, kc: torch.Tensor, v: torch.Tensor, comm=No
     # 1-2: local work, no rank waits for another
     src, ltc, ltp, ltn = ops.segment_match(qc, kc, seg_len)
     _mark(marks, "segment_match")
-    mine = ops.sweep(qc, src, (ltc, ltp, ltn), seg_len, base)
+    mine = ops.sweep(qc, src, (ltc, ltp, ltn), seg_len, base, want_table=comm.world > 1)
     del ltc, ltp, ltn
     _mark(marks, "sweep")
     # 3-4: the shards' last-occurrence tables
-    tables = comm.all_gather(mine)
+    tables = comm.all_gather(mine) if comm.world > 1 else [None]
     _mark(marks, "lt_all_gather")
     earlier = list(tables[: comm.rank])
     ops.resolve(qc, src, earlier)

@@ -40,7 +40,7 @@ class PlainOps:
                 torch.from_numpy(ltn))
 
     @staticmethod
-    def sweep(qc, src, lt, seg_len, base):
+    def sweep(qc, src, lt, seg_len, base, want_table=True):
         ltc, ltp, ltn = (t.numpy() for t in lt)
         ltc = ltc.view(np.uint32)
         H, L = qc.shape

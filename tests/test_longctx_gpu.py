@@ -80,6 +80,30 @@ def test_sharded_edge_cases(cuda, kind):
     assert torch.equal(src, src1) and torch.equal(out, out1)
 
 
+@pytest.mark.parametrize("rows", [2, 4])
+def test_sweep_rows_per_head(cuda, rows):
+    # each head swept as independent rows, then merged: the same result
+    from latest_exact_match_attention_b200.longctx import CudaOps, ThreadComm, _Board
+    q, k, v = case(4, 2 * 8 * 1024, SMALL_POOL, seed=11)
+    src1, out1 = prefill_match(q, k, v)
+    L = q.shape[1] // 2
+    board = _Board(2)
+    res = [None, None]
+    import threading
+
+    def run(r):
+        sl = slice(r * L, (r + 1) * L)
+        res[r] = sharded_prefill(q[:, sl], k[:, sl], v[:, sl], ThreadComm(board, r),
+                                 CudaOps(q.device, rows_per_head=rows), seg_len=1024)
+    th = [threading.Thread(target=run, args=(r,)) for r in range(2)]
+    for t in th:
+        t.start()
+    for t in th:
+        t.join()
+    assert torch.equal(torch.cat([res[0][0], res[1][0]], 1), src1)
+    assert torch.equal(torch.cat([res[0][1], res[1][1]], 1), out1)
+
+
 def test_single_rank_entry_point(cuda):
     q, k, v = case(3, 4096, SMALL_POOL, seed=1)
     src1, out1 = prefill_match(q, k, v)
