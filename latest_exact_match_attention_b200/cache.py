@@ -151,6 +151,18 @@ class HashStore:
         if check:
             self.check()
 
+    def dump(self):
+        """Every entry of the store: (groups int64 [n], codes int64 [n], rows [n, d_v] in the
+        store's dtype), in slot order. Codes are the stored 64-bit words (an int32 code's bit
+        pattern zero-extended). Reads the table as it is on the device (synchronises)."""
+        hdr = self.table.view(-1)[: 16 * self.cap].view(torch.int64).view(self.cap, 2)
+        rows = self.table.view(-1)[16 * self.cap:].view(self.cap, self.stride - 16)
+        live = (hdr[:, 1] >= 2).nonzero().squeeze(1)
+        groups = hdr[live, 1] - 2
+        codes = hdr[live, 0]
+        vals = rows[live].view(self.dtype)[:, : self.d_v]
+        return groups, codes, vals
+
     def check(self):
         """Raise if a kernel reported a full table (or an internal probe limit). Syncs."""
         s = int(self.status.item())
@@ -282,3 +294,34 @@ class LemaCache:
     def check(self):
         """Raise if any exchange since the last check found the table full."""
         self.store.check()
+
+    def dump(self, layer: int | None = None):
+        """Entries as (layer, batch, head, code, row) tensors, all layers or one."""
+        g, c, v = self.store.dump()
+        P = self.batch * self.cfg.num_heads
+        lay, rest = g // P, g % P
+        if layer is not None:
+            keep = lay == layer
+            lay, rest, c, v = lay[keep], rest[keep], c[keep], v[keep]
+        return lay, rest // self.cfg.num_heads, rest % self.cfg.num_heads, c, v
+
+
+def worst_case_codes(depth: int):
+    """A codes hook (LemaCache(codes_hook=...)) for stress runs: every layer's query AND key
+    codes are replaced by fresh random 64-bit codes, so every lookup misses after probing its
+    run and every insert claims a new slot at a random place -- the worst access pattern a
+    model could produce (the stress mode of code/experiments/main_inference/common.py:170-196).
+    All layers' codes are drawn at layer 0 in one kernel into a buffer the later layers view;
+    inside a CUDA graph the generator advances on every replay, so each step draws anew."""
+    bufs = {}
+
+    def hook(layer, qc, kc):
+        key = (qc.device, tuple(qc.shape))
+        if layer == 0 or key not in bufs:
+            if key not in bufs:
+                bufs[key] = torch.empty((depth, 2) + tuple(qc.shape), dtype=torch.int64,
+                                        device=qc.device)
+            bufs[key].random_()
+        b = bufs[key]
+        return b[layer, 0], b[layer, 1]
+    return hook
