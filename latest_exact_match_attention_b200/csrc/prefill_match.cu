@@ -79,7 +79,7 @@ struct SmemCap<uint64_t> {
 constexpr double kOverflowFrac = 0.75;
 
 static_assert(SmemCap<uint32_t>::kSlots < (1u << 14) && SmemCap<uint64_t>::kSlots < (1u << 14),
-              "shared-memory slots (and the side slot) fit the 14 bit-sliced slot bits");
+              "shared-memory slot indices (and the side slot) stay small");
 
 template <typename CodeT>
 __host__ __device__ constexpr uint32_t overflow_limit() {
@@ -273,25 +273,21 @@ struct Params {
   int list_mode;  // global path: 1 = streams from ovf_list, 0 = all streams
 };
 
-// Key lanes of one step whose slot equals s, from the step's bit-sliced row: word b holds
-// ballot(bit b of each lane's slot) for b < kBits, word kBits the valid lanes. `sb[b]` is all
-// ones where bit b of s is set, so lanes agreeing on bit b are ~(row[b] ^ sb[b]).
-template <int kBits>
-__device__ __forceinline__ uint32_t sliced_lanes(const uint32_t* row, const uint32_t (&sb)[kBits]) {
-  constexpr int kVec = (kBits + 1 + 3) / 4;
-  uint32_t w[4 * kVec];
-#pragma unroll
-  for (int k = 0; k < kVec; ++k) {
-    const uint4 x = reinterpret_cast<const uint4*>(row)[k];
-    w[4 * k] = x.x;
-    w[4 * k + 1] = x.y;
-    w[4 * k + 2] = x.z;
-    w[4 * k + 3] = x.w;
+// Per step of a chunk, two small shared arrays replace any warp-wide matching:
+//   ls[step][b]   bit j set iff key lane j of the step holds a slot with (slot % kLsBuckets) == b
+//   ks[step][j]   the slot of key lane j (kNoSlot for none)
+// The key lanes of a step holding slot s are the bits of ls[step][s % kLsBuckets] whose ks is s;
+// two slots sharing a bucket in one step only cost a second look.
+constexpr int kLsBuckets = 64;
+
+// The highest lane of `cand` whose key slot is s, or -1.
+__device__ __forceinline__ int lane_with_slot(uint32_t cand, const uint32_t* ks, uint32_t s) {
+  while (cand) {
+    const int j = 31 - __clz(cand);
+    if (ks[j] == s) return j;
+    cand &= ~(1u << j);
   }
-  uint32_t m = w[kBits];
-#pragma unroll
-  for (int b = 0; b < kBits; ++b) m &= ~(w[b] ^ sb[b]);
-  return m;
+  return -1;
 }
 
 __device__ __forceinline__ void match_barrier() { __syncthreads(); }
@@ -303,10 +299,8 @@ __global__ void __launch_bounds__(kThreads) match_kernel(const Params p) {
   extern __shared__ __align__(16) unsigned char smem[];
   constexpr uint32_t kCap = SmemCap<CodeT>::kSlots;
   constexpr size_t kTableBytes = kSmemTable ? round_up16(Tab::bytes(kCap)) : 0;
-  // slot bits of the bit-sliced step rows: table slots are < 2^14 on the shared-memory path
-  constexpr int kBits = kSmemTable ? 14 : 32;
-  constexpr int kRowWords = kSmemTable ? 16 : 36;
-  uint32_t* srow = reinterpret_cast<uint32_t*>(smem + kTableBytes);  // [kSteps][kRowWords]
+  uint32_t* s_ls = reinterpret_cast<uint32_t*>(smem + kTableBytes);  // [kSteps][kLsBuckets]
+  uint32_t* s_ks = s_ls + kSteps * kLsBuckets;                         // [kSteps][32]
   __shared__ uint32_t s_used, s_ovf, s_lt;
 
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
@@ -326,6 +320,7 @@ __global__ void __launch_bounds__(kThreads) match_kernel(const Params p) {
     const int64_t n = (!kSmemTable && p.list_mode) ? static_cast<int64_t>(p.ovf_list[wi]) : wi;
     const int64_t row0 = n * p.T;
     tab.clear(tid, kThreads);
+    for (int k = tid; k < kSteps * kLsBuckets; k += kThreads) s_ls[k] = 0u;
     if (tid == 0) {
       s_used = 0;
       s_ovf = 0;
@@ -350,7 +345,6 @@ __global__ void __launch_bounds__(kThreads) match_kernel(const Params p) {
         // ---------------------------------------------- P1: keys into the table, step bits
         const int32_t base32 = static_cast<int32_t>(base);
         uint32_t kslot[kPerLane], qslot[kPerLane];
-        uint32_t klast = 0;  // bit u: this lane is the last key of its slot in step u
 #pragma unroll
         for (int u = 0; u < kPerLane; ++u) {
           const int step = warp + u * kMatchWarps;
@@ -364,29 +358,16 @@ __global__ void __launch_bounds__(kThreads) match_kernel(const Params p) {
             kslot[u] = tab.insert_fast(kr[u], claimed);
             if (kslot[u] == kNoSlot) s_ovf = 1;
           }
-          // publish the step's key slots bit-sliced; the same ballots tell each lane which
-          // lanes share its slot, so only the first sets the step bit and the last is known
+          // the step's key lanes per slot bucket, and each lane's slot; every key lane sets its
+          // step's bit in the slot's mask (lanes sharing a slot set the same bit)
           const uint32_t ks = kslot[u];
-          uint32_t bal[kRowWords];
-#pragma unroll
-          for (int b = 0; b < kBits; ++b) bal[b] = __ballot_sync(kFullMask, (ks >> b) & 1u);
-          bal[kBits] = __ballot_sync(kFullMask, ks != kNoSlot);
-#pragma unroll
-          for (int b = kBits + 1; b < kRowWords; ++b) bal[b] = 0u;
-          uint32_t same = bal[kBits];
-#pragma unroll
-          for (int b = 0; b < kBits; ++b) same &= ((ks >> b) & 1u) ? bal[b] : ~bal[b];
+          s_ks[step * 32 + lane] = ks;
           if (ks != kNoSlot) {
-            if ((same & lanemask_lt()) == 0u) atomicOr(tab.mask + ks, 1u << step);
-            if ((same >> lane) == 1u) klast |= 1u << u;
+            atomicOr(s_ls + step * kLsBuckets + (ks & (kLsBuckets - 1)), 1u << lane);
+            atomicOr(tab.mask + ks, 1u << step);
           }
           const uint32_t nclaim = __popc(__ballot_sync(kFullMask, claimed != 0));
-          if (lane == 0) {
-            if (nclaim) atomicAdd(&s_used, nclaim);
-            uint4* row = reinterpret_cast<uint4*>(srow + step * kRowWords);
-#pragma unroll
-            for (int k = 0; k < kRowWords / 4; ++k) row[k] = make_uint4(bal[4 * k], bal[4 * k + 1], bal[4 * k + 2], bal[4 * k + 3]);
-          }
+          if (lane == 0 && nclaim) atomicAdd(&s_used, nclaim);
           // the query's slot, looked up after this step's own inserts: a code this step inserted
           // is always found; a miss may be stale (another warp's concurrent insert) and is
           // looked up again after the barrier
@@ -405,45 +386,38 @@ __global__ void __launch_bounds__(kThreads) match_kernel(const Params p) {
             const int i = step * 32 + lane;
             if (step >= kSteps || step * 32 >= cnt) continue;  // uniform per warp
             const bool valid = i < cnt;
-            if ((klast >> u) & 1u) {
-              if ((31 - __clz(tab.mask[kslot[u]])) == step) clast |= 1u << u;
-            }
+            if (kslot[u] != kNoSlot && (31 - __clz(tab.mask[kslot[u]])) == step) clast |= 1u << u;
             uint32_t sl = qslot[u];
             if (valid && sl == kNoSlot) sl = tab.find_fast(qr[u]);
-            const uint32_t m = sl != kNoSlot ? tab.mask[sl] : 0u;
-            uint32_t sb[kBits];
-#pragma unroll
-            for (int b = 0; b < kBits; ++b) sb[b] = 0u - ((sl >> b) & 1u);
             int32_t a = -1;
-            bool done = !valid || sl == kNoSlot;
-            // own step: every lane reads the same row (a broadcast), keeps key lanes < its own
-            if (__any_sync(kFullMask, !done && ((m >> step) & 1u))) {
-              const uint32_t lanes = sliced_lanes<kBits>(srow + step * kRowWords, sb) & lanemask_lt();
-              if (!done && ((m >> step) & 1u) && lanes) {
-                a = base32 + step * 32 + (31 - __clz(lanes));
-                done = true;
+            if (valid && sl != kNoSlot) {
+              const uint32_t m = tab.mask[sl];
+              const uint32_t bk = sl & (kLsBuckets - 1);
+              int j = -1, st = step;
+              // own step: the highest key lane below this one holding the slot
+              if ((m >> step) & 1u)
+                j = lane_with_slot(s_ls[step * kLsBuckets + bk] & lanemask_lt(), s_ks + step * 32, sl);
+              // else the latest earlier step holding it: its highest lane with the slot
+              const uint32_t me = m & ((1u << step) - 1u);
+              if (j < 0 && me) {
+                st = 31 - __clz(me);
+                j = lane_with_slot(s_ls[st * kLsBuckets + bk], s_ks + st * 32, sl);
               }
+              a = j >= 0 ? base32 + st * 32 + j
+                         : static_cast<int32_t>(tab.carry[sl]) - 1;  // 0 (none) gives -1
             }
-            // the latest earlier step holding the code: its highest lane with the slot
-            const uint32_t me = m & ((1u << step) - 1u);
-            if (__any_sync(kFullMask, !done && me)) {
-              const int st = me ? 31 - __clz(me) : 0;
-              const uint32_t lanes = sliced_lanes<kBits>(srow + st * kRowWords, sb);
-              if (!done && me) {
-                a = base32 + st * 32 + (31 - __clz(lanes | 1u));
-                done = true;
-              }
-            }
-            if (!done) a = static_cast<int32_t>(tab.carry[sl]) - 1;  // 0 (none) gives -1
             if (valid) ab[i] = a;
           }
           match_barrier();
           // ---------------------------------------------- P3: carries of the chunk's last keys
 #pragma unroll
           for (int u = 0; u < kPerLane; ++u) {
+            const int step = warp + u * kMatchWarps;
+            if (step >= kSteps || kslot[u] == kNoSlot) continue;
+            s_ls[step * kLsBuckets + (kslot[u] & (kLsBuckets - 1))] = 0u;  // clean for the next chunk
             if ((clast >> u) & 1u) {
-              const int i = (warp + u * kMatchWarps) * 32 + lane;
-              tab.carry[kslot[u]] = static_cast<uint32_t>(base32 + i + 1);  // the slot's unique last key
+              // the keys of the slot's last step: the latest of them becomes the carry
+              atomicMax(tab.carry + kslot[u], static_cast<uint32_t>(base32 + step * 32 + lane + 1));
               tab.mask[kslot[u]] = 0u;
             }
           }
@@ -577,10 +551,10 @@ int run_gather(const MatchLaunch& a, const int32_t* src) {
 }
 
 // ---------------------------------------------------------------- host side
-// bit-sliced step rows
+// per-step lane sets and key slots
 template <bool kSmemTable>
 constexpr size_t chunk_smem() {
-  return kSteps * (kSmemTable ? 16 : 36) * sizeof(uint32_t);
+  return kSteps * (kLsBuckets + 32) * sizeof(uint32_t);  // lane-set buckets and key slots
 }
 constexpr int64_t kMaxOverflowTables = 64;
 constexpr uint64_t kOverflowTableBudget = uint64_t(1) << 30;  // bytes of global tables
