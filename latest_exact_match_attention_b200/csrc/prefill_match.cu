@@ -29,7 +29,7 @@
 // counted once per warp.
 // No warp-wide match instructions are used: on this part they cost far more than the table
 // traffic they would save.
-// All 16 warps of a CTA run the phases (two steps each per chunk); CTA barriers separate them.
+// All 32 warps of a CTA run the phases (one step each per chunk); CTA barriers separate them.
 // The value rows are copied by a separate kernel afterwards (see gather_kernel).
 //
 // The table is bucketed: 8 slots per bucket, read with vector loads, linear probing over
@@ -54,7 +54,7 @@
 namespace lema {
 namespace k2 {
 
-constexpr int kThreads = 512;
+constexpr int kThreads = 1024;  // 32 warps: one step of 32 positions each per chunk
 constexpr int kChunk = 1024;                   // positions per chunk: 32 steps of 32
 constexpr int kSteps = kChunk / 32;
 constexpr int kMatchWarps = kThreads / 32;                         // every warp matches
@@ -294,7 +294,7 @@ __device__ __forceinline__ void match_barrier() { __syncthreads(); }
 
 
 template <typename CodeT, bool kSmemTable>
-__global__ void __launch_bounds__(kThreads) match_kernel(const Params p) {
+__global__ void __launch_bounds__(kThreads, 2) match_kernel(const Params p) {
   using Tab = Table<CodeT, uint32_t>;
   extern __shared__ __align__(16) unsigned char smem[];
   constexpr uint32_t kCap = SmemCap<CodeT>::kSlots;
