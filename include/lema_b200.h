@@ -98,6 +98,26 @@ int lema_proj_codes(const void* x, const void* w_qk, int64_t M, int64_t K,
                     int64_t T, int hq, int hk, int d_qk, uint32_t* qcodes,
                     uint32_t* kcodes, uint32_t* status, void* stream);
 
+/*
+ * lema_proj_codes with the value projection and the norm folded in: w_all stacks the
+ * query and key weights ((hq + hk) * 32 rows) and n_v value rows (v_proj.weight), each
+ * column-scaled by the RMSNorm weight; x is the UN-normalised residual stream. The
+ * codes are those of the normalised input (the norm's positive row scale cannot change
+ * a sign); the n_v value columns are written as bf16 v_out[m][c] = row_scale[m] * z,
+ * row_scale = 1 / sqrt(mean(x[m]^2) + eps) from lema_row_rms (NULL: 1). n_v = 0 is
+ * lema_proj_codes. v_out 16-byte aligned.
+ * Replaces: code/lema/model.py:224-227 (`Block.gpu_pre`: norm1, q/k/v projections,
+ * pack_codes) in one GEMM.
+ */
+int lema_proj_codes_v(const void* x, const void* w_all, int64_t M, int64_t K, int64_t T,
+                      int hq, int hk, int d_qk, uint32_t* qcodes, uint32_t* kcodes,
+                      int64_t n_v, void* v_out, const float* row_scale, uint32_t* status,
+                      void* stream);
+
+/* out[m] = 1 / sqrt(mean over K of x[m][k]^2 + eps) for bf16 rows x[M][K] (K % 8 == 0),
+ * fp32 sums: the RMSNorm row scale. */
+int lema_row_rms(const void* x, int64_t M, int64_t K, float eps, float* out, void* stream);
+
 /* ---------------------------------------------- (b) prefill latest match */
 /*
  * Bytes of device workspace lema_prefill_match needs for n_streams x T

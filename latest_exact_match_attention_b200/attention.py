@@ -26,7 +26,7 @@ from . import _lib
 from ._lib import DTYPE_TAG, LemaError, call, ptr, require_cuda, stream_handle
 
 __all__ = ["pack_codes", "proj_codes", "latest_prev_match", "lema_hard", "prefill_match",
-           "prefill_match_host", "HostPrefill", "code_bytes_of"]
+           "prefill_match_host", "HostPrefill", "proj_codes_v", "row_rms", "code_bytes_of"]
 
 
 def code_bytes_of(codes: torch.Tensor) -> int:
@@ -96,6 +96,36 @@ def proj_codes(x: torch.Tensor, w_qk: torch.Tensor, hq: int, hk: int,
     call("lema_proj_codes", ptr(x), ptr(w_qk), B * T, dim, T, hq, hk, 32, ptr(qc), ptr(kc),
          ptr(status), stream_handle(dev))
     return qc, kc
+
+
+def row_rms(x: torch.Tensor, eps: float) -> torch.Tensor:
+    """1 / sqrt(mean(x^2, -1) + eps) per row of a bf16 [..., K] tensor, fp32 [rows]."""
+    dev = require_cuda(x)
+    x = x.contiguous()
+    K = x.shape[-1]
+    out = torch.empty(x.numel() // K, dtype=torch.float32, device=dev)
+    call("lema_row_rms", ptr(x), out.numel(), K, float(eps), ptr(out), stream_handle(dev))
+    return out
+
+
+def proj_codes_v(x: torch.Tensor, w_all: torch.Tensor, hq: int, hk: int, n_v: int,
+                 row_scale: torch.Tensor | None = None, status: torch.Tensor | None = None):
+    """Codes and values in one tcgen05 GEMM: `w_all` [(hq + hk) * 32 + n_v, dim] stacks the
+    query, key and value projection weights (bf16). Returns (qcodes [B, hq, T], kcodes
+    [B, hk, T], v [B, T, n_v] bf16 = row_scale * (x @ w_v.T))."""
+    dev = require_cuda(x, w_all, row_scale)
+    if x.dtype != torch.bfloat16 or w_all.dtype != torch.bfloat16:
+        raise LemaError("proj_codes_v takes bf16 x and w_all")
+    B, T, dim = x.shape
+    if w_all.shape != ((hq + hk) * 32 + n_v, dim):
+        raise LemaError(f"w_all {tuple(w_all.shape)} does not fit hq={hq}, hk={hk}, n_v={n_v}")
+    x, w_all = x.contiguous(), w_all.contiguous()
+    qc = torch.empty((B, hq, T), dtype=torch.int32, device=dev)
+    kc = torch.empty((B, hk, T), dtype=torch.int32, device=dev)
+    v = torch.empty((B, T, n_v), dtype=torch.bfloat16, device=dev)
+    call("lema_proj_codes_v", ptr(x), ptr(w_all), B * T, dim, T, hq, hk, 32, ptr(qc), ptr(kc),
+         n_v, ptr(v), ptr(row_scale), ptr(status), stream_handle(dev))
+    return qc, kc, v
 
 
 def _workspace(nbytes: int, device) -> torch.Tensor | None:

@@ -21,6 +21,7 @@
 // status word; before the CTA exits, the producer waits (bounded again) for its copies in
 // flight, the MMA warp for its tensor-core work, and the TMEM is released.
 #include <cuda.h>  // CUtensorMap and its enums (types only; the encoder comes from the runtime)
+#include <cuda_bf16.h>
 #include <cuda_runtime.h>
 
 #include <algorithm>
@@ -63,6 +64,11 @@ struct Params {
   int k_blocks;
   int n_blocks;
   int hq, hk;
+  // optional value columns after the code heads: v_out[m][c] = bf16(row_scale[m] * z[m][c]),
+  // c < n_v (row_scale NULL: 1)
+  __nv_bfloat16* v_out;
+  const float* row_scale;
+  int n_v;
 };
 
 // ------------------------------------------------------------------ PTX wrappers
@@ -315,6 +321,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     const int quarter = warp & 3;  // a warp reads TMEM lanes 32 * (warp % 4) ... + 31
     const uint32_t lane_base = static_cast<uint32_t>(quarter * 32) << 16;
     const int n_heads = p.hq + p.hk;
+    const int n_groups = n_heads + (p.n_v + 31) / 32;  // 32-column groups: code heads, then values
     int acc = 0;
     uint32_t aph = 0;
     for (int64_t tile = blockIdx.x; tile < p.n_tiles; tile += gridDim.x) {
@@ -325,17 +332,42 @@ __global__ void __launch_bounds__(kThreads, 1)
       const bool live = m < p.M;
       const int64_t b = live ? m / p.T : 0;
       const int64_t t = live ? m - b * p.T : 0;
+      const float scale = (live && p.row_scale != nullptr) ? p.row_scale[m] : 1.0f;
       for (int j = 0; j < TL::kHeads; ++j) {
         const int h = h0 + j;
-        if (h >= n_heads) break;  // warp-uniform
+        if (h >= n_groups) break;  // warp-uniform
         uint32_t r[32];
         tmem_load32(tmem_base + lane_base + static_cast<uint32_t>(acc * BN + j * 32), r);
-        const uint32_t code = pack_signs(r);
-        if (live) {
-          if (h < p.hq)
-            p.qcodes[(b * p.hq + h) * p.T + t] = code;
-          else
-            p.kcodes[(b * p.hk + (h - p.hq)) * p.T + t] = code;
+        if (h < n_heads) {
+          const uint32_t code = pack_signs(r);
+          if (live) {
+            if (h < p.hq)
+              p.qcodes[(b * p.hq + h) * p.T + t] = code;
+            else
+              p.kcodes[(b * p.hk + (h - p.hq)) * p.T + t] = code;
+          }
+        } else if (live) {
+          // value columns: scaled, rounded to bf16, one row's 32 columns per thread
+          const int c0 = (h - n_heads) * 32;
+          __nv_bfloat16* dst = p.v_out + m * static_cast<int64_t>(p.n_v) + c0;
+          if (c0 + 32 <= p.n_v && (p.n_v % 8) == 0) {
+#pragma unroll
+            for (int q = 0; q < 4; ++q) {
+              uint4 w;
+              uint32_t* wp = reinterpret_cast<uint32_t*>(&w);
+#pragma unroll
+              for (int e = 0; e < 4; ++e) {
+                const __nv_bfloat162 pr = __floats2bfloat162_rn(__uint_as_float(r[8 * q + 2 * e]) * scale,
+                                                               __uint_as_float(r[8 * q + 2 * e + 1]) * scale);
+                wp[e] = *reinterpret_cast<const uint32_t*>(&pr);
+              }
+              reinterpret_cast<uint4*>(dst)[q] = w;
+            }
+          } else {
+#pragma unroll
+            for (int d = 0; d < 32; ++d)
+              if (c0 + d < p.n_v) dst[d] = __float2bfloat16_rn(__uint_as_float(r[d]) * scale);
+          }
         }
       }
       tc_fence_before();
@@ -399,9 +431,23 @@ int launch(const CUtensorMap& map_x, const CUtensorMap& map_w, const Params& prm
 
 }  // namespace k1
 
+int proj_codes_v(const void* x, const void* w_all, int64_t M, int64_t K, int64_t T, int hq, int hk, int d_qk,
+                 uint32_t* qcodes, uint32_t* kcodes, int64_t n_v, void* v_out, const float* row_scale,
+                 uint32_t* status, cudaStream_t stream);
+
 int proj_codes(const void* x, const void* w_qk, int64_t M, int64_t K, int64_t T, int hq, int hk, int d_qk,
                uint32_t* qcodes, uint32_t* kcodes, uint32_t* status, cudaStream_t stream) {
+  return proj_codes_v(x, w_qk, M, K, T, hq, hk, d_qk, qcodes, kcodes, 0, nullptr, nullptr, status, stream);
+}
+
+int proj_codes_v(const void* x, const void* w_all, int64_t M, int64_t K, int64_t T, int hq, int hk, int d_qk,
+                 uint32_t* qcodes, uint32_t* kcodes, int64_t n_v, void* v_out, const float* row_scale,
+                 uint32_t* status, cudaStream_t stream) {
   using namespace k1;
+  const void* w_qk = w_all;
+  if (n_v < 0 || n_v > (int64_t(1) << 20) || (n_v > 0 && v_out == nullptr))
+    return fail(LEMA_ERR_INVALID_ARGUMENT, "value columns: n_v = %lld (0 .. 2^20), v_out required", (long long)n_v);
+  if (n_v > 0 && !aligned(v_out, 16)) return fail(LEMA_ERR_INVALID_ARGUMENT, "v_out must be 16-byte aligned");
   if (d_qk != 32)
     return fail(LEMA_ERR_INVALID_ARGUMENT, "lema_proj_codes packs d_qk = 32 only (got %d); "
                 "use lema_pack_codes on a projected z for other widths", d_qk);
@@ -412,7 +458,7 @@ int proj_codes(const void* x, const void* w_qk, int64_t M, int64_t K, int64_t T,
   if (M % T != 0) return fail(LEMA_ERR_INVALID_ARGUMENT, "M = %lld rows is not whole sequences of T = %lld", (long long)M, (long long)T);
   if (M >= (int64_t(1) << 31) || K >= (int64_t(1) << 24) || hq + hk > (1 << 16))
     return fail(LEMA_ERR_INVALID_ARGUMENT, "shape too large (M=%lld K=%lld heads=%d)", (long long)M, (long long)K, hq + hk);
-  if (M == 0 || hq + hk == 0) return LEMA_OK;
+  if (M == 0 || hq + hk + n_v == 0) return LEMA_OK;
   if (x == nullptr || w_qk == nullptr) return fail(LEMA_ERR_INVALID_ARGUMENT, "null x or w_qk");
   if ((hq > 0 && qcodes == nullptr) || (hk > 0 && kcodes == nullptr))
     return fail(LEMA_ERR_INVALID_ARGUMENT, "null code output");
@@ -424,7 +470,7 @@ int proj_codes(const void* x, const void* w_qk, int64_t M, int64_t K, int64_t T,
   EncodeTiledFn enc = encode_tiled();
   if (enc == nullptr) return fail(LEMA_ERR_CUDA, "cuTensorMapEncodeTiled is not available from the driver");
 
-  const int64_t n_cols = static_cast<int64_t>(hq + hk) * 32;
+  const int64_t n_cols = static_cast<int64_t>(hq + hk) * 32 + n_v;
   // the widest tile that still gives every SM a tile; narrower tiles only for small M
   const int64_t m_blocks = (M + kBM - 1) / kBM;
   int bn = 256;
@@ -443,6 +489,9 @@ int proj_codes(const void* x, const void* w_qk, int64_t M, int64_t K, int64_t T,
   prm.hq = hq;
   prm.hk = hk;
   prm.k_blocks = static_cast<int>(K / kBK);
+  prm.v_out = static_cast<__nv_bfloat16*>(v_out);
+  prm.row_scale = row_scale;
+  prm.n_v = static_cast<int>(n_v);
   prm.n_blocks = static_cast<int>((n_cols + bn - 1) / bn);
   prm.n_tiles = m_blocks * prm.n_blocks;
   const int64_t grid = std::min<int64_t>(prm.n_tiles, dev->sms);
@@ -453,4 +502,51 @@ int proj_codes(const void* x, const void* w_qk, int64_t M, int64_t K, int64_t T,
   }
 }
 
+// RMS scale of each row: out[m] = 1 / sqrt(mean(x[m]^2) + eps), fp32 sums; one warp per row.
+__global__ void row_rms_kernel(const __nv_bfloat16* x, int64_t M, int64_t K, float eps, float* out) {
+  const int64_t warps = (int64_t(gridDim.x) * blockDim.x) >> 5;
+  const int lane = threadIdx.x & 31;
+  for (int64_t m = (blockIdx.x * int64_t(blockDim.x) + threadIdx.x) >> 5; m < M; m += warps) {
+    const uint4* row = reinterpret_cast<const uint4*>(x + m * K);
+    float acc = 0.f;
+    for (int64_t k = lane; k < K / 8; k += 32) {
+      const uint4 w = row[k];
+      const __nv_bfloat162* h = reinterpret_cast<const __nv_bfloat162*>(&w);
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        const float2 f = __bfloat1622float2(h[e]);
+        acc += f.x * f.x + f.y * f.y;
+      }
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) acc += __shfl_xor_sync(0xFFFFFFFFu, acc, o);
+    if (lane == 0) out[m] = rsqrtf(acc / static_cast<float>(K) + eps);
+  }
+}
+
+int row_rms(const void* x, int64_t M, int64_t K, float eps, float* out, cudaStream_t stream) {
+  if (M < 0 || K <= 0 || K % 8 != 0) return fail(LEMA_ERR_INVALID_ARGUMENT, "row_rms: K = %lld must be a positive multiple of 8", (long long)K);
+  if (M == 0) return LEMA_OK;
+  if (x == nullptr || out == nullptr || !aligned(x, 16)) return fail(LEMA_ERR_INVALID_ARGUMENT, "row_rms: null or unaligned pointer");
+  const DeviceInfo* dev = current_device_info();
+  if (dev == nullptr) return LEMA_ERR_CUDA;
+  const int64_t blocks = std::min<int64_t>((M + 7) / 8, int64_t(dev->sms) * 16);
+  row_rms_kernel<<<static_cast<unsigned>(blocks), 256, 0, stream>>>(static_cast<const __nv_bfloat16*>(x), M, K, eps, out);
+  LEMA_CUDA_TRY(cudaGetLastError());
+  return LEMA_OK;
+}
+
 }  // namespace lema
+
+extern "C" int lema_proj_codes_v(const void* x, const void* w_all, int64_t M, int64_t K, int64_t T, int hq, int hk,
+                                 int d_qk, uint32_t* qcodes, uint32_t* kcodes, int64_t n_v, void* v_out,
+                                 const float* row_scale, uint32_t* status, void* stream) {
+  lema::clear_error();
+  return lema::proj_codes_v(x, w_all, M, K, T, hq, hk, d_qk, qcodes, kcodes, n_v, v_out, row_scale, status,
+                            static_cast<cudaStream_t>(stream));
+}
+
+extern "C" int lema_row_rms(const void* x, int64_t M, int64_t K, float eps, float* out, void* stream) {
+  lema::clear_error();
+  return lema::row_rms(x, M, K, eps, out, static_cast<cudaStream_t>(stream));
+}

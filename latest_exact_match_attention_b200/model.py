@@ -28,7 +28,7 @@ import torch
 import torch.nn.functional as F
 from torch import nn
 
-from .attention import pack_codes, prefill_match, proj_codes
+from .attention import pack_codes, prefill_match, proj_codes, proj_codes_v, row_rms
 
 ATTN_KINDS = ("lema",)
 
@@ -112,6 +112,7 @@ class Attention(nn.Module):
         self.o_proj = nn.Linear(H * cfg.d_v, cfg.dim, bias=False)
         self.hard = True
         self._wqk = None        # (key, stacked [q_proj; k_proj] weight) for K1
+        self._wall = None       # (key, stacked norm-folded [q; k; v] weight) for fused K1
 
     def project(self, x):
         """[B, T, dim] -> query and key pre-activations and values, [B, H, T, d]."""
@@ -138,6 +139,36 @@ class Attention(nn.Module):
         if self._wqk is None or self._wqk[0] != key:
             self._wqk = (key, torch.cat([q.detach(), k.detach()], 0).contiguous())
         return self._wqk[1]
+
+    def stacked_all(self, norm_weight: torch.Tensor) -> torch.Tensor:
+        """[q_proj; k_proj; v_proj] weights, each column scaled by the preceding RMSNorm's
+        weight (the norm folded into the GEMM), rebuilt only when any of them changes."""
+        ws = (self.q_proj.weight, self.k_proj.weight, self.v_proj.weight, norm_weight)
+        key = tuple((w.data_ptr(), w._version) for w in ws)
+        if getattr(self, "_wall", None) is None or self._wall[0] != key:
+            g = norm_weight.detach().float()[None, :]
+            w = torch.cat([(w.detach().float() * g) for w in ws[:3]], 0).to(torch.bfloat16)
+            self._wall = (key, w.contiguous())
+        return self._wall[1]
+
+    def codes_fused(self, x, norm: nn.RMSNorm):
+        """gpu_pre in one GEMM from the UN-normalised x: codes of norm(x) and
+        v = v_proj(norm(x)), with norm1 folded into the weights and its row scale applied in
+        the epilogue (K1's value columns). Codes equal those of the unfused path wherever
+        |z| is not within rounding of 0; v agrees to bf16 rounding."""
+        B, T, _ = x.shape
+        c = self.cfg
+        r = row_rms(x, norm.eps if norm.eps is not None else torch.finfo(torch.float32).eps)
+        qc, kc, v = proj_codes_v(x, self.stacked_all(norm.weight), c.num_heads, c.num_heads,
+                                 c.num_heads * c.d_v, row_scale=r)
+        return qc, kc, v.view(B, T, c.num_heads, c.d_v).transpose(1, 2)
+
+    def exact(self, qc, kc, v):
+        """The exact op on codes and values: [B, H, T, d_v] retrieved rows (zeros on a miss)."""
+        B, H, T = qc.shape
+        vv = v.reshape(B * H, T, -1) if v.is_contiguous() else v.contiguous().view(B * H, T, -1)
+        _, y = prefill_match(qc.reshape(B * H, T), kc.reshape(B * H, T), vv, want_src=False)
+        return y.view(B, H, T, -1)
 
     def codes(self, x):
         """[B, T, dim] (normalised) -> (qcodes [B, H, T], kcodes [B, H, T], v [B, H, T, d_v]).
@@ -168,9 +199,15 @@ class Block(nn.Module):
         self.norm2 = nn.RMSNorm(cfg.dim, eps=cfg.norm_eps)
         self.mlp = SwiGLU(cfg.dim, cfg.dim_ff)
         self.seg = None
+        self.fused_pre = False
 
     def gpu_pre(self, x):
-        """Normalise, project and pack: the codes the store needs and the values."""
+        """Normalise, project and pack: the codes the store needs and the values. With
+        `fused_pre` (opt-in, Transformer.set_fused_pre) the norm and all three projections
+        are one tcgen05 GEMM; its codes can differ from the reference recipe's marginally
+        more often (the norm weight is rounded into the weights), so it is off by default."""
+        if self.fused_pre and self.attn._k1_ok(x) and self.norm1.weight is not None:
+            return self.attn.codes_fused(x, self.norm1)
         return self.attn.codes(self.norm1(x))
 
     def gpu_post(self, x, got):
@@ -183,8 +220,8 @@ class Block(nn.Module):
             pre, post = self.seg or (self.gpu_pre, self.gpu_post)
             qc, kc, v = pre(x)
             return post(x, store.exchange(qc, kc, v))
-        x = x + self.attn(self.norm1(x))
-        return x + self.mlp(self.norm2(x))
+        qc, kc, v = self.gpu_pre(x)           # the same codes and values as the store path
+        return self.gpu_post(x, self.attn.exact(qc, kc, v))
 
 
 class Transformer(nn.Module):
@@ -212,6 +249,12 @@ class Transformer(nn.Module):
 
     def lema_layers(self):
         return [b.attn for b in self.blocks]
+
+    def set_fused_pre(self, on: bool = True):
+        """gpu_pre as one GEMM from the un-normalised residual (norm1 folded in; see
+        Block.gpu_pre). Off by default."""
+        for b in self.blocks:
+            b.fused_pre = on
 
     def set_hard(self, hard: bool = True):
         if not hard:
