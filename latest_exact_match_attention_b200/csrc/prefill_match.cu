@@ -11,24 +11,20 @@
 //   mask[slot]   bit s set iff a key with that code occurs in step s (32 positions) of the
 //                current chunk
 // A chunk is 32 steps of 32 positions and three phases, all parallel:
-//   P1 (keys)    each key inserts its code into -- or finds it in -- the table (its SLOT) and
-//                sets its step's bit in mask[slot]. The step's warp then publishes the step's
-//                key slots BIT-SLICED: word b of the step's row is ballot(bit b of the lane's
-//                slot), plus a word of valid lanes.
+//   P1 (keys)    each key inserts its code into -- or finds it in -- the table (its SLOT), sets
+//                its step's bit in mask[slot], records its slot in the step's key-slot array
+//                and ORs its lane into the step's lane-set bucket of the slot (slot % 64).
 //   P2 (queries) each query looks its code up; no slot means no key of that code so far (-1).
-//                The key lanes of a step holding slot s are AND_b (s_b ? row[b] : ~row[b]): a
-//                handful of logic ops instead of 32 compares. If the query's own step holds the
-//                code (mask bit), those lanes below its own give the answer; otherwise the
-//                highest mask bit below its step names the latest earlier step holding the
-//                code, whose highest such lane is the answer; with no such step the answer is
-//                carry[slot]. Each key also reads mask[slot] to learn whether its step is the
-//                code's last in the chunk.
-//   P3 (the last key of each code in the chunk) carry[slot] = 1 + position; mask[slot] = 0.
-// Shared-memory atomics are kept uncontended: the step's ballots tell each key lane which
-// lanes share its slot, so one lane per slot and step sets the mask bit, and claims are
-// counted once per warp.
-// No warp-wide match instructions are used: on this part they cost far more than the table
-// traffic they would save.
+//                If the query's own step holds the code (mask bit), the highest lane below its
+//                own in the step's bucket whose recorded slot is the query's answers it;
+//                otherwise the highest mask bit below its step names the latest earlier step
+//                holding the code, whose highest such lane is the answer; with no such step the
+//                answer is carry[slot]. Each key also notes whether its step is the last of its
+//                slot in the chunk.
+//   P3 (the keys of each slot's last step) carry[slot] = max(carry, 1 + position) by an
+//                atomic max, mask[slot] = 0; every key clears its bucket for the next chunk.
+// Two slots sharing a bucket in one step only cost a second look; no warp-wide ballot or match
+// instruction is needed (on this part those cost far more than the table traffic).
 // All 32 warps of a CTA run the phases (one step each per chunk); CTA barriers separate them.
 // The value rows are copied by a separate kernel afterwards (see gather_kernel).
 //
