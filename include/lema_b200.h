@@ -118,6 +118,11 @@ int lema_proj_codes_v(const void* x, const void* w_all, int64_t M, int64_t K, in
  * fp32 sums: the RMSNorm row scale. */
 int lema_row_rms(const void* x, int64_t M, int64_t K, float eps, float* out, void* stream);
 
+/* SwiGLU activation on a fused gate/up GEMM output gu[M][2F] (gate columns first):
+ * out[m][f] = silu(gu[m][f]) * gu[m][F + f], fp32 inside, dtype LEMA_F32/BF16/F16.
+ * Replaces: the silu and product of code/lema/model.py:85-93 (`SwiGLU.forward`). */
+int lema_swiglu(const void* gu, int dtype, int64_t M, int64_t F, void* out, void* stream);
+
 /* ---------------------------------------------- (b) prefill latest match */
 /*
  * Bytes of device workspace lema_prefill_match needs for n_streams x T

@@ -28,6 +28,7 @@ import torch
 import torch.nn.functional as F
 from torch import nn
 
+from ._lib import DTYPE_TAG, call, ptr, stream_handle
 from .attention import pack_codes, prefill_match, proj_codes, proj_codes_v, row_rms
 
 ATTN_KINDS = ("lema",)
@@ -87,14 +88,38 @@ class ModelConfig:
 
 
 class SwiGLU(nn.Module):
+    """down(silu(gate(x)) * up(x)), parameters named as code/lema/model.py:85-93. On a GPU the
+    gate and up projections are one GEMM on their stacked weights and the activation is one
+    kernel (lema_swiglu); `forward(x, residual)` adds the residual inside the down GEMM."""
+
     def __init__(self, dim: int, dim_ff: int):
         super().__init__()
         self.gate = nn.Linear(dim, dim_ff, bias=False)
         self.up = nn.Linear(dim, dim_ff, bias=False)
         self.down = nn.Linear(dim_ff, dim, bias=False)
+        self._wgu = None
 
-    def forward(self, x):
-        return self.down(F.silu(self.gate(x)) * self.up(x))
+    def gate_up_weight(self) -> torch.Tensor:
+        g, u = self.gate.weight, self.up.weight
+        key = (g.data_ptr(), u.data_ptr(), g._version, u._version)
+        if self._wgu is None or self._wgu[0] != key:
+            self._wgu = (key, torch.cat([g.detach(), u.detach()], 0).contiguous())
+        return self._wgu[1]
+
+    def forward(self, x, residual=None):
+        if not x.is_cuda or x.dtype not in DTYPE_TAG:
+            y = self.down(F.silu(self.gate(x)) * self.up(x))
+            return y if residual is None else residual + y
+        lead, dim = x.shape[:-1], x.shape[-1]
+        x2 = x.reshape(-1, dim)
+        gu = x2 @ self.gate_up_weight().t()
+        Fd = self.gate.weight.shape[0]
+        act = torch.empty((x2.shape[0], Fd), dtype=x.dtype, device=x.device)
+        call("lema_swiglu", ptr(gu), DTYPE_TAG[x.dtype], x2.shape[0], Fd, ptr(act),
+             stream_handle(x.device))
+        w = self.down.weight.t()
+        y = act @ w if residual is None else torch.addmm(residual.reshape(-1, dim), act, w)
+        return y.view(*lead, dim)
 
 
 class Attention(nn.Module):
@@ -211,9 +236,13 @@ class Block(nn.Module):
         return self.attn.codes(self.norm1(x))
 
     def gpu_post(self, x, got):
-        """Merge the retrieved values and finish the layer."""
-        x = x + self.attn.merge(got)
-        return x + self.mlp(self.norm2(x))
+        """Merge the retrieved values and finish the layer: x + o_proj(merged heads) as one
+        GEMM with the residual added in, then x + mlp(norm2(x)) likewise."""
+        B, H, T, dv = got.shape
+        dim = x.shape[-1]
+        y = got.transpose(1, 2).reshape(B * T, H * dv)
+        x = torch.addmm(x.reshape(B * T, dim), y, self.attn.o_proj.weight.t()).view(B, T, dim)
+        return self.mlp(self.norm2(x), residual=x)
 
     def forward(self, x, store=None):
         if store is not None:

@@ -108,3 +108,17 @@ def test_graph_decoder_reproduces_eager(cuda, temperature, fused):
         toks = torch.cat(graph, 1)
         assert toks.min() >= 0 and toks.max() < m.cfg.vocab_size
         assert len(set(toks.flatten().tolist())) > 4      # fresh noise on every replay
+
+
+@pytest.mark.parametrize("dtype,tol", [(torch.float32, 1e-6), (torch.bfloat16, 1e-2)])
+def test_swiglu_mlp_matches_torch(cuda, dtype, tol):
+    from latest_exact_match_attention_b200.model import SwiGLU
+    torch.manual_seed(3)
+    mlp = SwiGLU(256, 640).to(cuda).to(dtype)
+    x = torch.randn(5, 7, 256, device=cuda).to(dtype)
+    r = torch.randn(5, 7, 256, device=cuda).to(dtype)
+    with torch.no_grad():
+        ref = (mlp.down((torch.nn.functional.silu(mlp.gate(x).float()) * mlp.up(x).float()).to(dtype))
+               .float() + r.float())
+        got = mlp(x, residual=r).float()
+    torch.testing.assert_close(got, ref, rtol=tol, atol=tol)
