@@ -6,7 +6,7 @@ import pytest
 import torch
 
 import oracle
-from latest_exact_match_attention_b200 import latest_prev_match, lema_hard, pack_codes, prefill_match
+from latest_exact_match_attention_b200 import latest_prev_match, lema_hard, pack_codes, prefill_match, synth
 from tests import golden_data as G
 
 pytestmark = pytest.mark.gpu
@@ -194,3 +194,17 @@ def test_lema_hard_dense(cuda, d_qk, dtype):
                             else v.cpu().view(torch.int16).view(B * H, T, dv).numpy())
     got = y.cpu() if dtype != torch.bfloat16 else y.cpu().view(torch.int16)
     np.testing.assert_array_equal(got.reshape(B * H, T, dv).numpy(), want)
+
+
+@pytest.mark.parametrize("N,T", [(400, 2048), (340, 8192)])
+def test_more_streams_than_one_matcher_wave(cuda, N, T):
+    # above one full wave of matcher CTAs (2 per SM) the first wave's rows are gathered on a
+    # side stream while the rest is matched; T > 6144 also runs the overflow kernel per wave
+    qc, kc = synth.code_streams(N, T, synth.CONFIG2, seed=N, config_id=2)
+    v = np.random.default_rng(N).integers(0, 1 << 16, size=(N, T, 8), dtype=np.uint16)
+    q = torch.from_numpy(qc.view(np.int32)).to(cuda)
+    k = torch.from_numpy(kc.view(np.int32)).to(cuda)
+    src, out = prefill_match(q, k, torch.from_numpy(v).to(cuda))
+    want = oracle.latest_prev_match(qc, kc)
+    assert np.array_equal(src.cpu().numpy(), want)
+    assert np.array_equal(out.cpu().numpy(), oracle.gather(want, v))
