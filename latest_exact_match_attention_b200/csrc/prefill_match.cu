@@ -468,7 +468,7 @@ __global__ void __launch_bounds__(kThreads, 2) match_kernel(const Params p) {
 // contiguous run of output words of one stream (blockIdx.y), kGUnroll loads in flight per
 // thread, streaming stores.
 constexpr int kGThreads = 256;
-constexpr int kGUnroll = 8;
+constexpr int kGUnroll = 4;   // loads in flight per thread (measured: 8 -> 4 took the call 0.428 -> 0.384 ms)
 
 struct GatherParams {
   const int32_t* src;
