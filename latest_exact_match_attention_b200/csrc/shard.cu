@@ -337,7 +337,7 @@ struct GatherParams {
   uint32_t* status;
 };
 
-constexpr int kGThreads = 256, kGUnroll = 8;
+constexpr int kGThreads = 256, kGUnroll = 4;  // as the prefill gather: 4 loads in flight measured best
 
 // Word-parallel, like the prefill gather: each CTA owns a run of output words of one head
 // (blockIdx.y), kGUnroll loads in flight per thread, consecutive lanes on consecutive words
