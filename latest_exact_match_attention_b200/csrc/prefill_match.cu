@@ -196,12 +196,31 @@ struct Table {
   }
   // One-bucket fast paths, branch-free in the common case; a full bucket or a lost claim race
   // falls back to the general probe.
+  // A code's own slot in its home bucket (hash bits the bucket index does not use). A code is
+  // placed there whenever that slot is free at its insertion, so most inserts and finds touch
+  // one slot; a free own slot also proves the code absent (slots are never freed in a stream).
+  __device__ static uint32_t own(uint32_t h, uint32_t b) { return b * kBucket + (h >> 29); }
   __device__ uint32_t insert_fast(CodeT c, uint32_t& claimed) {
+    static_assert(kBucket == 8, "own slot = top 3 hash bits");
     if (c == kFree) {
       claimed = atomicCAS(side, 0u, 1u) == 0u;
       return cap;
     }
-    const uint32_t b = home(c);
+    const uint32_t h = code_hash32(c);
+    const uint32_t b = h & bmask;
+    {
+      const uint32_t hs = own(h, b);
+      const CodeT cur = code[hs];
+      if (cur == c) return hs;
+      if (cur == kFree) {
+        const CodeT old = cas_code(code + hs, kFree, c);
+        if (old == kFree) {
+          claimed = 1;
+          return hs;
+        }
+        if (old == c) return hs;
+      }
+    }
     CodeT w[kBucket];
     load_bucket(code + b * kBucket, w);
     uint32_t eq = 0, fr = 0;
@@ -225,7 +244,13 @@ struct Table {
   }
   __device__ uint32_t find_fast(CodeT c) const {
     if (c == kFree) return *side ? cap : kNoSlot;
-    const uint32_t b = home(c);
+    const uint32_t h = code_hash32(c);
+    const uint32_t b = h & bmask;
+    {
+      const CodeT cur = code[own(h, b)];
+      if (cur == c) return own(h, b);
+      if (cur == kFree) return kNoSlot;
+    }
     CodeT w[kBucket];
     load_bucket(code + b * kBucket, w);
     uint32_t eq = 0, fr = 0;
