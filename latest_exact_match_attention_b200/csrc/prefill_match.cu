@@ -113,6 +113,7 @@ struct Table {
   uint32_t* side;   // 1 word
   uint32_t cap;
   uint32_t bmask;   // buckets - 1
+  uint32_t bshift;  // 32 - log2(buckets): the bucket is the top bits of mix(code)
 
   __host__ __device__ static constexpr size_t bytes(uint32_t slots) {
     return round_up16(slots * sizeof(CodeT)) + round_up16((slots + 1) * sizeof(CarryT)) +
@@ -121,6 +122,7 @@ struct Table {
   __device__ void init(void* base, uint32_t slots) {
     cap = slots;
     bmask = slots / kBucket - 1;
+    bshift = 32 - (31 - __clz(slots / kBucket));  // buckets: a power of two, >= 2
     unsigned char* b = static_cast<unsigned char*>(base);
     code = reinterpret_cast<CodeT*>(b);
     b += round_up16(slots * sizeof(CodeT));
@@ -138,7 +140,13 @@ struct Table {
     }
     if (tid == 0) *side = 0;
   }
-  __device__ uint32_t home(CodeT c) const { return code_hash32(c) & bmask; }
+  // Fibonacci (multiplicative) hashing: one multiply; the bucket is the product's top bits and
+  // the code's own slot in it the next three. Placement only, never results.
+  __device__ static uint32_t mix(uint32_t c) { return c * 0x9E3779B1u; }
+  __device__ static uint32_t mix(uint64_t c) {
+    return static_cast<uint32_t>((c * 0x9E3779B97F4A7C15ull) >> 32);
+  }
+  __device__ uint32_t home(CodeT c) const { return mix(c) >> bshift; }
   // Insert-or-find from the bucket contents `w` already loaded from `home(c)`; the general
   // probe (CAS races, full buckets) continues from there. Returns the slot, or kNoSlot when
   // every bucket was full.
@@ -196,18 +204,18 @@ struct Table {
   }
   // One-bucket fast paths, branch-free in the common case; a full bucket or a lost claim race
   // falls back to the general probe.
-  // A code's own slot in its home bucket (hash bits the bucket index does not use). A code is
+  // A code's own slot in its home bucket (hash bits below the bucket's). A code is
   // placed there whenever that slot is free at its insertion, so most inserts and finds touch
   // one slot; a free own slot also proves the code absent (slots are never freed in a stream).
-  __device__ static uint32_t own(uint32_t h, uint32_t b) { return b * kBucket + (h >> 29); }
+  __device__ uint32_t own(uint32_t h, uint32_t b) const { return b * kBucket + ((h >> (bshift - 3)) & 7u); }
   __device__ uint32_t insert_fast(CodeT c, uint32_t& claimed) {
-    static_assert(kBucket == 8, "own slot = top 3 hash bits");
+    static_assert(kBucket == 8, "own slot = 3 hash bits");
     if (c == kFree) {
       claimed = atomicCAS(side, 0u, 1u) == 0u;
       return cap;
     }
-    const uint32_t h = code_hash32(c);
-    const uint32_t b = h & bmask;
+    const uint32_t h = mix(c);
+    const uint32_t b = h >> bshift;
     {
       const uint32_t hs = own(h, b);
       const CodeT cur = code[hs];
@@ -244,8 +252,8 @@ struct Table {
   }
   __device__ uint32_t find_fast(CodeT c) const {
     if (c == kFree) return *side ? cap : kNoSlot;
-    const uint32_t h = code_hash32(c);
-    const uint32_t b = h & bmask;
+    const uint32_t h = mix(c);
+    const uint32_t b = h >> bshift;
     {
       const CodeT cur = code[own(h, b)];
       if (cur == c) return own(h, b);
