@@ -373,13 +373,12 @@ __global__ void __launch_bounds__(kThreads, 2) match_kernel(const Params p) {
         }
         // ---------------------------------------------- P1: keys into the table, step bits
         const int32_t base32 = static_cast<int32_t>(base);
-        uint32_t kslot[kPerLane], qslot[kPerLane];
+        uint32_t kslot[kPerLane];
 #pragma unroll
         for (int u = 0; u < kPerLane; ++u) {
           const int step = warp + u * kMatchWarps;
           const int i = step * 32 + lane;
           kslot[u] = kNoSlot;
-          qslot[u] = kNoSlot;
           if (step >= kSteps || step * 32 >= cnt) continue;  // uniform per warp
           const bool valid = i < cnt;
           uint32_t claimed = 0;
@@ -397,11 +396,6 @@ __global__ void __launch_bounds__(kThreads, 2) match_kernel(const Params p) {
           }
           const uint32_t nclaim = __popc(__ballot_sync(kFullMask, claimed != 0));
           if (lane == 0 && nclaim) atomicAdd(&s_used, nclaim);
-          // the query's slot, looked up after this step's own inserts: a code this step inserted
-          // is always found; a miss may be stale (another warp's concurrent insert) and is
-          // looked up again after the barrier
-          __syncwarp();
-          if (valid) qslot[u] = tab.find_fast(qr[u]);
         }
         match_barrier();
         if (s_ovf != 0 || (kSmemTable && s_used > overflow_limit<CodeT>())) {
@@ -416,8 +410,8 @@ __global__ void __launch_bounds__(kThreads, 2) match_kernel(const Params p) {
             if (step >= kSteps || step * 32 >= cnt) continue;  // uniform per warp
             const bool valid = i < cnt;
             if (kslot[u] != kNoSlot && (31 - __clz(tab.mask[kslot[u]])) == step) clast |= 1u << u;
-            uint32_t sl = qslot[u];
-            if (valid && sl == kNoSlot) sl = tab.find_fast(qr[u]);
+            // the query's slot, looked up once every key of the chunk is in the table
+            const uint32_t sl = valid ? tab.find_fast(qr[u]) : kNoSlot;
             int32_t a = -1;
             if (valid && sl != kNoSlot) {
               const uint32_t m = tab.mask[sl];
