@@ -151,6 +151,22 @@ int lema_prefill_match(const void* qcodes, const void* kcodes, int code_bytes,
                        void* stream);
 
 /*
+ * lema_prefill_match with strided value rows: stream n = b * heads + h (codes stay
+ * [n_streams][T]); value row t of stream n at values + b * v_sb + h * v_sh + t * v_st
+ * bytes, output row at out + b * o_sb + h * o_sh + t * o_st. This reads a projection's
+ * [B][T][H][d_v] output and writes the [B][T][H][d_v] rows the output projection takes,
+ * with no transposing copy either side. n_streams must be a multiple of heads.
+ * Replaces: code/lema/attention.py:150-158 on the transposed views of
+ * code/lema/model.py:168-180 (`project`, `merge`).
+ */
+int lema_prefill_match_strided(const void* qcodes, const void* kcodes, int code_bytes,
+                               int64_t n_streams, int64_t T, int32_t* src,
+                               const void* values, int64_t vbytes, void* out, int64_t heads,
+                               int64_t v_sb, int64_t v_sh, int64_t v_st, int64_t o_sb,
+                               int64_t o_sh, int64_t o_st, void* workspace,
+                               size_t workspace_bytes, uint32_t* status, void* stream);
+
+/*
  * lema_prefill_match_noalloc: lema_prefill_match without a workspace argument, for callers
  * that cannot allocate device memory -- a plugin that is handed only its input and output
  * tensors by a host engine owning all device memory, a C program with no device allocator,

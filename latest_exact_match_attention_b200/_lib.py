@@ -39,6 +39,8 @@ _SIGNATURES = {
     "lema_prefill_workspace_bytes": ([_I64, _I64, _I], _SZ),
     "lema_prefill_match": ([_P, _P, _I, _I64, _I64, _P, _P, _I64, _P, _P, _SZ, _P, _P], _I),
     "lema_prefill_match_noalloc": ([_P, _P, _I, _I64, _I64, _P, _P, _I64, _P, _P, _P], _I),
+    "lema_prefill_match_strided": ([_P, _P, _I, _I64, _I64, _P, _P, _I64, _P, _I64, _I64, _I64,
+                                    _I64, _I64, _I64, _I64, _P, _SZ, _P, _P], _I),
     "lema_store_exchange_seg": ([_P, _I64, _I64, _P, _P, _I, _P, _P, _I64, _I64, _I64, _P, _P,
                                  _P, _SZ, _I64, _I64, _P], _I),
     "lema_segment_workspace_bytes": ([_I64, _I64, _I], _SZ),

@@ -129,6 +129,41 @@ int lema_prefill_match(const void* qcodes, const void* kcodes, int code_bytes, i
   return lema::launch_match(m);
 }
 
+int lema_prefill_match_strided(const void* qcodes, const void* kcodes, int code_bytes, int64_t n_streams,
+                               int64_t T, int32_t* src, const void* values, int64_t vbytes, void* out,
+                               int64_t heads, int64_t v_sb, int64_t v_sh, int64_t v_st, int64_t o_sb,
+                               int64_t o_sh, int64_t o_st, void* workspace, size_t workspace_bytes,
+                               uint32_t* status, void* stream) {
+  lema::clear_error();
+  if (heads < 1 || (n_streams > 0 && n_streams % heads != 0))
+    return lema::fail(LEMA_ERR_INVALID_ARGUMENT, "streams (%lld) must be whole groups of heads (%lld)",
+                      (long long)n_streams, (long long)heads);
+  if (v_sb < 0 || v_sh < 0 || v_st < 0 || o_sb < 0 || o_sh < 0 || o_st < 0)
+    return lema::fail(LEMA_ERR_INVALID_ARGUMENT, "negative stride");
+  lema::MatchLaunch m;
+  m.qc = qcodes;
+  m.kc = kcodes;
+  m.code_bytes = code_bytes;
+  m.N = n_streams;
+  m.T = T;
+  m.src = src;
+  m.v = values;
+  m.vbytes = vbytes;
+  m.out = out;
+  m.heads = heads;
+  m.v_sb = v_sb;
+  m.v_sh = v_sh;
+  m.v_st = v_st;
+  m.o_sb = o_sb;
+  m.o_sh = o_sh;
+  m.o_st = o_st;
+  m.ws = workspace;
+  m.ws_bytes = workspace_bytes;
+  m.status = status;
+  m.stream = static_cast<cudaStream_t>(stream);
+  return lema::launch_match(m);
+}
+
 int64_t lema_store_slot_bytes(int64_t vbytes) { return lema::store_slot_bytes(vbytes); }
 
 size_t lema_store_workspace_bytes(int64_t n, int64_t T, int code_bytes) {

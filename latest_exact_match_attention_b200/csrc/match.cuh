@@ -21,6 +21,9 @@ struct MatchLaunch {
   void* lt_code = nullptr;
   int32_t* lt_pos = nullptr;
   int32_t* lt_count = nullptr;
+  // optional strided value rows (heads > 0): row (n, t) at v + (n / heads) * v_sb +
+  // (n % heads) * v_sh + t * v_st bytes, out likewise; heads = 0: [N][T] rows of vbytes
+  int64_t heads = 0, v_sb = 0, v_sh = 0, v_st = 0, o_sb = 0, o_sh = 0, o_st = 0;
   void* ws = nullptr;
   size_t ws_bytes = 0;
   uint32_t* status = nullptr;

@@ -502,6 +502,9 @@ struct GatherParams {
   const unsigned char* v;
   unsigned char* out;
   int64_t N, T;
+  // row (n, t) of the values at v + (n / heads) * v_sb + (n % heads) * v_sh + t * v_st, of the
+  // output likewise (bytes); a plain [N][T] layout is heads = 1, sb = T * row, st = row
+  int64_t heads, v_sb, v_sh, v_st, o_sb, o_sh, o_st;
   uint32_t wpr;        // vector words per row
   uint32_t words;      // words per stream = T * wpr (< 2^32)
   int div_shift;       // log2(wpr) when a power of two, else -1
@@ -513,24 +516,30 @@ __global__ void __launch_bounds__(kGThreads) gather_kernel(const GatherParams g)
   const uint32_t w0 = blockIdx.x * (kGThreads * kGUnroll) + threadIdx.x;
   for (int64_t n = blockIdx.y; n < g.N; n += gridDim.y) {
     const int32_t* src = g.src + n * g.T;
-    const Vec* v = reinterpret_cast<const Vec*>(g.v) + n * static_cast<int64_t>(g.words);
-    Vec* o = reinterpret_cast<Vec*>(g.out) + n * static_cast<int64_t>(g.words);
+    const int64_t b = n / g.heads, h = n - b * g.heads;
+    const unsigned char* v = g.v + b * g.v_sb + h * g.v_sh;
+    unsigned char* o = g.out + b * g.o_sb + h * g.o_sh;
     Vec val[kGUnroll];
+    uint32_t row[kGUnroll], col[kGUnroll];
 #pragma unroll
     for (int u = 0; u < kGUnroll; ++u) {
       const uint32_t w = w0 + u * kGThreads;
       val[u] = zero_vec<Vec>();
+      row[u] = 0;
+      col[u] = 0;
       if (w < g.words) {
         const uint32_t r = g.div_shift >= 0 ? (w >> g.div_shift)
                                             : (g.div_magic ? __umulhi(w, g.div_magic) : w / g.wpr);
+        row[u] = r;
+        col[u] = w - r * g.wpr;
         const int32_t s = __ldg(src + r);
-        if (s >= 0) val[u] = __ldg(v + static_cast<int64_t>(s) * g.wpr + (w - r * g.wpr));
+        if (s >= 0) val[u] = __ldg(reinterpret_cast<const Vec*>(v + s * g.v_st) + col[u]);
       }
     }
 #pragma unroll
     for (int u = 0; u < kGUnroll; ++u) {
       const uint32_t w = w0 + u * kGThreads;
-      if (w < g.words) store_stream(o + w, val[u]);
+      if (w < g.words) store_stream(reinterpret_cast<Vec*>(o + row[u] * g.o_st) + col[u], val[u]);
     }
   }
 }
@@ -543,6 +552,16 @@ int launch_gather(const MatchLaunch& a, const int32_t* src) {
   g.out = static_cast<unsigned char*>(a.out);
   g.N = a.N;
   g.T = a.T;
+  if (a.heads > 0) {
+    g.heads = a.heads;
+    g.v_sb = a.v_sb; g.v_sh = a.v_sh; g.v_st = a.v_st;
+    g.o_sb = a.o_sb; g.o_sh = a.o_sh; g.o_st = a.o_st;
+  } else {
+    g.heads = 1;
+    g.v_sb = g.o_sb = a.T * a.vbytes;
+    g.v_sh = g.o_sh = 0;
+    g.v_st = g.o_st = a.vbytes;
+  }
   const uint64_t wpr = static_cast<uint64_t>(a.vbytes) / sizeof(Vec);
   const uint64_t words = static_cast<uint64_t>(a.T) * wpr;
   if (words >= (uint64_t(1) << 32)) return fail(LEMA_ERR_INVALID_ARGUMENT, "T * row words = %llu exceeds 2^32", (unsigned long long)words);
@@ -564,9 +583,11 @@ int launch_gather(const MatchLaunch& a, const int32_t* src) {
 }
 
 int run_gather(const MatchLaunch& a, const int32_t* src) {
-  const bool a16 = a.vbytes % 16 == 0 && aligned(a.v, 16) && aligned(a.out, 16);
-  const bool a8 = a.vbytes % 8 == 0 && aligned(a.v, 8) && aligned(a.out, 8);
-  const bool a4 = a.vbytes % 4 == 0 && aligned(a.v, 4) && aligned(a.out, 4);
+  // every row must start on the vector boundary: pointers, row size and (strided) strides
+  const uint64_t st = a.heads > 0 ? static_cast<uint64_t>(a.v_sb | a.v_sh | a.v_st | a.o_sb | a.o_sh | a.o_st) : 0;
+  const bool a16 = a.vbytes % 16 == 0 && st % 16 == 0 && aligned(a.v, 16) && aligned(a.out, 16);
+  const bool a8 = a.vbytes % 8 == 0 && st % 8 == 0 && aligned(a.v, 8) && aligned(a.out, 8);
+  const bool a4 = a.vbytes % 4 == 0 && st % 4 == 0 && aligned(a.v, 4) && aligned(a.out, 4);
   if (a16) return launch_gather<uint4>(a, src);
   if (a8) return launch_gather<uint2>(a, src);
   if (a4) return launch_gather<uint32_t>(a, src);

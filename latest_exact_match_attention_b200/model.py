@@ -28,6 +28,7 @@ import torch
 import torch.nn.functional as F
 from torch import nn
 
+from . import _lib
 from ._lib import DTYPE_TAG, call, ptr, stream_handle
 from .attention import pack_codes, prefill_match, proj_codes, proj_codes_v, row_rms
 
@@ -189,11 +190,24 @@ class Attention(nn.Module):
         return qc, kc, v.view(B, T, c.num_heads, c.d_v).transpose(1, 2)
 
     def exact(self, qc, kc, v):
-        """The exact op on codes and values: [B, H, T, d_v] retrieved rows (zeros on a miss)."""
+        """The exact op on codes and values: [B, H, T, d_v] retrieved rows (zeros on a miss),
+        as a transposed view of [B, T, H, d_v] memory -- what `merge` reads without a copy.
+        v may be any [B, H, T, d_v] view with unit last stride (the projection's transposed
+        output): the gather reads it in place."""
         B, H, T = qc.shape
-        vv = v.reshape(B * H, T, -1) if v.is_contiguous() else v.contiguous().view(B * H, T, -1)
-        _, y = prefill_match(qc.reshape(B * H, T), kc.reshape(B * H, T), vv, want_src=False)
-        return y.view(B, H, T, -1)
+        dv = v.shape[-1]
+        if v.stride(-1) != 1:
+            v = v.contiguous()
+        es = v.element_size()
+        out = torch.empty((B, T, H, dv), dtype=v.dtype, device=v.device)
+        q2, k2 = qc.reshape(B * H, T).contiguous(), kc.reshape(B * H, T).contiguous()
+        cb = 4 if q2.dtype == torch.int32 else 8
+        nb = int(_lib.lib().lema_prefill_workspace_bytes(B * H, T, cb))
+        ws = torch.empty(nb, dtype=torch.uint8, device=v.device) if nb else None
+        call("lema_prefill_match_strided", ptr(q2), ptr(k2), cb, B * H, T, None, ptr(v), dv * es,
+             ptr(out), H, v.stride(0) * es, v.stride(1) * es, v.stride(2) * es,
+             T * H * dv * es, dv * es, H * dv * es, ptr(ws), nb, None, stream_handle(v.device))
+        return out.transpose(1, 2)
 
     def codes(self, x):
         """[B, T, dim] (normalised) -> (qcodes [B, H, T], kcodes [B, H, T], v [B, H, T, d_v]).
