@@ -307,11 +307,14 @@ def run_b200(args):
     achieved = alg_bytes / (per_launch_ms / 1e3) / 1e9
     # DRAM bytes per call of the three kernels, from the full-size ncu capture summarised in
     # profiles/ (only meaningful for the default 512-stream workload)
+    # K2 runs pipelined (one launch matches and copies rows) unless LEMA_K2_PIPELINE=0
+    pipelined = os.environ.get("LEMA_K2_PIPELINE", "")[:1] != "0"
     traffic = None
     tf = ROOT / "profiles" / "prefill_match_cfg2.md"
     if tf.exists() and N_STREAMS == 512:
         import re
-        m = re.search(r"traffic_bytes_per_call:\s*(\d+)", tf.read_text())
+        key = "traffic_bytes_per_call_pipelined" if pipelined else "traffic_bytes_per_call"
+        m = re.search(key + r":\s*(\d+)", tf.read_text())
         traffic = int(m.group(1)) if m else None
     if world > 1:
         import torch.distributed as dist
@@ -326,7 +329,8 @@ def run_b200(args):
         "config": {"workload": WORKLOAD, "streams_per_gpu": N_STREAMS, "positions_per_gpu": n_pos,
                    "seq_len": T, "value_bytes": VBYTES, "parallelism": f"streams x{world}, no collective",
                    "l2": "inputs+outputs 0.9 GB > 126 MB L2 (no flush)", "hit_rate": round(hit_rate, 4),
-                   "distinct_sources": U},
+                   "distinct_sources": U,
+                   "k2_mode": "pipelined" if pipelined else "two-kernel"},
         "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
                      "frac": round(achieved / peak, 4), "traffic": traffic,
                      "peak_source": peak_src, "alg_bytes_per_launch": alg_bytes,
@@ -334,10 +338,10 @@ def run_b200(args):
         "e2e": {"value": e2e_value and round(e2e_value, 2), "unit": UNIT, "h2d_bytes_per_step": h2d,
                 "d2h_bytes_per_step": d2h, "steps": e2e_steps},
         "cpu_baseline": cpu,
-        # per step: the shared-memory match kernel, the overflow-path kernel (launched whenever a
-        # stream could outgrow the shared table, T > 6144; it exits at once when none did) and
-        # the value gather kernel
-        "gpu_launches": args.steps * (3 if T > 6144 else 2),
+        # per step: the shared-memory match kernel (pipelined: it also copies the rows), the
+        # overflow-path kernel (launched whenever a stream could outgrow the shared table,
+        # T > 6144; it exits at once when none did) and, two-kernel path only, the row gather
+        "gpu_launches": args.steps * ((1 if pipelined else 2) + (1 if T > 6144 else 0)),
         "clocks": clocks,
     }
     print(json.dumps(line), flush=True)

@@ -128,7 +128,10 @@ int lema_swiglu(const void* gu, int dtype, int64_t M, int64_t F, void* out, void
  * Bytes of device workspace lema_prefill_match needs for n_streams x T
  * positions: room for the indices (used when src is NULL) plus, when a stream can
  * hold more distinct key codes than the on-chip table takes, the overflow-path
- * tables. 256-byte aligned workspace required.
+ * tables, plus the control words (4 KiB + 4 bytes per stream) of the pipelined
+ * mode, in which one launch matches and copies the value rows at once. A smaller
+ * workspace that still holds the first two runs the matcher and the row copy as
+ * two kernels: the same results. 256-byte aligned workspace required.
  */
 size_t lema_prefill_workspace_bytes(int64_t n_streams, int64_t T, int code_bytes);
 

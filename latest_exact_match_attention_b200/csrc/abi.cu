@@ -105,7 +105,7 @@ int lema_proj_codes(const void* x, const void* w_qk, int64_t M, int64_t K, int64
 }
 
 size_t lema_prefill_workspace_bytes(int64_t n_streams, int64_t T, int code_bytes) {
-  return lema::match_workspace_bytes(n_streams, T, code_bytes);
+  return lema::match_workspace_bytes(n_streams, T, code_bytes, true, true);
 }
 
 int lema_prefill_match(const void* qcodes, const void* kcodes, int code_bytes, int64_t n_streams,

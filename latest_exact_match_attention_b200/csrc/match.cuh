@@ -30,8 +30,10 @@ struct MatchLaunch {
   cudaStream_t stream = nullptr;
 };
 
-// need_src = false: the caller passes src, so no index scratch is counted.
-size_t match_workspace_bytes(int64_t N, int64_t T, int code_bytes, bool need_src = true);
+// need_src = false: the caller passes src, so no index scratch is counted. pipe = true also
+// counts the pipelined mode's control words (calls that gather rows; without them such a
+// call takes the two-kernel path).
+size_t match_workspace_bytes(int64_t N, int64_t T, int code_bytes, bool need_src = true, bool pipe = false);
 int launch_match(const MatchLaunch& a);
 
 }  // namespace lema

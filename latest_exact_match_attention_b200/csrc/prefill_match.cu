@@ -26,7 +26,9 @@
 // Two slots sharing a bucket in one step only cost a second look; no warp-wide ballot or match
 // instruction is needed (on this part those cost far more than the table traffic).
 // All 32 warps of a CTA run the phases (one step each per chunk); CTA barriers separate them.
-// The value rows are copied by a separate kernel afterwards (see gather_kernel).
+// The value rows are copied by CTAs on other SMs of the same launch as the matchers publish
+// their progress (the pipelined mode, below), or by a separate kernel afterwards
+// (gather_kernel: the two-kernel path).
 //
 // The table is bucketed: 8 slots per bucket, read with vector loads, linear probing over
 // buckets; a claim is one compare-and-swap of a free code word (all ones), and the all-ones
@@ -40,6 +42,7 @@
 #include <cuda_runtime.h>
 
 #include <algorithm>
+#include <cstdlib>
 #include <cstring>
 #include <mutex>
 #include <type_traits>
@@ -283,6 +286,41 @@ struct Table {
 };
 
 // ---------------------------------------------------------------- the kernel
+// Rows to gather: out[n][i] = v[n][src[n][i]] (zeros where src is -1), in Vec words.
+struct GatherParams {
+  const int32_t* src;
+  const unsigned char* v;
+  unsigned char* out;
+  int64_t N, T;
+  // row (n, t) of the values at v + (n / heads) * v_sb + (n % heads) * v_sh + t * v_st, of the
+  // output likewise (bytes); a plain [N][T] layout is heads = 1, sb = T * row, st = row
+  int64_t heads, v_sb, v_sh, v_st, o_sb, o_sh, o_st;
+  uint32_t wpr;        // vector words per row
+  uint32_t words;      // words per stream = T * wpr (< 2^32)
+  int div_shift;       // log2(wpr) when a power of two, else -1
+  uint32_t div_magic;  // floor(2^32 / wpr) + 1 when exact for every word index, else 0
+};
+
+// Pipelined mode: ONE launch matches and gathers. The CTAs of the first `match_sms` SMs to
+// start match streams (taken from a counter, so they run in claim order); the other SMs' CTAs
+// copy value rows of the positions already matched, a unit (kUnitChunks chunks of one stream)
+// at a time, as the matchers publish their progress; a matcher with no stream left turns to
+// the rows too. The row traffic then overlaps the issue-bound matching, and the two never
+// share an SM (value loads beside a shared-memory table slow every table access).
+constexpr int kUnitChunks = 4;                    // chunks per gather unit and per publication
+constexpr uint32_t kProgOvf = 0x80000000u;        // progress word of a stream handed to the overflow path
+constexpr int kMaxSmIds = 512;                    // %smid values with a role slot
+constexpr uint32_t kRoleMatch = 1, kRoleGather = 2;
+constexpr unsigned long long kWaitNs = 4000000000ull;  // a wait for a unit gives up after 4 s
+struct PipeCtl {
+  uint32_t sm_seen[kMaxSmIds];  // CTAs started per SM
+  uint32_t sm_role[kMaxSmIds];  // the role of each SM, set by its first CTA
+  uint32_t sm_ticket;           // SMs seen
+  uint32_t next_stream;         // streams claimed by matchers
+  uint32_t next_unit;           // gather units claimed
+  uint32_t failed;              // a wait ran out: every later wait gives up at once
+};
+
 struct Params {
   const void* qc;
   const void* kc;
@@ -300,7 +338,67 @@ struct Params {
   int64_t gtable_bytes;
   uint32_t gslots;
   int list_mode;  // global path: 1 = streams from ovf_list, 0 = all streams
+  // pipelined mode (zeroed control block and per-stream progress in the workspace)
+  PipeCtl* ctl;
+  uint32_t* progress;     // [N]: chunks matched and published, or kProgOvf
+  uint32_t match_sms;     // SMs whose CTAs match
+  uint32_t wave;          // streams matched at once: the gather units' order
+  int gather_inline;      // overflow path: gather each stream right after matching it
+  GatherParams g;         // uint4 words (pipelined and inline gathers)
 };
+
+__device__ __forceinline__ void st_release(uint32_t* p, uint32_t v) {
+  asm volatile("st.release.gpu.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+__device__ __forceinline__ uint32_t ld_acquire(const uint32_t* p) {
+  uint32_t v;
+  asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+  return v;
+}
+__device__ __forceinline__ void prefetch_l2(const void* p) {
+  asm volatile("prefetch.global.L2 [%0];" ::"l"(p));
+}
+__device__ __forceinline__ unsigned long long global_ns() {
+  unsigned long long t;
+  asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+  return t;
+}
+
+// Rows [t0, t1) of stream n by the kThr threads of a CTA, kGUnroll loads in flight per thread.
+// The indices come through L2 (__ldcg): other CTAs of the same launch may have written them.
+constexpr int kGUnroll = 4;   // loads in flight per thread (measured: 8 -> 4 took the call 0.428 -> 0.384 ms)
+template <typename Vec, int kThr>
+__device__ __forceinline__ void gather_span(const GatherParams& g, int64_t n, uint32_t t0, uint32_t t1,
+                                            int tid) {
+  const int32_t* src = g.src + n * g.T;
+  const int64_t b = n / g.heads, h = n - b * g.heads;
+  const unsigned char* v = g.v + b * g.v_sb + h * g.v_sh;
+  unsigned char* o = g.out + b * g.o_sb + h * g.o_sh;
+  const uint32_t w_end = t1 * g.wpr;
+  for (uint32_t w0 = t0 * g.wpr + tid; w0 < w_end; w0 += kThr * kGUnroll) {
+    Vec val[kGUnroll];
+#pragma unroll
+    for (int u = 0; u < kGUnroll; ++u) {
+      const uint32_t w = w0 + u * kThr;
+      val[u] = zero_vec<Vec>();
+      if (w < w_end) {
+        const uint32_t r = g.div_shift >= 0 ? (w >> g.div_shift)
+                                            : (g.div_magic ? __umulhi(w, g.div_magic) : w / g.wpr);
+        const int32_t s = __ldcg(src + r);
+        if (s >= 0) val[u] = __ldg(reinterpret_cast<const Vec*>(v + s * g.v_st) + (w - r * g.wpr));
+      }
+    }
+#pragma unroll
+    for (int u = 0; u < kGUnroll; ++u) {
+      const uint32_t w = w0 + u * kThr;
+      if (w < w_end) {
+        const uint32_t r = g.div_shift >= 0 ? (w >> g.div_shift)
+                                            : (g.div_magic ? __umulhi(w, g.div_magic) : w / g.wpr);
+        store_stream(reinterpret_cast<Vec*>(o + r * g.o_st) + (w - r * g.wpr), val[u]);
+      }
+    }
+  }
+}
 
 // Per step of a chunk, two small shared arrays replace any warp-wide matching:
 //   ls[step][b]   bit j set iff key lane j of the step holds a slot with (slot % kLsBuckets) == b
@@ -322,7 +420,135 @@ __device__ __forceinline__ int lane_with_slot(uint32_t cand, const uint32_t* ks,
 __device__ __forceinline__ void match_barrier() { __syncthreads(); }
 
 
-template <typename CodeT, bool kSmemTable>
+__device__ __forceinline__ void cp_async16(void* smem_dst, const void* gsrc, bool fill) {
+  const uint32_t d = static_cast<uint32_t>(__cvta_generic_to_shared(smem_dst));
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(d), "l"(gsrc), "r"(fill ? 16 : 0)
+               : "memory");
+}
+
+// Rows [t0, t1) of stream n through this CTA's shared memory (kThreads threads; `buf` holds
+// `rows_per_pass` <= 2 * kThreads rows): every thread fetches its rows of a pass with
+// asynchronous 16-byte copies (zero fill on a miss), so a pass keeps the whole buffer in
+// flight without holding registers; the indices of the next pass load meanwhile; then the
+// CTA writes the pass out with coalesced streaming stores. A CTA whose table is idle (a
+// row-copying CTA, or a matcher with no stream left) lends its shared memory to this.
+__device__ void gather_unit_staged(const GatherParams& g, int64_t n, uint32_t t0, uint32_t t1, int tid,
+                                   uint4* buf, uint32_t rows_per_pass) {
+  const int32_t* src = g.src + n * g.T;
+  const int64_t b = n / g.heads, h = n - b * g.heads;
+  const unsigned char* v = g.v + b * g.v_sb + h * g.v_sh;
+  unsigned char* o = g.out + b * g.o_sb + h * g.o_sh;
+  const uint32_t wpr = g.wpr;
+  int32_t s0 = -1, s1 = -1;  // indices of this thread's two rows of the coming pass
+  {
+    const uint32_t lim = min(t1, t0 + rows_per_pass);
+    if (t0 + tid < lim) s0 = __ldcg(src + t0 + tid);
+    if (t0 + kThreads + tid < lim) s1 = __ldcg(src + t0 + kThreads + tid);
+  }
+  for (uint32_t r0 = t0; r0 < t1; r0 += rows_per_pass) {
+    const uint32_t cnt = min(rows_per_pass, t1 - r0);
+    if (static_cast<uint32_t>(tid) < cnt) {
+      const unsigned char* row = v + static_cast<int64_t>(max(s0, 0)) * g.v_st;
+      for (uint32_t c = 0; c < wpr; ++c) cp_async16(buf + tid * wpr + c, row + 16 * c, s0 >= 0);
+    }
+    if (static_cast<uint32_t>(kThreads + tid) < cnt) {
+      const unsigned char* row = v + static_cast<int64_t>(max(s1, 0)) * g.v_st;
+      for (uint32_t c = 0; c < wpr; ++c) cp_async16(buf + (kThreads + tid) * wpr + c, row + 16 * c, s1 >= 0);
+    }
+    asm volatile("cp.async.commit_group;" ::: "memory");
+    const uint32_t r1 = r0 + rows_per_pass;
+    s0 = s1 = -1;
+    if (r1 < t1) {
+      const uint32_t lim = min(t1, r1 + rows_per_pass);
+      if (r1 + tid < lim) s0 = __ldcg(src + r1 + tid);
+      if (r1 + kThreads + tid < lim) s1 = __ldcg(src + r1 + kThreads + tid);
+    }
+    asm volatile("cp.async.wait_all;" ::: "memory");
+    __syncthreads();
+    for (uint32_t w = tid; w < cnt * wpr; w += kThreads) {
+      const uint32_t r = g.div_shift >= 0 ? (w >> g.div_shift)
+                                          : (g.div_magic ? __umulhi(w, g.div_magic) : w / wpr);
+      store_stream(reinterpret_cast<uint4*>(o + static_cast<int64_t>(r0 + r) * g.o_st) + (w - r * wpr), buf[w]);
+    }
+    __syncthreads();  // the buffer is refilled by the next pass
+  }
+}
+
+// Pipelined mode: this CTA's role, the same for both CTAs of an SM (the first to start on an
+// SM draws it: the first match_sms SMs match).
+__device__ uint32_t pipe_role(const Params& p, int tid) {
+  __shared__ uint32_t s_role;
+  if (tid == 0) {
+    uint32_t smid;
+    asm volatile("mov.u32 %0, %%smid;" : "=r"(smid));
+    uint32_t role = kRoleMatch;
+    if (smid < static_cast<uint32_t>(kMaxSmIds)) {
+      if (atomicAdd(&p.ctl->sm_seen[smid], 1u) == 0u) {
+        role = atomicAdd(&p.ctl->sm_ticket, 1u) < p.match_sms ? kRoleMatch : kRoleGather;
+        st_release(&p.ctl->sm_role[smid], role);
+      } else {
+        // the SM's first CTA publishes its role right after drawing it
+        uint32_t r = 0;
+        const unsigned long long t0 = global_ns();
+        while ((r = ld_acquire(&p.ctl->sm_role[smid])) == 0u && global_ns() - t0 < 1000000ull) __nanosleep(64);
+        role = r != 0u ? r : kRoleMatch;
+      }
+    }
+    s_role = role;
+  }
+  __syncthreads();
+  return s_role;
+}
+
+// Pipelined mode: gather units until none is left. Unit u covers kUnitChunks chunks of one
+// stream; units are numbered wave by wave (streams [k * wave, (k + 1) * wave) are matched at
+// about the same time), chunk group by chunk group, so a unit's turn comes about when its
+// rows are matched. A unit waits for its stream's published progress (bounded); a stream
+// handed to the overflow path is gathered there.
+__device__ void pipe_gather(const Params& p, int tid, uint4* buf, uint32_t rows_per_pass) {
+  __shared__ uint32_t s_n, s_t0, s_t1;
+  __shared__ int s_go;
+  const uint32_t n_chunks = static_cast<uint32_t>((p.T + kChunk - 1) / kChunk);
+  const uint32_t ng = (n_chunks + kUnitChunks - 1) / kUnitChunks;
+  const uint32_t N = static_cast<uint32_t>(p.N);
+  const uint32_t total = N * ng;  // < 2^31 (host)
+  for (;;) {
+    if (tid == 0) {
+      const uint32_t u = atomicAdd(&p.ctl->next_unit, 1u);
+      s_go = -1;
+      if (u < total) {
+        const uint32_t full = p.wave * ng;
+        const uint32_t blk = u / full, rem = u - blk * full;
+        const uint32_t n0 = blk * p.wave, bsz = min(p.wave, N - n0);
+        const uint32_t cg = rem / bsz, n = n0 + (rem - cg * bsz);
+        const uint32_t need = min((cg + 1) * kUnitChunks, n_chunks);
+        uint32_t v = ld_acquire(p.progress + n);
+        if (v < need) {
+          const unsigned long long t0 = global_ns();
+          while ((v = ld_acquire(p.progress + n)) < need) {
+            if (ld_acquire(&p.ctl->failed) != 0u || global_ns() - t0 > kWaitNs) {
+              atomicExch(&p.ctl->failed, 1u);
+              raise_status(p.status, LEMA_STATUS_PROBE_LIMIT);
+              break;
+            }
+            __nanosleep(256);
+          }
+        }
+        s_go = (v >= need && (v & kProgOvf) == 0u) ? 1 : 0;
+        s_n = n;
+        s_t0 = cg * kUnitChunks * kChunk;
+        s_t1 = static_cast<uint32_t>(min(static_cast<int64_t>(need) * kChunk, p.T));
+      }
+    }
+    __syncthreads();
+    const int go = s_go;
+    if (go < 0) break;
+    if (go) gather_unit_staged(p.g, s_n, s_t0, s_t1, tid, buf, rows_per_pass);
+    __syncthreads();  // s_* are rewritten for the next unit
+  }
+}
+
+template <typename CodeT, bool kSmemTable, bool kPipe = false>
 __global__ void __launch_bounds__(kThreads, 2) match_kernel(const Params p) {
   using Tab = Table<CodeT, uint32_t>;
   extern __shared__ __align__(16) unsigned char smem[];
@@ -331,6 +557,7 @@ __global__ void __launch_bounds__(kThreads, 2) match_kernel(const Params p) {
   uint32_t* s_ls = reinterpret_cast<uint32_t*>(smem + kTableBytes);  // [kSteps][kLsBuckets]
   uint32_t* s_ks = s_ls + kSteps * kLsBuckets;                         // [kSteps][32]
   __shared__ uint32_t s_used, s_ovf, s_lt;
+  __shared__ uint32_t s_claim;
 
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const CodeT* qc = static_cast<const CodeT*>(p.qc);
@@ -344,8 +571,27 @@ __global__ void __launch_bounds__(kThreads, 2) match_kernel(const Params p) {
   }
   const int64_t n_work = (!kSmemTable && p.list_mode) ? static_cast<int64_t>(*p.ovf_count) : p.N;
   const int64_t n_chunks = (p.T + kChunk - 1) / kChunk;
+  // pipelined: streams in claim order from a counter (each CTA takes the next when it is free)
+  auto claim = [&]() -> int64_t {
+    if (tid == 0) s_claim = atomicAdd(&p.ctl->next_stream, 1u);
+    __syncthreads();
+    const int64_t w = s_claim;
+    __syncthreads();
+    return w;
+  };
+  // pipelined: the whole dynamic shared memory stages rows once this CTA copies them
+  const uint32_t stage_rows = kPipe ? min(2u * kThreads, static_cast<uint32_t>(
+                                              (kTableBytes + kSteps * (kLsBuckets + 32) * sizeof(uint32_t)) /
+                                              (16u * p.g.wpr))) : 0u;
+  if constexpr (kPipe) {
+    if (pipe_role(p, tid) != kRoleMatch) {
+      pipe_gather(p, tid, reinterpret_cast<uint4*>(smem), stage_rows);
+      return;
+    }
+  }
 
-  for (int64_t wi = blockIdx.x; wi < n_work; wi += gridDim.x) {
+  for (int64_t wi = kPipe ? claim() : static_cast<int64_t>(blockIdx.x); wi < n_work;
+       wi = kPipe ? claim() : wi + gridDim.x) {
     const int64_t n = (!kSmemTable && p.list_mode) ? static_cast<int64_t>(p.ovf_list[wi]) : wi;
     const int64_t row0 = n * p.T;
     tab.clear(tid, kThreads);
@@ -370,6 +616,15 @@ __global__ void __launch_bounds__(kThreads, 2) match_kernel(const Params p) {
           const int i = (warp + u * kMatchWarps) * 32 + lane;
           kr[u] = (i < cnt && warp + u * kMatchWarps < kSteps) ? kc[row0 + base + i] : CodeT(0);
           qr[u] = (i < cnt && warp + u * kMatchWarps < kSteps) ? qc[row0 + base + i] : CodeT(0);
+        }
+        {
+          // the next chunk's codes into L2 meanwhile: its loads then wait on L2, not on HBM
+          // (which row copies elsewhere on the chip may keep busy)
+          constexpr int kLines = kChunk * static_cast<int>(sizeof(CodeT)) / 128;
+          if (tid < 2 * kLines) {
+            const int64_t e = base + kChunk + (tid % kLines) * (128 / static_cast<int>(sizeof(CodeT)));
+            if (e < p.T) prefetch_l2((tid < kLines ? kc : qc) + row0 + e);
+          }
         }
         // ---------------------------------------------- P1: keys into the table, step bits
         const int32_t base32 = static_cast<int32_t>(base);
@@ -451,6 +706,11 @@ __global__ void __launch_bounds__(kThreads, 2) match_kernel(const Params p) {
         aborted = true;
         break;
       }
+      if (kPipe && tid == 0 && ((r + 1) % kUnitChunks == 0 || r + 1 == n_chunks)) {
+        // every thread's indices of chunks <= r are stored (barrier above): a release store
+        // by one thread after the barrier publishes them
+        st_release(p.progress + n, static_cast<uint32_t>(r + 1));
+      }
     }
 
     if (aborted) {
@@ -458,6 +718,7 @@ __global__ void __launch_bounds__(kThreads, 2) match_kernel(const Params p) {
         if (kSmemTable) {
           const uint32_t k = atomicAdd(p.ovf_count, 1u);
           p.ovf_list[k] = static_cast<uint32_t>(n);
+          if (kPipe) st_release(p.progress + n, kProgOvf);  // its rows are gathered there
         } else {
           // a global table holds 2T slots, so this cannot happen; report, never loop
           raise_status(p.status, LEMA_STATUS_PROBE_LIMIT);
@@ -484,33 +745,25 @@ __global__ void __launch_bounds__(kThreads, 2) match_kernel(const Params p) {
       if (tid == 0) p.lt_count[n] = static_cast<int32_t>(s_lt);
     }
     __syncthreads();
+    if (!kSmemTable && p.gather_inline) {
+      // overflow path of a pipelined call: this CTA's own indices, visible after the barrier
+      gather_span<uint4, kThreads>(p.g, n, 0u, static_cast<uint32_t>(p.T), tid);
+      __syncthreads();
+    }
   }
+  // no stream left: copy rows with the others
+  if constexpr (kPipe) pipe_gather(p, tid, reinterpret_cast<uint4*>(smem), stage_rows);
 }
 
 
 // ---------------------------------------------------------------- the value gather
-// out[n][i] = v[n][src[n][i]] (vbytes-byte rows), zeros where src is -1. A separate kernel
-// on purpose: value traffic in the same SM as the matcher's shared-memory table multiplies
-// the latency of every table access, so the two do not share SMs. Each CTA owns one
+// out[n][i] = v[n][src[n][i]] (vbytes-byte rows), zeros where src is -1: the two-kernel path
+// (rows not 16-byte aligned, 64-bit codes, no room for the pipelined mode's control words).
+// Value traffic in the same SM as the matcher's shared-memory table multiplies the latency of
+// every table access, so the two never share SMs. Each CTA owns one
 // contiguous run of output words of one stream (blockIdx.y), kGUnroll loads in flight per
 // thread, streaming stores.
 constexpr int kGThreads = 256;
-constexpr int kGUnroll = 4;   // loads in flight per thread (measured: 8 -> 4 took the call 0.428 -> 0.384 ms)
-
-struct GatherParams {
-  const int32_t* src;
-  const unsigned char* v;
-  unsigned char* out;
-  int64_t N, T;
-  // row (n, t) of the values at v + (n / heads) * v_sb + (n % heads) * v_sh + t * v_st, of the
-  // output likewise (bytes); a plain [N][T] layout is heads = 1, sb = T * row, st = row
-  int64_t heads, v_sb, v_sh, v_st, o_sb, o_sh, o_st;
-  uint32_t wpr;        // vector words per row
-  uint32_t words;      // words per stream = T * wpr (< 2^32)
-  int div_shift;       // log2(wpr) when a power of two, else -1
-  uint32_t div_magic;  // floor(2^32 / wpr) + 1 when exact for every word index, else 0
-};
-
 template <typename Vec>
 __global__ void __launch_bounds__(kGThreads) gather_kernel(const GatherParams g) {
   const uint32_t w0 = blockIdx.x * (kGThreads * kGUnroll) + threadIdx.x;
@@ -545,8 +798,8 @@ __global__ void __launch_bounds__(kGThreads) gather_kernel(const GatherParams g)
 }
 
 template <typename Vec>
-int launch_gather(const MatchLaunch& a, const int32_t* src) {
-  GatherParams g{};
+int make_gather(const MatchLaunch& a, const int32_t* src, GatherParams& g) {
+  g = GatherParams{};
   g.src = src;
   g.v = static_cast<const unsigned char*>(a.v);
   g.out = static_cast<unsigned char*>(a.out);
@@ -574,6 +827,15 @@ int launch_gather(const MatchLaunch& a, const int32_t* src) {
   } else if (words * wpr < (uint64_t(1) << 32)) {  // multiply-high is exact for w * wpr < 2^32
     g.div_magic = static_cast<uint32_t>(0xFFFFFFFFull / wpr + 1);
   }
+  return LEMA_OK;
+}
+
+template <typename Vec>
+int launch_gather(const MatchLaunch& a, const int32_t* src) {
+  GatherParams g;
+  const int rc = make_gather<Vec>(a, src, g);
+  if (rc != LEMA_OK) return rc;
+  const uint64_t words = g.words;
   const uint64_t per_cta = kGThreads * kGUnroll;
   const dim3 grid(static_cast<unsigned>((words + per_cta - 1) / per_cta),
                   static_cast<unsigned>(std::min<int64_t>(a.N, 65535)));
@@ -582,10 +844,16 @@ int launch_gather(const MatchLaunch& a, const int32_t* src) {
   return LEMA_OK;
 }
 
+// every row starts on a 16-byte boundary: pointers, row size and (strided) strides
+bool rows_16(const MatchLaunch& a) {
+  const uint64_t st = a.heads > 0 ? static_cast<uint64_t>(a.v_sb | a.v_sh | a.v_st | a.o_sb | a.o_sh | a.o_st) : 0;
+  return a.vbytes % 16 == 0 && st % 16 == 0 && aligned(a.v, 16) && aligned(a.out, 16);
+}
+
 int run_gather(const MatchLaunch& a, const int32_t* src) {
   // every row must start on the vector boundary: pointers, row size and (strided) strides
   const uint64_t st = a.heads > 0 ? static_cast<uint64_t>(a.v_sb | a.v_sh | a.v_st | a.o_sb | a.o_sh | a.o_st) : 0;
-  const bool a16 = a.vbytes % 16 == 0 && st % 16 == 0 && aligned(a.v, 16) && aligned(a.out, 16);
+  const bool a16 = rows_16(a);
   const bool a8 = a.vbytes % 8 == 0 && st % 8 == 0 && aligned(a.v, 8) && aligned(a.out, 8);
   const bool a4 = a.vbytes % 4 == 0 && st % 4 == 0 && aligned(a.v, 4) && aligned(a.out, 4);
   if (a16) return launch_gather<uint4>(a, src);
@@ -618,7 +886,17 @@ struct Plan {
   int64_t gtable_bytes = 0;
   int64_t n_gtables = 0;
   size_t off_list = 0, off_tables = 0, total = 0;
+  // pipelined mode's control block and progress words, last; a workspace of min_total bytes
+  // (without them) runs the two-kernel path
+  size_t off_ctl = 0, ctl_bytes = 0, min_total = 0;
 };
+
+void add_ctl(Plan& pl, int64_t N) {
+  pl.min_total = pl.total;
+  pl.off_ctl = round_up(pl.total, 256);
+  pl.ctl_bytes = round_up(sizeof(PipeCtl) + 4 * static_cast<size_t>(N), 256);
+  pl.total = pl.off_ctl + pl.ctl_bytes;
+}
 
 // need_src: the caller passes no index output, so the indices live in the workspace.
 Plan make_plan(int64_t N, int64_t T, int code_bytes, bool need_src = true) {
@@ -630,7 +908,10 @@ Plan make_plan(int64_t N, int64_t T, int code_bytes, bool need_src = true) {
       need_src ? round_up(4 * static_cast<size_t>(N) * static_cast<size_t>(T), 256) : 0;
   pl.total = src_bytes;
   const bool may_overflow = T > static_cast<int64_t>(limit);
-  if (!may_overflow) return pl;
+  if (!may_overflow) {
+    add_ctl(pl, N);
+    return pl;
+  }
   pl.global = true;
   pl.list_mode = pl.fast;
   pl.gslots = static_cast<uint32_t>(next_pow2(static_cast<uint64_t>(std::max<int64_t>(2 * T, 2 * kBucket))));
@@ -643,7 +924,70 @@ Plan make_plan(int64_t N, int64_t T, int code_bytes, bool need_src = true) {
   pl.off_list = src_bytes + 256;
   pl.off_tables = round_up(pl.off_list + 4 * static_cast<size_t>(N), 256);
   pl.total = pl.off_tables + static_cast<size_t>(pl.n_gtables * pl.gtable_bytes);
+  add_ctl(pl, N);
   return pl;
+}
+
+// The pipelined mode serves calls that gather 16-byte-aligned rows of at most 4 KiB (27 or more
+// staged per pass), with the control words in the workspace, streams short enough that a
+// unit's wait stays far below its bound, and unit and word counts inside 32 bits.
+// LEMA_K2_PIPELINE=0 in the environment selects the two-kernel path instead (the same results).
+constexpr int64_t kPipeMaxT = int64_t(1) << 22;
+bool use_pipe(const MatchLaunch& a, const Plan& pl) {
+  const char* e = std::getenv("LEMA_K2_PIPELINE");
+  const bool enabled = !(e != nullptr && e[0] == '0');
+  if (!enabled || a.out == nullptr || pl.ctl_bytes == 0 || a.ws == nullptr || a.ws_bytes < pl.total ||
+      !aligned(a.ws, 256))
+    return false;
+  if (!rows_16(a) || a.T > kPipeMaxT || a.vbytes > 4096) return false;
+  const uint64_t ng = (static_cast<uint64_t>(a.T) + kChunk * kUnitChunks - 1) / (kChunk * kUnitChunks);
+  const uint64_t words = static_cast<uint64_t>(a.T) * static_cast<uint64_t>(a.vbytes / 16);
+  return static_cast<uint64_t>(a.N) * ng < (uint64_t(1) << 31) &&
+         words + static_cast<uint64_t>(kThreads) * kGUnroll < (uint64_t(1) << 32);
+}
+
+// SMs that match: enough CTAs for the streams in whole waves, at most kMatchFrac of the SMs
+// (LEMA_K2_MATCH_FRAC overrides), so that the others copy rows while the matching runs.
+uint32_t match_sms(int64_t N, int per_sm, int sms) {
+  const char* e = std::getenv("LEMA_K2_MATCH_FRAC");
+  const double f = e != nullptr ? std::atof(e) : 0.0;
+  const double frac = (f > 0.0 && f <= 1.0) ? f : 0.87;
+  const int64_t cap = std::max<int64_t>(1, static_cast<int64_t>(frac * sms));
+  const int64_t per_wave = static_cast<int64_t>(per_sm) * cap;
+  const int64_t waves = (N + per_wave - 1) / per_wave;
+  const int64_t per = static_cast<int64_t>(per_sm) * waves;
+  return static_cast<uint32_t>(std::min<int64_t>(sms, (N + per - 1) / per));
+}
+
+template <typename CodeT>
+int run_pipe(const MatchLaunch& a, const Plan& pl, const DeviceInfo& dev, Params p) {
+  unsigned char* ws = static_cast<unsigned char*>(a.ws);
+  int rc = make_gather<uint4>(a, p.src, p.g);
+  if (rc != LEMA_OK) return rc;
+  p.ctl = reinterpret_cast<PipeCtl*>(ws + pl.off_ctl);
+  p.progress = reinterpret_cast<uint32_t*>(ws + pl.off_ctl + sizeof(PipeCtl));
+  LEMA_CUDA_TRY(cudaMemsetAsync(ws + pl.off_ctl, 0, pl.ctl_bytes, a.stream));
+  auto kern = match_kernel<CodeT, true, true>;
+  const size_t sm = smem_bytes<CodeT>(true);
+  LEMA_CUDA_TRY(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(sm)));
+  int per_sm = 0;
+  LEMA_CUDA_TRY(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kern, kThreads, sm));
+  per_sm = std::max(per_sm, 1);
+  p.match_sms = match_sms(a.N, per_sm, dev.sms);
+  p.wave = p.match_sms * static_cast<uint32_t>(per_sm);
+  kern<<<static_cast<unsigned>(per_sm * dev.sms), kThreads, sm, a.stream>>>(p);
+  LEMA_CUDA_TRY(cudaGetLastError());
+  if (pl.global) {
+    // streams that overflowed the shared-memory table: matched and gathered here
+    p.list_mode = pl.list_mode ? 1 : 0;
+    p.gather_inline = 1;
+    auto gk = match_kernel<CodeT, false>;
+    const size_t gsm = smem_bytes<CodeT>(false);
+    LEMA_CUDA_TRY(cudaFuncSetAttribute(gk, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(gsm)));
+    gk<<<static_cast<unsigned>(pl.n_gtables), kThreads, gsm, a.stream>>>(p);
+    LEMA_CUDA_TRY(cudaGetLastError());
+  }
+  return LEMA_OK;
 }
 
 template <typename CodeT>
@@ -666,6 +1010,9 @@ int run(const MatchLaunch& a, const Plan& pl, const DeviceInfo& dev) {
     p.gtable_bytes = pl.gtable_bytes;
     p.gslots = pl.gslots;
     if (pl.list_mode) LEMA_CUDA_TRY(cudaMemsetAsync(p.ovf_count, 0, sizeof(uint32_t), a.stream));
+  }
+  if constexpr (sizeof(CodeT) == 4) {  // 64-bit codes: the two-kernel path (no spare registers)
+    if (pl.fast && use_pipe(a, pl)) return run_pipe<CodeT>(a, pl, dev, p);
   }
   if (pl.fast) {
     auto kern = match_kernel<CodeT, true>;
@@ -691,8 +1038,9 @@ int run(const MatchLaunch& a, const Plan& pl, const DeviceInfo& dev) {
 
 }  // namespace k2
 
-size_t match_workspace_bytes(int64_t N, int64_t T, int code_bytes, bool need_src) {
-  return k2::make_plan(N, T, code_bytes, need_src).total;
+size_t match_workspace_bytes(int64_t N, int64_t T, int code_bytes, bool need_src, bool pipe) {
+  const k2::Plan pl = k2::make_plan(N, T, code_bytes, need_src);
+  return pipe ? pl.total : pl.min_total;
 }
 
 int launch_match(const MatchLaunch& a) {
@@ -711,10 +1059,10 @@ int launch_match(const MatchLaunch& a) {
   const bool lt_any = a.lt_code || a.lt_pos || a.lt_count;
   if (lt_any && !(a.lt_code && a.lt_pos && a.lt_count)) return fail(LEMA_ERR_INVALID_ARGUMENT, "last-occurrence outputs: all three or none");
   const k2::Plan pl = k2::make_plan(a.N, a.T, a.code_bytes, a.src == nullptr);
-  if (a.ws_bytes < pl.total || (pl.total > 0 && a.ws == nullptr)) {
-    return fail(LEMA_ERR_WORKSPACE, "workspace of %zu bytes, %zu needed", a.ws_bytes, pl.total);
+  if (a.ws_bytes < pl.min_total || (pl.min_total > 0 && a.ws == nullptr)) {
+    return fail(LEMA_ERR_WORKSPACE, "workspace of %zu bytes, %zu needed", a.ws_bytes, pl.min_total);
   }
-  if (pl.total > 0 && !aligned(a.ws, 256)) return fail(LEMA_ERR_INVALID_ARGUMENT, "workspace must be 256-byte aligned");
+  if (pl.min_total > 0 && !aligned(a.ws, 256)) return fail(LEMA_ERR_INVALID_ARGUMENT, "workspace must be 256-byte aligned");
   const DeviceInfo* dev = current_device_info();
   if (dev == nullptr) return LEMA_ERR_CUDA;
   if (dev->cc_major != 10) return fail(LEMA_ERR_UNSUPPORTED, "built for sm_100a; device is sm_%d%d", dev->cc_major, dev->cc_minor);
@@ -758,6 +1106,7 @@ Plan make_plan_within(int64_t N, int64_t T, int code_bytes, bool need_src, size_
     if (pl.off_tables + static_cast<size_t>(pl.gtable_bytes) > budget) {
       fits = false;
       pl.total = pl.off_tables + static_cast<size_t>(pl.gtable_bytes);
+      pl.min_total = pl.total;
       return pl;
     }
     pl.n_gtables = std::min<int64_t>(
@@ -765,6 +1114,12 @@ Plan make_plan_within(int64_t N, int64_t T, int code_bytes, bool need_src, size_
     pl.total = pl.off_tables + static_cast<size_t>(pl.n_gtables * pl.gtable_bytes);
   }
   fits = pl.total <= budget;
+  pl.min_total = pl.total;
+  if (fits) {
+    Plan q = pl;
+    add_ctl(q, N);
+    if (q.total <= budget) pl = q;  // room for the pipelined mode's control words
+  }
   return pl;
 }
 

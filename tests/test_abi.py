@@ -38,8 +38,9 @@ def test_sizes():
     assert L.lema_store_slot_bytes(48) == 64          # 16-byte header + 48-byte bf16 row
     assert L.lema_store_slot_bytes(256) == 272
     assert L.lema_store_slot_bytes(8) == 32           # rows padded to 16 bytes
-    # index scratch (used when the caller passes no src) ...
-    assert L.lema_prefill_workspace_bytes(8, 4096, 4) == 8 * 4096 * 4
+    # index scratch (used when the caller passes no src) and the pipelined mode's control
+    # words (4 KiB + 4 bytes per stream, 256-byte rounded) ...
+    assert L.lema_prefill_workspace_bytes(8, 4096, 4) == 8 * 4096 * 4 + 4352
     # ... plus global-table room when a stream can outgrow the shared-memory table
     assert L.lema_prefill_workspace_bytes(512, 16384, 4) > 512 * 16384 * 4
     assert L.lema_store_workspace_bytes(1024, 1, 4) == 0        # a decode step needs none

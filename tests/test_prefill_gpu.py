@@ -97,7 +97,8 @@ def test_overflow_path_many_distinct(cuda):
     """More distinct key codes than the shared-memory table takes: the global-table path."""
     rng = np.random.default_rng(21)
     T = 16384
-    kc = rng.permutation(1 << 30)[: 3 * T].astype(np.uint32).reshape(3, T)
+    # 3T distinct codes: an odd multiplier is a bijection modulo 2^30
+    kc = ((np.arange(3 * T, dtype=np.uint64) * 2654435761 + 12345) & ((1 << 30) - 1)).astype(np.uint32).reshape(3, T)
     qc = kc.copy()
     for n in range(3):  # queries repeat keys from a little earlier, or miss
         back = rng.integers(-5, 200, size=T)
@@ -198,8 +199,8 @@ def test_lema_hard_dense(cuda, d_qk, dtype):
 
 @pytest.mark.parametrize("N,T", [(400, 2048), (340, 8192)])
 def test_more_streams_than_one_matcher_wave(cuda, N, T):
-    # above one full wave of matcher CTAs (2 per SM) the first wave's rows are gathered on a
-    # side stream while the rest is matched; T > 6144 also runs the overflow kernel per wave
+    # more streams than one wave of matcher CTAs (2 per SM); T > 6144 also launches the
+    # overflow kernel
     qc, kc = synth.code_streams(N, T, synth.CONFIG2, seed=N, config_id=2)
     v = np.random.default_rng(N).integers(0, 1 << 16, size=(N, T, 8), dtype=np.uint16)
     q = torch.from_numpy(qc.view(np.int32)).to(cuda)
