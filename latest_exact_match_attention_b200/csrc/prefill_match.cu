@@ -19,10 +19,9 @@
 //                own in the step's bucket whose recorded slot is the query's answers it;
 //                otherwise the highest mask bit below its step names the latest earlier step
 //                holding the code, whose highest such lane is the answer; with no such step the
-//                answer is carry[slot]. Each key also notes whether its step is the last of its
-//                slot in the chunk.
-//   P3 (the keys of each slot's last step) carry[slot] = max(carry, 1 + position) by an
-//                atomic max, mask[slot] = 0; every key clears its bucket for the next chunk.
+//                answer is carry[slot].
+//   P3 (keys)    carry[slot] = max(carry, 1 + position) by an atomic max, mask[slot] = 0, and
+//                every key clears its bucket for the next chunk.
 // Two slots sharing a bucket in one step only cost a second look; no warp-wide ballot or match
 // instruction is needed (on this part those cost far more than the table traffic).
 // All 32 warps of a CTA run the phases (one step each per chunk); CTA barriers separate them.
@@ -556,7 +555,8 @@ __global__ void __launch_bounds__(kThreads, 2) match_kernel(const Params p) {
   constexpr size_t kTableBytes = kSmemTable ? round_up16(Tab::bytes(kCap)) : 0;
   uint32_t* s_ls = reinterpret_cast<uint32_t*>(smem + kTableBytes);  // [kSteps][kLsBuckets]
   uint32_t* s_ks = s_ls + kSteps * kLsBuckets;                         // [kSteps][32]
-  __shared__ uint32_t s_used, s_ovf, s_lt;
+  __shared__ uint32_t s_ovf, s_lt;
+  __shared__ uint32_t s_used[2];  // slots claimed in the stream before chunk r: s_used[r & 1]
   __shared__ uint32_t s_claim;
 
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
@@ -597,9 +597,9 @@ __global__ void __launch_bounds__(kThreads, 2) match_kernel(const Params p) {
     tab.clear(tid, kThreads);
     for (int k = tid; k < kSteps * kLsBuckets; k += kThreads) s_ls[k] = 0u;
     if (tid == 0) {
-      s_used = 0;
       s_ovf = 0;
       s_lt = 0;
+      s_used[0] = 0;
     }
     __syncthreads();
 
@@ -629,6 +629,8 @@ __global__ void __launch_bounds__(kThreads, 2) match_kernel(const Params p) {
         // ---------------------------------------------- P1: keys into the table, step bits
         const int32_t base32 = static_cast<int32_t>(base);
         uint32_t kslot[kPerLane];
+        uint32_t claims = 0;  // 0 or 1: one key per thread
+        static_assert(kPerLane == 1, "one key per thread per chunk: the barrier counts claims");
 #pragma unroll
         for (int u = 0; u < kPerLane; ++u) {
           const int step = warp + u * kMatchWarps;
@@ -639,8 +641,9 @@ __global__ void __launch_bounds__(kThreads, 2) match_kernel(const Params p) {
           uint32_t claimed = 0;
           if (valid) {
             kslot[u] = tab.insert_fast(kr[u], claimed);
-            if (kslot[u] == kNoSlot) s_ovf = 1;
+            if (!kSmemTable && kslot[u] == kNoSlot) s_ovf = 1;
           }
+          claims += claimed;
           // the step's key lanes per slot bucket, and each lane's slot; every key lane sets its
           // step's bit in the slot's mask (lanes sharing a slot set the same bit)
           const uint32_t ks = kslot[u];
@@ -649,22 +652,23 @@ __global__ void __launch_bounds__(kThreads, 2) match_kernel(const Params p) {
             atomicOr(s_ls + step * kLsBuckets + (ks & (kLsBuckets - 1)), 1u << lane);
             atomicOr(tab.mask + ks, 1u << step);
           }
-          const uint32_t nclaim = __popc(__ballot_sync(kFullMask, claimed != 0));
-          if (lane == 0 && nclaim) atomicAdd(&s_used, nclaim);
         }
-        match_barrier();
-        if (s_ovf != 0 || (kSmemTable && s_used > overflow_limit<CodeT>())) {
+        // claims counted by the barrier; every thread stores the same new total (the other
+        // word of the pair, read only after the next chunk's count). A key that finds no slot
+        // at all means every slot is claimed, which is past the limit too.
+        const uint32_t used = s_used[r & 1] + static_cast<uint32_t>(__syncthreads_count(claims != 0));
+        s_used[(r + 1) & 1] = used;
+        const bool over = kSmemTable ? used > overflow_limit<CodeT>() : s_ovf != 0;
+        if (over) {
           // the whole CTA learns it after the round barrier; P2/P3 are skipped
         } else {
-          // ---------------------------------------------- P2: queries; keys' last step
-          uint32_t clast = 0;
+          // ---------------------------------------------- P2: queries
 #pragma unroll
           for (int u = 0; u < kPerLane; ++u) {
             const int step = warp + u * kMatchWarps;
             const int i = step * 32 + lane;
             if (step >= kSteps || step * 32 >= cnt) continue;  // uniform per warp
             const bool valid = i < cnt;
-            if (kslot[u] != kNoSlot && (31 - __clz(tab.mask[kslot[u]])) == step) clast |= 1u << u;
             // the query's slot, looked up once every key of the chunk is in the table
             const uint32_t sl = valid ? tab.find_fast(qr[u]) : kNoSlot;
             int32_t a = -1;
@@ -687,22 +691,21 @@ __global__ void __launch_bounds__(kThreads, 2) match_kernel(const Params p) {
             if (valid) ab[i] = a;
           }
           match_barrier();
-          // ---------------------------------------------- P3: carries of the chunk's last keys
+          // ---------------------------------------------- P3: carries
 #pragma unroll
           for (int u = 0; u < kPerLane; ++u) {
             const int step = warp + u * kMatchWarps;
             if (step >= kSteps || kslot[u] == kNoSlot) continue;
             s_ls[step * kLsBuckets + (kslot[u] & (kLsBuckets - 1))] = 0u;  // clean for the next chunk
-            if ((clast >> u) & 1u) {
-              // the keys of the slot's last step: the latest of them becomes the carry
-              atomicMax(tab.carry + kslot[u], static_cast<uint32_t>(base32 + step * 32 + lane + 1));
-              tab.mask[kslot[u]] = 0u;
-            }
+            // every key of the chunk: the latest one per slot becomes the carry (one atomic max
+            // per key is cheaper than finding each slot's last step first)
+            atomicMax(tab.carry + kslot[u], static_cast<uint32_t>(base32 + step * 32 + lane + 1));
+            tab.mask[kslot[u]] = 0u;
           }
         }
       }
       __syncthreads();
-      if (s_ovf != 0 || (kSmemTable && s_used > overflow_limit<CodeT>())) {
+      if (kSmemTable ? s_used[(r + 1) & 1] > overflow_limit<CodeT>() : s_ovf != 0) {
         aborted = true;
         break;
       }
