@@ -66,6 +66,18 @@ def test_argument_validation_on_host():
     assert rc("lema_prefill_match", P, P, 4, 1, 8, None, P, 3, P, None, 0, None, None) == 1
     # workspace too small (config 2 needs one)
     assert rc("lema_prefill_match", P, P, 4, 512, 16384, None, None, 0, None, None, 0, None, None) == 3
+    # the pipelined mode's control words (4 KiB + 4 bytes per stream, 256-byte rounded) are the
+    # workspace's last bytes and optional: one byte less than the rest is refused, while the
+    # rest alone passes validation (the call would run the two-kernel path) and, with no GPU
+    # here, gets as far as looking for a device. Never run that half with a GPU present: the
+    # pointers are fake.
+    W = ctypes.c_void_p(1 << 20)   # 256-byte aligned, never dereferenced
+    full = _lib.lib().lema_prefill_workspace_bytes(512, 16384, 4)
+    ctl = (4112 + 4 * 512 + 255) // 256 * 256
+    assert rc("lema_prefill_match", P, P, 4, 512, 16384, None, None, 0, None, W, full - ctl - 1, None, None) == 3
+    assert b"needed" in _lib.lib().lema_last_error()
+    if not torch.cuda.is_available():
+        assert rc("lema_prefill_match", P, P, 4, 512, 16384, None, None, 0, None, W, full - ctl, None, None) == 2
     # store: value row not a multiple of 8, n not partitions x T, zero capacity
     assert rc("lema_store_exchange", P, 100, 12, P, P, 4, P, P, 8, 1, 0, P, None, None, 0, None) == 1
     assert rc("lema_store_exchange", P, 100, 16, P, P, 4, P, P, 10, 4, 0, P, None, None, 0, None) == 1

@@ -122,3 +122,29 @@ def test_pipe_repeated_calls_reuse_workspace(cuda):
     assert int(st.item()) == 0
     assert np.array_equal(src.cpu().numpy(), want)
     assert np.array_equal(out.cpu().numpy(), wv)
+
+
+def test_workspace_without_control_words_runs_two_kernels(cuda):
+    # a workspace that holds everything but the pipelined mode's control words (its last
+    # 4 KiB + 4 bytes per stream, 256-byte rounded) is accepted and gives the same results
+    N, T = 300, 7000
+    qc, kc = codes(N, T, seed=30)
+    v = np.random.default_rng(30).integers(0, 1 << 16, size=(N, T, 24), dtype=np.uint16)
+    q = torch.from_numpy(qc.view(np.int32)).to(cuda)
+    k = torch.from_numpy(kc.view(np.int32)).to(cuda)
+    vd = torch.from_numpy(v).to(cuda)
+    full = int(_lib.lib().lema_prefill_workspace_bytes(N, T, 4))
+    ctl = (4112 + 4 * N + 255) // 256 * 256
+    want = oracle.latest_prev_match(qc, kc)
+    wv = oracle.gather(want, v)
+    for nb in (full, full - ctl):
+        ws = torch.empty(nb, dtype=torch.uint8, device=cuda)
+        src = torch.empty((N, T), dtype=torch.int32, device=cuda)
+        out = torch.empty_like(vd)
+        st = torch.zeros(1, dtype=torch.int32, device=cuda)
+        call("lema_prefill_match", ptr(q), ptr(k), 4, N, T, ptr(src), ptr(vd), 48, ptr(out),
+             ptr(ws), nb, ptr(st), torch.cuda.current_stream(cuda).cuda_stream)
+        torch.cuda.synchronize()
+        assert int(st.item()) == 0
+        assert np.array_equal(src.cpu().numpy(), want)
+        assert np.array_equal(out.cpu().numpy(), wv)
