@@ -933,16 +933,20 @@ Plan make_plan(int64_t N, int64_t T, int code_bytes, bool need_src = true) {
 
 // The pipelined mode serves calls that gather 16-byte-aligned rows of at most 4 KiB (27 or more
 // staged per pass), with the control words in the workspace, streams short enough that a
-// unit's wait stays far below its bound, and unit and word counts inside 32 bits.
-// LEMA_K2_PIPELINE=0 in the environment selects the two-kernel path instead (the same results).
+// unit's wait stays far below its bound, and unit and word counts inside 32 bits; and calls
+// of at least one full wave of matchers (2 per SM): with fewer streams the two-kernel path
+// runs each matcher alone on its SM, faster than two per SM on fewer SMs (measured: 128
+// streams of config 2 take 0.185 ms in two kernels, 0.224 ms pipelined; 512 streams 0.344
+// and 0.322). LEMA_K2_PIPELINE=0 in the environment selects the two-kernel path (the same
+// results).
 constexpr int64_t kPipeMaxT = int64_t(1) << 22;
-bool use_pipe(const MatchLaunch& a, const Plan& pl) {
+bool use_pipe(const MatchLaunch& a, const Plan& pl, int sms) {
   const char* e = std::getenv("LEMA_K2_PIPELINE");
   const bool enabled = !(e != nullptr && e[0] == '0');
   if (!enabled || a.out == nullptr || pl.ctl_bytes == 0 || a.ws == nullptr || a.ws_bytes < pl.total ||
       !aligned(a.ws, 256))
     return false;
-  if (!rows_16(a) || a.T > kPipeMaxT || a.vbytes > 4096) return false;
+  if (!rows_16(a) || a.T > kPipeMaxT || a.vbytes > 4096 || a.N < 2 * static_cast<int64_t>(sms)) return false;
   const uint64_t ng = (static_cast<uint64_t>(a.T) + kChunk * kUnitChunks - 1) / (kChunk * kUnitChunks);
   const uint64_t words = static_cast<uint64_t>(a.T) * static_cast<uint64_t>(a.vbytes / 16);
   return static_cast<uint64_t>(a.N) * ng < (uint64_t(1) << 31) &&
@@ -1015,7 +1019,7 @@ int run(const MatchLaunch& a, const Plan& pl, const DeviceInfo& dev) {
     if (pl.list_mode) LEMA_CUDA_TRY(cudaMemsetAsync(p.ovf_count, 0, sizeof(uint32_t), a.stream));
   }
   if constexpr (sizeof(CodeT) == 4) {  // 64-bit codes: the two-kernel path (no spare registers)
-    if (pl.fast && use_pipe(a, pl)) return run_pipe<CodeT>(a, pl, dev, p);
+    if (pl.fast && use_pipe(a, pl, dev.sms)) return run_pipe<CodeT>(a, pl, dev, p);
   }
   if (pl.fast) {
     auto kern = match_kernel<CodeT, true>;

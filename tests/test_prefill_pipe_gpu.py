@@ -1,6 +1,7 @@
 """K2's pipelined mode (one launch: matcher CTAs on most SMs, row-copying CTAs on the rest,
 following the matchers' published progress) against the two-kernel path and the oracle.
-LEMA_K2_PIPELINE=0 selects the two-kernel path; LEMA_K2_MATCH_FRAC moves the SM split.
+Calls of fewer streams than one wave of matchers (2 per SM: 296 on a B200) take the
+two-kernel path; LEMA_K2_PIPELINE=0 selects it always; LEMA_K2_MATCH_FRAC moves the SM split.
 Every case must give the same indices and rows bit for bit, and leave the status word 0
 (no bounded wait ran out)."""
 import numpy as np
@@ -30,7 +31,8 @@ def run(qc, kc, v, dev):
 
 
 @pytest.mark.parametrize("N,T,d", [
-    (1, 20000, 24),      # one stream: one matcher, every other SM copies rows
+    (1, 20000, 24),      # one stream: the two-kernel path
+    (296, 20000, 8),     # one full wave of matchers; 5 units per stream, the last ragged
     (600, 5000, 24),     # three waves of matchers, a ragged last unit and chunk
     (2048, 1024, 8),     # many one-chunk streams (one unit each)
     (300, 4096, 64),     # 128-byte rows, a unit = the whole stream
@@ -82,7 +84,7 @@ def test_pipe_with_overflow_streams(cuda):
 
 def test_pipe_strided_rows(cuda):
     # the model's layout: values [B, T, H, dv] read in place, output [B, T, H, dv]
-    B, H, T, dv = 3, 40, 3000, 32
+    B, H, T, dv = 3, 100, 3000, 32
     qc, kc = codes(B * H, T, seed=3)
     vals = torch.from_numpy(np.random.default_rng(3).integers(0, 1 << 16, size=(B, T, H, dv),
                                                              dtype=np.uint16).view(np.int16)).to(cuda)
