@@ -123,6 +123,13 @@ int lema_row_rms(const void* x, int64_t M, int64_t K, float eps, float* out, voi
  * Replaces: the silu and product of code/lema/model.py:85-93 (`SwiGLU.forward`). */
 int lema_swiglu(const void* gu, int dtype, int64_t M, int64_t F, void* out, void* stream);
 
+/* RMSNorm of 16-bit rows: out[m] = (x[m] * rstd) * weight, rstd = 1 / sqrt(mean(x[m]^2) +
+ * eps), fp32 inside, rounded once; dtype LEMA_BF16 or LEMA_F16, D a multiple of 8, x, weight
+ * and out 16-byte aligned (else LEMA_ERR_UNSUPPORTED: use the framework's own norm).
+ * Replaces: nn.RMSNorm of code/lema/model.py:215-217, 264 (norm1, norm2, norm_f). */
+int lema_rms_norm(const void* x, const void* weight, int dtype, int64_t M, int64_t D, float eps,
+                  void* out, void* stream);
+
 /* ---------------------------------------------- (b) prefill latest match */
 /*
  * Bytes of device workspace lema_prefill_match needs for n_streams x T

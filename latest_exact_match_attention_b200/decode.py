@@ -22,6 +22,7 @@ from __future__ import annotations
 import torch
 
 from .cache import HashStore, LemaCache
+from .model import rms_norm
 
 
 def _chooser(temperature: float):
@@ -62,7 +63,7 @@ class LemaDecoder:
             for blk, view in zip(model.blocks, views):
                 qc, kc, v = blk.gpu_pre(x)
                 x = blk.gpu_post(x, view.exchange(qc, kc, v, check=False))
-            logits = model.lm_head(model.norm_f(x))
+            logits = model.lm_head(rms_norm(model.norm_f, x))
             self.tok.copy_(choose(logits).view(B, 1))
             return logits
 

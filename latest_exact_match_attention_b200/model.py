@@ -88,6 +88,23 @@ class ModelConfig:
                 f"dim_ff {self.dim_ff} attn {self.attn}")
 
 
+def rms_norm(norm: nn.RMSNorm, x: torch.Tensor) -> torch.Tensor:
+    """`norm(x)` (code/lema/model.py:215-217, 264): one pass of lema_rms_norm for 16-bit rows
+    on the GPU (torch's kernel reads the rows at under half the HBM rate at config 3), the
+    module itself otherwise (fp32, CPU, odd widths)."""
+    D = x.shape[-1]
+    w = norm.weight
+    if (x.is_cuda and x.dtype in (torch.bfloat16, torch.float16) and w is not None
+            and w.dtype == x.dtype and D % 8 == 0 and x.is_contiguous()
+            and x.data_ptr() % 16 == 0 and w.data_ptr() % 16 == 0):
+        out = torch.empty_like(x)
+        eps = norm.eps if norm.eps is not None else torch.finfo(x.dtype).eps
+        call("lema_rms_norm", ptr(x), ptr(w), DTYPE_TAG[x.dtype], x.numel() // D, D, eps, ptr(out),
+             stream_handle(x.device))
+        return out
+    return norm(x)
+
+
 class SwiGLU(nn.Module):
     """down(silu(gate(x)) * up(x)), parameters named as code/lema/model.py:85-93. On a GPU the
     gate and up projections are one GEMM on their stacked weights and the activation is one
@@ -247,7 +264,7 @@ class Block(nn.Module):
         more often (the norm weight is rounded into the weights), so it is off by default."""
         if self.fused_pre and self.attn._k1_ok(x) and self.norm1.weight is not None:
             return self.attn.codes_fused(x, self.norm1)
-        return self.attn.codes(self.norm1(x))
+        return self.attn.codes(rms_norm(self.norm1, x))
 
     def gpu_post(self, x, got):
         """Merge the retrieved values and finish the layer: x + o_proj(merged heads) as one
@@ -256,7 +273,7 @@ class Block(nn.Module):
         dim = x.shape[-1]
         y = got.transpose(1, 2).reshape(B * T, H * dv)
         x = torch.addmm(x.reshape(B * T, dim), y, self.attn.o_proj.weight.t()).view(B, T, dim)
-        return self.mlp(self.norm2(x), residual=x)
+        return self.mlp(rms_norm(self.norm2, x), residual=x)
 
     def forward(self, x, store=None):
         if store is not None:
@@ -328,7 +345,7 @@ class Transformer(nn.Module):
             x = blk(x, store=(cache.layer(li) if cache is not None else None))
         if cache is not None:
             cache.t += idx.shape[-1]
-        return self.lm_head(self.norm_f(x)) if return_logits else None
+        return self.lm_head(rms_norm(self.norm_f, x)) if return_logits else None
 
     def n_params(self, embedding: bool = True) -> int:
         n = sum(p.numel() for p in self.parameters())

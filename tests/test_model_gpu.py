@@ -122,3 +122,28 @@ def test_swiglu_mlp_matches_torch(cuda, dtype, tol):
                .float() + r.float())
         got = mlp(x, residual=r).float()
     torch.testing.assert_close(got, ref, rtol=tol, atol=tol)
+
+
+@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float16])
+@pytest.mark.parametrize("M,D", [(1, 8), (3, 1024), (257, 1536), (64, 2056), (5, 4096), (7, 100)])
+def test_rms_norm_matches_fp32(cuda, dtype, M, D):
+    """lema_rms_norm (16-bit rows, D % 8 == 0; the module itself for D = 100) against the fp32
+    formula rounded once: at most one unit in the last place apart (summation order), almost
+    everywhere equal."""
+    from latest_exact_match_attention_b200.model import rms_norm
+    torch.manual_seed(M + D)
+    norm = torch.nn.RMSNorm(D, eps=1e-5).to(cuda)
+    with torch.no_grad():
+        norm.weight.copy_(torch.randn(D, device=cuda) * 0.5 + 1.0)
+    norm = norm.to(dtype)
+    x = (torch.randn(M, D, device=cuda) * 3).to(dtype)
+    with torch.no_grad():
+        got = rms_norm(norm, x)
+        xf = x.float()
+        ref = ((xf * torch.rsqrt(xf.pow(2).mean(-1, keepdim=True) + 1e-5)) * norm.weight.float()).to(dtype)
+    ulp = 2.0 ** (-7 if dtype == torch.bfloat16 else -10)
+    diff = (got.float() - ref.float()).abs()
+    assert bool((diff <= ulp * ref.float().abs().clamp_min(1e-3) + 1e-6).all())
+    assert float((got == ref).float().mean()) > 0.98
+    torch.testing.assert_close(got.float(), torch.nn.functional.rms_norm(
+        x.float(), (D,), norm.weight.float(), 1e-5), rtol=2 * ulp, atol=1e-3)
