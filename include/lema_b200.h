@@ -123,6 +123,16 @@ int lema_row_rms(const void* x, int64_t M, int64_t K, float eps, float* out, voi
  * Replaces: the silu and product of code/lema/model.py:85-93 (`SwiGLU.forward`). */
 int lema_swiglu(const void* gu, int dtype, int64_t M, int64_t F, void* out, void* stream);
 
+/* The MLP's gate/up GEMM with SwiGLU in its epilogue (K1's tcgen05 pipeline):
+ * act[m][f] = bf16(silu(x[m] . gate[f]) * (x[m] . up[f])), fp32 accumulators, for bf16 x
+ * [M][K] and w_il [2F][K] holding the gate and up rows interleaved in blocks of 128 (rows
+ * 256 b .. 256 b + 127 = gate rows 128 b ..; the next 128 = up rows 128 b ..). K a multiple
+ * of 64, F of 128; pointers 16-byte aligned. The [M][2F] product never reaches HBM.
+ * Replaces: gate(x), up(x) and silu(.) * (.) of code/lema/model.py:85-93 (SwiGLU.forward);
+ * the down projection stays a GEMM. status as for lema_proj_codes. */
+int lema_gemm_swiglu(const void* x, const void* w_il, int64_t M, int64_t K, int64_t F, void* act_out,
+                     uint32_t* status, void* stream);
+
 /* RMSNorm of 16-bit rows: out[m] = (x[m] * rstd) * weight, rstd = 1 / sqrt(mean(x[m]^2) +
  * eps), fp32 inside, rounded once; dtype LEMA_BF16 or LEMA_F16, D a multiple of 8, x, weight
  * and out 16-byte aligned (else LEMA_ERR_UNSUPPORTED: use the framework's own norm).

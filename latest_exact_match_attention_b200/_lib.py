@@ -37,6 +37,7 @@ _SIGNATURES = {
     "lema_row_rms": ([_P, _I64, _I64, ctypes.c_float, _P, _P], _I),
     "lema_swiglu": ([_P, _I, _I64, _I64, _P, _P], _I),
     "lema_rms_norm": ([_P, _P, _I, _I64, _I64, ctypes.c_float, _P, _P], _I),
+    "lema_gemm_swiglu": ([_P, _P, _I64, _I64, _I64, _P, _P, _P], _I),
     "lema_prefill_workspace_bytes": ([_I64, _I64, _I], _SZ),
     "lema_prefill_match": ([_P, _P, _I, _I64, _I64, _P, _P, _I64, _P, _P, _SZ, _P, _P], _I),
     "lema_prefill_match_noalloc": ([_P, _P, _I, _I64, _I64, _P, _P, _I64, _P, _P, _P], _I),

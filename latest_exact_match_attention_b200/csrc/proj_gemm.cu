@@ -69,6 +69,11 @@ struct Params {
   __nv_bfloat16* v_out;
   const float* row_scale;
   int n_v;
+  // SwiGLU mode (act_out set, no codes, BN = 256): the weight rows of tile column block nb are
+  // 128 gate rows then the 128 up rows of the same features f = 128 nb ...;
+  // act_out[m][f] = bf16(silu(gate) * up) from the fp32 accumulators, act_f = F features
+  __nv_bfloat16* act_out;
+  int64_t act_f;
 };
 
 // ------------------------------------------------------------------ PTX wrappers
@@ -333,7 +338,34 @@ __global__ void __launch_bounds__(kThreads, 1)
       const int64_t b = live ? m / p.T : 0;
       const int64_t t = live ? m - b * p.T : 0;
       const float scale = (live && p.row_scale != nullptr) ? p.row_scale[m] : 1.0f;
-      for (int j = 0; j < TL::kHeads; ++j) {
+      if (p.act_out != nullptr) {
+        // SwiGLU: gate columns j * 32 ... and up columns BN / 2 + j * 32 ... of the same 32
+        // features; silu(g) * u in fp32 (the formula of lema_swiglu), rounded once
+        const int64_t f0 = (tile % p.n_blocks) * (BN / 2);
+        for (int j = 0; j < BN / 64; ++j) {
+          uint32_t g[32], u[32];
+          tmem_load32(tmem_base + lane_base + static_cast<uint32_t>(acc * BN + j * 32), g);
+          tmem_load32(tmem_base + lane_base + static_cast<uint32_t>(acc * BN + BN / 2 + j * 32), u);
+          if (live) {
+            uint4* dst = reinterpret_cast<uint4*>(p.act_out + m * p.act_f + f0 + j * 32);
+#pragma unroll
+            for (int q = 0; q < 4; ++q) {
+              uint4 w;
+              uint32_t* wp = reinterpret_cast<uint32_t*>(&w);
+#pragma unroll
+              for (int e = 0; e < 4; ++e) {
+                const float g0 = __uint_as_float(g[8 * q + 2 * e]), g1 = __uint_as_float(g[8 * q + 2 * e + 1]);
+                const float u0 = __uint_as_float(u[8 * q + 2 * e]), u1 = __uint_as_float(u[8 * q + 2 * e + 1]);
+                const __nv_bfloat162 pr =
+                    __floats2bfloat162_rn(g0 / (1.0f + expf(-g0)) * u0, g1 / (1.0f + expf(-g1)) * u1);
+                wp[e] = *reinterpret_cast<const uint32_t*>(&pr);
+              }
+              dst[q] = w;
+            }
+          }
+        }
+      }
+      for (int j = 0; p.act_out == nullptr && j < TL::kHeads; ++j) {
         const int h = h0 + j;
         if (h >= n_groups) break;  // warp-uniform
         uint32_t r[32];
@@ -502,6 +534,42 @@ int proj_codes_v(const void* x, const void* w_all, int64_t M, int64_t K, int64_t
   }
 }
 
+// The MLP's gate/up GEMM with SwiGLU in the epilogue: act[m][f] = silu(x[m] . gate[f]) *
+// (x[m] . up[f]) for x [M][K] and w_il [2F][K], the gate and up rows interleaved in blocks of
+// 128 (rows 256 nb ... 256 nb + 127: gate rows 128 nb ...; the next 128: the up rows of the
+// same features). The [M][2F] product never goes to HBM.
+int gemm_swiglu(const void* x, const void* w_il, int64_t M, int64_t K, int64_t F, void* act_out,
+                uint32_t* status, cudaStream_t stream) {
+  using namespace k1;
+  if (M < 0 || K <= 0 || F <= 0) return fail(LEMA_ERR_INVALID_ARGUMENT, "gemm_swiglu: bad shape M=%lld K=%lld F=%lld", (long long)M, (long long)K, (long long)F);
+  if (K % kBK != 0 || F % 128 != 0) return fail(LEMA_ERR_INVALID_ARGUMENT, "gemm_swiglu: K (%lld) a multiple of 64, F (%lld) of 128", (long long)K, (long long)F);
+  if (M >= (int64_t(1) << 31) || K >= (int64_t(1) << 24) || F >= (int64_t(1) << 24))
+    return fail(LEMA_ERR_INVALID_ARGUMENT, "gemm_swiglu: shape too large");
+  if (M == 0) return LEMA_OK;
+  if (x == nullptr || w_il == nullptr || act_out == nullptr) return fail(LEMA_ERR_INVALID_ARGUMENT, "gemm_swiglu: null pointer");
+  if (!aligned(x, 16) || !aligned(w_il, 16) || !aligned(act_out, 16))
+    return fail(LEMA_ERR_INVALID_ARGUMENT, "gemm_swiglu: x, w and act must be 16-byte aligned");
+  const DeviceInfo* dev = current_device_info();
+  if (dev == nullptr) return LEMA_ERR_CUDA;
+  if (dev->cc_major != 10) return fail(LEMA_ERR_UNSUPPORTED, "built for sm_100a; device is sm_%d%d", dev->cc_major, dev->cc_minor);
+  EncodeTiledFn enc = encode_tiled();
+  if (enc == nullptr) return fail(LEMA_ERR_CUDA, "cuTensorMapEncodeTiled is not available from the driver");
+  CUtensorMap map_x, map_w;
+  if (!encode_kmajor(enc, &map_x, x, M, K, kBM) || !encode_kmajor(enc, &map_w, w_il, 2 * F, K, 256))
+    return fail(LEMA_ERR_INVALID_ARGUMENT, "gemm_swiglu: tensor map encoding failed (M=%lld K=%lld F=%lld)", (long long)M, (long long)K, (long long)F);
+  Params prm{};
+  prm.status = status;
+  prm.M = M;
+  prm.T = M;
+  prm.k_blocks = static_cast<int>(K / kBK);
+  prm.act_out = static_cast<__nv_bfloat16*>(act_out);
+  prm.act_f = F;
+  prm.n_blocks = static_cast<int>(2 * F / 256);
+  prm.n_tiles = ((M + kBM - 1) / kBM) * prm.n_blocks;
+  const int64_t grid = std::min<int64_t>(prm.n_tiles, dev->sms);
+  return launch<256>(map_x, map_w, prm, grid, stream);
+}
+
 // RMS scale of each row: out[m] = 1 / sqrt(mean(x[m]^2) + eps), fp32 sums; one warp per row.
 __global__ void row_rms_kernel(const __nv_bfloat16* x, int64_t M, int64_t K, float eps, float* out) {
   const int64_t warps = (int64_t(gridDim.x) * blockDim.x) >> 5;
@@ -544,6 +612,12 @@ extern "C" int lema_proj_codes_v(const void* x, const void* w_all, int64_t M, in
   lema::clear_error();
   return lema::proj_codes_v(x, w_all, M, K, T, hq, hk, d_qk, qcodes, kcodes, n_v, v_out, row_scale, status,
                             static_cast<cudaStream_t>(stream));
+}
+
+extern "C" int lema_gemm_swiglu(const void* x, const void* w_il, int64_t M, int64_t K, int64_t F, void* act_out,
+                                uint32_t* status, void* stream) {
+  lema::clear_error();
+  return lema::gemm_swiglu(x, w_il, M, K, F, act_out, status, static_cast<cudaStream_t>(stream));
 }
 
 extern "C" int lema_row_rms(const void* x, int64_t M, int64_t K, float eps, float* out, void* stream) {

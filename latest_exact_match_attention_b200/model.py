@@ -106,9 +106,14 @@ def rms_norm(norm: nn.RMSNorm, x: torch.Tensor) -> torch.Tensor:
 
 
 class SwiGLU(nn.Module):
-    """down(silu(gate(x)) * up(x)), parameters named as code/lema/model.py:85-93. On a GPU the
-    gate and up projections are one GEMM on their stacked weights and the activation is one
-    kernel (lema_swiglu); `forward(x, residual)` adds the residual inside the down GEMM."""
+    """down(silu(gate(x)) * up(x)), parameters named as code/lema/model.py:85-93. On a GPU, for
+    bf16 prefill-sized inputs (at least FUSED_MIN_ROWS rows) the gate and up projections and
+    the activation are one tcgen05 GEMM with SwiGLU in its epilogue (lema_gemm_swiglu, on the
+    gate/up weights interleaved in blocks of 128 rows); otherwise one GEMM on the stacked
+    weights and one activation kernel (lema_swiglu). `forward(x, residual)` adds the residual
+    inside the down GEMM."""
+
+    FUSED_MIN_ROWS = 4096  # below this the fused GEMM has too few 128-row tiles per SM
 
     def __init__(self, dim: int, dim_ff: int):
         super().__init__()
@@ -116,6 +121,7 @@ class SwiGLU(nn.Module):
         self.up = nn.Linear(dim, dim_ff, bias=False)
         self.down = nn.Linear(dim_ff, dim, bias=False)
         self._wgu = None
+        self._wil = None
 
     def gate_up_weight(self) -> torch.Tensor:
         g, u = self.gate.weight, self.up.weight
@@ -124,17 +130,37 @@ class SwiGLU(nn.Module):
             self._wgu = (key, torch.cat([g.detach(), u.detach()], 0).contiguous())
         return self._wgu[1]
 
+    def gate_up_interleaved(self) -> torch.Tensor:
+        """[2F, dim]: gate rows 128 b ... 128 b + 127, then the up rows of the same features."""
+        g, u = self.gate.weight, self.up.weight
+        key = (g.data_ptr(), u.data_ptr(), g._version, u._version)
+        if getattr(self, "_wil", None) is None or self._wil[0] != key:
+            Fd, dim = g.shape
+            w = torch.stack([g.detach().view(Fd // 128, 128, dim), u.detach().view(Fd // 128, 128, dim)], 1)
+            self._wil = (key, w.reshape(2 * Fd, dim).contiguous())
+        return self._wil[1]
+
+    def _fused_ok(self, x2) -> bool:
+        Fd, dim = self.gate.weight.shape
+        return (x2.dtype == torch.bfloat16 and x2.shape[0] >= self.FUSED_MIN_ROWS and Fd % 128 == 0
+                and dim % 64 == 0 and x2.is_contiguous() and x2.data_ptr() % 16 == 0
+                and self.gate.weight.dtype == torch.bfloat16 and torch.cuda.get_device_capability(x2.device)[0] == 10)
+
     def forward(self, x, residual=None):
         if not x.is_cuda or x.dtype not in DTYPE_TAG:
             y = self.down(F.silu(self.gate(x)) * self.up(x))
             return y if residual is None else residual + y
         lead, dim = x.shape[:-1], x.shape[-1]
         x2 = x.reshape(-1, dim)
-        gu = x2 @ self.gate_up_weight().t()
         Fd = self.gate.weight.shape[0]
         act = torch.empty((x2.shape[0], Fd), dtype=x.dtype, device=x.device)
-        call("lema_swiglu", ptr(gu), DTYPE_TAG[x.dtype], x2.shape[0], Fd, ptr(act),
-             stream_handle(x.device))
+        if self._fused_ok(x2):
+            call("lema_gemm_swiglu", ptr(x2), ptr(self.gate_up_interleaved()), x2.shape[0], dim, Fd,
+                 ptr(act), None, stream_handle(x.device))
+        else:
+            gu = x2 @ self.gate_up_weight().t()
+            call("lema_swiglu", ptr(gu), DTYPE_TAG[x.dtype], x2.shape[0], Fd, ptr(act),
+                 stream_handle(x.device))
         w = self.down.weight.t()
         y = act @ w if residual is None else torch.addmm(residual.reshape(-1, dim), act, w)
         return y.view(*lead, dim)

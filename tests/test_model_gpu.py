@@ -147,3 +147,32 @@ def test_rms_norm_matches_fp32(cuda, dtype, M, D):
     assert float((got == ref).float().mean()) > 0.98
     torch.testing.assert_close(got.float(), torch.nn.functional.rms_norm(
         x.float(), (D,), norm.weight.float(), 1e-5), rtol=2 * ulp, atol=1e-3)
+
+
+@pytest.mark.parametrize("M,dim,Fd", [(4096, 256, 640), (4400, 1024, 4096), (130 * 128 + 3, 512, 128)])
+def test_fused_gemm_swiglu_matches_two_pass(cuda, M, dim, Fd):
+    """lema_gemm_swiglu (gate/up GEMM with SwiGLU on the fp32 accumulators) against the fp32
+    formula on the same bf16 inputs: within bf16 rounding (the two-pass path rounds the GEMM
+    output to bf16 first, the fused one does not), and the MLP built on it against torch."""
+    from latest_exact_match_attention_b200.model import SwiGLU
+    torch.manual_seed(M)
+    mlp = SwiGLU(dim, Fd).to(cuda).to(torch.bfloat16)
+    x = (torch.randn(M, dim, device=cuda) * 0.5).to(torch.bfloat16)
+    r = torch.randn(M, dim, device=cuda).to(torch.bfloat16)
+    st = torch.zeros(1, dtype=torch.int32, device=cuda)
+    act = torch.empty(M, Fd, dtype=torch.bfloat16, device=cuda)
+    from latest_exact_match_attention_b200._lib import call, ptr, stream_handle
+    call("lema_gemm_swiglu", ptr(x), ptr(mlp.gate_up_interleaved()), M, dim, Fd, ptr(act), ptr(st),
+         stream_handle(x.device))
+    torch.cuda.synchronize()
+    assert int(st.item()) == 0
+    with torch.no_grad():
+        g = x.float() @ mlp.gate.weight.float().t()
+        u = x.float() @ mlp.up.weight.float().t()
+        ref = torch.nn.functional.silu(g) * u
+    torch.testing.assert_close(act.float(), ref, rtol=2e-2, atol=2e-2 * float(ref.abs().mean()))
+    assert mlp._fused_ok(x)
+    with torch.no_grad():
+        got = mlp(x.view(1, M, dim), residual=r.view(1, M, dim)).float().view(M, dim)
+        want = (ref.to(torch.bfloat16).float() @ mlp.down.weight.float().t()) + r.float()
+    torch.testing.assert_close(got, want, rtol=3e-2, atol=3e-2 * float(want.abs().mean()))
