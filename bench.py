@@ -307,8 +307,11 @@ def run_b200(args):
     achieved = alg_bytes / (per_launch_ms / 1e3) / 1e9
     # DRAM bytes per call of the three kernels, from the full-size ncu capture summarised in
     # profiles/ (only meaningful for the default 512-stream workload)
-    # K2 runs pipelined (one launch matches and copies rows) unless LEMA_K2_PIPELINE=0
-    pipelined = os.environ.get("LEMA_K2_PIPELINE", "")[:1] != "0"
+    # K2 runs pipelined (one launch matches and copies rows) from one full wave of matchers
+    # (2 per SM) on, unless LEMA_K2_PIPELINE=0; the rows here are 48 bytes (16-byte aligned)
+    sms = torch.cuda.get_device_properties(dev).multi_processor_count
+    pipelined = (os.environ.get("LEMA_K2_PIPELINE", "")[:1] != "0" and N_STREAMS >= 2 * sms
+                 and T <= (1 << 22))
     traffic = None
     tf = ROOT / "profiles" / "prefill_match_cfg2.md"
     if tf.exists() and N_STREAMS == 512:
