@@ -89,6 +89,16 @@ def test_argument_validation_on_host():
     assert rc("lema_proj_codes", P, P, 128, 64, 128, 1, 1, 16, P, P, None, None) == 1
     assert rc("lema_proj_codes", P, P, 128, 96, 128, 1, 1, 32, P, P, None, None) == 1
     assert rc("lema_proj_codes", P, P, 100, 64, 64, 1, 1, 32, P, P, None, None) == 1
+    # fused gate/up GEMM + SwiGLU: K a multiple of 64, F of 128, no null pointers
+    assert rc("lema_gemm_swiglu", P, P, 4096, 100, 128, P, None, None) == 1
+    assert rc("lema_gemm_swiglu", P, P, 4096, 128, 100, P, None, None) == 1
+    assert rc("lema_gemm_swiglu", P, None, 4096, 128, 128, P, None, None) == 1
+    assert rc("lema_gemm_swiglu", None, None, 0, 128, 128, None, None, None) == 0   # no rows: no-op
+    # RMSNorm: 16-bit rows only, D a multiple of 8 (else the caller's own norm), no nulls
+    assert rc("lema_rms_norm", P, P, 0, 4, 64, ctypes.c_float(1e-5), P, None) == 4      # fp32
+    assert rc("lema_rms_norm", P, P, 1, 4, 100, ctypes.c_float(1e-5), P, None) == 4     # D % 8
+    assert rc("lema_rms_norm", P, None, 1, 4, 64, ctypes.c_float(1e-5), P, None) == 1
+    assert rc("lema_rms_norm", None, None, 1, 0, 64, ctypes.c_float(1e-5), None, None) == 0
 
 
 def test_python_layer_refuses_cpu_tensors():
