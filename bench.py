@@ -475,7 +475,6 @@ def run_decode(args):
     Bd, prefix = args.decode_batch, args.prefix
     torch.manual_seed(0)
     model = Transformer(cfg).to(dev).to(torch.bfloat16).eval()
-    model.set_fused_pre(args.fused_pre)
     idx = torch.from_numpy(synth.token_stream(Bd, prefix + 1, 50304, seed=0, config_id=4)).to(dev)
     P = Bd * cfg.num_heads
     per_part = args.entries_per_partition or (prefix + args.steps + args.warmup + 8)
@@ -511,7 +510,6 @@ def run_decode(args):
         "ms_per_step": round(ms, 4), "higher_is_better": True, "dtype": "bf16",
         "data": "synthetic Zipf(1.1) tokens, 20% bigram copies; random-init weights",
         "config": {"workload": f"cfg4: {cfg.summary()}, B={Bd}, prefix {prefix}",
-                   "fused_pre": bool(args.fused_pre),
                    "store_slots": cap, "store_gb": round(cache.nbytes() / 1e9, 2),
                    "store_load": round(cache.load(), 4),
                    "entries_per_partition_by_layer": [round(float(x), 1) for x in counts.mean((1, 2))],
@@ -632,8 +630,6 @@ def main():
     ap.add_argument("--entries-per-partition", type=int, default=0,
                     help="--workload decode: store sizing (0 = worst case, one entry per token)")
     ap.add_argument("--max-load", type=float, default=0.8, help="--workload decode: table load")
-    ap.add_argument("--fused-pre", action="store_true",
-                    help="--workload decode: norm1 + q/k/v projections as one K1 GEMM")
     ap.add_argument("--heads", type=int, nargs="+", default=[8, 16, 32, 64],
                     help="--workload proj: query (= key) heads per layer")
     ap.add_argument("--proj-batch", type=int, default=32, help="--workload proj: sequences")

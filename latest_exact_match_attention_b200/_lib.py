@@ -93,6 +93,54 @@ def call(name: str, *args) -> None:
         raise LemaError(f"{name} failed (code {rc}): {msg}")
 
 
+_status_words: dict[int, torch.Tensor] = {}
+
+
+def device_status(device) -> torch.Tensor:
+    """The package's status word on `device` (int32 [1], zero-initialised): every product call
+    that is given no status word of its own ORs its device-side conditions into it (a bounded
+    wait that ran out, a full table). Allocated on first use, which must not be inside a CUDA
+    graph capture (one eager call first: the decoder's warm-up steps make it)."""
+    dev = torch.device(device)
+    idx = dev.index if dev.index is not None else torch.cuda.current_device()
+    st = _status_words.get(idx)
+    if st is None:
+        if torch.cuda.is_current_stream_capturing():
+            raise LemaError("the device status word is allocated on first use: make one call "
+                            "outside CUDA graph capture first")
+        st = torch.zeros(1, dtype=torch.int32, device=torch.device("cuda", idx))
+        _status_words[idx] = st
+    return st
+
+
+def check_status(device, what: str = "LEMA kernel") -> None:
+    """Raise LemaError if a call that used the package's status word on `device` reported a
+    device-side condition since the last check (then clear the word). Reads the word, so it
+    waits for the work queued so far; does nothing inside a CUDA graph capture (check after
+    the replay instead)."""
+    dev = torch.device(device)
+    idx = dev.index if dev.index is not None else torch.cuda.current_device()
+    st = _status_words.get(idx)
+    if st is None or torch.cuda.is_current_stream_capturing():
+        return
+    s = int(st.item())
+    if s:
+        st.zero_()
+        raise LemaError(status_message(s, what))
+
+
+def status_message(s: int, what: str) -> str:
+    parts = []
+    if s & LEMA_STATUS_PROBE_LIMIT:
+        parts.append("a bounded device-side wait or probe ran out: the outputs are incomplete")
+    if s & LEMA_STATUS_TABLE_FULL:
+        parts.append("hash table full")
+    rest = s & ~(LEMA_STATUS_PROBE_LIMIT | LEMA_STATUS_TABLE_FULL)
+    if rest:
+        parts.append(f"status bits {rest:#x}")
+    return f"{what}: " + "; ".join(parts)
+
+
 def stream_handle(device: torch.device | None = None) -> int:
     """The raw cudaStream_t of torch's current stream on `device`."""
     return torch.cuda.current_stream(device).cuda_stream

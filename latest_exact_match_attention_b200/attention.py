@@ -23,7 +23,7 @@ from __future__ import annotations
 import torch
 
 from . import _lib
-from ._lib import DTYPE_TAG, LemaError, call, ptr, require_cuda, stream_handle
+from ._lib import DTYPE_TAG, LemaError, call, check_status, device_status, ptr, require_cuda, stream_handle
 
 __all__ = ["pack_codes", "proj_codes", "latest_prev_match", "lema_hard", "prefill_match",
            "prefill_match_host", "HostPrefill", "proj_codes_v", "row_rms", "code_bytes_of"]
@@ -81,6 +81,8 @@ def proj_codes(x: torch.Tensor, w_qk: torch.Tensor, hq: int, hk: int,
     The tensor-core GEMM accumulates in fp32, so a bit can differ from a bf16 GEMM followed
     by pack_codes only where that pre-activation is within rounding of zero.
     Mirrors code/lema/model.py:224-227 (`Block.gpu_pre`) minus the norm and v_proj.
+    Device-side conditions go to `status`, or to the package's status word of the device
+    (`_lib.check_status` raises on them).
     """
     dev = require_cuda(x, w_qk)
     if x.dtype != torch.bfloat16 or w_qk.dtype != torch.bfloat16:
@@ -93,6 +95,8 @@ def proj_codes(x: torch.Tensor, w_qk: torch.Tensor, hq: int, hk: int,
     B, T, dim = x.shape
     qc = torch.empty((B, hq, T), dtype=torch.int32, device=dev)
     kc = torch.empty((B, hk, T), dtype=torch.int32, device=dev)
+    if status is None:
+        status = device_status(dev)
     call("lema_proj_codes", ptr(x), ptr(w_qk), B * T, dim, T, hq, hk, 32, ptr(qc), ptr(kc),
          ptr(status), stream_handle(dev))
     return qc, kc
@@ -123,6 +127,8 @@ def proj_codes_v(x: torch.Tensor, w_all: torch.Tensor, hq: int, hk: int, n_v: in
     qc = torch.empty((B, hq, T), dtype=torch.int32, device=dev)
     kc = torch.empty((B, hk, T), dtype=torch.int32, device=dev)
     v = torch.empty((B, T, n_v), dtype=torch.bfloat16, device=dev)
+    if status is None:
+        status = device_status(dev)
     call("lema_proj_codes_v", ptr(x), ptr(w_all), B * T, dim, T, hq, hk, 32, ptr(qc), ptr(kc),
          n_v, ptr(v), ptr(row_scale), ptr(status), stream_handle(dev))
     return qc, kc, v
@@ -139,7 +145,8 @@ def prefill_match(qc: torch.Tensor, kc: torch.Tensor, v: torch.Tensor | None = N
     ...] value rows (optional). Returns (src, out): src [N, T] int32 (latest j < i with an
     equal key code, else -1) when want_src, out like v with the gathered rows (zeros on a
     miss) when v is given. Device status bits are OR-ed into `status` (an int32 [1] device
-    tensor) when given."""
+    tensor) when given, else into the package's status word of the device, which
+    `_lib.check_status` reads."""
     dev = require_cuda(qc, kc, v, status)
     if qc.dim() != 2 or qc.shape != kc.shape:
         raise ValueError(f"qc and kc must be [N, T] of one shape, got {tuple(qc.shape)} and "
@@ -158,6 +165,8 @@ def prefill_match(qc: torch.Tensor, kc: torch.Tensor, v: torch.Tensor | None = N
         out = torch.empty_like(v)
         vbytes = v[0, 0].numel() * v.element_size() if N * T else 0
     ws = _workspace(_lib.lib().lema_prefill_workspace_bytes(N, T, cb), dev)
+    if status is None and N * T:
+        status = device_status(dev)
     call("lema_prefill_match", ptr(qc), ptr(kc), cb, N, T, ptr(src), ptr(v), vbytes or 0,
          ptr(out), ptr(ws), 0 if ws is None else ws.numel(), ptr(status), stream_handle(dev))
     return src, out
@@ -165,8 +174,11 @@ def prefill_match(qc: torch.Tensor, kc: torch.Tensor, v: torch.Tensor | None = N
 
 def latest_prev_match(qc: torch.Tensor, kc: torch.Tensor) -> torch.Tensor:
     """For each i, the largest j < i with kc[j] == qc[i], else -1 (int64 [N, T], as
-    code/lema/attention.py:100-132 returns)."""
+    code/lema/attention.py:100-132 returns). Raises LemaError if a device-side bound ran out
+    (the check reads the device status word, so the call returns once the kernels are done;
+    inside a CUDA graph capture it is skipped)."""
     src, _ = prefill_match(qc, kc)
+    check_status(src.device, "latest_prev_match")
     return src.to(torch.int64)
 
 
@@ -177,6 +189,7 @@ def lema_hard(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, store=None) -> 
     read); v: [B, H, T, d_v]. With a `store` (a LayerStore) the rule is one exchange
     against it, so this window's queries also see every key fed before; without one it is
     a self-contained forward over the window. Returns [B, H, T, d_v] in v's dtype.
+    Raises LemaError if a device-side bound ran out (see latest_prev_match).
     """
     B, H, T, D = q.shape
     narrow = D <= 32
@@ -186,6 +199,7 @@ def lema_hard(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, store=None) -> 
     d_v = v.shape[-1]
     _, out = prefill_match(qc.view(B * H, T), kc.view(B * H, T),
                            v.reshape(B * H, T, d_v), want_src=False)
+    check_status(out.device, "lema_hard")
     return out.view(B, H, T, d_v)
 
 
@@ -219,6 +233,8 @@ class HostPrefill:
     def __call__(self, qc, kc, v=None, src_out=None, out=None, status=None):
         s_in, s_cp, s_out = self.streams
         cur = torch.cuda.current_stream(self.device)
+        if status is None:
+            status = device_status(self.device)
         N = qc.shape[0]
         for s in self.streams:
             s.wait_stream(cur)

@@ -292,8 +292,11 @@ class LemaCache:
         return self.store.load()
 
     def check(self):
-        """Raise if any exchange since the last check found the table full."""
+        """Raise if any exchange since the last check found the table full, or if a kernel of
+        the model's steps (codes, MLP) reported that a bounded device wait ran out. Reads the
+        device status words: call it after stepping (outside graph capture)."""
         self.store.check()
+        _lib.check_status(self.store.device, "LEMA step")
 
     def dump(self, layer: int | None = None):
         """Entries as (layer, batch, head, code, row) tensors, all layers or one."""

@@ -3,6 +3,7 @@
 #include <cuda_runtime.h>
 
 #include <cstdarg>
+#include <cstdlib>
 #include <cstdio>
 #include <mutex>
 
@@ -51,6 +52,15 @@ int cuda_fail(cudaError_t e, const char* what) {
   snprintf(g_err, sizeof(g_err), "CUDA error %d (%s) in %s", static_cast<int>(e),
            cudaGetErrorString(e), what);
   return LEMA_ERR_CUDA;
+}
+
+unsigned long long wait_limit_ns() {
+  const char* e = std::getenv("LEMA_WAIT_NS");
+  if (e != nullptr) {
+    const unsigned long long v = std::strtoull(e, nullptr, 10);
+    if (v > 0) return v;
+  }
+  return 4000000000ull;
 }
 
 const DeviceInfo* current_device_info() {

@@ -90,6 +90,12 @@ struct DeviceInfo {
 // Cached per device; queried once. Returns nullptr (and sets the error) on failure.
 const DeviceInfo* current_device_info();
 
+// Bound, in nanoseconds, of every device-side wait on another warp's, CTA's or pipeline
+// stage's progress: 4 s, or LEMA_WAIT_NS from the environment (read at each launch; tests
+// shorten it to make a wait run out on purpose). A wait that runs out sets
+// LEMA_STATUS_PROBE_LIMIT and returns; it never traps.
+unsigned long long wait_limit_ns();
+
 #define LEMA_CUDA_TRY(expr)                                \
   do {                                                     \
     cudaError_t _e = (expr);                               \

@@ -121,6 +121,16 @@ struct Table {
     return round_up16(slots * sizeof(CodeT)) + round_up16((slots + 1) * sizeof(CarryT)) +
            round_up16((slots + 1) * sizeof(uint32_t)) + 16;
   }
+  // codes and the side word only (the dictionary of the sweep path: no carries, no masks)
+  __device__ void init_dict(void* base, uint32_t slots) {
+    cap = slots;
+    bmask = slots / kBucket - 1;
+    bshift = 32 - (31 - __clz(slots / kBucket));
+    code = static_cast<CodeT*>(base);
+    side = reinterpret_cast<uint32_t*>(static_cast<unsigned char*>(base) + slots * sizeof(CodeT));
+    carry = nullptr;
+    mask = nullptr;
+  }
   __device__ void init(void* base, uint32_t slots) {
     cap = slots;
     bmask = slots / kBucket - 1;
@@ -310,7 +320,6 @@ constexpr int kUnitChunks = 4;                    // chunks per gather unit and 
 constexpr uint32_t kProgOvf = 0x80000000u;        // progress word of a stream handed to the overflow path
 constexpr int kMaxSmIds = 512;                    // %smid values with a role slot
 constexpr uint32_t kRoleMatch = 1, kRoleGather = 2;
-constexpr unsigned long long kWaitNs = 4000000000ull;  // a wait for a unit gives up after 4 s
 struct PipeCtl {
   uint32_t sm_seen[kMaxSmIds];  // CTAs started per SM
   uint32_t sm_role[kMaxSmIds];  // the role of each SM, set by its first CTA
@@ -344,6 +353,7 @@ struct Params {
   uint32_t wave;          // streams matched at once: the gather units' order
   int gather_inline;      // overflow path: gather each stream right after matching it
   GatherParams g;         // uint4 words (pipelined and inline gathers)
+  unsigned long long wait_ns;  // bound of every wait on another warp's or CTA's progress
 };
 
 __device__ __forceinline__ void st_release(uint32_t* p, uint32_t v) {
@@ -425,12 +435,13 @@ __device__ __forceinline__ void cp_async16(void* smem_dst, const void* gsrc, boo
                : "memory");
 }
 
-// Rows [t0, t1) of stream n through this CTA's shared memory (kThreads threads; `buf` holds
-// `rows_per_pass` <= 2 * kThreads rows): every thread fetches its rows of a pass with
+// Rows [t0, t1) of stream n through this CTA's shared memory (kThr threads; `buf` holds
+// `rows_per_pass` <= 2 * kThr rows): every thread fetches its rows of a pass with
 // asynchronous 16-byte copies (zero fill on a miss), so a pass keeps the whole buffer in
 // flight without holding registers; the indices of the next pass load meanwhile; then the
 // CTA writes the pass out with coalesced streaming stores. A CTA whose table is idle (a
 // row-copying CTA, or a matcher with no stream left) lends its shared memory to this.
+template <int kThr>
 __device__ void gather_unit_staged(const GatherParams& g, int64_t n, uint32_t t0, uint32_t t1, int tid,
                                    uint4* buf, uint32_t rows_per_pass) {
   const int32_t* src = g.src + n * g.T;
@@ -442,7 +453,7 @@ __device__ void gather_unit_staged(const GatherParams& g, int64_t n, uint32_t t0
   {
     const uint32_t lim = min(t1, t0 + rows_per_pass);
     if (t0 + tid < lim) s0 = __ldcg(src + t0 + tid);
-    if (t0 + kThreads + tid < lim) s1 = __ldcg(src + t0 + kThreads + tid);
+    if (t0 + kThr + tid < lim) s1 = __ldcg(src + t0 + kThr + tid);
   }
   for (uint32_t r0 = t0; r0 < t1; r0 += rows_per_pass) {
     const uint32_t cnt = min(rows_per_pass, t1 - r0);
@@ -450,9 +461,9 @@ __device__ void gather_unit_staged(const GatherParams& g, int64_t n, uint32_t t0
       const unsigned char* row = v + static_cast<int64_t>(max(s0, 0)) * g.v_st;
       for (uint32_t c = 0; c < wpr; ++c) cp_async16(buf + tid * wpr + c, row + 16 * c, s0 >= 0);
     }
-    if (static_cast<uint32_t>(kThreads + tid) < cnt) {
+    if (static_cast<uint32_t>(kThr + tid) < cnt) {
       const unsigned char* row = v + static_cast<int64_t>(max(s1, 0)) * g.v_st;
-      for (uint32_t c = 0; c < wpr; ++c) cp_async16(buf + (kThreads + tid) * wpr + c, row + 16 * c, s1 >= 0);
+      for (uint32_t c = 0; c < wpr; ++c) cp_async16(buf + (kThr + tid) * wpr + c, row + 16 * c, s1 >= 0);
     }
     asm volatile("cp.async.commit_group;" ::: "memory");
     const uint32_t r1 = r0 + rows_per_pass;
@@ -460,11 +471,11 @@ __device__ void gather_unit_staged(const GatherParams& g, int64_t n, uint32_t t0
     if (r1 < t1) {
       const uint32_t lim = min(t1, r1 + rows_per_pass);
       if (r1 + tid < lim) s0 = __ldcg(src + r1 + tid);
-      if (r1 + kThreads + tid < lim) s1 = __ldcg(src + r1 + kThreads + tid);
+      if (r1 + kThr + tid < lim) s1 = __ldcg(src + r1 + kThr + tid);
     }
     asm volatile("cp.async.wait_all;" ::: "memory");
     __syncthreads();
-    for (uint32_t w = tid; w < cnt * wpr; w += kThreads) {
+    for (uint32_t w = tid; w < cnt * wpr; w += kThr) {
       const uint32_t r = g.div_shift >= 0 ? (w >> g.div_shift)
                                           : (g.div_magic ? __umulhi(w, g.div_magic) : w / wpr);
       store_stream(reinterpret_cast<uint4*>(o + static_cast<int64_t>(r0 + r) * g.o_st) + (w - r * wpr), buf[w]);
@@ -504,6 +515,7 @@ __device__ uint32_t pipe_role(const Params& p, int tid) {
 // about the same time), chunk group by chunk group, so a unit's turn comes about when its
 // rows are matched. A unit waits for its stream's published progress (bounded); a stream
 // handed to the overflow path is gathered there.
+template <int kThr>
 __device__ void pipe_gather(const Params& p, int tid, uint4* buf, uint32_t rows_per_pass) {
   __shared__ uint32_t s_n, s_t0, s_t1;
   __shared__ int s_go;
@@ -525,7 +537,7 @@ __device__ void pipe_gather(const Params& p, int tid, uint4* buf, uint32_t rows_
         if (v < need) {
           const unsigned long long t0 = global_ns();
           while ((v = ld_acquire(p.progress + n)) < need) {
-            if (ld_acquire(&p.ctl->failed) != 0u || global_ns() - t0 > kWaitNs) {
+            if (ld_acquire(&p.ctl->failed) != 0u || global_ns() - t0 > p.wait_ns) {
               atomicExch(&p.ctl->failed, 1u);
               raise_status(p.status, LEMA_STATUS_PROBE_LIMIT);
               break;
@@ -542,7 +554,7 @@ __device__ void pipe_gather(const Params& p, int tid, uint4* buf, uint32_t rows_
     __syncthreads();
     const int go = s_go;
     if (go < 0) break;
-    if (go) gather_unit_staged(p.g, s_n, s_t0, s_t1, tid, buf, rows_per_pass);
+    if (go) gather_unit_staged<kThr>(p.g, s_n, s_t0, s_t1, tid, buf, rows_per_pass);
     __syncthreads();  // s_* are rewritten for the next unit
   }
 }
@@ -585,7 +597,7 @@ __global__ void __launch_bounds__(kThreads, 2) match_kernel(const Params p) {
                                               (16u * p.g.wpr))) : 0u;
   if constexpr (kPipe) {
     if (pipe_role(p, tid) != kRoleMatch) {
-      pipe_gather(p, tid, reinterpret_cast<uint4*>(smem), stage_rows);
+      pipe_gather<kThreads>(p, tid, reinterpret_cast<uint4*>(smem), stage_rows);
       return;
     }
   }
@@ -755,9 +767,322 @@ __global__ void __launch_bounds__(kThreads, 2) match_kernel(const Params p) {
     }
   }
   // no stream left: copy rows with the others
-  if constexpr (kPipe) pipe_gather(p, tid, reinterpret_cast<uint4*>(smem), stage_rows);
+  if constexpr (kPipe) pipe_gather<kThreads>(p, tid, reinterpret_cast<uint4*>(smem), stage_rows);
 }
 
+
+// ---------------------------------------------------------------- dictionary + sweep
+// A second matcher for streams of at most kSweepMaxT positions. One CTA of kSwThreads threads
+// owns a stream at a time (kSwPerSm CTAs per SM):
+//   A (dictionary, order-free). Every key code goes into a shared-memory table of the stream's
+//     distinct key codes, all threads at once; its slot is the key's ID. After a barrier every
+//     query code is looked up: its ID is that slot, or kNone when no key of the stream holds
+//     the code. Position i's two IDs (key | query << 16) are written over src[i], which the
+//     sweep then reads and overwrites with the answer. Each lookup first tries the code's own
+//     slot (one shared load); the lanes that need more (a slot held by another code) are
+//     queued per warp and served together after each round, so a warp pays for the longer
+//     probe once per round instead of once per position.
+//   B (sweep, ordered). One warp walks the stream in steps of 32 positions with two arrays
+//     indexed by ID, laid over the table's memory:
+//       last[id]   1 + the latest key position with that ID before the step (0: none)
+//       lanes[id]  the step's key lanes holding that ID (cleared after every step)
+//     Per step: keys OR their lane into lanes[id]; a query answers with the highest key lane
+//     below its own in lanes[its id], else last[its id] - 1; the highest key lane of each ID
+//     writes last[id]. About twenty warp instructions per 32 positions, no divergence.
+// Used for calls without value rows (src only) of at least one wave of CTAs (kSwPerSm per SM
+// on half the SMs): measured on config 2 (512 streams x 16384) 0.149 ms against the chunked
+// matcher's 0.181 ms. Its cost per stream is a latency chain (phase B: ~64 us at T = 16384)
+// rather than issue slots, so with fewer streams the chunked matcher, whose 32 warps share a
+// stream, is faster, and with value rows the row copy (bandwidth-bound, ~0.13 ms) dominates
+// either way: row traffic on the same SM slows the sweep's shared-memory chain, and copying
+// rows through the bulk-copy engine instead topped out at ~2 TB/s for 48-byte rows.
+// A stream whose distinct key codes would load the table beyond kOverflowFrac goes to the
+// overflow path (the global-table match_kernel) as in the chunked path; results never depend
+// on the path.
+constexpr int kSwThreads = 256;
+constexpr int kSwWarps = kSwThreads / 32;
+constexpr int kSwPerSm = 4;
+constexpr int64_t kSweepMaxT = 65535;  // 1 + a position fits the 16-bit last[] words
+constexpr int kSwBatch = 16;           // steps whose IDs the sweep loads at once
+constexpr uint32_t kPending = 0xFFFFFFFEu;  // own-slot attempt inconclusive: queued
+
+template <typename CodeT>
+struct SweepLayout {
+  static constexpr uint32_t kSlots = SmemCap<CodeT>::kSlots;
+  static constexpr uint32_t kSide = kSlots;       // slot of the all-ones code
+  static constexpr uint32_t kDummy = kSlots + 1;  // key ID of lanes past the end
+  static constexpr uint32_t kNone = kSlots + 2;   // query ID: no key holds the code
+  static constexpr uint32_t kIds = kSlots + 3;
+  static constexpr int kRound = sizeof(CodeT) == 4 ? 8 : 4;  // positions per thread per round
+  static constexpr size_t kDictBytes = round_up16(kSlots * sizeof(CodeT) + sizeof(uint32_t));
+  // per warp during phase A: codes and positions of the queued lanes of one round
+  static constexpr size_t kQueueCodeBytes = round_up16(kRound * 32 * sizeof(CodeT));
+  static constexpr size_t kQueueBytes = kQueueCodeBytes + round_up16(kRound * 32 * sizeof(uint16_t));
+  static constexpr size_t kPhaseABytes = kDictBytes + kSwWarps * kQueueBytes;
+  static constexpr size_t kLanesBytes = round_up16(kIds * sizeof(uint32_t));
+  static constexpr size_t kLastBytes = round_up16(kIds * sizeof(uint16_t));
+  static constexpr size_t kBytes =
+      kPhaseABytes > kLanesBytes + kLastBytes ? kPhaseABytes : kLanesBytes + kLastBytes;
+  static_assert(kIds < 65536, "IDs are 16-bit");
+};
+
+// The code's own slot only: the slot, kNoSlot (find: the own slot is free, so the code is
+// absent), or kPending (the slot holds another code; the all-ones code always queues).
+template <typename Tab, typename CodeT>
+__device__ __forceinline__ uint32_t own_insert(Tab& tab, CodeT c, uint32_t& claimed) {
+  if (c == Tab::kFree) return kPending;
+  const uint32_t h = Tab::mix(c);
+  const uint32_t o = tab.own(h, h >> tab.bshift);
+  const CodeT cur = tab.code[o];
+  if (cur == c) return o;
+  if (cur == Tab::kFree) {
+    const CodeT old = cas_code(tab.code + o, Tab::kFree, c);
+    if (old == Tab::kFree) {
+      claimed = 1;
+      return o;
+    }
+    if (old == c) return o;
+  }
+  return kPending;
+}
+template <typename Tab, typename CodeT>
+__device__ __forceinline__ uint32_t own_find(const Tab& tab, CodeT c) {
+  if (c == Tab::kFree) return kPending;
+  const uint32_t h = Tab::mix(c);
+  const uint32_t o = tab.own(h, h >> tab.bshift);
+  const CodeT cur = tab.code[o];
+  if (cur == c) return o;
+  return cur == Tab::kFree ? kNoSlot : kPending;
+}
+
+// Queue the lanes whose slot[u] is kPending (their code and position) in this warp's queue;
+// returns the count. Entry order: round item u, then lane.
+template <typename L, typename CodeT>
+__device__ __forceinline__ uint32_t queue_pending(const uint32_t (&slot)[L::kRound], const CodeT (&c)[L::kRound],
+                                                  uint32_t i0, int tid, CodeT* qcode, uint16_t* qpos) {
+  uint32_t n = 0;
+#pragma unroll
+  for (int u = 0; u < L::kRound; ++u) {
+    const bool pend = slot[u] == kPending;
+    const uint32_t m = __ballot_sync(kFullMask, pend);
+    if (pend) {
+      const uint32_t e = n + __popc(m & lanemask_lt());
+      qcode[e] = c[u];
+      qpos[e] = static_cast<uint16_t>(i0 + u * kSwThreads + tid);
+    }
+    n += __popc(m);
+  }
+  __syncwarp();
+  return n;
+}
+
+// Phase A, keys: every key code of the stream into the table; the low half of ids[i] = the
+// key's slot. No barrier between rounds (a barrier would wait for the next round's code loads,
+// issued one round ahead): a thread whose claims push the table past the overflow limit
+// raises s_over, and every warp stops at its next round. Ends with a barrier; the caller then
+// reads s_over.
+template <typename L, typename CodeT, typename Tab>
+__device__ __forceinline__ void dict_keys(Tab& tab, const CodeT* kc, uint32_t T, uint32_t* ids, int tid,
+                                          CodeT* qcode, uint16_t* qpos, uint32_t* s_claims,
+                                          volatile uint32_t* s_over) {
+  constexpr uint32_t kLimit = overflow_limit<CodeT>();
+  constexpr int R = L::kRound;
+  constexpr uint32_t kStride = kSwThreads * R;
+  const int lane = tid & 31;
+  CodeT nxt[R];
+#pragma unroll
+  for (int u = 0; u < R; ++u) {
+    const uint32_t i = u * kSwThreads + tid;
+    nxt[u] = i < T ? kc[i] : CodeT(0);
+  }
+  for (uint32_t i0 = 0; i0 < T; i0 += kStride) {
+    // one read per warp, broadcast: the whole warp leaves together
+    if (__shfl_sync(kFullMask, *s_over, 0) != 0u) break;
+    CodeT c[R];
+    uint32_t slot[R];
+    uint32_t claims = 0;
+#pragma unroll
+    for (int u = 0; u < R; ++u) {
+      c[u] = nxt[u];
+      const uint32_t i = i0 + kStride + u * kSwThreads + tid;
+      nxt[u] = i < T ? kc[i] : CodeT(0);
+    }
+#pragma unroll
+    for (int u = 0; u < R; ++u) {
+      const uint32_t i = i0 + u * kSwThreads + tid;
+      slot[u] = kNoSlot;
+      if (i < T) {
+        uint32_t cl = 0;
+        slot[u] = own_insert(tab, c[u], cl);
+        claims += cl;
+        if (slot[u] != kPending) reinterpret_cast<uint16_t*>(ids + i)[0] = static_cast<uint16_t>(slot[u]);
+      }
+    }
+    const uint32_t nq = queue_pending<L>(slot, c, i0, tid, qcode, qpos);
+    bool bad = false;
+    for (uint32_t e = lane; e < nq; e += 32) {
+      uint32_t cl = 0;
+      const uint32_t sl = tab.insert_fast(qcode[e], cl);
+      claims += cl;
+      bad |= sl == kNoSlot;
+      reinterpret_cast<uint16_t*>(ids + qpos[e])[0] = static_cast<uint16_t>(sl);
+    }
+    if ((claims != 0 && atomicAdd(s_claims, claims) + claims > kLimit) || bad) *s_over = 1u;
+    __syncwarp();  // the queue is refilled next round
+  }
+  __syncthreads();
+}
+
+// Phase A, queries (after the keys): the high half of ids[i] = the slot of the query's code,
+// or kNone.
+template <typename L, typename CodeT, typename Tab>
+__device__ __forceinline__ void dict_queries(const Tab& tab, const CodeT* qc, uint32_t T, uint32_t* ids,
+                                             int tid, CodeT* qcode, uint16_t* qpos) {
+  constexpr int R = L::kRound;
+  constexpr uint32_t kStride = kSwThreads * R;
+  const int lane = tid & 31;
+  CodeT nxt[R];
+#pragma unroll
+  for (int u = 0; u < R; ++u) {
+    const uint32_t i = u * kSwThreads + tid;
+    nxt[u] = i < T ? qc[i] : CodeT(0);
+  }
+  for (uint32_t i0 = 0; i0 < T; i0 += kStride) {
+    CodeT c[R];
+    uint32_t slot[R];
+#pragma unroll
+    for (int u = 0; u < R; ++u) {
+      c[u] = nxt[u];
+      const uint32_t i = i0 + kStride + u * kSwThreads + tid;
+      nxt[u] = i < T ? qc[i] : CodeT(0);
+    }
+#pragma unroll
+    for (int u = 0; u < R; ++u) {
+      const uint32_t i = i0 + u * kSwThreads + tid;
+      slot[u] = kNoSlot;
+      if (i < T) {
+        slot[u] = own_find(tab, c[u]);
+        if (slot[u] != kPending)
+          reinterpret_cast<uint16_t*>(ids + i)[1] = static_cast<uint16_t>(slot[u] == kNoSlot ? L::kNone : slot[u]);
+      }
+    }
+    const uint32_t nq = queue_pending<L>(slot, c, i0, tid, qcode, qpos);
+    for (uint32_t e = lane; e < nq; e += 32) {
+      const uint32_t sl = tab.find_fast(qcode[e]);
+      reinterpret_cast<uint16_t*>(ids + qpos[e])[1] = static_cast<uint16_t>(sl == kNoSlot ? L::kNone : sl);
+    }
+    __syncwarp();  // the queue is refilled next round
+  }
+}
+
+// Phase B by one warp: ids[i] (key ID | query ID << 16) becomes the answer for position i.
+// The IDs of kSwBatch steps are loaded at once and their answers stored at once: a global
+// access pending at a __syncwarp costs the step its whole latency.
+template <typename L>
+__device__ __forceinline__ void sweep_warp(uint32_t* ids, uint32_t T, uint32_t* lanes, uint16_t* last,
+                                           int lane) {
+  constexpr uint32_t kTail = (L::kNone << 16) | L::kDummy;
+  const uint32_t steps = (T + 31) / 32;
+  const uint32_t below = lanemask_lt();
+  int32_t* ans_out = reinterpret_cast<int32_t*>(ids);
+  for (uint32_t s0 = 0; s0 < steps; s0 += kSwBatch) {
+    uint32_t id[kSwBatch];
+    int32_t a[kSwBatch];
+#pragma unroll
+    for (int d = 0; d < kSwBatch; ++d) {
+      const uint32_t i = (s0 + d) * 32 + lane;
+      id[d] = i < T ? ids[i] : kTail;
+    }
+    // steps past the end (last batch) run on the tail IDs: a dummy key and a query of no code
+#pragma unroll
+    for (int d = 0; d < kSwBatch; ++d) {
+      const uint32_t st = s0 + d;
+      const uint32_t k = id[d] & 0xFFFFu, q = id[d] >> 16;
+      atomicOr(lanes + k, 1u << lane);
+      __syncwarp();
+      const uint32_t mq = lanes[q], mk = lanes[k];
+      const uint32_t lq = last[q];
+      const uint32_t bel = mq & below;
+      a[d] = bel ? static_cast<int32_t>(st * 32 + 31 - __clz(bel)) : static_cast<int32_t>(lq) - 1;
+      __syncwarp();
+      if (31 - __clz(mk) == lane) last[k] = static_cast<uint16_t>(st * 32 + lane + 1);
+      lanes[k] = 0u;
+      __syncwarp();
+    }
+#pragma unroll
+    for (int d = 0; d < kSwBatch; ++d) {
+      const uint32_t i = (s0 + d) * 32 + lane;
+      if (i < T) ans_out[i] = a[d];
+    }
+  }
+}
+
+template <typename CodeT>
+__global__ void __launch_bounds__(kSwThreads, kSwPerSm) sweep_kernel(const Params p) {
+  using L = SweepLayout<CodeT>;
+  using Tab = Table<CodeT, uint32_t>;
+  extern __shared__ __align__(16) unsigned char smem[];
+  __shared__ uint32_t s_claims, s_lt;
+  __shared__ volatile uint32_t s_over;
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const CodeT* qc = static_cast<const CodeT*>(p.qc);
+  const CodeT* kc = static_cast<const CodeT*>(p.kc);
+  const uint32_t T = static_cast<uint32_t>(p.T);
+  Tab tab;
+  tab.init_dict(smem, L::kSlots);
+  CodeT* qcode = reinterpret_cast<CodeT*>(smem + L::kDictBytes + warp * L::kQueueBytes);
+  uint16_t* qpos = reinterpret_cast<uint16_t*>(smem + L::kDictBytes + warp * L::kQueueBytes + L::kQueueCodeBytes);
+  uint32_t* lanes = reinterpret_cast<uint32_t*>(smem);
+  uint16_t* last = reinterpret_cast<uint16_t*>(smem + L::kLanesBytes);
+  for (int64_t n = blockIdx.x; n < p.N; n += gridDim.x) {
+    const int64_t row0 = n * p.T;
+    uint32_t* ids = reinterpret_cast<uint32_t*>(p.src + row0);
+    // ------------------------------------------------ A: the dictionary
+    for (uint32_t s = tid; s < L::kSlots; s += kSwThreads) tab.code[s] = Tab::kFree;
+    if (tid == 0) {
+      *tab.side = 0u;
+      s_claims = 0u;
+      s_over = 0u;
+      s_lt = 0u;
+    }
+    __syncthreads();
+    dict_keys<L>(tab, kc + row0, T, ids, tid, qcode, qpos, &s_claims, &s_over);
+    const bool over = s_over != 0u;
+    if (!over) dict_queries<L>(tab, qc + row0, T, ids, tid, qcode, qpos);
+    __syncthreads();
+    if (over) {
+      if (tid == 0) {
+        const uint32_t k = atomicAdd(p.ovf_count, 1u);
+        p.ovf_list[k] = static_cast<uint32_t>(n);
+      }
+      continue;  // every thread is past the last read of the table
+    }
+    // ------------------------------------------------ B: the sweep, over the table's memory
+    for (uint32_t s = tid; s < L::kIds; s += kSwThreads) {
+      lanes[s] = 0u;
+      last[s] = 0;
+    }
+    __syncthreads();
+    if (warp == 0) sweep_warp<L>(ids, T, lanes, last, lane);
+    __syncthreads();
+    if (p.lt_count != nullptr) {
+      // last-occurrence table: every key code of the stream with its last position
+      CodeT* ltc = static_cast<CodeT*>(p.lt_code) + row0;
+      int32_t* ltp = p.lt_pos + row0;
+      for (uint32_t s = tid; s <= L::kSide; s += kSwThreads) {
+        const uint32_t l = last[s];
+        if (l != 0u) {
+          const uint32_t k = atomicAdd(&s_lt, 1u);
+          ltc[k] = kc[row0 + l - 1];
+          ltp[k] = static_cast<int32_t>(l - 1);
+        }
+      }
+      __syncthreads();
+      if (tid == 0) p.lt_count[n] = static_cast<int32_t>(s_lt);
+    }
+    __syncthreads();  // the arrays are cleared for the next stream
+  }
+}
 
 // ---------------------------------------------------------------- the value gather
 // out[n][i] = v[n][src[n][i]] (vbytes-byte rows), zeros where src is -1: the two-kernel path
@@ -997,10 +1322,46 @@ int run_pipe(const MatchLaunch& a, const Plan& pl, const DeviceInfo& dev, Params
   return LEMA_OK;
 }
 
+// The dictionary + sweep path serves calls without value rows of at least one wave of sweep
+// CTAs and streams of at most kSweepMaxT positions. LEMA_K2_SWEEP=0 turns it off, =1 takes it
+// for every call it can serve (rows then copied by the gather kernel); same results.
+bool use_sweep(const MatchLaunch& a, const Plan& pl, int sms) {
+  if (!pl.fast || a.T > kSweepMaxT) return false;
+  const char* e = std::getenv("LEMA_K2_SWEEP");
+  if (e != nullptr && e[0] == '0') return false;
+  if (e != nullptr && e[0] == '1') return true;
+  return a.out == nullptr && a.N >= static_cast<int64_t>(kSwPerSm) * sms / 2;
+}
+
+template <typename CodeT>
+int run_sweep(const MatchLaunch& a, const Plan& pl, const DeviceInfo& dev, Params p) {
+  auto kern = sweep_kernel<CodeT>;
+  const size_t sm = SweepLayout<CodeT>::kBytes;
+  LEMA_CUDA_TRY(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(sm)));
+  int per_sm = 0;
+  LEMA_CUDA_TRY(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kern, kSwThreads, sm));
+  const int64_t grid = std::min<int64_t>(a.N, static_cast<int64_t>(std::max(per_sm, 1)) * dev.sms);
+  kern<<<static_cast<unsigned>(grid), kSwThreads, sm, a.stream>>>(p);
+  LEMA_CUDA_TRY(cudaGetLastError());
+  if (pl.global) {
+    // streams that outgrew the shared-memory table are matched here
+    p.list_mode = 1;
+    p.gather_inline = 0;
+    auto gk = match_kernel<CodeT, false>;
+    const size_t gsm = smem_bytes<CodeT>(false);
+    LEMA_CUDA_TRY(cudaFuncSetAttribute(gk, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(gsm)));
+    gk<<<static_cast<unsigned>(pl.n_gtables), kThreads, gsm, a.stream>>>(p);
+    LEMA_CUDA_TRY(cudaGetLastError());
+  }
+  if (a.out != nullptr) return run_gather(a, p.src);
+  return LEMA_OK;
+}
+
 template <typename CodeT>
 int run(const MatchLaunch& a, const Plan& pl, const DeviceInfo& dev) {
   unsigned char* ws = static_cast<unsigned char*>(a.ws);
   Params p{};
+  p.wait_ns = wait_limit_ns();
   p.qc = a.qc;
   p.kc = a.kc;
   p.N = a.N;
@@ -1018,6 +1379,7 @@ int run(const MatchLaunch& a, const Plan& pl, const DeviceInfo& dev) {
     p.gslots = pl.gslots;
     if (pl.list_mode) LEMA_CUDA_TRY(cudaMemsetAsync(p.ovf_count, 0, sizeof(uint32_t), a.stream));
   }
+  if (use_sweep(a, pl, dev.sms)) return run_sweep<CodeT>(a, pl, dev, p);
   if constexpr (sizeof(CodeT) == 4) {  // 64-bit codes: the two-kernel path (no spare registers)
     if (pl.fast && use_pipe(a, pl, dev.sms)) return run_pipe<CodeT>(a, pl, dev, p);
   }

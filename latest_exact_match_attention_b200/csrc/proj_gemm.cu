@@ -35,7 +35,7 @@ namespace k1 {
 constexpr int kBM = 128, kBK = 64;  // tile rows, K per stage
 constexpr int kABytes = kBM * kBK * 2;  // 16 KiB
 constexpr int kThreads = 192;           // 6 warps: producer, MMA, 4 x epilogue
-constexpr uint64_t kWaitNs = 4000000000ull;  // a pipeline wait gives up after 4 s
+constexpr uint64_t kDrainNs = 4000000000ull;  // a wait for work already in flight at exit: 4 s
 
 // A tile is 128 rows x BN columns (BN / 32 heads). Per width: as many stages as fit in about
 // 192 KiB of shared memory (at most 8), two BN-column fp32 TMEM accumulators, and the
@@ -59,6 +59,7 @@ struct Params {
   uint32_t* qcodes;
   uint32_t* kcodes;
   uint32_t* status;
+  uint64_t wait_ns;  // bound of a pipeline wait (wait_limit_ns(): 4 s unless LEMA_WAIT_NS)
   int64_t M, T;
   int64_t n_tiles;
   int k_blocks;
@@ -159,8 +160,9 @@ __device__ __forceinline__ void tmem_load32(uint32_t taddr, uint32_t (&r)[32]) {
 }
 
 // Waits for the phase of `bar` with parity `parity`. Returns false when another role has
-// given up, or after kWaitNs (then this wait raises the abort flag and the status bit).
-__device__ bool wait_phase(uint32_t bar, uint32_t parity, volatile uint32_t* abort_flag, uint32_t* status) {
+// given up, or after wait_ns (then this wait raises the abort flag and the status bit).
+__device__ bool wait_phase(uint32_t bar, uint32_t parity, volatile uint32_t* abort_flag, uint32_t* status,
+                           uint64_t wait_ns) {
   uint64_t deadline = 0;
   for (uint32_t i = 1;; ++i) {
     if (mbar_try_wait(bar, parity)) return true;
@@ -168,7 +170,7 @@ __device__ bool wait_phase(uint32_t bar, uint32_t parity, volatile uint32_t* abo
       if (*abort_flag) return false;
       const uint64_t now = globaltimer();
       if (deadline == 0) {
-        deadline = now + kWaitNs;
+        deadline = now + wait_ns;
       } else if (now > deadline) {
         *abort_flag = 1;
         raise_status(status, LEMA_STATUS_PROBE_LIMIT);
@@ -178,7 +180,8 @@ __device__ bool wait_phase(uint32_t bar, uint32_t parity, volatile uint32_t* abo
   }
 }
 
-// The same wait for draining work already in flight at exit: ignores the abort flag.
+// The same wait for draining work already in flight at exit: ignores the abort flag and keeps
+// its own bound (kDrainNs), whatever wait_ns is: copies and MMAs in flight always complete.
 __device__ void drain_phase(uint32_t bar, uint32_t parity, uint32_t* status) {
   uint64_t deadline = 0;
   for (uint32_t i = 1;; ++i) {
@@ -186,7 +189,7 @@ __device__ void drain_phase(uint32_t bar, uint32_t parity, uint32_t* status) {
     if ((i & 63) == 0) {
       const uint64_t now = globaltimer();
       if (deadline == 0) {
-        deadline = now + kWaitNs;
+        deadline = now + kDrainNs;
       } else if (now > deadline) {
         raise_status(status, LEMA_STATUS_PROBE_LIMIT);
         return;
@@ -262,7 +265,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         const int m0 = static_cast<int>(tile / p.n_blocks) * kBM;
         const int n0 = static_cast<int>(tile % p.n_blocks) * BN;
         for (int kb = 0; kb < p.k_blocks; ++kb) {
-          if (!wait_phase(empty_bar(s), ph ^ 1u, s_abort, p.status)) {
+          if (!wait_phase(empty_bar(s), ph ^ 1u, s_abort, p.status, p.wait_ns)) {
             ok = false;
             break;
           }
@@ -290,11 +293,11 @@ __global__ void __launch_bounds__(kThreads, 1)
       uint32_t ph = 0, aph = 0;
       bool ok = true;
       for (int64_t tile = blockIdx.x; ok && tile < p.n_tiles; tile += gridDim.x) {
-        if (!wait_phase(acce_bar(acc), aph ^ 1u, s_abort, p.status)) break;
+        if (!wait_phase(acce_bar(acc), aph ^ 1u, s_abort, p.status, p.wait_ns)) break;
         tc_fence_after();
         const uint32_t d_tmem = tmem_base + static_cast<uint32_t>(acc * BN);
         for (int kb = 0; kb < p.k_blocks; ++kb) {
-          if (!wait_phase(full_bar(s), ph, s_abort, p.status)) {
+          if (!wait_phase(full_bar(s), ph, s_abort, p.status, p.wait_ns)) {
             ok = false;
             break;
           }
@@ -330,7 +333,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     int acc = 0;
     uint32_t aph = 0;
     for (int64_t tile = blockIdx.x; tile < p.n_tiles; tile += gridDim.x) {
-      if (!wait_phase(accf_bar(acc), aph, s_abort, p.status)) break;
+      if (!wait_phase(accf_bar(acc), aph, s_abort, p.status, p.wait_ns)) break;
       tc_fence_after();
       const int64_t m = (tile / p.n_blocks) * kBM + quarter * 32 + lane;
       const int h0 = static_cast<int>(tile % p.n_blocks) * TL::kHeads;
@@ -516,6 +519,7 @@ int proj_codes_v(const void* x, const void* w_all, int64_t M, int64_t K, int64_t
   prm.qcodes = qcodes;
   prm.kcodes = kcodes;
   prm.status = status;
+  prm.wait_ns = wait_limit_ns();
   prm.M = M;
   prm.T = T;
   prm.hq = hq;
@@ -559,6 +563,7 @@ int gemm_swiglu(const void* x, const void* w_il, int64_t M, int64_t K, int64_t F
     return fail(LEMA_ERR_INVALID_ARGUMENT, "gemm_swiglu: tensor map encoding failed (M=%lld K=%lld F=%lld)", (long long)M, (long long)K, (long long)F);
   Params prm{};
   prm.status = status;
+  prm.wait_ns = wait_limit_ns();
   prm.M = M;
   prm.T = M;
   prm.k_blocks = static_cast<int>(K / kBK);

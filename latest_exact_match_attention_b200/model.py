@@ -29,8 +29,8 @@ import torch.nn.functional as F
 from torch import nn
 
 from . import _lib
-from ._lib import DTYPE_TAG, call, ptr, stream_handle
-from .attention import pack_codes, prefill_match, proj_codes, proj_codes_v, row_rms
+from ._lib import DTYPE_TAG, call, check_status, device_status, ptr, stream_handle
+from .attention import pack_codes, prefill_match, proj_codes
 
 ATTN_KINDS = ("lema",)
 
@@ -156,7 +156,7 @@ class SwiGLU(nn.Module):
         act = torch.empty((x2.shape[0], Fd), dtype=x.dtype, device=x.device)
         if self._fused_ok(x2):
             call("lema_gemm_swiglu", ptr(x2), ptr(self.gate_up_interleaved()), x2.shape[0], dim, Fd,
-                 ptr(act), None, stream_handle(x.device))
+                 ptr(act), ptr(device_status(x.device)), stream_handle(x.device))
         else:
             gu = x2 @ self.gate_up_weight().t()
             call("lema_swiglu", ptr(gu), DTYPE_TAG[x.dtype], x2.shape[0], Fd, ptr(act),
@@ -181,7 +181,6 @@ class Attention(nn.Module):
         self.o_proj = nn.Linear(H * cfg.d_v, cfg.dim, bias=False)
         self.hard = True
         self._wqk = None        # (key, stacked [q_proj; k_proj] weight) for K1
-        self._wall = None       # (key, stacked norm-folded [q; k; v] weight) for fused K1
 
     def project(self, x):
         """[B, T, dim] -> query and key pre-activations and values, [B, H, T, d]."""
@@ -209,29 +208,6 @@ class Attention(nn.Module):
             self._wqk = (key, torch.cat([q.detach(), k.detach()], 0).contiguous())
         return self._wqk[1]
 
-    def stacked_all(self, norm_weight: torch.Tensor) -> torch.Tensor:
-        """[q_proj; k_proj; v_proj] weights, each column scaled by the preceding RMSNorm's
-        weight (the norm folded into the GEMM), rebuilt only when any of them changes."""
-        ws = (self.q_proj.weight, self.k_proj.weight, self.v_proj.weight, norm_weight)
-        key = tuple((w.data_ptr(), w._version) for w in ws)
-        if getattr(self, "_wall", None) is None or self._wall[0] != key:
-            g = norm_weight.detach().float()[None, :]
-            w = torch.cat([(w.detach().float() * g) for w in ws[:3]], 0).to(torch.bfloat16)
-            self._wall = (key, w.contiguous())
-        return self._wall[1]
-
-    def codes_fused(self, x, norm: nn.RMSNorm):
-        """gpu_pre in one GEMM from the UN-normalised x: codes of norm(x) and
-        v = v_proj(norm(x)), with norm1 folded into the weights and its row scale applied in
-        the epilogue (K1's value columns). Codes equal those of the unfused path wherever
-        |z| is not within rounding of 0; v agrees to bf16 rounding."""
-        B, T, _ = x.shape
-        c = self.cfg
-        r = row_rms(x, norm.eps if norm.eps is not None else torch.finfo(torch.float32).eps)
-        qc, kc, v = proj_codes_v(x, self.stacked_all(norm.weight), c.num_heads, c.num_heads,
-                                 c.num_heads * c.d_v, row_scale=r)
-        return qc, kc, v.view(B, T, c.num_heads, c.d_v).transpose(1, 2)
-
     def exact(self, qc, kc, v):
         """The exact op on codes and values: [B, H, T, d_v] retrieved rows (zeros on a miss),
         as a transposed view of [B, T, H, d_v] memory -- what `merge` reads without a copy.
@@ -249,7 +225,8 @@ class Attention(nn.Module):
         ws = torch.empty(nb, dtype=torch.uint8, device=v.device) if nb else None
         call("lema_prefill_match_strided", ptr(q2), ptr(k2), cb, B * H, T, None, ptr(v), dv * es,
              ptr(out), H, v.stride(0) * es, v.stride(1) * es, v.stride(2) * es,
-             T * H * dv * es, dv * es, H * dv * es, ptr(ws), nb, None, stream_handle(v.device))
+             T * H * dv * es, dv * es, H * dv * es, ptr(ws), nb, ptr(device_status(v.device)),
+             stream_handle(v.device))
         return out.transpose(1, 2)
 
     def codes(self, x):
@@ -281,15 +258,10 @@ class Block(nn.Module):
         self.norm2 = nn.RMSNorm(cfg.dim, eps=cfg.norm_eps)
         self.mlp = SwiGLU(cfg.dim, cfg.dim_ff)
         self.seg = None
-        self.fused_pre = False
 
     def gpu_pre(self, x):
-        """Normalise, project and pack: the codes the store needs and the values. With
-        `fused_pre` (opt-in, Transformer.set_fused_pre) the norm and all three projections
-        are one tcgen05 GEMM; its codes can differ from the reference recipe's marginally
-        more often (the norm weight is rounded into the weights), so it is off by default."""
-        if self.fused_pre and self.attn._k1_ok(x) and self.norm1.weight is not None:
-            return self.attn.codes_fused(x, self.norm1)
+        """Normalise, project and pack: the codes the store needs and the values
+        (code/lema/model.py:224-227)."""
         return self.attn.codes(rms_norm(self.norm1, x))
 
     def gpu_post(self, x, got):
@@ -336,12 +308,6 @@ class Transformer(nn.Module):
     def lema_layers(self):
         return [b.attn for b in self.blocks]
 
-    def set_fused_pre(self, on: bool = True):
-        """gpu_pre as one GEMM from the un-normalised residual (norm1 folded in; see
-        Block.gpu_pre). Off by default."""
-        for b in self.blocks:
-            b.fused_pre = on
-
     def set_hard(self, hard: bool = True):
         if not hard:
             raise ValueError("this build serves the exact (hard) op only")
@@ -371,7 +337,11 @@ class Transformer(nn.Module):
             x = blk(x, store=(cache.layer(li) if cache is not None else None))
         if cache is not None:
             cache.t += idx.shape[-1]
-        return self.lm_head(rms_norm(self.norm_f, x)) if return_logits else None
+        out = self.lm_head(rms_norm(self.norm_f, x)) if return_logits else None
+        # device-side conditions of this forward's kernels (a bounded wait that ran out):
+        # raised here, once per forward, outside graph capture
+        check_status(x.device, "Transformer.forward")
+        return out
 
     def n_params(self, embedding: bool = True) -> int:
         n = sum(p.numel() for p in self.parameters())

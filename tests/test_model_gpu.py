@@ -62,12 +62,10 @@ def bf16_model(dev, depth=2, vocab=512, dim=256, H=8):
                                    d_qk=32, d_v=32)).to(dev).to(torch.bfloat16).eval()
 
 
-@pytest.mark.parametrize("fused", [False, True])
-def test_bf16_block_store_equals_dense(cuda, fused):
+def test_bf16_block_store_equals_dense(cuda):
     # the K1 path: one block, the whole sequence at once through the store and densely;
     # the same GEMM shapes on both sides, so the outputs are bitwise equal
     m = bf16_model(cuda)
-    m.set_fused_pre(fused)
     idx = torch.randint(0, 60, (3, 200), device=cuda)
     x = m.tok_emb(idx)
     blk = m.blocks[0]
@@ -79,10 +77,9 @@ def test_bf16_block_store_equals_dense(cuda, fused):
     cache.check()
 
 
-@pytest.mark.parametrize("temperature,fused", [(0.0, False), (0.8, False), (0.0, True)])
-def test_graph_decoder_reproduces_eager(cuda, temperature, fused):
+@pytest.mark.parametrize("temperature", [0.0, 0.8])
+def test_graph_decoder_reproduces_eager(cuda, temperature):
     m = bf16_model(cuda)
-    m.set_fused_pre(fused)
     prompt = torch.randint(0, 60, (4, 16), device=cuda)
     # eager
     c = m.new_cache("hbm", max_cache_len=64, batch=4)

@@ -94,36 +94,26 @@ def test_proj_codes_zero_rows_and_repeat(cuda):
 
 
 @pytest.mark.parametrize("B,T,dim,H,dv", [(2, 300, 256, 8, 32), (256, 1, 1536, 64, 24), (4, 1024, 1024, 16, 64)])
-def test_fused_norm_and_value_projection(cuda, B, T, dim, H, dv):
-    """gpu_pre as one GEMM (norm1 folded into the weights, its row scale in the epilogue):
-    codes obey the flip rule against an fp64 z of the NORMALISED input; values match
-    v_proj(norm1(x)) to bf16 rounding."""
-    from latest_exact_match_attention_b200.model import ModelConfig, Transformer
-    torch.manual_seed(B + H)
-    m = Transformer(ModelConfig(vocab_size=128, depth=1, dim=dim, num_heads=H, d_qk=32,
-                                d_v=dv)).to(cuda).to(torch.bfloat16)
-    m.set_fused_pre(True)
-    blk = m.blocks[0]
-    with torch.no_grad():
-        blk.norm1.weight.uniform_(0.5, 1.5)
-        x = (3 * torch.randn(B, T, dim, device=cuda)).to(torch.bfloat16)
-        qc, kc, v = blk.gpu_pre(x)
-        h = torch.nn.functional.rms_norm(x.float(), (dim,), blk.norm1.weight.float(),
-                                         blk.norm1.eps).double()   # the normalised input
-        wq = blk.attn.q_proj.weight.double()
-        wk = blk.attn.k_proj.weight.double()
-        zq = (h @ wq.T).view(B, T, H, 32).permute(0, 2, 1, 3)
-        zk = (h @ wk.T).view(B, T, H, 32).permute(0, 2, 1, 3)
-        # the weights are rounded to bf16 after the norm weight is folded in, so near-zero
-        # signs move more often than with the unfused recipe (which the default path uses):
-        # flips are counted; outside the |z| < 1e-3 ||z_row|| band they stay below 1e-6
-        bits = zq.numel() + zk.numel()
-        n = 0
-        for codes, z in ((qc, zq), (kc, zk)):
-            diff = bits_of(codes) != (z >= 0)
-            band = z.abs() < TOL * z.norm(dim=-1, keepdim=True)
-            n += int(diff.sum())
-            assert int((diff & ~band).sum()) <= max(2, bits // 1000000)
-        assert n <= max(8, bits // 500), n
-        ref_v = blk.attn.v_proj(blk.norm1(x)).view(B, T, H, dv).transpose(1, 2).float()
-        torch.testing.assert_close(v.float(), ref_v, rtol=3e-2, atol=3e-2)
+def test_value_columns_in_one_gemm(cuda, B, T, dim, H, dv):
+    """lema_proj_codes_v: the q/k codes and the value projection of the same (normalised)
+    rows in one tcgen05 GEMM. The codes obey the flip rule against an fp64 z with no flip
+    outside the band (the same rows and weights as the codes-only kernel, so the same
+    accumulation); the value columns equal the fp64 product to bf16 rounding, times the row
+    scale when one is given."""
+    from latest_exact_match_attention_b200.attention import proj_codes_v
+    g = torch.Generator(device=cuda).manual_seed(B + H)
+    x = torch.randn((B, T, dim), generator=g, device=cuda).to(torch.bfloat16)
+    w = (0.05 * torch.randn(((2 * H) * 32 + H * dv, dim), generator=g, device=cuda)).to(torch.bfloat16)
+    status = torch.zeros(1, dtype=torch.int32, device=cuda)
+    qc, kc, v = proj_codes_v(x, w, H, H, H * dv, status=status)
+    rs = (0.5 + torch.rand(B * T, generator=g, device=cuda)).float()
+    _, _, v2 = proj_codes_v(x, w, H, H, H * dv, row_scale=rs, status=status)
+    torch.cuda.synchronize()
+    assert int(status.item()) == 0
+    zq, zk = exact_z(x, w[: 2 * H * 32], H, H)
+    print(f"flips (all inside the band): {flips(qc, zq) + flips(kc, zk)} of {zq.numel() + zk.numel()} bits")
+    q1, k1 = proj_codes(x, w[: 2 * H * 32], H, H)
+    assert torch.equal(q1, qc) and torch.equal(k1, kc)
+    zv = (x.double() @ w[2 * H * 32:].double().T).float()
+    torch.testing.assert_close(v.float(), zv, rtol=1e-2, atol=1e-2)
+    torch.testing.assert_close(v2.float(), zv * rs.view(B, T, 1), rtol=1e-2, atol=1e-2)
