@@ -8,19 +8,21 @@ rows of 24 bf16 (48 bytes). One step = the exact op over the whole batch: for ev
 the latest earlier position whose key code equals its query code, and its value row gathered
 (zeros on a miss) -- code/lema/attention.py:100-158 -- through lema_prefill_match (K2).
 
-Metric: Mpos/s (positions per second, whole job). Inputs are resident in HBM when the timed
-region starts; codes + values + outputs (~0.9 GB) exceed the 126 MB L2, so no flush is
-needed between steps. `e2e` is the same metric through the C ABI with host buffers: every
-step copies its codes and values host->device from pinned memory and its outputs back.
+Metric: Mpos/s of the whole job. Inputs are resident in HBM when the timed region starts;
+codes + values + outputs (~0.9 GB) exceed the 126 MB L2, so no flush is needed between
+steps. `e2e` is the same metric through the public host-buffer call (attention.HostPrefill)
+with host buffers: every step copies its codes and values host->device from pinned memory
+and its outputs back.
 
-Multi-GPU (torchrun, one process per GPU): the streams are independent, so every rank runs
-its own full batch (different seeds) with no collective on the data path ("scaling": weak);
-the time is the max over ranks of CUDA-event time.
+Multi-GPU (torchrun, one process per GPU): the 512 streams are independent, so they are split
+by head over the ranks (512 / N streams each, "scaling": "strong") with no collective on the
+data path; the time is the max over ranks of CUDA-event time. The line also carries a small
+batched-decode record (config 4's model, batch split over the ranks, short prefix).
 
 --impl reference: the reference's own CPU implementation of the path -- its C++ store
-(code/lema/csrc/store.cpp, built from source into oracle/_ref) exchanging every stream's
-positions in one call on all host cores, as code/lema/cache.py:184-201 does -- timed on a
-bounded sample of the same workload. Rank 0 alone runs it.
+(code/lema/csrc/store.cpp, built from source into oracle/_ref) exchanging all 512 streams'
+positions in one call on all host cores, as code/lema/cache.py:184-201 does. Rank 0 alone
+runs it.
 """
 from __future__ import annotations
 
@@ -120,14 +122,17 @@ def dist_setup(n_gpus: int):
     return rank, world
 
 
-def make_inputs(rank: int, device, n_streams: int):
+def make_inputs(device, n_total: int, lo: int, hi: int):
+    """Streams [lo, hi) of the config-2 workload (all n_total streams drawn with one seed, so
+    every GPU count sees the same data)."""
     import torch
 
     from latest_exact_match_attention_b200 import synth
-    qc, kc = synth.code_streams(n_streams, T, synth.CONFIG2, seed=rank, config_id=2)
+    qc, kc = synth.code_streams(n_total, T, synth.CONFIG2, seed=0, config_id=2)
+    qc, kc = np.ascontiguousarray(qc[lo:hi]), np.ascontiguousarray(kc[lo:hi])
     q = torch.from_numpy(qc.view(np.int32)).to(device)
     k = torch.from_numpy(kc.view(np.int32)).to(device)
-    v = synth.values_torch(n_streams, T, D_V, torch.bfloat16, device, seed=rank, config_id=2)
+    v = synth.values_torch(n_total, T, D_V, torch.bfloat16, device, seed=0, config_id=2)[lo:hi].contiguous()
     return qc, kc, q, k, v
 
 
@@ -171,14 +176,14 @@ def run_reference(args):
     if rank != 0:
         return
     from latest_exact_match_attention_b200 import synth
-    sample = 32                                   # streams per step: ~0.5M positions
-    qc, kc = synth.code_streams(sample, T, synth.CONFIG2, seed=0, config_id=2)
+    n = args.streams                              # the whole workload: 512 streams
+    qc, kc = synth.code_streams(n, T, synth.CONFIG2, seed=0, config_id=2)
     vals = []
     for _ in range(args.warmup):
-        cpu_reference_sample(qc, kc, sample, reps=0)
+        cpu_reference_sample(qc, kc, n, reps=0)
     t0 = time.perf_counter()
     for _ in range(args.steps):
-        v, cores, kind, desc = cpu_reference_sample(qc, kc, sample, reps=0)
+        v, cores, kind, desc = cpu_reference_sample(qc, kc, n, reps=0)
         vals.append(v)
     wall = time.perf_counter() - t0
     value = statistics.median(vals)
@@ -186,9 +191,9 @@ def run_reference(args):
         "impl": "reference", "metric": METRIC, "value": round(value, 3), "unit": UNIT,
         "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
         "ms_per_step": round(1e3 * wall / max(1, args.steps), 3), "higher_is_better": True,
-        "scaling": "weak", "vs_baseline": None, "dtype": "u32", "data": "synthetic",
-        "config": {"workload": WORKLOAD, "sample_streams": sample, "global_batch": N_STREAMS,
-                   "seq_len": T, "parallelism": "cpu"},
+        "scaling": "strong", "vs_baseline": None, "dtype": "u32", "data": "synthetic",
+        "config": {"workload": WORKLOAD, "streams": n, "global_batch": N_STREAMS,
+                   "seq_len": T, "parallelism": "cpu", "same_config": n == N_STREAMS},
         "cpu_baseline": {"value": round(value, 3), "unit": UNIT, "cores": cores, "kind": kind,
                          "sample": desc},
         "e2e": {"value": round(value, 3), "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
@@ -205,24 +210,36 @@ def run_b200(args):
     local = int(os.environ.get("LOCAL_RANK", "0"))
     torch.cuda.set_device(local)
     dev = torch.device("cuda", local)
-    N_STREAMS = args.streams
-    qc, kc, q, k, v = make_inputs(rank, dev, N_STREAMS)
-    n_pos = N_STREAMS * T
-    src = torch.empty((N_STREAMS, T), dtype=torch.int32, device=dev)
+    n_total = args.streams
+    if n_total % world:
+        raise SystemExit(f"{n_total} streams do not split over {world} GPUs")
+    n_rank = n_total // world                 # heads split over the ranks: strong scaling
+    lo, hi = rank * n_rank, (rank + 1) * n_rank
+    qc, kc, q, k, v = make_inputs(dev, n_total, lo, hi)
+    n_pos = n_rank * T
+    src = torch.empty((n_rank, T), dtype=torch.int32, device=dev)
     out = torch.empty_like(v)
     status = torch.zeros(1, dtype=torch.int32, device=dev)
-    ws_bytes = int(_lib.lib().lema_prefill_workspace_bytes(N_STREAMS, T, 4))
+    ws_bytes = int(_lib.lib().lema_prefill_workspace_bytes(n_rank, T, 4))
     ws = torch.empty(max(ws_bytes, 1), dtype=torch.uint8, device=dev)
     stream = torch.cuda.current_stream(dev)
 
     def step():
-        call("lema_prefill_match", ptr(q), ptr(k), 4, N_STREAMS, T, ptr(src), ptr(v), VBYTES,
+        call("lema_prefill_match", ptr(q), ptr(k), 4, n_rank, T, ptr(src), ptr(v), VBYTES,
              ptr(out), ptr(ws), ws_bytes, ptr(status), stream.cuda_stream)
 
     def barrier():
         if world > 1:
             import torch.distributed as dist
             dist.barrier()
+
+    def max_over_ranks(x: float) -> float:
+        if world == 1:
+            return x
+        import torch.distributed as dist
+        t = torch.tensor([x], device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        return float(t.item())
 
     for _ in range(max(3, args.warmup)):
         step()
@@ -232,7 +249,7 @@ def run_b200(args):
     # algorithmic bytes per step: codes in, index + row out, each distinct source row read once
     s = src.to(torch.int64)
     hit = s >= 0
-    ids = (torch.arange(N_STREAMS, device=dev, dtype=torch.int64)[:, None] * T + s)[hit]
+    ids = (torch.arange(n_rank, device=dev, dtype=torch.int64)[:, None] * T + s)[hit]
     U = int(torch.unique(ids).numel())
     alg_bytes = n_pos * (4 + 4 + VBYTES + 4) + U * VBYTES
     hit_rate = float(hit.float().mean())
@@ -252,32 +269,42 @@ def run_b200(args):
             ev[i][1].record(stream)
         t1.record(stream)
         torch.cuda.synchronize()
+        barrier()
+        # sustained: repeats of >= 0.1 s each (>= 0.5 s in all), median per step, under the
+        # same clock sampling -- the K-step region above is only a few milliseconds
+        per_step = max(1e-3, t0.elapsed_time(t1) / args.steps)
+        reps_steps = max(1, int(100.0 / per_step))
+        sustained = []
+        for _ in range(5):
+            a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            a.record(stream)
+            for _ in range(reps_steps):
+                step()
+            b.record(stream)
+            torch.cuda.synchronize()
+            sustained.append(a.elapsed_time(b) / reps_steps)
     barrier()
     clocks = clk.summary()
-    total_ms = t0.elapsed_time(t1)
+    total_ms = max_over_ranks(t0.elapsed_time(t1))
     per_launch_ms = statistics.mean(a.elapsed_time(b) for a, b in ev)
-    if world > 1:
-        import torch.distributed as dist
-        tt = torch.tensor([total_ms], device=dev)
-        dist.all_reduce(tt, op=dist.ReduceOp.MAX)
-        total_ms = float(tt.item())
+    sustained_ms = max_over_ranks(statistics.median(sustained))
     assert int(status.item()) == 0, "device status raised during the timed region"
     ms_per_step = total_ms / args.steps
-    value = world * n_pos * args.steps / (total_ms / 1e3) / 1e6
+    value = n_total * T * args.steps / (total_ms / 1e3) / 1e6
 
-    # end to end through the C ABI with host buffers (pinned), copies inside the timed region
+    # end to end through the public host-buffer call, copies inside the timed region
     e2e_steps = 0 if args.no_e2e else max(1, min(args.steps, 5))
     hq = torch.from_numpy(qc.view(np.int32)).pin_memory()
     hk = torch.from_numpy(kc.view(np.int32)).pin_memory()
     hv = v.cpu().pin_memory()
     ho = torch.empty_like(hv).pin_memory()
-    hs = torch.empty((N_STREAMS, T), dtype=torch.int32).pin_memory()
+    hs = torch.empty((n_rank, T), dtype=torch.int32).pin_memory()
     h2d = hq.numel() * 4 + hk.numel() * 4 + hv.numel() * 2
     d2h = ho.numel() * 2 + hs.numel() * 4
     # the public host-buffer call: batches of 64 streams, copies both ways overlapped with the
     # kernels (attention.HostPrefill); one untimed call first
     from latest_exact_match_attention_b200.attention import HostPrefill
-    hp = HostPrefill(dev, T, torch.int32, (D_V,), torch.bfloat16, batch=64)
+    hp = HostPrefill(dev, T, torch.int32, (D_V,), torch.bfloat16, batch=min(64, n_rank))
     if e2e_steps:
         hp(hq, hk, hv, hs, ho)
     barrier()
@@ -290,31 +317,34 @@ def run_b200(args):
         hp(hq, hk, hv, hs, ho)
     e1.record(stream)
     torch.cuda.synchronize()
-    e2e_ms = e0.elapsed_time(e1)
-    if world > 1:
-        import torch.distributed as dist
-        tt = torch.tensor([e2e_ms], device=dev)
-        dist.all_reduce(tt, op=dist.ReduceOp.MAX)
-        e2e_ms = float(tt.item())
-    e2e_value = world * n_pos * e2e_steps / (e2e_ms / 1e3) / 1e6 if e2e_steps else None
+    e2e_ms = max_over_ranks(e0.elapsed_time(e1))
+    e2e_value = n_total * T * e2e_steps / (e2e_ms / 1e3) / 1e6 if e2e_steps else None
+    _lib.check_status(dev, "bench e2e")
 
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
-        cv, cores, kind, desc = cpu_reference_sample(qc, kc, 32, reps=1)
+        cv, cores, kind, desc = cpu_reference_sample(qc, kc, n_rank, reps=1)
         cpu = {"value": round(cv, 3), "unit": UNIT, "cores": cores, "kind": kind, "sample": desc}
+
+    decode = None
+    if not args.no_decode:
+        try:
+            decode = decode_record(args, rank, world, dev, small=True)
+        except Exception as e:      # the headline line is printed whatever happens here
+            decode = {"error": f"{type(e).__name__}: {e}"[:300]}
 
     peak, peak_src = peaks()
     achieved = alg_bytes / (per_launch_ms / 1e3) / 1e9
-    # DRAM bytes per call of the three kernels, from the full-size ncu capture summarised in
-    # profiles/ (only meaningful for the default 512-stream workload)
     # K2 runs pipelined (one launch matches and copies rows) from one full wave of matchers
     # (2 per SM) on, unless LEMA_K2_PIPELINE=0; the rows here are 48 bytes (16-byte aligned)
     sms = torch.cuda.get_device_properties(dev).multi_processor_count
-    pipelined = (os.environ.get("LEMA_K2_PIPELINE", "")[:1] != "0" and N_STREAMS >= 2 * sms
+    pipelined = (os.environ.get("LEMA_K2_PIPELINE", "")[:1] != "0" and n_rank >= 2 * sms
                  and T <= (1 << 22))
+    # DRAM bytes per call: not observable without a profiler, so taken from the ncu capture
+    # of this workload summarised in profiles/ (full 512-stream calls only), and labelled
     traffic = None
     tf = ROOT / "profiles" / "prefill_match_cfg2.md"
-    if tf.exists() and N_STREAMS == 512:
+    if tf.exists() and n_rank == 512:
         import re
         key = "traffic_bytes_per_call_pipelined" if pipelined else "traffic_bytes_per_call"
         m = re.search(key + r":\s*(\d+)", tf.read_text())
@@ -327,20 +357,29 @@ def run_b200(args):
     line = {
         "metric": METRIC, "value": round(value, 2), "unit": UNIT, "n_gpus": world,
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms_per_step, 4),
-        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "u32",
+        "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "u32",
         "data": "synthetic (seeded Zipf-pool codes, N(0,1) bf16 values)",
-        "config": {"workload": WORKLOAD, "streams_per_gpu": N_STREAMS, "positions_per_gpu": n_pos,
-                   "seq_len": T, "value_bytes": VBYTES, "parallelism": f"streams x{world}, no collective",
+        "value_scope": "whole job: all streams' positions / max-over-ranks time",
+        "value_per_gpu": round(value / world, 2),
+        "config": {"workload": WORKLOAD, "streams_total": n_total, "streams_per_gpu": n_rank,
+                   "positions_per_gpu": n_pos, "seq_len": T, "value_bytes": VBYTES,
+                   "parallelism": f"heads split over {world} GPU(s), no collective",
                    "l2": "inputs+outputs 0.9 GB > 126 MB L2 (no flush)", "hit_rate": round(hit_rate, 4),
                    "distinct_sources": U,
                    "k2_mode": "pipelined" if pipelined else "two-kernel"},
+        "sustained": {"ms_per_step_median": round(sustained_ms, 4), "repeats": 5,
+                      "steps_per_repeat": reps_steps,
+                      "value": round(n_total * T / (sustained_ms / 1e3) / 1e6, 2)},
         "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
                      "frac": round(achieved / peak, 4), "traffic": traffic,
+                     "traffic_source": "ncu capture of this workload (profiles/prefill_match_cfg2.md)"
+                     if traffic else None,
                      "peak_source": peak_src, "alg_bytes_per_launch": alg_bytes,
                      "launch_ms": round(per_launch_ms, 4)},
         "e2e": {"value": e2e_value and round(e2e_value, 2), "unit": UNIT, "h2d_bytes_per_step": h2d,
                 "d2h_bytes_per_step": d2h, "steps": e2e_steps},
         "cpu_baseline": cpu,
+        "decode": decode,
         # per step: the shared-memory match kernel (pipelined: it also copies the rows), the
         # overflow-path kernel (launched whenever a stream could outgrow the shared table,
         # T > 6144; it exits at once when none did) and, two-kernel path only, the row gather
@@ -391,6 +430,18 @@ def run_proj(args):
             z = (x @ w.T).view(Bp, Tp, 2 * H, 32)
             return ((z >= 0).to(torch.int64) * pw).sum(-1)
         ref_ms = None if args.no_recipe else timed(reference_recipe, max(2, args.steps // 4))
+        # code flips against an fp64 z (the benchmark's rule: a bit may differ from the exact
+        # sign only where |z_d| < 1e-3 ||z_row||), on the first 65536 rows
+        qc, kc = proj_codes(x, w, H, H, status=status)
+        rows = min(65536, Tp)
+        z = (x[0, :rows].double() @ w.double().T).view(rows, 2 * H, 32)
+        codes = torch.cat([qc[0, :, :rows], kc[0, :, :rows]], 0).transpose(0, 1).to(torch.int64) & 0xFFFFFFFF
+        bits = ((codes[..., None] >> torch.arange(32, device=dev)) & 1).bool()
+        diff = bits != (z >= 0)
+        band = z.abs() < 1e-3 * z.norm(dim=-1, keepdim=True)
+        flips = {"rows": rows, "bits": int(z.numel()), "code_flips": int(diff.sum()),
+                 "code_flips_outside_band": int((diff & ~band).sum())}
+        del z, codes, bits, diff, band
         flops = 2.0 * Bp * Tp * dim * (2 * H * 32)
         tf = flops / (ms / 1e3) / 1e12
         print(json.dumps({
@@ -401,7 +452,7 @@ def run_proj(args):
                        "rows": Bp * Tp, "cols": 2 * H * 32, "l2": "x 1 GiB > L2"},
             "roofline": {"bound": "tensor", "achieved": round(tf, 1), "peak": peak, "unit": "TFLOP/s",
                          "frac": round(tf / peak, 4), "peak_source": peak_src},
-            "reference_recipe_ms": ref_ms and round(ref_ms, 4),
+            "reference_recipe_ms": ref_ms and round(ref_ms, 4), "codes_vs_fp64": flips,
             "speedup_vs_reference_recipe": ref_ms and round(ref_ms / ms, 2),
             "gpu_launches": args.steps, "clocks": clk.summary(),
         }), flush=True)
@@ -457,71 +508,172 @@ def run_model_prefill(args):
         torch.cuda.empty_cache()
 
 
-def run_decode(args):
-    """Config 4: batched greedy decode of a random-init 834M-shaped LEMA LM (bf16). Each
-    sequence's store is pre-filled from a --prefix-token bigram-structured prefix (chunked
-    prefill through the store), then every step is one CUDA-graph replay (all 24 layers'
-    store exchanges inside). Value: tokens/s = batch x steps / time."""
+def decode_record(args, rank: int, world: int, dev, small: bool = False, worst_load: float | None = None):
+    """Config 4: batched greedy decode of a random-init 834M-shaped LEMA LM (bf16), the batch
+    split over the ranks (each its own store and graph, no collective). Each sequence's store
+    is pre-filled from a bigram-structured prefix (chunked prefill through the store), then
+    every step is one CUDA-graph replay (all 24 layers' store exchanges inside). `small`: the
+    sub-record of the headline line (prefix 512, 32 steps). `worst_load`: the stress mode --
+    every layer's codes replaced by fresh random codes (cache.worst_case_codes, the reference's
+    worst-case hook), the store sized so that it ends at that load. Returns the record (rank 0)
+    with tokens/s of the whole job = all ranks' tokens / max-over-ranks time."""
     import math
 
     import torch
 
     from latest_exact_match_attention_b200 import synth
+    from latest_exact_match_attention_b200.cache import worst_case_codes
     from latest_exact_match_attention_b200.decode import decoder
     from latest_exact_match_attention_b200.model import Transformer
-    dev = torch.device("cuda", int(os.environ.get("LOCAL_RANK", "0")))
-    torch.cuda.set_device(dev)
     cfg = _model_cfg(4)
-    Bd, prefix = args.decode_batch, args.prefix
+    B_all = args.decode_batch if worst_load is None else args.worst_batch
+    prefix = 512 if small else args.prefix
+    steps = 32 if small else args.steps
+    warm = 3 if small else max(3, args.warmup)
+    if B_all % world:
+        raise SystemExit(f"decode batch {B_all} does not split over {world} GPUs")
+    Bd = B_all // world
     torch.manual_seed(0)
     model = Transformer(cfg).to(dev).to(torch.bfloat16).eval()
-    idx = torch.from_numpy(synth.token_stream(Bd, prefix + 1, 50304, seed=0, config_id=4)).to(dev)
+    toks = synth.token_stream(B_all, prefix + 1, 50304, seed=0, config_id=4)
+    idx = torch.from_numpy(toks[rank * Bd:(rank + 1) * Bd]).to(dev)
     P = Bd * cfg.num_heads
-    per_part = args.entries_per_partition or (prefix + args.steps + args.warmup + 8)
-    cap = math.ceil(cfg.depth * P * per_part / args.max_load)
-    cache = model.new_cache("hbm", capacity=cap, batch=Bd)
+    # the decoder's warm-up runs on a scratch store; the real store takes the prefix, the
+    # warm-up-free timed steps and the first replays
+    tokens = prefix + warm + steps + 8
+    if worst_load is not None:
+        per_part, load = tokens, worst_load          # one new entry per token per partition
+    else:
+        per_part = (min(args.entries_per_partition, tokens) if args.entries_per_partition else tokens)
+        load = args.max_load
+    cap = math.ceil(cfg.depth * P * per_part / load)
+    hook = worst_case_codes(cfg.depth) if worst_load is not None else None
+    cache = model.new_cache("hbm", capacity=cap, batch=Bd, codes_hook=hook)
     stream = torch.cuda.current_stream(dev)
+
+    def maxr(x):
+        if world == 1:
+            return x
+        t = torch.tensor([x], device=dev)
+        torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
+        return float(t.item())
+
     a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     a.record(stream)
-    for s in range(0, prefix, args.chunk):
-        model(idx[:, s:min(prefix, s + args.chunk)], cache=cache, return_logits=False)
+    for s0 in range(0, prefix, args.chunk):
+        model(idx[:, s0:min(prefix, s0 + args.chunk)], cache=cache, return_logits=False)
     b.record(stream)
     torch.cuda.synchronize()
-    prefill_ms = a.elapsed_time(b)
+    prefill_ms = maxr(a.elapsed_time(b))
     cache.check()
     counts = cache.counts().float()            # [depth, batch, heads]
     d = decoder(model, cache, tok=idx[:, prefix:prefix + 1])
-    for _ in range(max(3, args.warmup)):
+    for _ in range(warm):
         d.step()
     torch.cuda.synchronize()
+    if world > 1:
+        torch.distributed.barrier()
     with ClockSampler(dev.index) as clk:
         a.record(stream)
-        for _ in range(args.steps):
+        for _ in range(steps):
             d.step()
         b.record(stream)
         torch.cuda.synchronize()
     cache.check()
-    ms = a.elapsed_time(b) / args.steps
+    ms = maxr(a.elapsed_time(b)) / steps
     weights = sum(p.numel() * p.element_size() for p in model.parameters())
     store_bytes = cfg.depth * P * 216          # per (layer, seq, head) op: codes, row, slots
-    print(json.dumps({
-        "metric": "LEMA batched decode tok/s (config 4)", "value": round(Bd * 1e3 / ms, 1),
-        "unit": "tok/s", "n_gpus": 1, "steps": args.steps, "warmup": args.warmup,
-        "ms_per_step": round(ms, 4), "higher_is_better": True, "dtype": "bf16",
+    rec = {
+        "metric": "LEMA batched decode tok/s (config 4)" + (" worst-case codes" if hook else ""),
+        "value": round(B_all * 1e3 / ms, 1), "unit": "tok/s", "n_gpus": world, "steps": steps,
+        "warmup": warm, "ms_per_step": round(ms, 4), "higher_is_better": True, "dtype": "bf16",
+        "scaling": "strong" if world > 1 else None,
         "data": "synthetic Zipf(1.1) tokens, 20% bigram copies; random-init weights",
-        "config": {"workload": f"cfg4: {cfg.summary()}, B={Bd}, prefix {prefix}",
-                   "store_slots": cap, "store_gb": round(cache.nbytes() / 1e9, 2),
+        "config": {"workload": f"cfg4: {cfg.summary()}, B={B_all} ({Bd} per GPU), prefix {prefix}",
+                   "parallelism": f"batch split over {world} GPU(s), own store and graph each",
+                   "store_slots_per_gpu": cap, "store_gb_per_gpu": round(cache.nbytes() / 1e9, 2),
                    "store_load": round(cache.load(), 4),
-                   "entries_per_partition_by_layer": [round(float(x), 1) for x in counts.mean((1, 2))],
+                   "entries_per_partition_mean": round(float(counts.mean()), 1),
                    "entries_per_partition_max": int(counts.max())},
-        "roofline": {"bound": "hbm", "bytes_per_step": weights + store_bytes,
+        "roofline": {"bound": "hbm", "bytes_per_step_per_gpu": weights + store_bytes,
                      "achieved": round((weights + store_bytes) / (ms / 1e3) / 1e9, 1),
                      "peak": peaks()[0], "unit": "GB/s",
                      "frac": round((weights + store_bytes) / (ms / 1e3) / 1e9 / peaks()[0], 4)},
-        "prefill": {"tokens": Bd * prefix, "ms": round(prefill_ms, 1),
-                    "tok_s": round(Bd * prefix / prefill_ms * 1e3, 1), "chunk": args.chunk},
-        "gpu_launches": None, "clocks": clk.summary(),
-    }), flush=True)
+        "prefill": {"tokens": B_all * prefix, "ms": round(prefill_ms, 1),
+                    "tok_s": round(B_all * prefix / prefill_ms * 1e3, 1), "chunk": args.chunk},
+        "clocks": clk.summary(),
+    }
+    del d, cache, model
+    torch.cuda.empty_cache()
+    return rec
+
+
+def run_decode(args):
+    """Config 4 (see decode_record); --worst-case: the stress mode at store loads 0.5 / 0.9 /
+    0.95 at the end of the run, batch --worst-batch, against context --prefix."""
+    import torch
+    rank, world = dist_setup(args.gpus)
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    loads = [None] if not args.worst_case else [0.5, 0.9, 0.95]
+    for ld in loads:
+        rec = decode_record(args, rank, world, dev, worst_load=ld)
+        if rank == 0:
+            if ld is not None:
+                rec["worst_case"] = {"store_load_target": ld,
+                                     "ms_per_token": rec["ms_per_step"],
+                                     "reference_published": "RTX 3090 + host store, 834M (24 heads), B=1: "
+                                     "3.045 ms/tok @1.4k ctx ... 4.059 @573k (load 0.95), "
+                                     "code/experiments/main_inference/out/gen_08B_ram.jsonl"}
+            print(json.dumps(rec), flush=True)
+    if world > 1:
+        torch.distributed.destroy_process_group()
+
+
+def check_longctx_heads(args, rank, world, dev, src, out, v, H, T, L):
+    """Config 5 parity at full length: for heads 0 .. args.check_heads - 1 the indices of the
+    whole sequence (every rank's shard, gathered on rank 0) equal the oracle's
+    latest_prev_match over the single unsharded sequence (code/lema/attention.py:100-132),
+    regenerated on rank 0; each rank checks the value rows of 2^16 sampled positions whose
+    source lies in its own shard (and zeros where there is none)."""
+    import torch
+
+    import oracle
+    from latest_exact_match_attention_b200 import synth
+    base = rank * L
+    res = {"heads": [], "rows_checked": 0, "rows_equal": True}
+    g = torch.Generator(device=dev).manual_seed(rank)
+    for h in range(min(args.check_heads, H)):
+        idx = torch.randint(0, L, (1 << 16,), generator=g, device=dev)
+        s = src[h, idx].long()
+        local = s >= base
+        ok = torch.equal(out[h, idx[local]], v[h, s[local] - base])
+        ok = ok and bool((out[h, idx[s < 0]] == 0).all())
+        res["rows_checked"] += int(local.sum()) + int((s < 0).sum())
+        res["rows_equal"] = res["rows_equal"] and ok
+        mine = src[h].contiguous()
+        if world > 1:
+            parts = [torch.empty_like(mine) for _ in range(world)]
+            torch.distributed.all_gather(parts, mine)
+            full = torch.cat(parts)
+        else:
+            full = mine
+        if rank == 0:
+            q1, k1, _ = synth.long_code_shard(H, 0, T, synth.CONFIG5, seed=0, device=dev, heads=[h],
+                                              values=False)
+            qn, kn = q1.cpu().numpy().view(np.uint32), k1.cpu().numpy().view(np.uint32)
+            del q1, k1
+            t0 = time.perf_counter()
+            want = oracle.latest_prev_match(qn, kn)[0]
+            cpu_s = time.perf_counter() - t0
+            got = full.cpu().numpy().astype(np.int64)
+            res["heads"].append({"head": h, "positions": T, "indices_equal": bool(np.array_equal(got, want)),
+                                 "mismatches": int((got != want).sum()),
+                                 "oracle_cpu_s": round(cpu_s, 2)})
+            del qn, kn, want, got
+        del full
+    return res
 
 
 def run_longctx(args):
@@ -557,7 +709,7 @@ def run_longctx(args):
     hit = 0.0
     times, phases = [], {}
     with ClockSampler(local) as clk:
-        for _ in range(args.steps):
+        for it in range(args.steps):
             barrier()
             torch.cuda.synchronize()
             marks = []
@@ -571,8 +723,13 @@ def run_longctx(args):
                 phases[name] = phases.get(name, 0.0) + prev.elapsed_time(e) / args.steps
                 prev = e
             hit = float((src >= 0).float().mean())
-            del src, out
+            if it < args.steps - 1 or not args.check_heads:
+                del src, out           # the last step's results are checked below
     barrier()
+    check = None
+    if args.check_heads:
+        check = check_longctx_heads(args, rank, world, dev, src, out, v, H, T, L)
+        del src, out
     ms = statistics.mean(times)
     names = list(phases)
     pmax = dict(phases)
@@ -597,6 +754,7 @@ def run_longctx(args):
         "config": {"workload": f"cfg5: T={T} H={H} 32-bit codes pool 2^20 Zipf 1.05 5% fresh, d_v 64 bf16",
                    "positions_per_gpu": n // world, "seg_len": args.seg_len, "hit_rate": round(hit, 4),
                    "parallelism": f"sequence x{world}, NCCL all-gather + all-to-all"},
+        "parity_check": check,
         "phases_ms_rank0": {k: round(x, 3) for k, x in phases.items()},
         "phases_ms_max_over_ranks": {k: round(x, 3) for k, x in pmax.items()},
         "roofline": {"bound": "hbm", "alg_bytes_per_gpu_lower": alg // world,
@@ -618,6 +776,8 @@ def main():
                     help="streams per GPU (default: the workload's 512); smaller for profiling")
     ap.add_argument("--long-t", type=int, default=1 << 26, help="--workload longctx: positions")
     ap.add_argument("--seg-len", type=int, default=8192, help="--workload longctx: segment")
+    ap.add_argument("--check-heads", type=int, default=0,
+                    help="--workload longctx: compare this many full-length heads with the oracle")
     ap.add_argument("--sweep-rows", type=int, default=0,
                     help="--workload longctx: sweep rows per head (0 = chosen automatically)")
     ap.add_argument("--workload", choices=["prefill", "proj", "model-prefill", "decode", "longctx"],
@@ -630,6 +790,11 @@ def main():
     ap.add_argument("--entries-per-partition", type=int, default=0,
                     help="--workload decode: store sizing (0 = worst case, one entry per token)")
     ap.add_argument("--max-load", type=float, default=0.8, help="--workload decode: table load")
+    ap.add_argument("--worst-case", action="store_true",
+                    help="--workload decode: worst-case codes at store loads 0.5 / 0.9 / 0.95")
+    ap.add_argument("--worst-batch", type=int, default=1, help="--workload decode --worst-case: batch")
+    ap.add_argument("--no-decode", action="store_true",
+                    help="headline line: skip its small batched-decode record")
     ap.add_argument("--heads", type=int, nargs="+", default=[8, 16, 32, 64],
                     help="--workload proj: query (= key) heads per layer")
     ap.add_argument("--proj-batch", type=int, default=32, help="--workload proj: sequences")

@@ -95,6 +95,19 @@ __device__ __forceinline__ void mbar_arrive(uint32_t bar) {
 __device__ __forceinline__ void mbar_arrive_expect_tx(uint32_t bar, uint32_t bytes) {
   asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(bar), "r"(bytes) : "memory");
 }
+// The same with a bound (ns) on how long the thread may be suspended in one try: the caller
+// then checks its deadline at least that often.
+__device__ __forceinline__ bool mbar_try_wait_for(uint32_t bar, uint32_t parity, uint32_t suspend_ns) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(ok)
+      : "r"(bar), "r"(parity), "r"(suspend_ns)
+      : "memory");
+  return ok != 0;
+}
 __device__ __forceinline__ bool mbar_try_wait(uint32_t bar, uint32_t parity) {
   uint32_t ok;
   asm volatile(
@@ -163,10 +176,13 @@ __device__ __forceinline__ void tmem_load32(uint32_t taddr, uint32_t (&r)[32]) {
 // given up, or after wait_ns (then this wait raises the abort flag and the status bit).
 __device__ bool wait_phase(uint32_t bar, uint32_t parity, volatile uint32_t* abort_flag, uint32_t* status,
                            uint64_t wait_ns) {
+  // each try suspends at most ~wait_ns (between 32 ns and 1 ms); the deadline is checked
+  // every 4 tries, so a short bound (LEMA_WAIT_NS) is honoured within a few microseconds
+  const uint32_t suspend = static_cast<uint32_t>(wait_ns < 32 ? 32 : (wait_ns > 1000000 ? 1000000 : wait_ns));
   uint64_t deadline = 0;
   for (uint32_t i = 1;; ++i) {
-    if (mbar_try_wait(bar, parity)) return true;
-    if ((i & 63) == 0) {
+    if (mbar_try_wait_for(bar, parity, suspend)) return true;
+    if ((i & 3) == 0) {
       if (*abort_flag) return false;
       const uint64_t now = globaltimer();
       if (deadline == 0) {

@@ -149,7 +149,8 @@ def _mix32_torch(x):
 
 
 def long_code_shard(H: int, start: int, length: int, spec: CodeSpec = CONFIG5, seed: int = 0,
-                    device="cuda", chunk: int = 1 << 20, d_v: int = 64):
+                    device="cuda", chunk: int = 1 << 20, d_v: int = 64, heads=None,
+                    values: bool = True):
     """Positions [start, start + length) of config 5's single long sequence, generated on the
     device: (qcodes [H, length] int32, kcodes [H, length] int32, values [H, length, d_v] bf16).
 
@@ -160,7 +161,9 @@ def long_code_shard(H: int, start: int, length: int, spec: CodeSpec = CONFIG5, s
     [2^31, 3 * 2^30)) and query-fresh codes (inputs in [3 * 2^30, 2^32)) -- so query-fresh codes
     match no key. Ranks
     are drawn Zipf(spec.alpha) over the pool; a fraction spec.fresh of queries and of keys is
-    fresh. start and length must be multiples of `chunk`."""
+    fresh. start and length must be multiples of `chunk`. `heads` (a list of head indices
+    below H) generates only those heads, the same codes as in the full draw; values=False
+    skips the value rows (returns None for them)."""
     import torch
     if start % chunk or length % chunk:
         raise ValueError("start and length must be whole chunks")
@@ -168,11 +171,12 @@ def long_code_shard(H: int, start: int, length: int, spec: CodeSpec = CONFIG5, s
         raise ValueError("pool <= 2^20 codes per head and H <= 1024")
     dev = torch.device(device)
     cdf = torch.from_numpy(zipf_cdf(spec.pool, spec.alpha)).to(dev)
-    qc = torch.empty((H, length), dtype=torch.int32, device=dev)
-    kc = torch.empty((H, length), dtype=torch.int32, device=dev)
-    v = torch.empty((H, length, d_v), dtype=torch.bfloat16, device=dev)
+    heads = list(range(H)) if heads is None else list(heads)
+    qc = torch.empty((len(heads), length), dtype=torch.int32, device=dev)
+    kc = torch.empty((len(heads), length), dtype=torch.int32, device=dev)
+    v = torch.empty((len(heads), length, d_v), dtype=torch.bfloat16, device=dev) if values else None
     g = torch.Generator(device=dev)
-    for h in range(H):
+    for row, h in enumerate(heads):
         for c0 in range(0, length, chunk):
             c = (start + c0) // chunk
             g.manual_seed(((seed * 1009 + h) * 1_000_003 + c) & ((1 << 62) - 1))
@@ -184,6 +188,7 @@ def long_code_shard(H: int, start: int, length: int, spec: CodeSpec = CONFIG5, s
                 fx = torch.randint(0, 1 << 30, (chunk,), generator=g, device=dev) + ((2 + which) << 30)
                 x = torch.where(fresh, fx, x)
                 code = _mix32_torch(x)
-                out[h, c0:c0 + chunk] = (code - ((code >> 31) << 32)).to(torch.int32)
-            v[h, c0:c0 + chunk] = torch.randn((chunk, d_v), generator=g, device=dev).to(torch.bfloat16)
+                out[row, c0:c0 + chunk] = (code - ((code >> 31) << 32)).to(torch.int32)
+            if values:
+                v[row, c0:c0 + chunk] = torch.randn((chunk, d_v), generator=g, device=dev).to(torch.bfloat16)
     return qc, kc, v
