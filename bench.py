@@ -764,6 +764,167 @@ def run_longctx(args):
     }), flush=True)
 
 
+def run_cpu_baselines(args):
+    """The CPU timings the benchmark plan asks for beside the GPU (rank 0, host cores of the
+    box), each next to the same work on the GPU through this library:
+      config 1  the reference's C++ store (oracle/_ref): one prefill exchange of 8 partitions x
+                4096 positions, then 512 single-position exchanges (16-bit codes, fp32 d_v 64);
+      config 4  store work of one decode step: 24 single-position exchanges of P = 256 x 64
+                partitions against a table holding a 3050-entry prefix state per partition;
+      config 5  the index oracle (C restatement of code/lema/attention.py:100-132, one thread)
+                over one full head of 2^26 positions.
+    One JSON line each."""
+    import torch
+
+    import oracle
+    from latest_exact_match_attention_b200 import synth
+    from latest_exact_match_attention_b200.cache import HashStore
+    dev = torch.device("cuda", 0)
+    cores = len(os.sched_getaffinity(0))
+    torch.set_num_threads(cores)
+    ref = oracle.ref_store()
+    kind = "reference" if ref is not None else "port"
+
+    def cpu_exchange(table, q, k, vals, out, Tx, cap, vb):
+        if ref is not None:
+            ref.exchange(table, q, k, vals, out, Tx, 0, cap, vb)
+        else:
+            oracle.store_exchange(table.numpy(), q.numpy(), k.numpy(), vals.numpy(), Tx, 0)
+
+    def gpu_time(fn, reps=3):
+        fn()
+        torch.cuda.synchronize()
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a.record()
+        for _ in range(reps):
+            fn()
+        b.record()
+        torch.cuda.synchronize()
+        return a.elapsed_time(b) / reps
+
+    # ---------------------------------------------------------------- config 1
+    P1, T1, S1, dv1 = 8, 4096, 512, 64
+    qc, kc = synth.code_streams(P1, T1 + S1, synth.CONFIG1, seed=0, config_id=1)
+    q64, k64 = qc.astype(np.int64), kc.astype(np.int64)
+    vals = torch.from_numpy(synth.values_np(P1, T1 + S1, dv1, seed=0, config_id=1))
+    cap1, vb1 = 4 * P1 * (T1 + S1), dv1 * 4
+    times = []
+    for _ in range(2):
+        table = torch.zeros((cap1, 16 + vb1), dtype=torch.uint8)
+        out = torch.empty((P1 * T1, dv1), dtype=torch.float32)
+        t0 = time.perf_counter()
+        cpu_exchange(table, torch.from_numpy(q64[:, :T1].reshape(-1).copy()),
+                     torch.from_numpy(k64[:, :T1].reshape(-1).copy()),
+                     vals[:, :T1].reshape(-1, dv1).contiguous(), out, T1, cap1, vb1)
+        t1 = time.perf_counter()
+        o1 = torch.empty((P1, dv1), dtype=torch.float32)
+        for t in range(T1, T1 + S1):
+            cpu_exchange(table, torch.from_numpy(q64[:, t].copy()), torch.from_numpy(k64[:, t].copy()),
+                         vals[:, t].contiguous(), o1, 1, cap1, vb1)
+        times.append((t1 - t0, time.perf_counter() - t1))
+    cpu_pre, cpu_dec = times[-1]
+    # the same on the GPU: the HBM store (K3), codes and values resident
+    qd = torch.from_numpy(qc.astype(np.uint32).view(np.int32)).to(dev)
+    kd = torch.from_numpy(kc.astype(np.uint32).view(np.int32)).to(dev)
+    vd = vals.to(dev)
+
+    def gpu_run():
+        st = HashStore(dv1, groups=P1, dtype=torch.float32, capacity=cap1, device=dev)
+        o = torch.empty((P1 * T1, dv1), dtype=torch.float32, device=dev)
+        o1 = torch.empty((P1, dv1), dtype=torch.float32, device=dev)
+        st.exchange(qd[:, :T1].reshape(-1), kd[:, :T1].reshape(-1), vd[:, :T1].reshape(-1, dv1), o, T1, 0,
+                    check=False)
+        e = torch.cuda.Event(enable_timing=True)
+        e.record()
+        for t in range(T1, T1 + S1):
+            st.exchange(qd[:, t].contiguous(), kd[:, t].contiguous(), vd[:, t].contiguous(), o1, 1, 0,
+                        check=False)
+        return e
+    gpu_run()
+    torch.cuda.synchronize()
+    a = torch.cuda.Event(enable_timing=True)
+    a.record()
+    e = gpu_run()
+    b = torch.cuda.Event(enable_timing=True)
+    b.record()
+    torch.cuda.synchronize()
+    print(json.dumps({
+        "metric": "config 1 store: prefill Mpos/s and decode us/step", "n_gpus": 1,
+        "config": {"workload": "cfg1: B=1 H=8, 16-bit codes, fp32 d_v 64, prefill 4096 + 512 decode steps"},
+        "cpu_baseline": {"kind": kind, "cores": cores, "prefill_mpos_s": round(P1 * T1 / cpu_pre / 1e6, 3),
+                         "decode_us_per_step": round(cpu_dec / S1 * 1e6, 2),
+                         "sample": "code/lema/csrc/store.cpp exchange: one call of 8 x 4096, then 512 calls of 8 x 1"},
+        "gpu": {"prefill_plus_setup_ms": round(a.elapsed_time(e), 3),
+                "decode_us_per_step": round(e.elapsed_time(b) / S1 * 1e3, 2),
+                "note": "HBM store, one exchange launch per step (not graph-captured here)"},
+    }), flush=True)
+    del table
+
+    # ---------------------------------------------------------------- config 4 (store only)
+    P4, E4, dv4, L4 = 256 * 64, 3050, 24, 24
+    rng = np.random.default_rng(4)
+    cap4 = int(P4 * (E4 + 64) / 0.65)
+    kpre = rng.integers(0, 1 << 62, size=(P4, E4), dtype=np.int64)
+    vpre = torch.from_numpy(rng.integers(0, 1 << 16, size=(P4 * E4, dv4), dtype=np.uint16).view(np.int16))
+    qstep = [rng.integers(0, 1 << 62, size=P4, dtype=np.int64) for _ in range(L4)]
+    for i, qs in enumerate(qstep):                 # half of the lookups hit the prefix state
+        hit = rng.random(P4) < 0.5
+        qs[hit] = kpre[np.nonzero(hit)[0], rng.integers(0, E4, size=int(hit.sum()))]
+    kstep = [rng.integers(0, 1 << 62, size=P4, dtype=np.int64) for _ in range(L4)]
+    vstep = torch.from_numpy(rng.integers(0, 1 << 16, size=(P4, dv4), dtype=np.uint16).view(np.int16))
+    vb4 = dv4 * 2
+    table = torch.zeros((cap4, 16 + vb4), dtype=torch.uint8)
+    outp = torch.empty((P4 * E4, dv4), dtype=torch.int16)
+    t0 = time.perf_counter()
+    cpu_exchange(table, torch.from_numpy(kpre.reshape(-1)), torch.from_numpy(kpre.reshape(-1)), vpre, outp, E4,
+                 cap4, vb4)
+    fill_s = time.perf_counter() - t0
+    o4 = torch.empty((P4, dv4), dtype=torch.int16)
+    t0 = time.perf_counter()
+    for i in range(L4):
+        cpu_exchange(table, torch.from_numpy(qstep[i]), torch.from_numpy(kstep[i]), vstep, o4, 1, cap4, vb4)
+    cpu_step = time.perf_counter() - t0
+    del table, outp
+    st = HashStore(dv4, groups=P4, dtype=torch.bfloat16, capacity=cap4, device=dev)
+    st.exchange(torch.from_numpy(kpre.reshape(-1)).to(dev), torch.from_numpy(kpre.reshape(-1)).to(dev),
+                vpre.to(dev).view(torch.bfloat16), torch.empty((P4 * E4, dv4), dtype=torch.bfloat16, device=dev),
+                E4, 0, check=False)
+    qd4 = [torch.from_numpy(x).to(dev) for x in qstep]
+    kd4 = [torch.from_numpy(x).to(dev) for x in kstep]
+    vd4 = vstep.to(dev).view(torch.bfloat16)
+    od4 = torch.empty((P4, dv4), dtype=torch.bfloat16, device=dev)
+
+    def step4():
+        for i in range(L4):
+            st.exchange(qd4[i], kd4[i], vd4, od4, 1, 0, check=False)
+    g_ms = gpu_time(step4)
+    print(json.dumps({
+        "metric": "config 4 store work per decode step (24 layers x P = 256 x 64, T = 1)", "n_gpus": 1,
+        "config": {"workload": "cfg4 store only: 3050-entry prefix state per partition (64-bit codes), "
+                               "half the lookups hit, d_v 24 bf16",
+                   "table_load": round(P4 * (E4 + 2 * L4) / cap4, 3)},
+        "cpu_baseline": {"kind": kind, "cores": cores, "ms_per_step": round(cpu_step * 1e3, 3),
+                         "prefix_fill_s": round(fill_s, 2),
+                         "sample": "code/lema/csrc/store.cpp exchange, 24 calls of 16384 x 1"},
+        "gpu": {"ms_per_step": round(g_ms, 4)},
+    }), flush=True)
+    del st
+
+    # ---------------------------------------------------------------- config 5 (index oracle)
+    q5, k5, _ = synth.long_code_shard(16, 0, 1 << 26, synth.CONFIG5, seed=0, device=dev, heads=[0], values=False)
+    qn, kn = q5.cpu().numpy().view(np.uint32), k5.cpu().numpy().view(np.uint32)
+    t0 = time.perf_counter()
+    oracle.latest_prev_match(qn, kn)
+    o_s = time.perf_counter() - t0
+    print(json.dumps({
+        "metric": "config 5 index oracle, one head (Mpos/s)", "n_gpus": 0,
+        "config": {"workload": "cfg5 head 0: 2^26 positions, 32-bit codes"},
+        "cpu_baseline": {"kind": "port", "cores": 1, "value": round((1 << 26) / o_s / 1e6, 2), "unit": "Mpos/s",
+                         "seconds": round(o_s, 2),
+                         "sample": "oracle/lema_oracle.c latest_prev_match (dictionary sweep) over one full head"},
+    }), flush=True)
+
+
 def main():
     ap = argparse.ArgumentParser(description=__doc__.split("\n")[0])
     ap.add_argument("--gpus", type=int, default=1)
@@ -780,7 +941,8 @@ def main():
                     help="--workload longctx: compare this many full-length heads with the oracle")
     ap.add_argument("--sweep-rows", type=int, default=0,
                     help="--workload longctx: sweep rows per head (0 = chosen automatically)")
-    ap.add_argument("--workload", choices=["prefill", "proj", "model-prefill", "decode", "longctx"],
+    ap.add_argument("--workload", choices=["prefill", "proj", "model-prefill", "decode", "longctx",
+                                           "cpu-baselines"],
                     default="prefill",
                     help="prefill: the headline config-2 line; proj: K1 at config 3's shapes; "
                          "model-prefill: config 3; decode: config 4")
@@ -811,6 +973,8 @@ def main():
         run_decode(args)
     elif args.workload == "longctx":
         run_longctx(args)
+    elif args.workload == "cpu-baselines":
+        run_cpu_baselines(args)
     elif args.impl == "reference":
         run_reference(args)
     else:

@@ -197,9 +197,12 @@ int lema_prefill_match_strided(const void* qcodes, const void* kcodes, int code_
  *   - The first call on a device looks up that array's device address (with the device
  *     current); make that first call before any CUDA-graph stream capture.
  *   - All calls share the one array and it keeps the last call's contents: each call
- *     clears the one counter it needs at zero and assumes nothing else about it. Calls
- *     that overlap on the GPU -- on different streams, or from different host threads --
- *     race on it: order them on one stream.
+ *     clears what it needs at zero (the overflow counter and, when it runs the pipelined
+ *     mode, the control block and per-stream progress words) and assumes nothing else
+ *     about it. Calls that overlap on the GPU -- on different streams, or from different
+ *     host threads -- race on it: order them on one stream.
+ *   - The address looked up on a device is kept for the life of the process; it does not
+ *     survive cudaDeviceReset on that device. A failed look-up is retried by the next call.
  *   - A call whose scratch does not fit is rejected with LEMA_ERR_WORKSPACE: the scratch is
  *     4 * n_streams * T bytes when src is NULL, plus, when T > 6144 (32-bit codes) or
  *     T > 3072 (64-bit codes), room for at least one overflow-path table of about

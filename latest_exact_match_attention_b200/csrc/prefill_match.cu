@@ -1492,11 +1492,12 @@ Plan make_plan_within(int64_t N, int64_t T, int code_bytes, bool need_src, size_
   return pl;
 }
 
-// Device address of the array on each device, looked up once per device with that device
-// current (in host code the array's name is only a host-side stand-in for it).
-std::once_flag g_noalloc_once[64];
+// Device address of the array on each device, looked up with that device current (in host
+// code the array's name is only a host-side stand-in for it) by the first call on the device
+// and kept; a failed look-up is not kept, so the next call tries again. The address does not
+// survive cudaDeviceReset.
+std::mutex g_noalloc_mu;
 void* g_noalloc_ptr[64];
-cudaError_t g_noalloc_err[64];
 
 }  // namespace k2
 }  // namespace lema
@@ -1533,10 +1534,17 @@ extern "C" int lema_prefill_match_noalloc(const void* qcodes, const void* kcodes
   if (dev->cc_major != 10) return fail(LEMA_ERR_UNSUPPORTED, "built for sm_100a; device is sm_%d%d", dev->cc_major, dev->cc_minor);
   const int d = dev->device;
   if (d < 0 || d >= 64) return fail(LEMA_ERR_UNSUPPORTED, "device ordinal %d: lema_prefill_match_noalloc serves devices 0..63", d);
-  std::call_once(k2::g_noalloc_once[d], [d]() {
-    k2::g_noalloc_err[d] = cudaGetSymbolAddress(&k2::g_noalloc_ptr[d], k2::g_noalloc_scratch);
-  });
-  if (k2::g_noalloc_err[d] != cudaSuccess) return cuda_fail(k2::g_noalloc_err[d], "cudaGetSymbolAddress(noalloc scratch)");
+  void* scratch = nullptr;
+  {
+    std::lock_guard<std::mutex> lock(k2::g_noalloc_mu);
+    if (k2::g_noalloc_ptr[d] == nullptr) {
+      void* p = nullptr;
+      const cudaError_t e = cudaGetSymbolAddress(&p, k2::g_noalloc_scratch);
+      if (e != cudaSuccess) return cuda_fail(e, "cudaGetSymbolAddress(noalloc scratch)");
+      k2::g_noalloc_ptr[d] = p;
+    }
+    scratch = k2::g_noalloc_ptr[d];
+  }
   MatchLaunch m;
   m.qc = qcodes;
   m.kc = kcodes;
@@ -1547,7 +1555,7 @@ extern "C" int lema_prefill_match_noalloc(const void* qcodes, const void* kcodes
   m.v = values;
   m.vbytes = vbytes;
   m.out = out;
-  m.ws = k2::g_noalloc_ptr[d];
+  m.ws = scratch;
   m.ws_bytes = k2::kNoallocScratchBytes;
   m.status = status;
   m.stream = static_cast<cudaStream_t>(stream);

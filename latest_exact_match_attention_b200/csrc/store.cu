@@ -86,18 +86,28 @@ __device__ __forceinline__ void st_release(uint64_t* p, uint64_t v) {
   asm volatile("st.release.gpu.global.u64 [%0], %1;" ::"l"(p), "l"(v) : "memory");
 }
 
-template <typename Vec>
-__device__ __forceinline__ void copy_row(Vec* dst, const Vec* src, int wpr) {
-  for (int k = 0; k < wpr; ++k) dst[k] = src[k];
+// Probing is done by a GROUP of kG = 8 lanes per item: each round trip the group reads the
+// next kG consecutive headers (one per lane, 16 bytes each: 128 contiguous bytes) and decides
+// with one ballot which slot, in probe order, ends the probe (its entry, or an empty slot).
+// A chain of c slots then costs about c / 8 dependent round trips instead of c: at load 0.95
+// an unsuccessful linear probe averages ~200 slots.
+constexpr int kG = 8;
+
+struct Lane {
+  int j;           // index in the group
+  int gbase;       // the group's first lane in the warp
+  unsigned gmask;  // the group's lanes
+};
+__device__ __forceinline__ Lane group_lane() {
+  const int lane = threadIdx.x & 31;
+  return Lane{lane & (kG - 1), lane & ~(kG - 1), 0xFFu << (lane & ~(kG - 1))};
 }
 
-template <typename Vec>
-__device__ __forceinline__ void zero_row(Vec* dst, int wpr) {
-  const Vec z = zero_vec<Vec>();
-  for (int k = 0; k < wpr; ++k) dst[k] = z;
+__device__ __forceinline__ uint64_t wrap_add(uint64_t s, uint64_t d, uint64_t cap) {
+  s += d;
+  while (s >= cap) s -= cap;
+  return s;
 }
-
-constexpr int kSpecWords = 8;  // rows of up to 8 vector words are read with the home header
 
 __device__ __forceinline__ uint64_t* header(const Args& a, uint64_t s) {
   return reinterpret_cast<uint64_t*>(a.table) + 2 * s;
@@ -106,78 +116,106 @@ template <typename Vec>
 __device__ __forceinline__ Vec* row_of(const Args& a, uint64_t s) {
   return reinterpret_cast<Vec*>(a.rows + s * a.stride);
 }
+// (code, state) of slot s, through L2: other items of the same launch may claim slots of it
+__device__ __forceinline__ void read_header(const Args& a, uint64_t s, uint64_t& code, uint64_t& state) {
+  const ulonglong2 h = __ldcg(reinterpret_cast<const ulonglong2*>(header(a, s)));
+  code = h.x;
+  state = h.y;
+}
 
-// Copies the value stored under (group, code) into dst, or zeros. Returns whether it hit.
-// The home slot's header and (for rows of up to kSpecWords words) its row are read together,
-// with plain loads; further probes walk the dense header array. Plain loads are safe because a
-// lookup only runs where nothing else can be writing a slot of its group: in a decode step the
-// item's own insert comes after its lookup and every other item has another group; a prefill
-// chunk's lookups are a kernel of their own. A slot seen empty ends the probe: slots are never
-// freed, so every slot between an entry's home and the entry was occupied before this call.
+// The group's lanes copy / zero the row's vector words j, j + kG, ...
 template <typename Vec>
-__device__ bool lookup(const Args& a, uint64_t code, uint64_t group, Vec* dst) {
+__device__ __forceinline__ void copy_row_g(Vec* dst, const Vec* src, int wpr, int j) {
+  for (int k = j; k < wpr; k += kG) dst[k] = src[k];
+}
+template <typename Vec>
+__device__ __forceinline__ void zero_row_g(Vec* dst, int wpr, int j) {
+  const Vec z = zero_vec<Vec>();
+  for (int k = j; k < wpr; k += kG) dst[k] = z;
+}
+
+// Copies the value stored under (group, code) into dst, or zeros; all kG lanes of the group
+// call it. Returns whether it hit. The first round also reads the home slot's row (rows of up
+// to kG vector words), so a hit at home costs one round trip. A slot seen empty ends the
+// probe: slots are never freed, so every slot between an entry's home and the entry was
+// occupied before this launch (slots other items claim meanwhile only lengthen the scan).
+template <typename Vec>
+__device__ bool lookup(const Args& a, uint64_t code, uint64_t group, Vec* dst, const Lane& L) {
   const int wpr = static_cast<int>(a.vbytes / static_cast<int64_t>(sizeof(Vec)));
   const uint64_t tag = group + 2;
   uint64_t s = home(code, group, a);
-  if (wpr <= kSpecWords) {
-    Vec row[kSpecWords];
-    const uint64_t* h = header(a, s);
-    const uint64_t cd = h[0], st = h[1];
-    const Vec* src = row_of<const Vec>(a, s);
-#pragma unroll
-    for (int k = 0; k < kSpecWords; ++k)
-      if (k < wpr) row[k] = src[k];
-    if (st == kEmpty) {
-      zero_row(dst, wpr);
-      return false;
+  Vec spec = zero_vec<Vec>();
+  if (wpr <= kG && L.j < wpr) spec = row_of<const Vec>(a, s)[L.j];
+  for (uint64_t t = 0; t < a.cap; t += kG) {
+    uint64_t cd, st;
+    read_header(a, wrap_add(s, L.j, a.cap), cd, st);
+    const bool valid = t + L.j < a.cap;  // no slot twice within one cycle of the table
+    const unsigned hit = (__ballot_sync(L.gmask, valid && st == tag && cd == code) >> L.gbase) & 0xFFu;
+    const unsigned emp = (__ballot_sync(L.gmask, valid && st == kEmpty) >> L.gbase) & 0xFFu;
+    const unsigned stop = hit | emp;
+    if (stop) {
+      const int k = __ffs(stop) - 1;
+      if ((hit >> k) & 1u) {
+        if (t == 0 && k == 0 && wpr <= kG) {
+          if (L.j < wpr) dst[L.j] = spec;
+        } else {
+          copy_row_g(dst, row_of<const Vec>(a, wrap_add(s, k, a.cap)), wpr, L.j);
+        }
+        return true;
+      }
+      break;
     }
-    if (st == tag && cd == code) {
-#pragma unroll
-      for (int k = 0; k < kSpecWords; ++k)
-        if (k < wpr) dst[k] = row[k];
-      return true;
-    }
-    s = (s + 1 == a.cap) ? 0 : s + 1;
+    s = wrap_add(s, kG, a.cap);
   }
-  for (uint64_t t = 0; t < a.cap; ++t) {
-    const uint64_t* h = header(a, s);
-    const uint64_t st = h[1];
-    if (st == kEmpty) break;
-    if (st == tag && h[0] == code) {
-      copy_row(dst, row_of<const Vec>(a, s), wpr);
-      return true;
-    }
-    s = (s + 1 == a.cap) ? 0 : s + 1;
-  }
-  zero_row(dst, wpr);
+  zero_row_g(dst, wpr, L.j);
   return false;
 }
 
-// (group, code) -> row, latest write wins. Returns 1 for a newly claimed slot, 0 for an
-// overwrite, -1 when every slot was probed (the table is full). `first` is the state of the
-// home slot if the caller already read it (a stale read only costs a failed claim), else ~0.
+// (group, code) -> row, latest write wins; all kG lanes of the group call it. Returns 1 for a
+// newly claimed slot, 0 for an overwrite, -1 when every slot was probed (the table is full).
+// Only this item inserts this (group, code) in this launch (a decode step's items have
+// distinct groups; a chunk inserts each distinct code of a partition once), so an entry seen
+// for it was published by an earlier launch. A claim is one compare-and-swap EMPTY -> LOCKED
+// by the lane at the slot; the group writes code and row, then that lane publishes the state
+// with a release store (cumulative over the group's writes, ordered by the group barrier).
+// A lost claim (another item took the slot) continues from the next slot.
 template <typename Vec>
-__device__ int insert(const Args& a, uint64_t code, uint64_t group, const Vec* row, uint64_t first = ~0ull) {
+__device__ int insert(const Args& a, uint64_t code, uint64_t group, const Vec* row, const Lane& L) {
   const int wpr = static_cast<int>(a.vbytes / static_cast<int64_t>(sizeof(Vec)));
   const uint64_t tag = group + 2;
   uint64_t s = home(code, group, a);
-  for (uint64_t t = 0; t < a.cap; ++t) {
-    uint64_t* hdr = header(a, s);
-    uint64_t st = (t == 0 && first != ~0ull) ? first : ld_acquire(hdr + 1);
-    if (st == kEmpty) {
-      st = atomicCAS(reinterpret_cast<unsigned long long*>(hdr + 1), kEmpty, kLocked);
-      if (st == kEmpty) {
-        hdr[0] = code;
-        copy_row(row_of<Vec>(a, s), row, wpr);
-        st_release(hdr + 1, tag);
-        return 1;
-      }
+  uint64_t t = 0;
+  while (t < a.cap) {
+    uint64_t cd, st;
+    read_header(a, wrap_add(s, L.j, a.cap), cd, st);
+    const bool valid = t + L.j < a.cap;
+    const unsigned mine = (__ballot_sync(L.gmask, valid && st == tag && cd == code) >> L.gbase) & 0xFFu;
+    const unsigned emp = (__ballot_sync(L.gmask, valid && st == kEmpty) >> L.gbase) & 0xFFu;
+    const unsigned stop = mine | emp;
+    if (!stop) {
+      s = wrap_add(s, kG, a.cap);
+      t += kG;
+      continue;
     }
-    if (st == tag && hdr[0] == code) {
-      copy_row(row_of<Vec>(a, s), row, wpr);
+    const int k = __ffs(stop) - 1;
+    const uint64_t slot = wrap_add(s, k, a.cap);
+    uint64_t* hdr = header(a, slot);
+    if ((mine >> k) & 1u) {
+      copy_row_g(row_of<Vec>(a, slot), row, wpr, L.j);
       return 0;
     }
-    s = (s + 1 == a.cap) ? 0 : s + 1;
+    int won = 0;
+    if (L.j == k) won = atomicCAS(reinterpret_cast<unsigned long long*>(hdr + 1), kEmpty, kLocked) == kEmpty;
+    won = __shfl_sync(L.gmask, won, L.gbase + k);
+    if (won) {
+      if (L.j == k) hdr[0] = code;
+      copy_row_g(row_of<Vec>(a, slot), row, wpr, L.j);
+      __syncwarp(L.gmask);
+      if (L.j == k) st_release(hdr + 1, tag);
+      return 1;
+    }
+    s = wrap_add(slot, 1, a.cap);
+    t += static_cast<uint64_t>(k) + 1;
   }
   return -1;
 }
@@ -187,57 +225,61 @@ __device__ __forceinline__ uint64_t load_code(const void* p, int64_t i) {
   return static_cast<uint64_t>(static_cast<const CodeT*>(p)[i]);
 }
 
-// T == 1: item i is partition i; look up, then insert.
+// T == 1: item i is partition i; look up, then insert. kG lanes per item.
 template <typename CodeT, typename Vec>
 __global__ void __launch_bounds__(kThreads) exchange_step(const Args a) {
-  const int64_t i = static_cast<int64_t>(blockIdx.x) * kThreads + threadIdx.x;
-  if (i >= a.n) return;
+  const int64_t i = (static_cast<int64_t>(blockIdx.x) * kThreads + threadIdx.x) / kG;
+  if (i >= a.n) return;  // whole groups
+  const Lane L = group_lane();
   const int64_t wpr = a.vbytes / static_cast<int64_t>(sizeof(Vec));
   const uint64_t g = a.g0 + static_cast<uint64_t>(i);
-  const uint64_t kcode = load_code<CodeT>(a.kc, i);
-  // the insert's home slot state is read alongside the lookup (an independent load)
-  const uint64_t first = header(a, home(kcode, g, a))[1];
-  lookup<Vec>(a, load_code<CodeT>(a.qc, i), g, reinterpret_cast<Vec*>(a.out) + i * wpr);
-  const int r = insert<Vec>(a, kcode, g, reinterpret_cast<const Vec*>(a.v) + i * wpr, first);
-  if (r < 0) {
-    raise_status(a.status, LEMA_STATUS_TABLE_FULL);
-  } else if (r > 0) {
-    atomicAdd(reinterpret_cast<unsigned long long*>(a.counts + i), 1ull);
+  lookup<Vec>(a, load_code<CodeT>(a.qc, i), g, reinterpret_cast<Vec*>(a.out) + i * wpr, L);
+  const int r = insert<Vec>(a, load_code<CodeT>(a.kc, i), g, reinterpret_cast<const Vec*>(a.v) + i * wpr, L);
+  if (L.j == 0) {
+    if (r < 0) {
+      raise_status(a.status, LEMA_STATUS_TABLE_FULL);
+    } else if (r > 0) {
+      atomicAdd(reinterpret_cast<unsigned long long*>(a.counts + i), 1ull);
+    }
   }
 }
 
-// T > 1, phase (2): in-chunk match or store lookup.
+// T > 1, phase (2): in-chunk match or store lookup. kG lanes per item.
 template <typename CodeT, typename Vec>
 __global__ void __launch_bounds__(kThreads) exchange_resolve(const Args a) {
-  const int64_t i = static_cast<int64_t>(blockIdx.x) * kThreads + threadIdx.x;
+  const int64_t i = (static_cast<int64_t>(blockIdx.x) * kThreads + threadIdx.x) / kG;
   if (i >= a.n) return;
+  const Lane L = group_lane();
   const int64_t wpr = a.vbytes / static_cast<int64_t>(sizeof(Vec));
   const int64_t p = i / a.T;
   Vec* dst = reinterpret_cast<Vec*>(a.out) + i * wpr;
   const int32_t s = a.src[i];
   if (s >= 0) {
-    copy_row(dst, reinterpret_cast<const Vec*>(a.v) + (p * a.T + s) * wpr, static_cast<int>(wpr));
+    copy_row_g(dst, reinterpret_cast<const Vec*>(a.v) + (p * a.T + s) * wpr, static_cast<int>(wpr), L.j);
   } else {
-    lookup<Vec>(a, load_code<CodeT>(a.qc, i), a.g0 + static_cast<uint64_t>(p), dst);
+    lookup<Vec>(a, load_code<CodeT>(a.qc, i), a.g0 + static_cast<uint64_t>(p), dst, L);
   }
 }
 
 // T > 1, phase (3): insert each partition's distinct key codes with their last row.
 template <typename CodeT, typename Vec>
 __global__ void __launch_bounds__(kThreads) exchange_insert(const Args a) {
-  const int64_t i = static_cast<int64_t>(blockIdx.x) * kThreads + threadIdx.x;
+  const int64_t i = (static_cast<int64_t>(blockIdx.x) * kThreads + threadIdx.x) / kG;
   if (i >= a.n) return;
   const int64_t p = i / a.T;
   const int64_t e = i - p * a.T;
-  if (e >= a.lt_count[p]) return;
+  if (e >= a.lt_count[p]) return;  // whole groups
+  const Lane L = group_lane();
   const int64_t wpr = a.vbytes / static_cast<int64_t>(sizeof(Vec));
   const int32_t pos = a.lt_pos[i];
   const int r = insert<Vec>(a, load_code<CodeT>(a.lt_code, i), a.g0 + static_cast<uint64_t>(p),
-                            reinterpret_cast<const Vec*>(a.v) + (p * a.T + pos) * wpr);
-  if (r < 0) {
-    raise_status(a.status, LEMA_STATUS_TABLE_FULL);
-  } else if (r > 0) {
-    atomicAdd(reinterpret_cast<unsigned long long*>(a.counts + p), 1ull);
+                            reinterpret_cast<const Vec*>(a.v) + (p * a.T + pos) * wpr, L);
+  if (L.j == 0) {
+    if (r < 0) {
+      raise_status(a.status, LEMA_STATUS_TABLE_FULL);
+    } else if (r > 0) {
+      atomicAdd(reinterpret_cast<unsigned long long*>(a.counts + p), 1ull);
+    }
   }
 }
 
@@ -266,7 +308,7 @@ WsLayout layout(int64_t n, int64_t T, int code_bytes) {
 
 template <typename CodeT, typename Vec>
 int run(Args a, int64_t T, void* ws, size_t ws_bytes, int code_bytes, cudaStream_t stream) {
-  const unsigned blocks = static_cast<unsigned>((a.n + kThreads - 1) / kThreads);
+  const unsigned blocks = static_cast<unsigned>((a.n * kG + kThreads - 1) / kThreads);
   if (T == 1) {
     exchange_step<CodeT, Vec><<<blocks, kThreads, 0, stream>>>(a);
     LEMA_CUDA_TRY(cudaGetLastError());

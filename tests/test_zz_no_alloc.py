@@ -73,8 +73,32 @@ def test_noalloc_equals_workspace_entry_point_twice(cuda, want_src):
         assert torch.equal(out.view(torch.uint8), out_ref.view(torch.uint8))
 
 
+def test_noalloc_pipelined_mode_and_sweep_twice(cuda, monkeypatch):
+    """At least one wave of matchers (296 streams) of 32-bit codes with 16-byte rows and src
+    passed: the call takes the pipelined mode, whose control block and per-stream progress
+    words also live in the shared array (cleared by every call); without value rows the same
+    streams take the dictionary + sweep matcher. Two calls in a row each, then the two-kernel
+    path (LEMA_K2_PIPELINE=0) through the same array."""
+    q, k, v = config2_case(cuda, 320, 6)
+    src_ref, out_ref = prefill_match(q, k, v)
+    for _ in range(2):
+        src, out, status = noalloc(q, k, v)
+        torch.cuda.synchronize()
+        assert int(status.item()) == 0
+        assert torch.equal(src, src_ref) and torch.equal(out, out_ref)
+        src, _, status = noalloc(q, k, None)
+        torch.cuda.synchronize()
+        assert int(status.item()) == 0 and torch.equal(src, src_ref)
+    monkeypatch.setenv("LEMA_K2_PIPELINE", "0")
+    src, out, status = noalloc(q, k, v)
+    torch.cuda.synchronize()
+    assert int(status.item()) == 0
+    assert torch.equal(src, src_ref) and torch.equal(out, out_ref)
+
+
 def test_noalloc_rejects_oversized_calls(cuda):
-    # indices of 512 x 16384 positions alone need 32 MiB + 256 KiB of scratch
+    # the indices of 512 x 16384 positions alone fill the 32 MiB; the overflow counter, list
+    # and one overflow-path table on top of them do not fit
     q = torch.zeros((512, 16384), dtype=torch.int32, device=cuda)
     v = torch.zeros((512, 16384, 24), dtype=torch.bfloat16, device=cuda)
     with pytest.raises(LemaError, match="scratch"):
