@@ -80,8 +80,10 @@ class ModelConfig:
 
     @classmethod
     def from_dict(cls, d: dict) -> "ModelConfig":
-        names = {f.name for f in dataclasses.fields(cls)}
-        return cls(**{k: v for k, v in d.items() if k in names})
+        """A config from a saved dict (a checkpoint's config.json); keys that are not
+        fields of this config are ignored."""
+        known = {f.name: d[f.name] for f in dataclasses.fields(cls) if f.name in d}
+        return cls(**known)
 
     def summary(self) -> str:
         return (f"{self.depth}L d{self.dim} h{self.num_heads} d_qk {self.d_qk} d_v {self.d_v} "
@@ -344,7 +346,6 @@ class Transformer(nn.Module):
         return out
 
     def n_params(self, embedding: bool = True) -> int:
-        n = sum(p.numel() for p in self.parameters())
-        if not embedding:
-            n -= self.tok_emb.weight.numel() + self.lm_head.weight.numel()
-        return n
+        """Parameter count; embedding=False leaves out the token embedding and the head."""
+        skip = set() if embedding else {id(self.tok_emb.weight), id(self.lm_head.weight)}
+        return sum(p.numel() for p in self.parameters() if id(p) not in skip)

@@ -6,9 +6,10 @@ The reference JIT-builds code/lema/csrc/store.cpp with torch's extension builder
 the read-only reference checkout, with the same flags, into oracle/_ref/lema_store_ref.so.
 The system g++ is used because the environment's default CXX wrapper cannot link -fopenmp.
 Run in the build container (where the reference exists); the GPU box loads the prebuilt
-.so through `oracle.ref_store()`.
+.so through `oracle.ref_store()`. The checkout is the argument, else LEMA_REFERENCE_ROOT,
+else the build container's conventional location (`reference_root()`).
 
-    python -m oracle.build_ref [/root/reference]
+    python -m oracle.build_ref [REFERENCE_ROOT]
 """
 from __future__ import annotations
 
@@ -19,10 +20,17 @@ from pathlib import Path
 HERE = Path(__file__).resolve().parent
 OUT = HERE / "_ref"
 NAME = "lema_store_ref"
+_CONVENTIONAL_ROOT = "/root/reference"
 
 
-def build(reference_root: str | Path = "/root/reference") -> Path | None:
-    src = Path(reference_root) / "code" / "lema" / "csrc" / "store.cpp"
+def reference_root() -> Path:
+    """The read-only reference checkout: LEMA_REFERENCE_ROOT, else the conventional location."""
+    return Path(os.environ.get("LEMA_REFERENCE_ROOT", _CONVENTIONAL_ROOT))
+
+
+def build(reference_root_dir: str | Path | None = None) -> Path | None:
+    root = Path(reference_root_dir) if reference_root_dir is not None else reference_root()
+    src = root / "code" / "lema" / "csrc" / "store.cpp"
     if not src.exists():
         return None
     OUT.mkdir(parents=True, exist_ok=True)
@@ -47,4 +55,4 @@ def build(reference_root: str | Path = "/root/reference") -> Path | None:
 
 
 if __name__ == "__main__":
-    print(build(sys.argv[1] if len(sys.argv) > 1 else "/root/reference"))
+    print(build(sys.argv[1] if len(sys.argv) > 1 else None))

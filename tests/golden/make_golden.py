@@ -3,7 +3,7 @@
 Run in the build container, where the reference checkout exists (it does not on the GPU box,
 which only reads the committed .npz files):
 
-    CXX=/usr/bin/g++ CC=/usr/bin/gcc python tests/golden/make_golden.py [/root/reference]
+    CXX=/usr/bin/g++ CC=/usr/bin/gcc python tests/golden/make_golden.py [REFERENCE_ROOT]
 
 Inputs come from this repository's seeded generator (latest_exact_match_attention_b200.synth)
 and are stored in the fixtures, so the fixtures do not depend on the generator staying the
@@ -197,4 +197,5 @@ def main(ref_root: str):
 
 
 if __name__ == "__main__":
-    main(sys.argv[1] if len(sys.argv) > 1 else "/root/reference")
+    from oracle.build_ref import reference_root
+    main(sys.argv[1] if len(sys.argv) > 1 else str(reference_root()))
