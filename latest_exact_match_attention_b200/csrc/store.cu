@@ -90,17 +90,27 @@ __device__ __forceinline__ void st_release(uint64_t* p, uint64_t v) {
 // next kG consecutive headers (one per lane, 16 bytes each: 128 contiguous bytes) and decides
 // with one ballot which slot, in probe order, ends the probe (its entry, or an empty slot).
 // A chain of c slots then costs about c / 8 dependent round trips instead of c: at load 0.95
-// an unsuccessful linear probe averages ~200 slots.
+// an unsuccessful linear probe averages ~200 slots. Calls with few items (a batch-1 decode
+// step has 64 per layer) use whole warps instead (kWideG = 32 slots per round trip): the
+// lanes are there for free.
 constexpr int kG = 8;
+constexpr int kWideG = 32;
+constexpr int64_t kWideMaxItems = 16384;  // up to this many items per call: 32-lane groups
 
+template <int G>
 struct Lane {
   int j;           // index in the group
   int gbase;       // the group's first lane in the warp
   unsigned gmask;  // the group's lanes
+  __device__ __forceinline__ unsigned bits(unsigned ballot) const {
+    return G == 32 ? ballot : (ballot >> gbase) & ((1u << G) - 1u);
+  }
 };
-__device__ __forceinline__ Lane group_lane() {
+template <int G>
+__device__ __forceinline__ Lane<G> group_lane() {
   const int lane = threadIdx.x & 31;
-  return Lane{lane & (kG - 1), lane & ~(kG - 1), 0xFFu << (lane & ~(kG - 1))};
+  const int base = lane & ~(G - 1);
+  return Lane<G>{lane & (G - 1), base, G == 32 ? 0xFFFFFFFFu : (((1u << G) - 1u) << base)};
 }
 
 __device__ __forceinline__ uint64_t wrap_add(uint64_t s, uint64_t d, uint64_t cap) {
@@ -123,15 +133,15 @@ __device__ __forceinline__ void read_header(const Args& a, uint64_t s, uint64_t&
   state = h.y;
 }
 
-// The group's lanes copy / zero the row's vector words j, j + kG, ...
-template <typename Vec>
+// The group's lanes copy / zero the row's vector words j, j + G, ...
+template <int G, typename Vec>
 __device__ __forceinline__ void copy_row_g(Vec* dst, const Vec* src, int wpr, int j) {
-  for (int k = j; k < wpr; k += kG) dst[k] = src[k];
+  for (int k = j; k < wpr; k += G) dst[k] = src[k];
 }
-template <typename Vec>
+template <int G, typename Vec>
 __device__ __forceinline__ void zero_row_g(Vec* dst, int wpr, int j) {
   const Vec z = zero_vec<Vec>();
-  for (int k = j; k < wpr; k += kG) dst[k] = z;
+  for (int k = j; k < wpr; k += G) dst[k] = z;
 }
 
 // Copies the value stored under (group, code) into dst, or zeros; all kG lanes of the group
@@ -139,35 +149,35 @@ __device__ __forceinline__ void zero_row_g(Vec* dst, int wpr, int j) {
 // to kG vector words), so a hit at home costs one round trip. A slot seen empty ends the
 // probe: slots are never freed, so every slot between an entry's home and the entry was
 // occupied before this launch (slots other items claim meanwhile only lengthen the scan).
-template <typename Vec>
-__device__ bool lookup(const Args& a, uint64_t code, uint64_t group, Vec* dst, const Lane& L) {
+template <int G, typename Vec>
+__device__ bool lookup(const Args& a, uint64_t code, uint64_t group, Vec* dst, const Lane<G>& L) {
   const int wpr = static_cast<int>(a.vbytes / static_cast<int64_t>(sizeof(Vec)));
   const uint64_t tag = group + 2;
   uint64_t s = home(code, group, a);
   Vec spec = zero_vec<Vec>();
-  if (wpr <= kG && L.j < wpr) spec = row_of<const Vec>(a, s)[L.j];
-  for (uint64_t t = 0; t < a.cap; t += kG) {
+  if (wpr <= G && L.j < wpr) spec = row_of<const Vec>(a, s)[L.j];
+  for (uint64_t t = 0; t < a.cap; t += G) {
     uint64_t cd, st;
     read_header(a, wrap_add(s, L.j, a.cap), cd, st);
     const bool valid = t + L.j < a.cap;  // no slot twice within one cycle of the table
-    const unsigned hit = (__ballot_sync(L.gmask, valid && st == tag && cd == code) >> L.gbase) & 0xFFu;
-    const unsigned emp = (__ballot_sync(L.gmask, valid && st == kEmpty) >> L.gbase) & 0xFFu;
+    const unsigned hit = L.bits(__ballot_sync(L.gmask, valid && st == tag && cd == code));
+    const unsigned emp = L.bits(__ballot_sync(L.gmask, valid && st == kEmpty));
     const unsigned stop = hit | emp;
     if (stop) {
       const int k = __ffs(stop) - 1;
       if ((hit >> k) & 1u) {
-        if (t == 0 && k == 0 && wpr <= kG) {
+        if (t == 0 && k == 0 && wpr <= G) {
           if (L.j < wpr) dst[L.j] = spec;
         } else {
-          copy_row_g(dst, row_of<const Vec>(a, wrap_add(s, k, a.cap)), wpr, L.j);
+          copy_row_g<G>(dst, row_of<const Vec>(a, wrap_add(s, k, a.cap)), wpr, L.j);
         }
         return true;
       }
       break;
     }
-    s = wrap_add(s, kG, a.cap);
+    s = wrap_add(s, G, a.cap);
   }
-  zero_row_g(dst, wpr, L.j);
+  zero_row_g<G>(dst, wpr, L.j);
   return false;
 }
 
@@ -179,8 +189,8 @@ __device__ bool lookup(const Args& a, uint64_t code, uint64_t group, Vec* dst, c
 // by the lane at the slot; the group writes code and row, then that lane publishes the state
 // with a release store (cumulative over the group's writes, ordered by the group barrier).
 // A lost claim (another item took the slot) continues from the next slot.
-template <typename Vec>
-__device__ int insert(const Args& a, uint64_t code, uint64_t group, const Vec* row, const Lane& L) {
+template <int G, typename Vec>
+__device__ int insert(const Args& a, uint64_t code, uint64_t group, const Vec* row, const Lane<G>& L) {
   const int wpr = static_cast<int>(a.vbytes / static_cast<int64_t>(sizeof(Vec)));
   const uint64_t tag = group + 2;
   uint64_t s = home(code, group, a);
@@ -189,19 +199,19 @@ __device__ int insert(const Args& a, uint64_t code, uint64_t group, const Vec* r
     uint64_t cd, st;
     read_header(a, wrap_add(s, L.j, a.cap), cd, st);
     const bool valid = t + L.j < a.cap;
-    const unsigned mine = (__ballot_sync(L.gmask, valid && st == tag && cd == code) >> L.gbase) & 0xFFu;
-    const unsigned emp = (__ballot_sync(L.gmask, valid && st == kEmpty) >> L.gbase) & 0xFFu;
+    const unsigned mine = L.bits(__ballot_sync(L.gmask, valid && st == tag && cd == code));
+    const unsigned emp = L.bits(__ballot_sync(L.gmask, valid && st == kEmpty));
     const unsigned stop = mine | emp;
     if (!stop) {
-      s = wrap_add(s, kG, a.cap);
-      t += kG;
+      s = wrap_add(s, G, a.cap);
+      t += G;
       continue;
     }
     const int k = __ffs(stop) - 1;
     const uint64_t slot = wrap_add(s, k, a.cap);
     uint64_t* hdr = header(a, slot);
     if ((mine >> k) & 1u) {
-      copy_row_g(row_of<Vec>(a, slot), row, wpr, L.j);
+      copy_row_g<G>(row_of<Vec>(a, slot), row, wpr, L.j);
       return 0;
     }
     int won = 0;
@@ -209,7 +219,7 @@ __device__ int insert(const Args& a, uint64_t code, uint64_t group, const Vec* r
     won = __shfl_sync(L.gmask, won, L.gbase + k);
     if (won) {
       if (L.j == k) hdr[0] = code;
-      copy_row_g(row_of<Vec>(a, slot), row, wpr, L.j);
+      copy_row_g<G>(row_of<Vec>(a, slot), row, wpr, L.j);
       __syncwarp(L.gmask);
       if (L.j == k) st_release(hdr + 1, tag);
       return 1;
@@ -225,16 +235,16 @@ __device__ __forceinline__ uint64_t load_code(const void* p, int64_t i) {
   return static_cast<uint64_t>(static_cast<const CodeT*>(p)[i]);
 }
 
-// T == 1: item i is partition i; look up, then insert. kG lanes per item.
-template <typename CodeT, typename Vec>
+// T == 1: item i is partition i; look up, then insert. G lanes per item.
+template <typename CodeT, typename Vec, int G>
 __global__ void __launch_bounds__(kThreads) exchange_step(const Args a) {
-  const int64_t i = (static_cast<int64_t>(blockIdx.x) * kThreads + threadIdx.x) / kG;
+  const int64_t i = (static_cast<int64_t>(blockIdx.x) * kThreads + threadIdx.x) / G;
   if (i >= a.n) return;  // whole groups
-  const Lane L = group_lane();
+  const Lane<G> L = group_lane<G>();
   const int64_t wpr = a.vbytes / static_cast<int64_t>(sizeof(Vec));
   const uint64_t g = a.g0 + static_cast<uint64_t>(i);
-  lookup<Vec>(a, load_code<CodeT>(a.qc, i), g, reinterpret_cast<Vec*>(a.out) + i * wpr, L);
-  const int r = insert<Vec>(a, load_code<CodeT>(a.kc, i), g, reinterpret_cast<const Vec*>(a.v) + i * wpr, L);
+  lookup<G, Vec>(a, load_code<CodeT>(a.qc, i), g, reinterpret_cast<Vec*>(a.out) + i * wpr, L);
+  const int r = insert<G, Vec>(a, load_code<CodeT>(a.kc, i), g, reinterpret_cast<const Vec*>(a.v) + i * wpr, L);
   if (L.j == 0) {
     if (r < 0) {
       raise_status(a.status, LEMA_STATUS_TABLE_FULL);
@@ -244,35 +254,35 @@ __global__ void __launch_bounds__(kThreads) exchange_step(const Args a) {
   }
 }
 
-// T > 1, phase (2): in-chunk match or store lookup. kG lanes per item.
-template <typename CodeT, typename Vec>
+// T > 1, phase (2): in-chunk match or store lookup. G lanes per item.
+template <typename CodeT, typename Vec, int G>
 __global__ void __launch_bounds__(kThreads) exchange_resolve(const Args a) {
-  const int64_t i = (static_cast<int64_t>(blockIdx.x) * kThreads + threadIdx.x) / kG;
+  const int64_t i = (static_cast<int64_t>(blockIdx.x) * kThreads + threadIdx.x) / G;
   if (i >= a.n) return;
-  const Lane L = group_lane();
+  const Lane<G> L = group_lane<G>();
   const int64_t wpr = a.vbytes / static_cast<int64_t>(sizeof(Vec));
   const int64_t p = i / a.T;
   Vec* dst = reinterpret_cast<Vec*>(a.out) + i * wpr;
   const int32_t s = a.src[i];
   if (s >= 0) {
-    copy_row_g(dst, reinterpret_cast<const Vec*>(a.v) + (p * a.T + s) * wpr, static_cast<int>(wpr), L.j);
+    copy_row_g<G>(dst, reinterpret_cast<const Vec*>(a.v) + (p * a.T + s) * wpr, static_cast<int>(wpr), L.j);
   } else {
-    lookup<Vec>(a, load_code<CodeT>(a.qc, i), a.g0 + static_cast<uint64_t>(p), dst, L);
+    lookup<G, Vec>(a, load_code<CodeT>(a.qc, i), a.g0 + static_cast<uint64_t>(p), dst, L);
   }
 }
 
 // T > 1, phase (3): insert each partition's distinct key codes with their last row.
-template <typename CodeT, typename Vec>
+template <typename CodeT, typename Vec, int G>
 __global__ void __launch_bounds__(kThreads) exchange_insert(const Args a) {
-  const int64_t i = (static_cast<int64_t>(blockIdx.x) * kThreads + threadIdx.x) / kG;
+  const int64_t i = (static_cast<int64_t>(blockIdx.x) * kThreads + threadIdx.x) / G;
   if (i >= a.n) return;
   const int64_t p = i / a.T;
   const int64_t e = i - p * a.T;
   if (e >= a.lt_count[p]) return;  // whole groups
-  const Lane L = group_lane();
+  const Lane<G> L = group_lane<G>();
   const int64_t wpr = a.vbytes / static_cast<int64_t>(sizeof(Vec));
   const int32_t pos = a.lt_pos[i];
-  const int r = insert<Vec>(a, load_code<CodeT>(a.lt_code, i), a.g0 + static_cast<uint64_t>(p),
+  const int r = insert<G, Vec>(a, load_code<CodeT>(a.lt_code, i), a.g0 + static_cast<uint64_t>(p),
                             reinterpret_cast<const Vec*>(a.v) + (p * a.T + pos) * wpr, L);
   if (L.j == 0) {
     if (r < 0) {
@@ -306,11 +316,11 @@ WsLayout layout(int64_t n, int64_t T, int code_bytes) {
   return w;
 }
 
-template <typename CodeT, typename Vec>
+template <typename CodeT, typename Vec, int G>
 int run(Args a, int64_t T, void* ws, size_t ws_bytes, int code_bytes, cudaStream_t stream) {
-  const unsigned blocks = static_cast<unsigned>((a.n * kG + kThreads - 1) / kThreads);
+  const unsigned blocks = static_cast<unsigned>((a.n * G + kThreads - 1) / kThreads);
   if (T == 1) {
-    exchange_step<CodeT, Vec><<<blocks, kThreads, 0, stream>>>(a);
+    exchange_step<CodeT, Vec, G><<<blocks, kThreads, 0, stream>>>(a);
     LEMA_CUDA_TRY(cudaGetLastError());
     return LEMA_OK;
   }
@@ -336,9 +346,9 @@ int run(Args a, int64_t T, void* ws, size_t ws_bytes, int code_bytes, cudaStream
   a.lt_code = m.lt_code;
   a.lt_pos = m.lt_pos;
   a.lt_count = m.lt_count;
-  exchange_resolve<CodeT, Vec><<<blocks, kThreads, 0, stream>>>(a);
+  exchange_resolve<CodeT, Vec, G><<<blocks, kThreads, 0, stream>>>(a);
   LEMA_CUDA_TRY(cudaGetLastError());
-  exchange_insert<CodeT, Vec><<<blocks, kThreads, 0, stream>>>(a);
+  exchange_insert<CodeT, Vec, G><<<blocks, kThreads, 0, stream>>>(a);
   LEMA_CUDA_TRY(cudaGetLastError());
   return LEMA_OK;
 }
@@ -397,12 +407,17 @@ int store_exchange(void* table, int64_t cap, int64_t vbytes, const void* qc, con
   a.seg_groups = static_cast<uint64_t>(seg_groups);
   a.seg_slots = static_cast<uint64_t>(seg_slots);
   const bool v16 = vbytes % 16 == 0 && aligned(values, 16) && aligned(out, 16);
+  const bool wide = n <= k3::kWideMaxItems;
   if (code_bytes == 4) {
-    return v16 ? k3::run<uint32_t, uint4>(a, T, ws, ws_bytes, code_bytes, stream)
-               : k3::run<uint32_t, uint2>(a, T, ws, ws_bytes, code_bytes, stream);
+    if (v16) return wide ? k3::run<uint32_t, uint4, k3::kWideG>(a, T, ws, ws_bytes, code_bytes, stream)
+                         : k3::run<uint32_t, uint4, k3::kG>(a, T, ws, ws_bytes, code_bytes, stream);
+    return wide ? k3::run<uint32_t, uint2, k3::kWideG>(a, T, ws, ws_bytes, code_bytes, stream)
+                : k3::run<uint32_t, uint2, k3::kG>(a, T, ws, ws_bytes, code_bytes, stream);
   }
-  return v16 ? k3::run<uint64_t, uint4>(a, T, ws, ws_bytes, code_bytes, stream)
-             : k3::run<uint64_t, uint2>(a, T, ws, ws_bytes, code_bytes, stream);
+  if (v16) return wide ? k3::run<uint64_t, uint4, k3::kWideG>(a, T, ws, ws_bytes, code_bytes, stream)
+                       : k3::run<uint64_t, uint4, k3::kG>(a, T, ws, ws_bytes, code_bytes, stream);
+  return wide ? k3::run<uint64_t, uint2, k3::kWideG>(a, T, ws, ws_bytes, code_bytes, stream)
+              : k3::run<uint64_t, uint2, k3::kG>(a, T, ws, ws_bytes, code_bytes, stream);
 }
 
 }  // namespace lema
