@@ -34,6 +34,7 @@
 #include <cuda_runtime.h>
 
 #include <algorithm>
+#include <cstdlib>
 
 #include "common.cuh"
 #include "match.cuh"
@@ -407,7 +408,10 @@ int store_exchange(void* table, int64_t cap, int64_t vbytes, const void* qc, con
   a.seg_groups = static_cast<uint64_t>(seg_groups);
   a.seg_slots = static_cast<uint64_t>(seg_slots);
   const bool v16 = vbytes % 16 == 0 && aligned(values, 16) && aligned(out, 16);
-  const bool wide = n <= k3::kWideMaxItems;
+  // LEMA_K3_WIDE_MAX overrides the item count up to which 32-lane groups probe (same results)
+  int64_t wide_max = k3::kWideMaxItems;
+  if (const char* e = std::getenv("LEMA_K3_WIDE_MAX")) wide_max = std::atoll(e);
+  const bool wide = n <= wide_max;
   if (code_bytes == 4) {
     if (v16) return wide ? k3::run<uint32_t, uint4, k3::kWideG>(a, T, ws, ws_bytes, code_bytes, stream)
                          : k3::run<uint32_t, uint4, k3::kG>(a, T, ws, ws_bytes, code_bytes, stream);
