@@ -389,6 +389,62 @@ def run_b200(args):
     print(json.dumps(line), flush=True)
 
 
+def run_match(args):
+    """Config 2's streams without value rows: the index half of the op (what
+    `latest_prev_match` computes, code/lema/attention.py:100-132), through lema_prefill_match
+    with src only, on the default matcher for such calls (the dictionary + sweep matcher from
+    one wave of streams) and on the chunked matcher (LEMA_K2_SWEEP=0). Algorithmic bytes: two
+    codes in and one index out per position."""
+    import torch
+
+    from latest_exact_match_attention_b200 import _lib
+    from latest_exact_match_attention_b200._lib import call, ptr
+    dev = torch.device("cuda", int(os.environ.get("LOCAL_RANK", "0")))
+    torch.cuda.set_device(dev)
+    n = args.streams
+    qc, kc, q, k, _ = make_inputs(dev, n, 0, n)
+    src = torch.empty((n, T), dtype=torch.int32, device=dev)
+    nb = int(_lib.lib().lema_prefill_workspace_bytes(n, T, 4))
+    ws = torch.empty(max(nb, 1), dtype=torch.uint8, device=dev)
+    st = torch.zeros(1, dtype=torch.int32, device=dev)
+    stream = torch.cuda.current_stream(dev)
+    peak, peak_src = peaks()
+    res = {}
+    for name, env in (("sweep", None), ("chunked", "0")):
+        if env is None:
+            os.environ.pop("LEMA_K2_SWEEP", None)
+        else:
+            os.environ["LEMA_K2_SWEEP"] = env
+
+        def step():
+            call("lema_prefill_match", ptr(q), ptr(k), 4, n, T, ptr(src), None, 0, None, ptr(ws), nb,
+                 ptr(st), stream.cuda_stream)
+        for _ in range(max(3, args.warmup)):
+            step()
+        torch.cuda.synchronize()
+        with ClockSampler(dev.index) as clk:
+            a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            a.record(stream)
+            for _ in range(args.steps):
+                step()
+            b.record(stream)
+            torch.cuda.synchronize()
+        ms = a.elapsed_time(b) / args.steps
+        assert int(st.item()) == 0
+        alg = n * T * 12
+        res[name] = {"ms": round(ms, 4), "mpos_s": round(n * T / ms / 1e3, 1),
+                     "roofline_frac": round(alg / (ms / 1e3) / 1e9 / peak, 4), "clocks": clk.summary()}
+    os.environ.pop("LEMA_K2_SWEEP", None)
+    print(json.dumps({
+        "metric": "latest_prev_match Mpos/s (config 2 streams, indices only)", "value": res["sweep"]["mpos_s"],
+        "unit": "Mpos/s", "n_gpus": 1, "steps": args.steps, "warmup": args.warmup,
+        "higher_is_better": True, "dtype": "u32", "data": "synthetic (seeded Zipf-pool codes)",
+        "config": {"workload": f"cfg2 streams without value rows: {n} x {T}", "alg_bytes_per_call": n * T * 12,
+                   "peak_gbs": peak, "peak_source": peak_src},
+        "matchers": res, "gpu_launches": args.steps * (1 + (1 if T > 6144 else 0)),
+    }), flush=True)
+
+
 def run_proj(args):
     """K1 alone at config 3's projection shapes: B=32 x T=16384 rows of dim 1024, d_qk 32,
     hq = hk = H for H in --heads. One JSON line per H (TFLOP/s against the measured bf16 GEMM
@@ -941,7 +997,7 @@ def main():
                     help="--workload longctx: compare this many full-length heads with the oracle")
     ap.add_argument("--sweep-rows", type=int, default=0,
                     help="--workload longctx: sweep rows per head (0 = chosen automatically)")
-    ap.add_argument("--workload", choices=["prefill", "proj", "model-prefill", "decode", "longctx",
+    ap.add_argument("--workload", choices=["prefill", "match", "proj", "model-prefill", "decode", "longctx",
                                            "cpu-baselines"],
                     default="prefill",
                     help="prefill: the headline config-2 line; proj: K1 at config 3's shapes; "
@@ -967,6 +1023,8 @@ def main():
         args.warmup = 3
     if args.workload == "proj":
         run_proj(args)
+    elif args.workload == "match":
+        run_match(args)
     elif args.workload == "model-prefill":
         run_model_prefill(args)
     elif args.workload == "decode":
