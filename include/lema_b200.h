@@ -275,6 +275,26 @@ int lema_store_exchange_seg(void* table, int64_t cap, int64_t vbytes,
                             void* workspace, size_t workspace_bytes, int64_t seg_groups,
                             int64_t seg_slots, void* stream);
 
+/*
+ * lema_store_exchange_seg with strided value and output rows: partition p = b * heads + h
+ * (n / T partitions, a multiple of heads), item (p, t) reads its value row at values +
+ * b * v_sb + h * v_sh + t * v_st and writes its retrieved row at out + b * o_sb + h * o_sh +
+ * t * o_st (bytes, multiples of 8). This takes a projection's [B][T][H][d_v] output as it is
+ * and writes the [B][T][H][d_v] rows the output projection reads, with no transposing copy
+ * either side of a prefill chunk.
+ * Replaces: code/lema/csrc/store.cpp:127-162 (`exchange`) on the item-major copies that
+ * code/lema/cache.py:272-291 makes of the [B, H, T, d_v] views, and the merge of
+ * code/lema/model.py:229-232 (`Block.gpu_post`).
+ */
+int lema_store_exchange_strided(void* table, int64_t cap, int64_t vbytes,
+                                const void* qcodes, const void* kcodes, int code_bytes,
+                                const void* values, void* out, int64_t n, int64_t T,
+                                int64_t g0, int64_t* counts, uint32_t* status,
+                                void* workspace, size_t workspace_bytes, int64_t seg_groups,
+                                int64_t seg_slots, int64_t heads, int64_t v_sb, int64_t v_sh,
+                                int64_t v_st, int64_t o_sb, int64_t o_sh, int64_t o_st,
+                                void* stream);
+
 /* ----------------------------------- (d) sequence-sharded prefill (config 5) */
 /*
  * One sequence too long for one pass (or one GPU) is cut into contiguous shards of L

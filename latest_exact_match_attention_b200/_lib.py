@@ -45,6 +45,9 @@ _SIGNATURES = {
                                     _I64, _I64, _I64, _I64, _P, _SZ, _P, _P], _I),
     "lema_store_exchange_seg": ([_P, _I64, _I64, _P, _P, _I, _P, _P, _I64, _I64, _I64, _P, _P,
                                  _P, _SZ, _I64, _I64, _P], _I),
+    "lema_store_exchange_strided": ([_P, _I64, _I64, _P, _P, _I, _P, _P, _I64, _I64, _I64, _P, _P,
+                                     _P, _SZ, _I64, _I64, _I64, _I64, _I64, _I64, _I64, _I64, _I64,
+                                     _P], _I),
     "lema_segment_workspace_bytes": ([_I64, _I64, _I], _SZ),
     "lema_segment_match": ([_P, _P, _I, _I64, _I64, _P, _P, _P, _P, _P, _SZ, _P, _P], _I),
     "lema_lt_table_slots": ([_I64], _I64),

@@ -121,11 +121,14 @@ class HashStore:
         return self._ws
 
     def exchange(self, qcodes: torch.Tensor, kcodes: torch.Tensor, values: torch.Tensor,
-                 out: torch.Tensor, T: int, g0: int, check: bool = True):
+                 out: torch.Tensor, T: int, g0: int, check: bool = True, rows=None):
         """One pass of P partitions x T positions against the store: item i (partition
         i // T, position i % T, group g0 + i // T) looks `qcodes[i]` up into `out[i]` (zeros
         on a miss) and then inserts `kcodes[i] -> values[i]`, each partition in position
-        order. Device tensors: codes [n] int32/int64, values/out [n, d_v]."""
+        order. Device tensors: codes [n] int32/int64, values/out [n, d_v]. With `rows` =
+        (heads, v_sb, v_sh, v_st, o_sb, o_sh, o_st) (bytes) the value and output rows of
+        partition b * heads + h, position t are read and written at those strides instead
+        (lema_store_exchange_strided): values and out may then be any views of that layout."""
         qcodes, kcodes = qcodes.reshape(-1), kcodes.reshape(-1)
         if qcodes.dtype != kcodes.dtype:
             kcodes = kcodes.to(qcodes.dtype)
@@ -134,20 +137,27 @@ class HashStore:
         P = n // T if T else 0
         if g0 < 0 or g0 + P > self.groups:
             raise ValueError(f"groups [{g0}, {g0 + P}) outside the store's {self.groups}")
-        if values.dim() != 2 or values.shape[0] != n or out.shape != values.shape:
-            raise ValueError(f"values and out must be [n, d_v] = [{n}, {self.d_v}], got "
+        if values.numel() != n * self.d_v or out.numel() != n * self.d_v or values.shape[-1] != self.d_v:
+            raise ValueError(f"values and out must hold [n, d_v] = [{n}, {self.d_v}] rows, got "
                              f"{tuple(values.shape)} and {tuple(out.shape)}")
-        if values.element_size() * values.shape[1] != self.vbytes:
-            raise ValueError(f"value rows of {values.element_size() * values.shape[1]} bytes, "
+        if values.element_size() * values.shape[-1] != self.vbytes:
+            raise ValueError(f"value rows of {values.element_size() * values.shape[-1]} bytes, "
                              f"the store holds {self.vbytes}")
-        if not out.is_contiguous():
-            raise ValueError("out must be contiguous")
         ws = self._workspace(n, T, cb)
-        qcodes, kcodes, values = qcodes.contiguous(), kcodes.contiguous(), values.contiguous()
-        call("lema_store_exchange_seg", ptr(self.table), self.cap, self.vbytes, ptr(qcodes),
-             ptr(kcodes), cb, ptr(values), ptr(out), n, T, g0,
-             ptr(self.counts) + 8 * g0, ptr(self.status), ptr(ws), 0 if ws is None else ws.numel(),
-             self.seg_groups, self.seg_slots, stream_handle(self.device))
+        qcodes, kcodes = qcodes.contiguous(), kcodes.contiguous()
+        if rows is None:
+            if values.dim() != 2 or out.dim() != 2 or not out.is_contiguous():
+                raise ValueError("values and out must be [n, d_v] (out contiguous), or pass rows=")
+            values = values.contiguous()
+            call("lema_store_exchange_seg", ptr(self.table), self.cap, self.vbytes, ptr(qcodes),
+                 ptr(kcodes), cb, ptr(values), ptr(out), n, T, g0,
+                 ptr(self.counts) + 8 * g0, ptr(self.status), ptr(ws), 0 if ws is None else ws.numel(),
+                 self.seg_groups, self.seg_slots, stream_handle(self.device))
+        else:
+            call("lema_store_exchange_strided", ptr(self.table), self.cap, self.vbytes, ptr(qcodes),
+                 ptr(kcodes), cb, ptr(values), ptr(out), n, T, g0,
+                 ptr(self.counts) + 8 * g0, ptr(self.status), ptr(ws), 0 if ws is None else ws.numel(),
+                 self.seg_groups, self.seg_slots, *rows, stream_handle(self.device))
         if check:
             self.check()
 
@@ -180,10 +190,11 @@ class Staging:
     and the retrieved rows. Unlike the reference's pinned host buffers these need no copy
     to cross a bus; they only fix the item-major layout."""
 
-    __slots__ = ("n", "qc", "kc", "vals", "out", "T")
+    __slots__ = ("n", "qc", "kc", "vals", "out", "T", "rows")
 
-    def __init__(self, qc, kc, vals, out, T):
+    def __init__(self, qc, kc, vals, out, T, rows=None):
         self.n, self.qc, self.kc, self.vals, self.out, self.T = qc.numel(), qc, kc, vals, out, T
+        self.rows = rows  # strides of vals and out (a prefill chunk in place), or None
 
 
 class Buffers:
@@ -225,6 +236,16 @@ class LayerStore:
             qc, kc = self.buffers.codes_hook(self.g0 // self.partitions, qc, kc)
         n, d_v = qc.numel(), v.shape[-1]
         T = n // self.partitions
+        if T > 1 and not self.persistent_out and v.dim() == 4 and v.stride(-1) == 1:
+            # a prefill chunk: the values are read where the projection left them ([B, T, H,
+            # d_v] memory seen as [B, H, T, d_v]) and the retrieved rows written in the layout
+            # the output projection reads, [B, T, H, d_v]: no copy either side
+            B, H = v.shape[0], v.shape[1]
+            es = v.element_size()
+            out = torch.empty((B, T, H, d_v), dtype=v.dtype, device=v.device)
+            rows = (H, v.stride(0) * es, v.stride(1) * es, v.stride(2) * es,
+                    T * H * d_v * es, d_v * es, H * d_v * es)
+            return Staging(qc.reshape(-1).contiguous(), kc.reshape(-1).contiguous(), v, out, T, rows)
         vals = v.reshape(-1, d_v)
         if not vals.is_contiguous():
             vals = vals.contiguous()
@@ -233,11 +254,16 @@ class LayerStore:
         return Staging(qc.reshape(-1).contiguous(), kc.reshape(-1).contiguous(), vals, out, T)
 
     def host(self, s: Staging, check: bool = True):
-        self.store.exchange(s.qc, s.kc, s.vals, s.out, s.T, self.g0, check=check)
+        self.store.exchange(s.qc, s.kc, s.vals, s.out, s.T, self.g0, check=check, rows=s.rows)
+
+    @staticmethod
+    def retrieved(s: Staging, shape) -> torch.Tensor:
+        """The retrieved rows as a [B, H, T, d_v] tensor (a view of the staging output)."""
+        return s.out.transpose(1, 2) if s.rows is not None else s.out.view(shape)
 
     @staticmethod
     def fetch(s: Staging, got: torch.Tensor):
-        got.copy_(s.out.view(got.shape), non_blocking=True)
+        got.copy_(LayerStore.retrieved(s, got.shape), non_blocking=True)
 
     def exchange(self, qc: torch.Tensor, kc: torch.Tensor, v: torch.Tensor,
                  check: bool = True) -> torch.Tensor:
@@ -245,7 +271,7 @@ class LayerStore:
         `[B, H, T, d_v]` like `v`, zeros where nothing matched."""
         s = self.stage(qc, kc, v)
         self.host(s, check=check and not torch.cuda.is_current_stream_capturing())
-        return s.out.view(v.shape)
+        return self.retrieved(s, v.shape)
 
 
 class LemaCache:

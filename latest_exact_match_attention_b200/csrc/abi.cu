@@ -20,7 +20,7 @@ size_t store_workspace_bytes(int64_t n, int64_t T, int code_bytes);
 int store_exchange(void* table, int64_t cap, int64_t vbytes, const void* qc, const void* kc,
                    int code_bytes, const void* values, void* out, int64_t n, int64_t T, int64_t g0,
                    int64_t* counts, uint32_t* status, void* ws, size_t ws_bytes, cudaStream_t stream,
-                   int64_t seg_groups, int64_t seg_slots);
+                   int64_t seg_groups, int64_t seg_slots, const int64_t* rows);
 int proj_codes(const void* x, const void* w_qk, int64_t M, int64_t K, int64_t T, int hq, int hk,
                int d_qk, uint32_t* qcodes, uint32_t* kcodes, uint32_t* status, cudaStream_t stream);
 
@@ -187,7 +187,7 @@ int lema_store_exchange(void* table, int64_t cap, int64_t vbytes, const void* qc
   lema::clear_error();
   return lema::store_exchange(table, cap, vbytes, qcodes, kcodes, code_bytes, values, out, n, T, g0,
                               counts, status, workspace, workspace_bytes,
-                              static_cast<cudaStream_t>(stream), 0, 0);
+                              static_cast<cudaStream_t>(stream), 0, 0, nullptr);
 }
 
 int lema_store_exchange_seg(void* table, int64_t cap, int64_t vbytes, const void* qcodes,
@@ -197,7 +197,20 @@ int lema_store_exchange_seg(void* table, int64_t cap, int64_t vbytes, const void
   lema::clear_error();
   return lema::store_exchange(table, cap, vbytes, qcodes, kcodes, code_bytes, values, out, n, T, g0,
                               counts, status, workspace, workspace_bytes,
-                              static_cast<cudaStream_t>(stream), seg_groups, seg_slots);
+                              static_cast<cudaStream_t>(stream), seg_groups, seg_slots, nullptr);
+}
+
+int lema_store_exchange_strided(void* table, int64_t cap, int64_t vbytes, const void* qcodes,
+                                const void* kcodes, int code_bytes, const void* values, void* out,
+                                int64_t n, int64_t T, int64_t g0, int64_t* counts, uint32_t* status,
+                                void* workspace, size_t workspace_bytes, int64_t seg_groups,
+                                int64_t seg_slots, int64_t heads, int64_t v_sb, int64_t v_sh,
+                                int64_t v_st, int64_t o_sb, int64_t o_sh, int64_t o_st, void* stream) {
+  lema::clear_error();
+  const int64_t rows[7] = {heads, v_sb, v_sh, v_st, o_sb, o_sh, o_st};
+  return lema::store_exchange(table, cap, vbytes, qcodes, kcodes, code_bytes, values, out, n, T, g0,
+                              counts, status, workspace, workspace_bytes,
+                              static_cast<cudaStream_t>(stream), seg_groups, seg_slots, rows);
 }
 
 }  // extern "C"

@@ -65,7 +65,25 @@ struct Args {
   const int32_t* lt_count;
   uint64_t seg_groups;  // > 0: groups [k * seg_groups, (k + 1) * seg_groups) have their home
   uint64_t seg_slots;   //   slots in [k * seg_slots, (k + 1) * seg_slots); probing still wraps cap
+  // strided value and output rows (heads > 0): item (partition p = b * heads + h, position t)
+  // reads its value row at v + b * v_sb + h * v_sh + t * v_st and writes its output row at
+  // out + b * o_sb + h * o_sh + t * o_st (bytes); heads = 0: rows of item i at i * vbytes
+  int64_t heads, v_sb, v_sh, v_st, o_sb, o_sh, o_st;
 };
+
+__device__ __forceinline__ int64_t row_off(const Args& a, int64_t p, int64_t t, bool out) {
+  if (a.heads == 0) return (p * a.T + t) * a.vbytes;
+  const int64_t b = p / a.heads, h = p - b * a.heads;
+  return out ? b * a.o_sb + h * a.o_sh + t * a.o_st : b * a.v_sb + h * a.v_sh + t * a.v_st;
+}
+template <typename Vec>
+__device__ __forceinline__ const Vec* v_row(const Args& a, int64_t p, int64_t t) {
+  return reinterpret_cast<const Vec*>(a.v + row_off(a, p, t, false));
+}
+template <typename Vec>
+__device__ __forceinline__ Vec* out_row(const Args& a, int64_t p, int64_t t) {
+  return reinterpret_cast<Vec*>(a.out + row_off(a, p, t, true));
+}
 
 // Home slot of (group, code): a 64-bit mix mapped by multiply-high onto the whole table, or,
 // when the table is segmented, onto the group's segment. Probing continues across segment
@@ -244,8 +262,8 @@ __global__ void __launch_bounds__(kThreads) exchange_step(const Args a) {
   const Lane<G> L = group_lane<G>();
   const int64_t wpr = a.vbytes / static_cast<int64_t>(sizeof(Vec));
   const uint64_t g = a.g0 + static_cast<uint64_t>(i);
-  lookup<G, Vec>(a, load_code<CodeT>(a.qc, i), g, reinterpret_cast<Vec*>(a.out) + i * wpr, L);
-  const int r = insert<G, Vec>(a, load_code<CodeT>(a.kc, i), g, reinterpret_cast<const Vec*>(a.v) + i * wpr, L);
+  lookup<G, Vec>(a, load_code<CodeT>(a.qc, i), g, out_row<Vec>(a, i, 0), L);
+  const int r = insert<G, Vec>(a, load_code<CodeT>(a.kc, i), g, v_row<Vec>(a, i, 0), L);
   if (L.j == 0) {
     if (r < 0) {
       raise_status(a.status, LEMA_STATUS_TABLE_FULL);
@@ -263,10 +281,10 @@ __global__ void __launch_bounds__(kThreads) exchange_resolve(const Args a) {
   const Lane<G> L = group_lane<G>();
   const int64_t wpr = a.vbytes / static_cast<int64_t>(sizeof(Vec));
   const int64_t p = i / a.T;
-  Vec* dst = reinterpret_cast<Vec*>(a.out) + i * wpr;
+  Vec* dst = out_row<Vec>(a, p, i - p * a.T);
   const int32_t s = a.src[i];
   if (s >= 0) {
-    copy_row_g<G>(dst, reinterpret_cast<const Vec*>(a.v) + (p * a.T + s) * wpr, static_cast<int>(wpr), L.j);
+    copy_row_g<G>(dst, v_row<Vec>(a, p, s), static_cast<int>(wpr), L.j);
   } else {
     lookup<G, Vec>(a, load_code<CodeT>(a.qc, i), a.g0 + static_cast<uint64_t>(p), dst, L);
   }
@@ -284,7 +302,7 @@ __global__ void __launch_bounds__(kThreads) exchange_insert(const Args a) {
   const int64_t wpr = a.vbytes / static_cast<int64_t>(sizeof(Vec));
   const int32_t pos = a.lt_pos[i];
   const int r = insert<G, Vec>(a, load_code<CodeT>(a.lt_code, i), a.g0 + static_cast<uint64_t>(p),
-                            reinterpret_cast<const Vec*>(a.v) + (p * a.T + pos) * wpr, L);
+                            v_row<Vec>(a, p, pos), L);
   if (L.j == 0) {
     if (r < 0) {
       raise_status(a.status, LEMA_STATUS_TABLE_FULL);
@@ -367,7 +385,7 @@ size_t store_workspace_bytes(int64_t n, int64_t T, int code_bytes) {
 int store_exchange(void* table, int64_t cap, int64_t vbytes, const void* qc, const void* kc,
                    int code_bytes, const void* values, void* out, int64_t n, int64_t T, int64_t g0,
                    int64_t* counts, uint32_t* status, void* ws, size_t ws_bytes,
-                   cudaStream_t stream, int64_t seg_groups, int64_t seg_slots) {
+                   cudaStream_t stream, int64_t seg_groups, int64_t seg_slots, const int64_t* rows) {
   if (code_bytes != 4 && code_bytes != 8) return fail(LEMA_ERR_INVALID_ARGUMENT, "code_bytes must be 4 or 8, got %d", code_bytes);
   if (vbytes <= 0 || vbytes % 8 != 0) return fail(LEMA_ERR_INVALID_ARGUMENT, "value row of %lld bytes: vbytes must be a positive multiple of 8", (long long)vbytes);
   if (cap < 1) return fail(LEMA_ERR_INVALID_ARGUMENT, "capacity must be >= 1 slot, got %lld", (long long)cap);
@@ -386,11 +404,24 @@ int store_exchange(void* table, int64_t cap, int64_t vbytes, const void* qc, con
   const size_t need = store_workspace_bytes(n, T, code_bytes);
   if (ws_bytes < need || (need > 0 && ws == nullptr)) return fail(LEMA_ERR_WORKSPACE, "workspace of %zu bytes, %zu needed", ws_bytes, need);
   if (need > 0 && !aligned(ws, 256)) return fail(LEMA_ERR_INVALID_ARGUMENT, "workspace must be 256-byte aligned");
+  if (rows != nullptr) {
+    const int64_t heads = rows[0];
+    if (heads <= 0 || (n / T) % heads != 0)
+      return fail(LEMA_ERR_INVALID_ARGUMENT, "strided rows: %lld partitions are not whole groups of heads = %lld",
+                  (long long)(n / T), (long long)heads);
+    for (int k = 1; k < 7; ++k)
+      if (rows[k] % 8 != 0) return fail(LEMA_ERR_INVALID_ARGUMENT, "strided rows: strides must be multiples of 8 bytes");
+  }
   const DeviceInfo* dev = current_device_info();
   if (dev == nullptr) return LEMA_ERR_CUDA;
   if (dev->cc_major != 10) return fail(LEMA_ERR_UNSUPPORTED, "built for sm_100a; device is sm_%d%d", dev->cc_major, dev->cc_minor);
 
   k3::Args a{};
+  if (rows != nullptr) {
+    a.heads = rows[0];
+    a.v_sb = rows[1]; a.v_sh = rows[2]; a.v_st = rows[3];
+    a.o_sb = rows[4]; a.o_sh = rows[5]; a.o_st = rows[6];
+  }
   a.table = static_cast<unsigned char*>(table);
   a.cap = static_cast<uint64_t>(cap);
   a.rows = a.table + 16 * a.cap;
@@ -407,7 +438,8 @@ int store_exchange(void* table, int64_t cap, int64_t vbytes, const void* qc, con
   a.status = status;
   a.seg_groups = static_cast<uint64_t>(seg_groups);
   a.seg_slots = static_cast<uint64_t>(seg_slots);
-  const bool v16 = vbytes % 16 == 0 && aligned(values, 16) && aligned(out, 16);
+  const uint64_t st = rows ? static_cast<uint64_t>(rows[1] | rows[2] | rows[3] | rows[4] | rows[5] | rows[6]) : 0;
+  const bool v16 = vbytes % 16 == 0 && st % 16 == 0 && aligned(values, 16) && aligned(out, 16);
   // LEMA_K3_WIDE_MAX overrides the item count up to which 32-lane groups probe (same results)
   int64_t wide_max = k3::kWideMaxItems;
   if (const char* e = std::getenv("LEMA_K3_WIDE_MAX")) wide_max = std::atoll(e);

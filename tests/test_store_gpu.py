@@ -133,3 +133,44 @@ def test_store_vs_oracle_store_random(cuda, segments):
         np.testing.assert_array_equal(o.cpu().numpy().view(np.uint16), want)
     counts = st.counts.cpu().numpy()
     assert counts.sum() == int((tab.view(np.uint64).reshape(cap, -1)[:, 1] != 0).sum())
+
+
+@pytest.mark.parametrize("dtype,dv", [(torch.bfloat16, 24), (torch.float32, 2), (torch.float16, 16)])
+def test_strided_rows_equal_item_major(cuda, dtype, dv):
+    """lema_store_exchange_strided on [B, T, H, d_v] value memory (seen as [B, H, T, d_v]) writing
+    [B, T, H, d_v] output rows: the same store state, counts and retrieved rows as the
+    item-major exchange, over prefill chunks and then single steps."""
+    rng = np.random.default_rng(dv)
+    B, H, T0, chunk, steps = 3, 5, 96, 32, 6
+    Ttot = T0 + steps
+    qc = rng.integers(0, 60, size=(B, H, Ttot)).astype(np.uint32)
+    kc = rng.integers(0, 60, size=(B, H, Ttot)).astype(np.uint32)
+    v_bthd = torch.from_numpy(rng.standard_normal((B, Ttot, H, dv)).astype(np.float32)).to(cuda, dtype)
+    outs = []
+    for strided in (False, True):
+        st = HashStore(dv, groups=B * H, dtype=dtype, capacity=4 * B * H * Ttot, device=cuda)
+        got = torch.empty((B, H, Ttot, dv), dtype=dtype, device=cuda)
+        es = v_bthd.element_size()
+        for t0 in list(range(0, T0, chunk)) + list(range(T0, Ttot)):
+            t1 = t0 + (chunk if t0 < T0 else 1)
+            q = dev_codes(qc[:, :, t0:t1].reshape(-1), cuda)
+            k = dev_codes(kc[:, :, t0:t1].reshape(-1), cuda)
+            vv = v_bthd[:, t0:t1].transpose(1, 2)              # [B, H, t, dv] view
+            n, T = B * H * (t1 - t0), t1 - t0
+            if strided:
+                o = torch.empty((B, T, H, dv), dtype=dtype, device=cuda)
+                rows = (H, vv.stride(0) * es, vv.stride(1) * es, vv.stride(2) * es,
+                        T * H * dv * es, dv * es, H * dv * es)
+                st.exchange(q, k, vv, o, T, 0, rows=rows)
+                got[:, :, t0:t1] = o.transpose(1, 2)
+            else:
+                o = torch.empty((n, dv), dtype=dtype, device=cuda)
+                st.exchange(q, k, vv.reshape(n, dv), o, T, 0)
+                got[:, :, t0:t1] = o.view(B, H, T, dv)
+        torch.cuda.synchronize()
+        outs.append((got.cpu(), st.counts.cpu(), len(st)))
+    assert torch.equal(outs[0][0].view(torch.uint8), outs[1][0].view(torch.uint8))
+    assert torch.equal(outs[0][1], outs[1][1]) and outs[0][2] == outs[1][2]
+    dense = oracle.lema_hard(qc.reshape(B * H, Ttot), kc.reshape(B * H, Ttot),
+                             v_bthd.transpose(1, 2).reshape(B * H, Ttot, dv).contiguous().view(torch.uint8).cpu().numpy())
+    assert np.array_equal(outs[1][0].view(torch.uint8).reshape(B * H, Ttot, -1).numpy(), dense)
