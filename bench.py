@@ -301,10 +301,10 @@ def run_b200(args):
     hs = torch.empty((n_rank, T), dtype=torch.int32).pin_memory()
     h2d = hq.numel() * 4 + hk.numel() * 4 + hv.numel() * 2
     d2h = ho.numel() * 2 + hs.numel() * 4
-    # the public host-buffer call: batches of 64 streams, copies both ways overlapped with the
-    # kernels (attention.HostPrefill); one untimed call first
+    # the public host-buffer call: batches of --e2e-batch streams, copies both ways overlapped
+    # with the kernels (attention.HostPrefill); one untimed call first
     from latest_exact_match_attention_b200.attention import HostPrefill
-    hp = HostPrefill(dev, T, torch.int32, (D_V,), torch.bfloat16, batch=min(64, n_rank))
+    hp = HostPrefill(dev, T, torch.int32, (D_V,), torch.bfloat16, batch=min(args.e2e_batch, n_rank))
     if e2e_steps:
         hp(hq, hk, hv, hs, ho)
     barrier()
@@ -377,7 +377,8 @@ def run_b200(args):
                      "peak_source": peak_src, "alg_bytes_per_launch": alg_bytes,
                      "launch_ms": round(per_launch_ms, 4)},
         "e2e": {"value": e2e_value and round(e2e_value, 2), "unit": UNIT, "h2d_bytes_per_step": h2d,
-                "d2h_bytes_per_step": d2h, "steps": e2e_steps},
+                "d2h_bytes_per_step": d2h, "steps": e2e_steps,
+                "batch_streams": min(args.e2e_batch, n_rank)},
         "cpu_baseline": cpu,
         "decode": decode,
         # per step: the shared-memory match kernel (pipelined: it also copies the rows), the
@@ -989,6 +990,9 @@ def main():
     ap.add_argument("--impl", choices=["b200", "reference"], default="b200")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-e2e", action="store_true")
+    ap.add_argument("--e2e-batch", type=int, default=64,
+                    help="streams per batch of the host-buffer call (e2e): smaller batches shorten "
+                         "the copy pipeline's fill and drain")
     ap.add_argument("--streams", type=int, default=N_STREAMS,
                     help="streams per GPU (default: the workload's 512); smaller for profiling")
     ap.add_argument("--long-t", type=int, default=1 << 26, help="--workload longctx: positions")
