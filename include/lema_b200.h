@@ -295,6 +295,22 @@ int lema_store_exchange_strided(void* table, int64_t cap, int64_t vbytes,
                                 int64_t v_st, int64_t o_sb, int64_t o_sh, int64_t o_st,
                                 void* stream);
 
+/*
+ * One decode step (T = 1) of lema_store_exchange_seg in two launches: phase 1 looks every
+ * item's query up into out (qcodes, out used), phase 2 inserts every item's key and value
+ * (kcodes, values, counts used). Phase 1 then phase 2 on the same items equals phase 3 (both,
+ * what lema_store_exchange_seg does): a decode step's items are distinct partitions, so no
+ * lookup of the step depends on an insert of the step. The inserts can then run beside later
+ * work that needs only the retrieved rows, as long as they finish before the next lookups of
+ * the same groups. No workspace (T = 1).
+ * Replaces: code/lema/csrc/store.cpp:84-117 (`Table::read`, `Table::insert`) as
+ * code/lema/csrc/store.cpp:150-156 calls them per item, split into its two halves.
+ */
+int lema_store_exchange_phase(void* table, int64_t cap, int64_t vbytes, const void* qcodes,
+                              const void* kcodes, int code_bytes, const void* values, void* out,
+                              int64_t n, int64_t g0, int64_t* counts, uint32_t* status,
+                              int64_t seg_groups, int64_t seg_slots, int phase, void* stream);
+
 /* ----------------------------------- (d) sequence-sharded prefill (config 5) */
 /*
  * One sequence too long for one pass (or one GPU) is cut into contiguous shards of L

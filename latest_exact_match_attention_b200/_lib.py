@@ -45,6 +45,8 @@ _SIGNATURES = {
                                     _I64, _I64, _I64, _I64, _P, _SZ, _P, _P], _I),
     "lema_store_exchange_seg": ([_P, _I64, _I64, _P, _P, _I, _P, _P, _I64, _I64, _I64, _P, _P,
                                  _P, _SZ, _I64, _I64, _P], _I),
+    "lema_store_exchange_phase": ([_P, _I64, _I64, _P, _P, _I, _P, _P, _I64, _I64, _P, _P, _I64,
+                                   _I64, _I, _P], _I),
     "lema_store_exchange_strided": ([_P, _I64, _I64, _P, _P, _I, _P, _P, _I64, _I64, _I64, _P, _P,
                                      _P, _SZ, _I64, _I64, _I64, _I64, _I64, _I64, _I64, _I64, _I64,
                                      _P], _I),

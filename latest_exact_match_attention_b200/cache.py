@@ -161,6 +161,23 @@ class HashStore:
         if check:
             self.check()
 
+    def exchange_phase(self, qcodes: torch.Tensor, kcodes: torch.Tensor, values: torch.Tensor,
+                       out: torch.Tensor, g0: int, phase: int):
+        """Half of a decode step's exchange (T = 1, one item per partition): phase 1 looks every
+        query up into `out`, phase 2 inserts every key -> value. Phase 1 then phase 2 equals
+        `exchange(..., T=1)`; the inserts may run beside later work that needs only `out`."""
+        if phase not in (1, 2):
+            raise ValueError(f"phase must be 1 (lookups) or 2 (inserts), got {phase}")
+        codes = qcodes if phase == 1 else kcodes
+        n = codes.numel()
+        if g0 < 0 or g0 + n > self.groups:
+            raise ValueError(f"groups [{g0}, {g0 + n}) outside the store's {self.groups}")
+        call("lema_store_exchange_phase", ptr(self.table), self.cap, self.vbytes,
+             ptr(qcodes) if phase == 1 else None, ptr(kcodes) if phase == 2 else None,
+             code_bytes_of(codes), ptr(values) if phase == 2 else None,
+             ptr(out) if phase == 1 else None, n, g0, ptr(self.counts) + 8 * g0, ptr(self.status),
+             self.seg_groups, self.seg_slots, phase, stream_handle(self.device))
+
     def dump(self):
         """Every entry of the store: (groups int64 [n], codes int64 [n], rows [n, d_v] in the
         store's dtype), in slot order. Codes are the stored 64-bit words (an int32 code's bit
@@ -264,6 +281,20 @@ class LayerStore:
     @staticmethod
     def fetch(s: Staging, got: torch.Tensor):
         got.copy_(LayerStore.retrieved(s, got.shape), non_blocking=True)
+
+    def lookup(self, qc: torch.Tensor, kc: torch.Tensor, v: torch.Tensor):
+        """The first half of a decode step's exchange (one position per partition): stages the
+        step and looks every query up. Returns (staging, retrieved rows `[B, H, 1, d_v]`);
+        `insert(staging)` is the second half, which must run before this layer's next lookup."""
+        s = self.stage(qc, kc, v)
+        if s.T != 1:
+            raise ValueError(f"lookup/insert split one decode step (T = 1), got T = {s.T}")
+        self.store.exchange_phase(s.qc, s.kc, s.vals, s.out, self.g0, 1)
+        return s, self.retrieved(s, v.shape)
+
+    def insert(self, s: Staging):
+        """The second half of `lookup`'s step: every key of the step into the store."""
+        self.store.exchange_phase(s.qc, s.kc, s.vals, s.out, self.g0, 2)
 
     def exchange(self, qc: torch.Tensor, kc: torch.Tensor, v: torch.Tensor,
                  check: bool = True) -> torch.Tensor:

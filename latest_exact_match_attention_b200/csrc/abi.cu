@@ -20,7 +20,7 @@ size_t store_workspace_bytes(int64_t n, int64_t T, int code_bytes);
 int store_exchange(void* table, int64_t cap, int64_t vbytes, const void* qc, const void* kc,
                    int code_bytes, const void* values, void* out, int64_t n, int64_t T, int64_t g0,
                    int64_t* counts, uint32_t* status, void* ws, size_t ws_bytes, cudaStream_t stream,
-                   int64_t seg_groups, int64_t seg_slots, const int64_t* rows);
+                   int64_t seg_groups, int64_t seg_slots, const int64_t* rows, int phase);
 int proj_codes(const void* x, const void* w_qk, int64_t M, int64_t K, int64_t T, int hq, int hk,
                int d_qk, uint32_t* qcodes, uint32_t* kcodes, uint32_t* status, cudaStream_t stream);
 
@@ -187,7 +187,7 @@ int lema_store_exchange(void* table, int64_t cap, int64_t vbytes, const void* qc
   lema::clear_error();
   return lema::store_exchange(table, cap, vbytes, qcodes, kcodes, code_bytes, values, out, n, T, g0,
                               counts, status, workspace, workspace_bytes,
-                              static_cast<cudaStream_t>(stream), 0, 0, nullptr);
+                              static_cast<cudaStream_t>(stream), 0, 0, nullptr, 3);
 }
 
 int lema_store_exchange_seg(void* table, int64_t cap, int64_t vbytes, const void* qcodes,
@@ -197,7 +197,7 @@ int lema_store_exchange_seg(void* table, int64_t cap, int64_t vbytes, const void
   lema::clear_error();
   return lema::store_exchange(table, cap, vbytes, qcodes, kcodes, code_bytes, values, out, n, T, g0,
                               counts, status, workspace, workspace_bytes,
-                              static_cast<cudaStream_t>(stream), seg_groups, seg_slots, nullptr);
+                              static_cast<cudaStream_t>(stream), seg_groups, seg_slots, nullptr, 3);
 }
 
 int lema_store_exchange_strided(void* table, int64_t cap, int64_t vbytes, const void* qcodes,
@@ -210,7 +210,17 @@ int lema_store_exchange_strided(void* table, int64_t cap, int64_t vbytes, const 
   const int64_t rows[7] = {heads, v_sb, v_sh, v_st, o_sb, o_sh, o_st};
   return lema::store_exchange(table, cap, vbytes, qcodes, kcodes, code_bytes, values, out, n, T, g0,
                               counts, status, workspace, workspace_bytes,
-                              static_cast<cudaStream_t>(stream), seg_groups, seg_slots, rows);
+                              static_cast<cudaStream_t>(stream), seg_groups, seg_slots, rows, 3);
+}
+
+int lema_store_exchange_phase(void* table, int64_t cap, int64_t vbytes, const void* qcodes,
+                              const void* kcodes, int code_bytes, const void* values, void* out,
+                              int64_t n, int64_t g0, int64_t* counts, uint32_t* status,
+                              int64_t seg_groups, int64_t seg_slots, int phase, void* stream) {
+  lema::clear_error();
+  return lema::store_exchange(table, cap, vbytes, qcodes, kcodes, code_bytes, values, out, n, 1, g0,
+                              counts, status, nullptr, 0, static_cast<cudaStream_t>(stream), seg_groups,
+                              seg_slots, nullptr, phase);
 }
 
 }  // extern "C"

@@ -69,6 +69,7 @@ struct Args {
   // reads its value row at v + b * v_sb + h * v_sh + t * v_st and writes its output row at
   // out + b * o_sb + h * o_sh + t * o_st (bytes); heads = 0: rows of item i at i * vbytes
   int64_t heads, v_sb, v_sh, v_st, o_sb, o_sh, o_st;
+  int phase;  // T == 1: 3 = look up then insert, 1 = look up only, 2 = insert only
 };
 
 __device__ __forceinline__ int64_t row_off(const Args& a, int64_t p, int64_t t, bool out) {
@@ -262,7 +263,8 @@ __global__ void __launch_bounds__(kThreads) exchange_step(const Args a) {
   const Lane<G> L = group_lane<G>();
   const int64_t wpr = a.vbytes / static_cast<int64_t>(sizeof(Vec));
   const uint64_t g = a.g0 + static_cast<uint64_t>(i);
-  lookup<G, Vec>(a, load_code<CodeT>(a.qc, i), g, out_row<Vec>(a, i, 0), L);
+  if (a.phase & 1) lookup<G, Vec>(a, load_code<CodeT>(a.qc, i), g, out_row<Vec>(a, i, 0), L);
+  if (!(a.phase & 2)) return;
   const int r = insert<G, Vec>(a, load_code<CodeT>(a.kc, i), g, v_row<Vec>(a, i, 0), L);
   if (L.j == 0) {
     if (r < 0) {
@@ -385,7 +387,8 @@ size_t store_workspace_bytes(int64_t n, int64_t T, int code_bytes) {
 int store_exchange(void* table, int64_t cap, int64_t vbytes, const void* qc, const void* kc,
                    int code_bytes, const void* values, void* out, int64_t n, int64_t T, int64_t g0,
                    int64_t* counts, uint32_t* status, void* ws, size_t ws_bytes,
-                   cudaStream_t stream, int64_t seg_groups, int64_t seg_slots, const int64_t* rows) {
+                   cudaStream_t stream, int64_t seg_groups, int64_t seg_slots, const int64_t* rows,
+                   int phase) {
   if (code_bytes != 4 && code_bytes != 8) return fail(LEMA_ERR_INVALID_ARGUMENT, "code_bytes must be 4 or 8, got %d", code_bytes);
   if (vbytes <= 0 || vbytes % 8 != 0) return fail(LEMA_ERR_INVALID_ARGUMENT, "value row of %lld bytes: vbytes must be a positive multiple of 8", (long long)vbytes);
   if (cap < 1) return fail(LEMA_ERR_INVALID_ARGUMENT, "capacity must be >= 1 slot, got %lld", (long long)cap);
@@ -396,11 +399,20 @@ int store_exchange(void* table, int64_t cap, int64_t vbytes, const void* qc, con
   if (seg_groups > 0 && n > 0 && ((g0 + n / T - 1) / seg_groups + 1) * seg_slots > cap)
     return fail(LEMA_ERR_INVALID_ARGUMENT, "group %lld's segment lies past the table's %lld slots",
                 (long long)(g0 + n / T - 1), (long long)cap);
+  if (phase < 1 || phase > 3 || (phase != 3 && T != 1))
+    return fail(LEMA_ERR_INVALID_ARGUMENT, "phase %d: 3 (both), or 1 / 2 (lookups / inserts only, T = 1)", phase);
   if (n == 0) return LEMA_OK;
   if (table == nullptr || !aligned(table, 16)) return fail(LEMA_ERR_INVALID_ARGUMENT, "table must be a 16-byte aligned device pointer");
-  if (qc == nullptr || kc == nullptr || values == nullptr || out == nullptr || counts == nullptr) return fail(LEMA_ERR_INVALID_ARGUMENT, "null pointer argument");
+  if (counts == nullptr || ((phase & 1) && (qc == nullptr || out == nullptr)) || ((phase & 2) && (kc == nullptr || values == nullptr)))
+    return fail(LEMA_ERR_INVALID_ARGUMENT, "null pointer argument");
   if (!aligned(qc, code_bytes) || !aligned(kc, code_bytes)) return fail(LEMA_ERR_INVALID_ARGUMENT, "codes not aligned to their width");
   if (!aligned(values, 8) || !aligned(out, 8) || !aligned(counts, 8)) return fail(LEMA_ERR_INVALID_ARGUMENT, "values, out and counts must be 8-byte aligned");
+  if (phase != 3) {  // the unused side of a split step: any aligned stand-in
+    if (qc == nullptr) qc = kc;
+    if (kc == nullptr) kc = qc;
+    if (values == nullptr) values = out;
+    if (out == nullptr) out = const_cast<void*>(values);
+  }
   const size_t need = store_workspace_bytes(n, T, code_bytes);
   if (ws_bytes < need || (need > 0 && ws == nullptr)) return fail(LEMA_ERR_WORKSPACE, "workspace of %zu bytes, %zu needed", ws_bytes, need);
   if (need > 0 && !aligned(ws, 256)) return fail(LEMA_ERR_INVALID_ARGUMENT, "workspace must be 256-byte aligned");
@@ -417,6 +429,7 @@ int store_exchange(void* table, int64_t cap, int64_t vbytes, const void* qc, con
   if (dev->cc_major != 10) return fail(LEMA_ERR_UNSUPPORTED, "built for sm_100a; device is sm_%d%d", dev->cc_major, dev->cc_minor);
 
   k3::Args a{};
+  a.phase = phase;
   if (rows != nullptr) {
     a.heads = rows[0];
     a.v_sb = rows[1]; a.v_sh = rows[2]; a.v_st = rows[3];

@@ -6,7 +6,10 @@ layer copies its codes and values down, synchronises, exchanges on the CPU and c
 retrieved rows back up. Here the store is in device memory and its exchange is a kernel
 (K3), so the whole step -- embedding, every layer's codes, exchange and MLP, the head and
 the choice of the next token -- is captured once and replayed as one graph. `step()` is
-one replay: no host synchronisation, no copy across the bus.
+one replay: no host synchronisation, no copy across the bus. For small batches each layer's
+store lookups stay on the step's path and its inserts run on a side branch of the graph beside
+the layer's output projection and MLP (a decode step's items are distinct partitions, so the
+split equals the combined exchange).
 
 The captured work is exactly `Transformer.forward(tok, cache=...)`, the same segment
 functions (`Block.gpu_pre`, `Block.gpu_post`) the eager path calls, so a replay reproduces
@@ -18,6 +21,8 @@ exactly as it was; the capture itself launches nothing. A full store is reported
 the store's device status word: call `cache.check()` after stepping.
 """
 from __future__ import annotations
+
+import os
 
 import torch
 
@@ -57,14 +62,39 @@ class LemaDecoder:
             self.tok.copy_(tok)
         choose = _chooser(temperature)
         views = [cache.layer(i) for i in range(cfg.depth)]
+        side = torch.cuda.Stream(device=dev)
+        self._staged = []
+        # the split pays where the inserts are few (a small batch: measured at B = 1, worst-case
+        # codes, load 0.95: 2.31 -> 2.10 ms per token); at B = 256 the side branch's 16384 items
+        # per layer compete with the layer's GEMMs for SMs (1.66-1.76 ms combined, 1.80 split).
+        # LEMA_DECODE_SPLIT=0/1 forces either (the same tokens).
+        env = os.environ.get("LEMA_DECODE_SPLIT", "")[:1]
+        split = env == "1" or (env != "0" and B * cfg.num_heads <= 4096)
 
         def step_fn():
+            # each layer's lookups stay on the step's path; its inserts (needed only by the
+            # next step's lookups) run on a side branch beside the layer's output projection
+            # and MLP, joined at the end of the step. The staged buffers are kept referenced
+            # so that nothing later in the capture reuses memory the side branch still reads.
+            staged = []
             x = model.tok_emb(self.tok)
+            cur = torch.cuda.current_stream(dev)
             for blk, view in zip(model.blocks, views):
                 qc, kc, v = blk.gpu_pre(x)
-                x = blk.gpu_post(x, view.exchange(qc, kc, v, check=False))
+                if split:
+                    st, got = view.lookup(qc, kc, v)
+                    side.wait_stream(cur)
+                    with torch.cuda.stream(side):
+                        view.insert(st)
+                    staged.append(st)
+                else:
+                    got = view.exchange(qc, kc, v, check=False)
+                x = blk.gpu_post(x, got)
             logits = model.lm_head(rms_norm(model.norm_f, x))
             self.tok.copy_(choose(logits).view(B, 1))
+            if split:
+                cur.wait_stream(side)
+            self._staged = staged
             return logits
 
         # warm up on a scratch store (same row size and groups, room for the warm-up's keys)
