@@ -604,6 +604,12 @@ def decode_record(args, rank: int, world: int, dev, small: bool = False, worst_l
         per_part = (min(args.entries_per_partition, tokens) if args.entries_per_partition else tokens)
         load = args.max_load
     cap = math.ceil(cfg.depth * P * per_part / load)
+    from latest_exact_match_attention_b200 import _lib
+    need = cap * int(_lib.lib().lema_store_slot_bytes(cfg.d_v * 2))
+    free = torch.cuda.mem_get_info(dev)[0]
+    if need > 0.9 * free - (4 << 30):
+        raise SystemExit(f"decode store of {cap} slots ({need / 2**30:.1f} GiB) does not fit the "
+                         f"{free / 2**30:.1f} GiB free; lower --entries-per-partition or --decode-batch")
     hook = worst_case_codes(cfg.depth) if worst_load is not None else None
     cache = model.new_cache("hbm", capacity=cap, batch=Bd, codes_hook=hook)
     stream = torch.cuda.current_stream(dev)
@@ -1009,9 +1015,11 @@ def main():
     ap.add_argument("--decode-batch", type=int, default=256, help="--workload decode: batch")
     ap.add_argument("--prefix", type=int, default=16384, help="--workload decode: prefix tokens")
     ap.add_argument("--chunk", type=int, default=1024, help="--workload decode: prefill chunk")
-    ap.add_argument("--entries-per-partition", type=int, default=0,
-                    help="--workload decode: store sizing (0 = worst case, one entry per token)")
-    ap.add_argument("--max-load", type=float, default=0.8, help="--workload decode: table load")
+    ap.add_argument("--entries-per-partition", type=int, default=4300,
+                    help="--workload decode: store sizing, entries per (layer, sequence, head) "
+                         "(the Zipf prefix of 16384 tokens leaves <= 3200; 0 = one per token)")
+    ap.add_argument("--max-load", type=float, default=0.9,
+                    help="--workload decode: table load at --entries-per-partition entries")
     ap.add_argument("--worst-case", action="store_true",
                     help="--workload decode: worst-case codes at store loads 0.5 / 0.9 / 0.95")
     ap.add_argument("--worst-batch", type=int, default=1, help="--workload decode --worst-case: batch")

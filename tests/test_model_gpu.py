@@ -77,8 +77,12 @@ def test_bf16_block_store_equals_dense(cuda):
     cache.check()
 
 
+@pytest.mark.parametrize("split", ["0", "1"])
 @pytest.mark.parametrize("temperature", [0.0, 0.8])
-def test_graph_decoder_reproduces_eager(cuda, temperature):
+def test_graph_decoder_reproduces_eager(cuda, temperature, split, monkeypatch):
+    # split=1: each layer's store lookups on the step's path, its inserts on a side branch of
+    # the graph; split=0: one combined exchange per layer. Both give the eager tokens.
+    monkeypatch.setenv("LEMA_DECODE_SPLIT", split)
     m = bf16_model(cuda)
     prompt = torch.randint(0, 60, (4, 16), device=cuda)
     # eager
