@@ -275,6 +275,122 @@ __global__ void __launch_bounds__(kThreads) exchange_step(const Args a) {
   }
 }
 
+// T == 1, both phases with the two probes interleaved: the lookup (query code) and the insert
+// (key code) walk independent probe sequences, so each round trip reads the next window of
+// both, and a lookup hit away from home loads its row before the insert's claim is issued.
+// Same results as exchange_step: the lookup's decisions rest on headers read before this
+// item's claim, and where both probes reach the same slot (query code == key code) each lane
+// reads the old row word before it writes the new one.
+template <typename CodeT, typename Vec, int G>
+__global__ void __launch_bounds__(kThreads, 4) exchange_both(const Args a) {
+  const int64_t i = (static_cast<int64_t>(blockIdx.x) * kThreads + threadIdx.x) / G;
+  if (i >= a.n) return;  // whole groups
+  const Lane<G> L = group_lane<G>();
+  const int wpr = static_cast<int>(a.vbytes / static_cast<int64_t>(sizeof(Vec)));
+  const uint64_t g = a.g0 + static_cast<uint64_t>(i);
+  const uint64_t tag = g + 2;
+  const uint64_t qcode = load_code<CodeT>(a.qc, i), kcode = load_code<CodeT>(a.kc, i);
+  Vec* dst = out_row<Vec>(a, i, 0);
+  const Vec* src = v_row<Vec>(a, i, 0);
+  uint64_t sq = home(qcode, g, a), sk = home(kcode, g, a);
+  uint64_t tq = 0, tk = 0;
+  const bool one = wpr <= G;  // one vector word per lane at most
+  Vec spec = zero_vec<Vec>(), mine_row = zero_vec<Vec>();
+  if (one && L.j < wpr) {
+    spec = row_of<const Vec>(a, sq)[L.j];
+    mine_row = src[L.j];
+  }
+  bool qdone = false;
+  int kres = 2;  // 2: probing; then 1 claimed, 0 overwritten, -1 full
+  while (!qdone || kres == 2) {
+    uint64_t qcd = 0, qst = 0, kcd = 0, kst = 0;
+    if (!qdone) read_header(a, wrap_add(sq, L.j, a.cap), qcd, qst);
+    if (kres == 2) read_header(a, wrap_add(sk, L.j, a.cap), kcd, kst);
+    bool deferred = false;
+    Vec got = zero_vec<Vec>();
+    if (!qdone) {
+      const bool valid = tq + L.j < a.cap;
+      const unsigned hit = L.bits(__ballot_sync(L.gmask, valid && qst == tag && qcd == qcode));
+      const unsigned emp = L.bits(__ballot_sync(L.gmask, valid && qst == kEmpty));
+      const unsigned stop = hit | emp;
+      if (stop) {
+        const int k = __ffs(stop) - 1;
+        qdone = true;
+        if ((hit >> k) & 1u) {
+          if (tq == 0 && k == 0 && one) {
+            got = spec;
+            deferred = true;
+          } else if (one) {
+            if (L.j < wpr) got = row_of<const Vec>(a, wrap_add(sq, k, a.cap))[L.j];
+            deferred = true;
+          } else {
+            copy_row_g<G>(dst, row_of<const Vec>(a, wrap_add(sq, k, a.cap)), wpr, L.j);
+          }
+        } else {
+          zero_row_g<G>(dst, wpr, L.j);
+        }
+      } else {
+        sq = wrap_add(sq, G, a.cap);
+        tq += G;
+        if (tq >= a.cap) {
+          zero_row_g<G>(dst, wpr, L.j);
+          qdone = true;
+        }
+      }
+    }
+    if (kres == 2) {
+      const bool valid = tk + L.j < a.cap;
+      const unsigned mine = L.bits(__ballot_sync(L.gmask, valid && kst == tag && kcd == kcode));
+      const unsigned emp = L.bits(__ballot_sync(L.gmask, valid && kst == kEmpty));
+      const unsigned stop = mine | emp;
+      if (stop) {
+        const int k = __ffs(stop) - 1;
+        const uint64_t slot = wrap_add(sk, k, a.cap);
+        if ((mine >> k) & 1u) {
+          if (one) {
+            if (L.j < wpr) row_of<Vec>(a, slot)[L.j] = mine_row;
+          } else {
+            copy_row_g<G>(row_of<Vec>(a, slot), src, wpr, L.j);
+          }
+          kres = 0;
+        } else {
+          uint64_t* hdr = header(a, slot);
+          int won = 0;
+          if (L.j == k) won = atomicCAS(reinterpret_cast<unsigned long long*>(hdr + 1), kEmpty, kLocked) == kEmpty;
+          won = __shfl_sync(L.gmask, won, L.gbase + k);
+          if (won) {
+            if (L.j == k) hdr[0] = kcode;
+            if (one) {
+              if (L.j < wpr) row_of<Vec>(a, slot)[L.j] = mine_row;
+            } else {
+              copy_row_g<G>(row_of<Vec>(a, slot), src, wpr, L.j);
+            }
+            __syncwarp(L.gmask);
+            if (L.j == k) st_release(hdr + 1, tag);
+            kres = 1;
+          } else {
+            sk = wrap_add(slot, 1, a.cap);
+            tk += static_cast<uint64_t>(k) + 1;
+            if (tk >= a.cap) kres = -1;
+          }
+        }
+      } else {
+        sk = wrap_add(sk, G, a.cap);
+        tk += G;
+        if (tk >= a.cap) kres = -1;
+      }
+    }
+    if (deferred && L.j < wpr) dst[L.j] = got;
+  }
+  if (L.j == 0) {
+    if (kres < 0) {
+      raise_status(a.status, LEMA_STATUS_TABLE_FULL);
+    } else if (kres > 0) {
+      atomicAdd(reinterpret_cast<unsigned long long*>(a.counts + i), 1ull);
+    }
+  }
+}
+
 // T > 1, phase (2): in-chunk match or store lookup. G lanes per item.
 template <typename CodeT, typename Vec, int G>
 __global__ void __launch_bounds__(kThreads) exchange_resolve(const Args a) {
@@ -337,11 +453,21 @@ WsLayout layout(int64_t n, int64_t T, int code_bytes) {
   return w;
 }
 
+// LEMA_K3_INTERLEAVE=0 runs a decode step's lookup and insert probes one after the other
+// (exchange_step) instead of interleaved (exchange_both); the same results either way.
+inline bool interleave() {
+  const char* e = std::getenv("LEMA_K3_INTERLEAVE");
+  return e == nullptr || e[0] != '0';
+}
+
 template <typename CodeT, typename Vec, int G>
 int run(Args a, int64_t T, void* ws, size_t ws_bytes, int code_bytes, cudaStream_t stream) {
   const unsigned blocks = static_cast<unsigned>((a.n * G + kThreads - 1) / kThreads);
   if (T == 1) {
-    exchange_step<CodeT, Vec, G><<<blocks, kThreads, 0, stream>>>(a);
+    if (a.phase == 3 && interleave())
+      exchange_both<CodeT, Vec, G><<<blocks, kThreads, 0, stream>>>(a);
+    else
+      exchange_step<CodeT, Vec, G><<<blocks, kThreads, 0, stream>>>(a);
     LEMA_CUDA_TRY(cudaGetLastError());
     return LEMA_OK;
   }
@@ -372,6 +498,13 @@ int run(Args a, int64_t T, void* ws, size_t ws_bytes, int code_bytes, cudaStream
   exchange_insert<CodeT, Vec, G><<<blocks, kThreads, 0, stream>>>(a);
   LEMA_CUDA_TRY(cudaGetLastError());
   return LEMA_OK;
+}
+
+template <typename CodeT, typename Vec>
+int run_g(int G, const Args& a, int64_t T, void* ws, size_t ws_bytes, int code_bytes, cudaStream_t stream) {
+  if (G == 32) return run<CodeT, Vec, 32>(a, T, ws, ws_bytes, code_bytes, stream);
+  if (G == 16) return run<CodeT, Vec, 16>(a, T, ws, ws_bytes, code_bytes, stream);
+  return run<CodeT, Vec, 8>(a, T, ws, ws_bytes, code_bytes, stream);
 }
 
 }  // namespace k3
@@ -456,17 +589,18 @@ int store_exchange(void* table, int64_t cap, int64_t vbytes, const void* qc, con
   // LEMA_K3_WIDE_MAX overrides the item count up to which 32-lane groups probe (same results)
   int64_t wide_max = k3::kWideMaxItems;
   if (const char* e = std::getenv("LEMA_K3_WIDE_MAX")) wide_max = std::atoll(e);
-  const bool wide = n <= wide_max;
-  if (code_bytes == 4) {
-    if (v16) return wide ? k3::run<uint32_t, uint4, k3::kWideG>(a, T, ws, ws_bytes, code_bytes, stream)
-                         : k3::run<uint32_t, uint4, k3::kG>(a, T, ws, ws_bytes, code_bytes, stream);
-    return wide ? k3::run<uint32_t, uint2, k3::kWideG>(a, T, ws, ws_bytes, code_bytes, stream)
-                : k3::run<uint32_t, uint2, k3::kG>(a, T, ws, ws_bytes, code_bytes, stream);
+  int G = n <= wide_max ? k3::kWideG : k3::kG;
+  // LEMA_K3_GROUP=8/16/32 sets the lanes per item for every call (same results)
+  if (const char* e = std::getenv("LEMA_K3_GROUP")) {
+    const int g = std::atoi(e);
+    if (g == 8 || g == 16 || g == 32) G = g;
   }
-  if (v16) return wide ? k3::run<uint64_t, uint4, k3::kWideG>(a, T, ws, ws_bytes, code_bytes, stream)
-                       : k3::run<uint64_t, uint4, k3::kG>(a, T, ws, ws_bytes, code_bytes, stream);
-  return wide ? k3::run<uint64_t, uint2, k3::kWideG>(a, T, ws, ws_bytes, code_bytes, stream)
-              : k3::run<uint64_t, uint2, k3::kG>(a, T, ws, ws_bytes, code_bytes, stream);
+  if (code_bytes == 4) {
+    if (v16) return k3::run_g<uint32_t, uint4>(G, a, T, ws, ws_bytes, code_bytes, stream);
+    return k3::run_g<uint32_t, uint2>(G, a, T, ws, ws_bytes, code_bytes, stream);
+  }
+  if (v16) return k3::run_g<uint64_t, uint4>(G, a, T, ws, ws_bytes, code_bytes, stream);
+  return k3::run_g<uint64_t, uint2>(G, a, T, ws, ws_bytes, code_bytes, stream);
 }
 
 }  // namespace lema

@@ -135,6 +135,39 @@ def test_store_vs_oracle_store_random(cuda, segments):
     assert counts.sum() == int((tab.view(np.uint64).reshape(cap, -1)[:, 1] != 0).sum())
 
 
+@pytest.mark.parametrize("dv", [8, 64])
+@pytest.mark.parametrize("group", ["8", "16", "32"])
+@pytest.mark.parametrize("interleave", ["0", "1"])
+def test_decode_steps_every_probe_mode(cuda, monkeypatch, interleave, group, dv):
+    """Decode-sized exchanges (T = 1) in every probe mode -- lookup and insert probes one after
+    the other or interleaved, 8 / 16 / 32 lanes per item -- against the oracle store, call by
+    call: a small code space on a tight table (hits at home and down the chain, long chains,
+    lost claims), a third of the items with query code == key code (both probes on the same
+    slots: the lookup must return the row from before the step's own write), and rows of one
+    (dv 8, fp16) or several (dv 64, fp32) 16-byte words per lane."""
+    monkeypatch.setenv("LEMA_K3_INTERLEAVE", interleave)
+    monkeypatch.setenv("LEMA_K3_GROUP", group)
+    rng = np.random.default_rng(int(group) + 100 * int(interleave) + dv)
+    P, cap = 400, 4000
+    dtype, u = (torch.float16, np.uint16) if dv == 8 else (torch.float32, np.uint32)
+    tab = oracle.new_table(cap, dv * np.dtype(u).itemsize)
+    st = HashStore(dv, groups=P, dtype=dtype, capacity=cap, device=cuda)
+    for step in range(12):
+        qc = rng.integers(0, 12, size=(P, 1)).astype(np.int64)
+        kc = rng.integers(0, 12, size=(P, 1)).astype(np.int64)
+        same = rng.random(P) < 0.33
+        kc[same, 0] = qc[same, 0]
+        v = rng.integers(0, 1 << 16, size=(P, dv)).astype(u)
+        want, added, full = oracle.store_exchange(tab, qc, kc, v, 1, 0)
+        assert not full
+        vd = torch.from_numpy(v.view(np.float16 if dv == 8 else np.float32)).to(cuda)
+        o = torch.empty_like(vd)
+        st.exchange(dev_codes(qc.reshape(-1), cuda), dev_codes(kc.reshape(-1), cuda), vd, o, 1, 0)
+        np.testing.assert_array_equal(o.cpu().numpy().view(u), want)
+    counts = st.counts.cpu().numpy()
+    assert counts.sum() == int((tab.view(np.uint64).reshape(cap, -1)[:, 1] != 0).sum())
+
+
 @pytest.mark.parametrize("dtype,dv", [(torch.bfloat16, 24), (torch.float32, 2), (torch.float16, 16)])
 def test_strided_rows_equal_item_major(cuda, dtype, dv):
     """lema_store_exchange_strided on [B, T, H, d_v] value memory (seen as [B, H, T, d_v]) writing
