@@ -38,6 +38,7 @@
 // kOverflowFrac is handed over whole to the same kernel running with a CTA-private table in
 // global memory sized for 2*T (the overflow path). No input can make the result wrong; an
 // unusual one only takes the slower path.
+#include <cooperative_groups.h>
 #include <cuda_runtime.h>
 
 #include <algorithm>
@@ -559,8 +560,57 @@ __device__ void pipe_gather(const Params& p, int tid, uint4* buf, uint32_t rows_
   }
 }
 
-template <typename CodeT, bool kSmemTable, bool kPipe = false>
+// Segmented mode, after a CTA's run of chunks [r_lo, r_hi) of stream n: a cluster barrier
+// (every run's table complete), then, unless some run of the stream overflowed its table
+// (the stream then goes once to the overflow path, which redoes it whole), every position of
+// this run still at -1 looks its query code up in the tables of the earlier runs, newest
+// first; a second cluster barrier keeps every table intact until the last remote read.
+template <typename CodeT, typename Tab>
+__device__ void seg_resolve(const Params& p, const Tab& tab, int64_t n, int64_t r_lo, int64_t r_hi,
+                            uint32_t rank, uint32_t count, int tid, uint32_t* s_abort) {
+  const cooperative_groups::cluster_group cl = cooperative_groups::this_cluster();
+  cl.sync();
+  bool any = false;
+  for (uint32_t k = 0; k < count; ++k) any |= *cl.map_shared_rank(s_abort, k) != 0u;
+  if (any) {
+    if (rank == 0 && tid == 0 && p.ovf_list != nullptr) {
+      const uint32_t k = atomicAdd(p.ovf_count, 1u);
+      p.ovf_list[k] = static_cast<uint32_t>(n);
+    }
+  } else if (rank > 0) {  // (rank 0's run starts the stream: nothing earlier to look up)
+    const CodeT* qc = static_cast<const CodeT*>(p.qc) + n * p.T;
+    int32_t* src = p.src + n * p.T;
+    const int64_t lo = r_lo * kChunk, hi = std::min<int64_t>(p.T, r_hi * kChunk);
+    for (int64_t i = lo + tid; i < hi; i += kThreads) {
+      if (src[i] != -1) continue;
+      const CodeT c = qc[i];
+      for (int k = static_cast<int>(rank) - 1; k >= 0; --k) {
+        Tab rt = tab;  // run k's table, through distributed shared memory
+        rt.code = cl.map_shared_rank(tab.code, k);
+        rt.carry = cl.map_shared_rank(tab.carry, k);
+        rt.side = cl.map_shared_rank(tab.side, k);
+        const uint32_t sl = rt.find_fast(c);
+        if (sl == kNoSlot) continue;
+        const uint32_t m = rt.carry[sl];
+        if (m != 0u) {
+          src[i] = static_cast<int32_t>(m) - 1;
+          break;
+        }
+      }
+    }
+  }
+  cl.sync();
+}
+
+// kSeg: segmented mode (launched in clusters of S CTAs, S = the cluster size). The S CTAs of a
+// cluster share one stream: CTA k matches the k-th run of whole chunks with its own shared-
+// memory table, then, after a cluster barrier, resolves its positions that found no earlier
+// key inside its run against the tables of runs k - 1, ..., 0 (newest first, read through
+// distributed shared memory): a table's carry is 1 + the latest key position of that run.
+// That is the latest earlier key over the whole stream, as one CTA walking every chunk finds.
+template <typename CodeT, bool kSmemTable, bool kPipe = false, bool kSeg = false>
 __global__ void __launch_bounds__(kThreads, 2) match_kernel(const Params p) {
+  static_assert(!kSeg || (kSmemTable && !kPipe), "segments: shared-memory tables, two-kernel path");
   using Tab = Table<CodeT, uint32_t>;
   extern __shared__ __align__(16) unsigned char smem[];
   constexpr uint32_t kCap = SmemCap<CodeT>::kSlots;
@@ -570,8 +620,19 @@ __global__ void __launch_bounds__(kThreads, 2) match_kernel(const Params p) {
   __shared__ uint32_t s_ovf, s_lt;
   __shared__ uint32_t s_used[2];  // slots claimed in the stream before chunk r: s_used[r & 1]
   __shared__ uint32_t s_claim;
+  __shared__ uint32_t s_abort;  // segmented mode: this CTA's run overflowed its table
 
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  // segmented mode: this CTA's rank in its cluster, the cluster's index and count
+  uint32_t seg_rank = 0, seg_count = 1;
+  int64_t seg_first = blockIdx.x, seg_stride = gridDim.x;
+  if constexpr (kSeg) {
+    const cooperative_groups::cluster_group cl = cooperative_groups::this_cluster();
+    seg_rank = cl.block_rank();
+    seg_count = cl.num_blocks();
+    seg_first = blockIdx.x / seg_count;
+    seg_stride = gridDim.x / seg_count;
+  }
   const CodeT* qc = static_cast<const CodeT*>(p.qc);
   const CodeT* kc = static_cast<const CodeT*>(p.kc);
 
@@ -602,8 +663,13 @@ __global__ void __launch_bounds__(kThreads, 2) match_kernel(const Params p) {
     }
   }
 
-  for (int64_t wi = kPipe ? claim() : static_cast<int64_t>(blockIdx.x); wi < n_work;
-       wi = kPipe ? claim() : wi + gridDim.x) {
+  // segmented mode: this CTA's run of chunks [r_lo, r_hi)
+  const int64_t seg_chunks = (n_chunks + seg_count - 1) / seg_count;
+  const int64_t r_lo = kSeg ? std::min<int64_t>(n_chunks, seg_rank * seg_chunks) : 0;
+  const int64_t r_hi = kSeg ? std::min<int64_t>(n_chunks, r_lo + seg_chunks) : n_chunks;
+
+  for (int64_t wi = kPipe ? claim() : seg_first; wi < n_work;
+       wi = kPipe ? claim() : wi + seg_stride) {
     const int64_t n = (!kSmemTable && p.list_mode) ? static_cast<int64_t>(p.ovf_list[wi]) : wi;
     const int64_t row0 = n * p.T;
     tab.clear(tid, kThreads);
@@ -611,12 +677,12 @@ __global__ void __launch_bounds__(kThreads, 2) match_kernel(const Params p) {
     if (tid == 0) {
       s_ovf = 0;
       s_lt = 0;
-      s_used[0] = 0;
+      s_used[r_lo & 1] = 0;
     }
     __syncthreads();
 
     bool aborted = false;
-    for (int64_t r = 0; r < n_chunks; ++r) {
+    for (int64_t r = r_lo; r < r_hi; ++r) {
       {
         // ==================================================== chunk r
         const int64_t base = r * kChunk;
@@ -728,6 +794,11 @@ __global__ void __launch_bounds__(kThreads, 2) match_kernel(const Params p) {
       }
     }
 
+    if constexpr (kSeg) {
+      if (tid == 0) s_abort = aborted ? 1u : 0u;
+      seg_resolve<CodeT>(p, tab, n, r_lo, r_hi, seg_rank, seg_count, tid, &s_abort);
+      continue;
+    }
     if (aborted) {
       if (tid == 0) {
         if (kSmemTable) {
@@ -1357,6 +1428,27 @@ int run_sweep(const MatchLaunch& a, const Plan& pl, const DeviceInfo& dev, Param
   return LEMA_OK;
 }
 
+// Segments per stream for the two-kernel path: calls of fewer streams than SMs split each
+// stream's chunks over a cluster of S CTAs (S = 2, 4 or 8: the most that keeps one CTA per SM,
+// with runs of at least 2 chunks), so the chain of chunks each CTA walks is S times shorter.
+// Measured on config 2's streams (T = 16384, rows gathered): 64 streams 0.084 -> 0.066 ms
+// (S = 2 or 4); at 128 and 256 streams two CTAs per SM gain nothing (the matcher is then
+// bound by its instruction issue, not its chain): 0.108 / 0.110 ms (S = 1 / 2), 0.174 / 0.202.
+// Not for calls that export last-occurrence tables. LEMA_K2_SEGMENTS=1/2/4/8 overrides (the
+// same results).
+int seg_count(const MatchLaunch& a, int sms) {
+  if (a.lt_count != nullptr) return 1;
+  const int64_t n_chunks = (a.T + kChunk - 1) / kChunk;
+  if (const char* e = std::getenv("LEMA_K2_SEGMENTS")) {
+    const int s = std::atoi(e);
+    if (s == 1 || s == 2 || s == 4 || s == 8) return n_chunks >= s ? s : 1;
+  }
+  int best = 1;
+  for (int s = 2; s <= 8; s *= 2)
+    if (a.N * s <= static_cast<int64_t>(sms) && n_chunks >= 2 * s) best = s;
+  return best;
+}
+
 template <typename CodeT>
 int run(const MatchLaunch& a, const Plan& pl, const DeviceInfo& dev) {
   unsigned char* ws = static_cast<unsigned char*>(a.ws);
@@ -1383,7 +1475,33 @@ int run(const MatchLaunch& a, const Plan& pl, const DeviceInfo& dev) {
   if constexpr (sizeof(CodeT) == 4) {  // 64-bit codes: the two-kernel path (no spare registers)
     if (pl.fast && use_pipe(a, pl, dev.sms)) return run_pipe<CodeT>(a, pl, dev, p);
   }
-  if (pl.fast) {
+  const int segs = pl.fast ? seg_count(a, dev.sms) : 1;
+  bool seg_done = false;
+  if (segs > 1) {
+    auto kern = match_kernel<CodeT, true, false, true>;
+    const size_t sm = smem_bytes<CodeT>(true);
+    LEMA_CUDA_TRY(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(sm)));
+    cudaLaunchConfig_t cfg{};
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeClusterDimension;
+    attr[0].val.clusterDim.x = static_cast<unsigned>(segs);
+    attr[0].val.clusterDim.y = 1;
+    attr[0].val.clusterDim.z = 1;
+    cfg.blockDim = dim3(kThreads, 1, 1);
+    cfg.dynamicSmemBytes = sm;
+    cfg.stream = a.stream;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    cfg.gridDim = dim3(static_cast<unsigned>(a.N * segs), 1, 1);
+    int clusters = 0;
+    LEMA_CUDA_TRY(cudaOccupancyMaxActiveClusters(&clusters, kern, &cfg));
+    if (clusters >= 1) {  // else: one CTA per stream
+      cfg.gridDim = dim3(static_cast<unsigned>(std::min<int64_t>(a.N, clusters) * segs), 1, 1);
+      LEMA_CUDA_TRY(cudaLaunchKernelEx(&cfg, kern, p));
+      seg_done = true;
+    }
+  }
+  if (pl.fast && !seg_done) {
     auto kern = match_kernel<CodeT, true>;
     const size_t sm = smem_bytes<CodeT>(true);
     LEMA_CUDA_TRY(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(sm)));

@@ -93,8 +93,13 @@ def test_unaligned_value_rows(cuda):
     np.testing.assert_array_equal(out.cpu().numpy(), oracle.gather(want, v.cpu().numpy()))
 
 
-def test_overflow_path_many_distinct(cuda):
-    """More distinct key codes than the shared-memory table takes: the global-table path."""
+@pytest.mark.parametrize("segs", ["1", "2", ""])
+def test_overflow_path_many_distinct(cuda, monkeypatch, segs):
+    """More distinct key codes than the shared-memory table takes: the global-table path
+    (one CTA per stream, or two segments of 8192 distinct keys each, both past the table's
+    limit; by default eight segments of 2048, which fit and are resolved across segments)."""
+    if segs:
+        monkeypatch.setenv("LEMA_K2_SEGMENTS", segs)
     rng = np.random.default_rng(21)
     T = 16384
     # 3T distinct codes: an odd multiplier is a bijection modulo 2^30
@@ -114,6 +119,32 @@ def test_overflow_path_many_distinct(cuda):
     want = oracle.latest_prev_match(qc, kc)
     np.testing.assert_array_equal(src, want)
     np.testing.assert_array_equal(out, oracle.gather(want, v))
+
+
+@pytest.mark.parametrize("segs", ["1", "2", "4", "8"])
+@pytest.mark.parametrize("width", [4, 8])
+def test_segmented_matcher(cuda, monkeypatch, segs, width):
+    """Streams split over a cluster of 1 / 2 / 4 / 8 CTAs (runs of whole chunks; with 9 chunks
+    and 8 CTAs the last runs are empty), misses resolved against the earlier runs' tables:
+    small, medium and huge code spaces, the all-ones code (kept beside the table), a stream
+    whose codes never repeat, and value rows -- against the oracle."""
+    monkeypatch.setenv("LEMA_K2_SEGMENTS", segs)
+    rng = np.random.default_rng(int(segs) * 10 + width)
+    dt = np.uint32 if width == 4 else np.uint64
+    ones = np.iinfo(dt).max
+    T = 9000
+    for space in (7, 4000, 1 << 31):
+        qc = rng.integers(0, space, size=(6, T)).astype(dt)
+        kc = rng.integers(0, space, size=(6, T)).astype(dt)
+        qc[:, ::97] = ones
+        kc[:, ::89] = ones
+        kc[5] = np.arange(T, dtype=dt) * 3 + 1        # stream 5: every key new
+        qc[5] = rng.integers(0, 3 * T, size=T).astype(dt)
+        v = rng.integers(0, 1 << 16, size=(6, T, 24), dtype=np.uint16)
+        src, out = run(qc, kc, v, cuda)
+        want = oracle.latest_prev_match(qc, kc)
+        np.testing.assert_array_equal(src, want)
+        np.testing.assert_array_equal(out, oracle.gather(want, v))
 
 
 def test_long_stream_direct_global_path(cuda):
