@@ -744,8 +744,9 @@ def run_longctx(args):
     32-bit codes (pool 2^20, Zipf 1.05, 5% fresh), 128-byte bf16 value rows, sharded by
     sequence over the torchrun ranks (one per GPU): each rank owns a contiguous slice of every
     head and the ranks exchange last-occurrence tables and value rows over NCCL
-    (latest_exact_match_attention_b200.longctx). Value: positions per second of the whole
-    sequence; time = max over ranks of CUDA-event time."""
+    (latest_exact_match_attention_b200.longctx; value rows read in place from the earlier
+    ranks' memory, or with LEMA_SHARD_PEER=0 requested and exchanged by all-to-all). Value:
+    positions per second of the whole sequence; time = max over ranks of CUDA-event time."""
     import torch
 
     from latest_exact_match_attention_b200 import synth
@@ -816,7 +817,9 @@ def run_longctx(args):
         "dtype": "u32", "data": "synthetic (device-generated, chunk-seeded)",
         "config": {"workload": f"cfg5: T={T} H={H} 32-bit codes pool 2^20 Zipf 1.05 5% fresh, d_v 64 bf16",
                    "positions_per_gpu": n // world, "seg_len": args.seg_len, "hit_rate": round(hit, 4),
-                   "parallelism": f"sequence x{world}, NCCL all-gather + all-to-all"},
+                   "parallelism": f"sequence x{world}, NCCL all-gather + " + (
+                       "all-to-all of rows" if "row_all_to_all" in phases else
+                       "rows read from peer GPUs' memory (CUDA IPC, NVLink)" if world > 1 else "none")},
         "parity_check": check,
         "phases_ms_rank0": {k: round(x, 3) for k, x in phases.items()},
         "phases_ms_max_over_ranks": {k: round(x, 3) for k, x in pmax.items()},

@@ -325,6 +325,8 @@ int lema_store_exchange_phase(void* table, int64_t cap, int64_t vbytes, const vo
  *   lema_lt_insert       + lema_lt_resolve: queries still unmatched look up the LTs of
  *                        the earlier ranks
  *   lema_shard_gather    rows from this shard or from rows fetched from earlier shards
+ *   lema_shard_gather_peer  rows from this shard or read in place from the earlier shards'
+ *                        values (peer GPUs' memory over NVLink, mapped by lema_ipc_import)
  * Hash tables: n_heads x slots uint64 words (slots a power of two, see
  * lema_lt_table_slots), ZERO-FILLED by the caller; an insert keeps the larger position.
  * Codes are 32-bit; global positions stay below 2^31 - 1.
@@ -390,6 +392,23 @@ int lema_lt_resolve_rows(const uint64_t* table, int64_t n_rows, int64_t slots, i
 int lema_shard_gather(const int32_t* src, int64_t base, const void* values,
                       const void* remote_rows, const int32_t* remote_idx, int64_t vbytes,
                       void* out, int64_t n_heads, int64_t L, uint32_t* status, void* stream);
+
+/* The same, with every earlier shard's rows read where they lie: peer_values is a HOST array
+ * of n_ranks pointers, rank k's [n_heads][L] values (k < this rank: this process's mapping of
+ * rank k's tensor, from lema_ipc_import; k = base / L: this rank's own values). All ranks
+ * share n_heads, L and vbytes; n_ranks <= 16. Plain loads only: the peers' values must stay
+ * unchanged until every rank's call has completed (the caller's collective after the call).
+ * Replaces the row request and exchange of lema_shard_gather's caller. */
+int lema_shard_gather_peer(const int32_t* src, int64_t base, const void* const* peer_values,
+                           int n_ranks, int64_t vbytes, void* out, int64_t n_heads, int64_t L,
+                           uint32_t* status, void* stream);
+
+/* CUDA IPC of a device tensor for lema_shard_gather_peer: export writes the 64-byte handle of
+ * the allocation holding ptr and ptr's offset in it; import (in another process of the same
+ * node) maps it and returns the tensor's address there; close unmaps it. */
+int lema_ipc_export(const void* ptr, void* handle, int64_t* offset);
+int lema_ipc_import(const void* handle, int64_t offset, void** ptr);
+int lema_ipc_close(void* ptr, int64_t offset);
 
 #ifdef __cplusplus
 }

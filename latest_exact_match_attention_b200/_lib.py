@@ -60,6 +60,10 @@ _SIGNATURES = {
     "lema_shard_sweep": ([_P, _I64, _I64, _P, _P, _I64, _I64, _P, _P, _P, _I64, _I64, _P, _P], _I),
     "lema_lt_resolve_rows": ([_P, _I64, _I64, _I64, _P, _P, _I64, _P], _I),
     "lema_shard_gather": ([_P, _I64, _P, _P, _P, _I64, _P, _I64, _I64, _P, _P], _I),
+    "lema_shard_gather_peer": ([_P, _I64, _P, _I, _I64, _P, _I64, _I64, _P, _P], _I),
+    "lema_ipc_export": ([_P, _P, _P], _I),
+    "lema_ipc_import": ([_P, _I64, _P], _I),
+    "lema_ipc_close": ([_P, _I64], _I),
     "lema_store_slot_bytes": ([_I64], _I64),
     "lema_store_workspace_bytes": ([_I64, _I64, _I], _SZ),
     "lema_store_exchange": ([_P, _I64, _I64, _P, _P, _I, _P, _P, _I64, _I64, _I64, _P, _P, _P,

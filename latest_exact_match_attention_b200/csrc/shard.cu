@@ -27,6 +27,7 @@
 #include <cuda_runtime.h>
 
 #include <algorithm>
+#include <cstring>
 
 #include "common.cuh"
 #include "match.cuh"
@@ -323,12 +324,17 @@ __global__ void __cluster_dims__(kClusterCtas, 1, 1) __launch_bounds__(kSweepThr
 }
 
 // ------------------------------------------------------------------ gather
+constexpr int kMaxPeers = 16;  // ranks whose values one peer gather reads
 struct GatherParams {
   const int32_t* src;  // [H][L] global positions or -1
   int64_t base, L, H;
   const unsigned char* v;       // [H][L] rows of this shard
   const unsigned char* remote;  // rows fetched from earlier shards
   const int32_t* remote_idx;    // [H][L] row of `remote` for a position before base
+  // peer mode (n_peers > 0): rank k's [H][L] values at peers[k] (this GPU's memory or a peer
+  // GPU's, mapped into this process); a position before base is read from its owner's rows
+  const unsigned char* peers[kMaxPeers];
+  int n_peers;
   unsigned char* out;
   uint32_t wpr;        // vector words per row
   uint32_t words;      // words per head = L * wpr (< 2^32)
@@ -363,6 +369,11 @@ __global__ void __launch_bounds__(kGThreads) shard_gather_kernel(const GatherPar
         const int32_t s = __ldg(src + r);
         if (s >= g.base) {
           val[u] = __ldg(v + (static_cast<int64_t>(s) - g.base) * g.wpr + col);
+        } else if (s >= 0 && g.n_peers > 0) {
+          // owner = s / L < base / L = this rank; its row h * L + (s - owner * L)
+          const uint32_t owner = static_cast<uint32_t>(s) / static_cast<uint32_t>(g.L);
+          const Vec* pv = reinterpret_cast<const Vec*>(g.peers[owner]) + h * static_cast<int64_t>(g.words);
+          val[u] = pv[(static_cast<int64_t>(s) - static_cast<int64_t>(owner) * g.L) * g.wpr + col];
         } else if (s >= 0) {
           const int32_t ri = ridx ? __ldg(ridx + r) : -1;
           if (ri >= 0)
@@ -567,6 +578,86 @@ extern "C" int lema_shard_sweep(uint64_t* table, int64_t n_heads, int64_t slots,
   k5::sweep_kernel<<<static_cast<unsigned>(n_heads * k5::kClusterCtas), k5::kSweepThreads, 0,
                      static_cast<cudaStream_t>(stream)>>>(p);
   LEMA_CUDA_TRY(cudaGetLastError());
+  return LEMA_OK;
+}
+
+extern "C" int lema_shard_gather_peer(const int32_t* src, int64_t base, const void* const* peer_values,
+                                      int n_ranks, int64_t vbytes, void* out, int64_t n_heads, int64_t L,
+                                      uint32_t* status, void* stream) {
+  clear_error();
+  if (n_heads < 0 || L <= 0 || base < 0 || vbytes <= 0 || vbytes % 2 != 0 || base % L != 0)
+    return fail(LEMA_ERR_INVALID_ARGUMENT, "bad shape (heads %lld, L %lld, base %lld) or value row of %lld bytes",
+                (long long)n_heads, (long long)L, (long long)base, (long long)vbytes);
+  const int64_t rank = base / L;
+  if (n_ranks < 1 || n_ranks > k5::kMaxPeers || rank >= n_ranks)
+    return fail(LEMA_ERR_INVALID_ARGUMENT, "rank %lld of %d ranks (at most %d)", (long long)rank, n_ranks, k5::kMaxPeers);
+  if (n_heads == 0) return LEMA_OK;
+  if (src == nullptr || peer_values == nullptr || out == nullptr) return fail(LEMA_ERR_INVALID_ARGUMENT, "null pointer argument");
+  const DeviceInfo* dev = k5::sm100();
+  if (dev == nullptr) return LEMA_ERR_UNSUPPORTED;
+  k5::GatherParams g{};
+  g.src = src;
+  g.base = base;
+  g.L = L;
+  g.H = n_heads;
+  g.out = static_cast<unsigned char*>(out);
+  g.status = status;
+  g.n_peers = static_cast<int>(rank) + 1;  // this rank and the earlier ones
+  uintptr_t a = reinterpret_cast<uintptr_t>(out) | static_cast<uintptr_t>(vbytes);
+  for (int k = 0; k < g.n_peers; ++k) {
+    if (peer_values[k] == nullptr) return fail(LEMA_ERR_INVALID_ARGUMENT, "rank %d's values: null pointer", k);
+    g.peers[k] = static_cast<const unsigned char*>(peer_values[k]);
+    a |= reinterpret_cast<uintptr_t>(peer_values[k]);
+  }
+  g.v = g.peers[rank];
+  const cudaStream_t s = static_cast<cudaStream_t>(stream);
+  if (a % 16 == 0) return k5::launch_shard_gather<uint4>(g, vbytes, s);
+  if (a % 8 == 0) return k5::launch_shard_gather<uint2>(g, vbytes, s);
+  if (a % 4 == 0) return k5::launch_shard_gather<unsigned int>(g, vbytes, s);
+  return k5::launch_shard_gather<unsigned short>(g, vbytes, s);
+}
+
+// CUDA IPC of one tensor's memory: the handle names the whole allocation holding `ptr`, so
+// the exporter also reports ptr's offset in it (allocation base from the driver).
+extern "C" int lema_ipc_export(const void* ptr, void* handle, int64_t* offset) {
+  clear_error();
+  if (ptr == nullptr || handle == nullptr || offset == nullptr) return fail(LEMA_ERR_INVALID_ARGUMENT, "null pointer argument");
+  using GetRange = int (*)(unsigned long long*, size_t*, unsigned long long);
+  static GetRange get_range = nullptr;
+  if (get_range == nullptr) {
+    void* f = nullptr;
+    cudaDriverEntryPointQueryResult q{};
+    if (cudaGetDriverEntryPoint("cuMemGetAddressRange", &f, cudaEnableDefault, &q) != cudaSuccess ||
+        q != cudaDriverEntryPointSuccess || f == nullptr)
+      return fail(LEMA_ERR_CUDA, "cuMemGetAddressRange is not available from the driver");
+    get_range = reinterpret_cast<GetRange>(f);
+  }
+  unsigned long long base = 0;
+  size_t size = 0;
+  if (get_range(&base, &size, reinterpret_cast<unsigned long long>(ptr)) != 0)
+    return fail(LEMA_ERR_INVALID_ARGUMENT, "not device memory of this process");
+  cudaIpcMemHandle_t h;
+  LEMA_CUDA_TRY(cudaIpcGetMemHandle(&h, reinterpret_cast<void*>(base)));
+  memcpy(handle, &h, sizeof(h));
+  *offset = static_cast<int64_t>(reinterpret_cast<unsigned long long>(ptr) - base);
+  return LEMA_OK;
+}
+
+extern "C" int lema_ipc_import(const void* handle, int64_t offset, void** ptr) {
+  clear_error();
+  if (handle == nullptr || ptr == nullptr || offset < 0) return fail(LEMA_ERR_INVALID_ARGUMENT, "bad argument");
+  cudaIpcMemHandle_t h;
+  memcpy(&h, handle, sizeof(h));
+  void* base = nullptr;
+  LEMA_CUDA_TRY(cudaIpcOpenMemHandle(&base, h, cudaIpcMemLazyEnablePeerAccess));
+  *ptr = static_cast<unsigned char*>(base) + offset;
+  return LEMA_OK;
+}
+
+extern "C" int lema_ipc_close(void* ptr, int64_t offset) {
+  clear_error();
+  if (ptr == nullptr || offset < 0) return fail(LEMA_ERR_INVALID_ARGUMENT, "bad argument");
+  LEMA_CUDA_TRY(cudaIpcCloseMemHandle(static_cast<unsigned char*>(ptr) - offset));
   return LEMA_OK;
 }
 

@@ -20,7 +20,12 @@ Per rank (kernels in csrc/shard.cu, K2 in csrc/prefill_match.cu):
                          by all-to-all, landing in this GPU's memory before any kernel reads
     6. gather            one kernel: own rows, fetched rows, or zeros
 
-Only step 3 and 5 talk to other ranks, and nothing waits for another rank before step 3.
+Where every rank can map every other rank's values (one node: CUDA IPC over NVLink; ranks as
+threads of one process: the same memory), steps 5 and 6 are one kernel instead: the gather
+reads an earlier shard's row where it lies, with plain loads of the peer GPU's memory, and a
+collective after it keeps every rank's values in place until the last read.
+
+Only steps 3 and 5 talk to other ranks, and nothing waits for another rank before step 3.
 The collectives go through a `Comm`: `TorchComm` (torch.distributed: NCCL on the GPU, gloo
 in the CPU tests), `ThreadComm` (ranks as threads of one process, for running the same code
 over virtual shards on one GPU), `SingleComm`. The per-rank device work goes through an ops
@@ -28,6 +33,8 @@ object (`CudaOps` here; the CPU tests plug in a restatement).
 """
 from __future__ import annotations
 
+import ctypes
+import os
 import threading
 
 import torch
@@ -42,6 +49,12 @@ __all__ = ["sharded_prefill", "emulated_sharded_prefill", "CudaOps", "TorchComm"
 # ---------------------------------------------------------------------------- comms
 class SingleComm:
     rank, world = 0, 1
+
+    def peer_values(self, t):
+        return [t.data_ptr()]
+
+    def after_peer_reads(self, device):
+        pass
 
     def all_gather(self, t):
         return [t]
@@ -59,6 +72,60 @@ class TorchComm:
         self.dist, self.group = dist, group
         self.rank = dist.get_rank(group)
         self.world = dist.get_world_size(group)
+        self._mapped: dict[int, tuple[bytes, int, int]] = {}  # rank -> (handle, offset, address)
+
+    def peer_values(self, t: torch.Tensor) -> list[int] | None:
+        """Every earlier rank's `t` mapped into this process (CUDA IPC), then this rank's own,
+        in rank order (0 for the later ranks, never read), or None on every rank when any rank
+        cannot (not NCCL, not CUDA, more than 16 ranks, a failed
+        export or import). A collective: every rank calls it."""
+        ok = t.is_cuda and self.world <= 16 and self.dist.get_backend(self.group) == "nccl"
+        if not ok:
+            return None        # the same on every rank: backend, world size and environment
+        rec = torch.zeros(80, dtype=torch.uint8)
+        handle = (ctypes.c_ubyte * 64)()
+        off = ctypes.c_int64(0)
+        if _lib.lib().lema_ipc_export(ctypes.c_void_p(t.data_ptr()), handle, ctypes.byref(off)) == 0:
+            rec[:64] = torch.tensor(list(handle), dtype=torch.uint8)
+            rec[64:72] = torch.tensor([off.value], dtype=torch.int64).view(torch.uint8)
+            rec[72] = 1
+        recs = torch.empty(self.world * 80, dtype=torch.uint8, device=t.device)
+        self.dist.all_gather_into_tensor(recs, rec.to(t.device), group=self.group)
+        recs = recs.cpu().view(self.world, 80)
+        ptrs, good = [], bool(recs[:, 72].all())
+        for r in range(self.world):
+            if r >= self.rank or not good:   # only the earlier ranks' rows are ever read
+                ptrs.append(t.data_ptr() if r == self.rank else 0)
+                continue
+            h = bytes(recs[r, :64].tolist())
+            o = int(recs[r, 64:72].view(torch.int64))
+            got = self._mapped.get(r)
+            if got is not None and got[:2] == (h, o):
+                ptrs.append(got[2])
+                continue
+            if got is not None:   # the rank's values moved since the last call: drop that map
+                _lib.lib().lema_ipc_close(ctypes.c_void_p(got[2]), got[1])
+                del self._mapped[r]
+            addr = ctypes.c_void_p(0)
+            if _lib.lib().lema_ipc_import(h, o, ctypes.byref(addr)) != 0:
+                good = False
+                ptrs.append(0)
+                continue
+            self._mapped[r] = (h, o, addr.value)
+            ptrs.append(addr.value)
+        flag = torch.tensor([1 if good else 0], dtype=torch.int32, device=t.device)
+        self.dist.all_reduce(flag, op=self.dist.ReduceOp.MIN, group=self.group)
+        return ptrs if int(flag.item()) == 1 else None
+
+    def after_peer_reads(self, device):
+        """Stream-ordered: no rank's later work on its values runs before every rank's gather."""
+        self.dist.all_reduce(torch.zeros(1, dtype=torch.int32, device=device), group=self.group)
+
+    def close(self):
+        """Unmap the other ranks' values (the maps also end with the process)."""
+        for _, o, a in self._mapped.values():
+            _lib.lib().lema_ipc_close(ctypes.c_void_p(a), o)
+        self._mapped.clear()
 
     def _counts(self, n: int, device) -> list[int]:
         c = torch.tensor([n], dtype=torch.int64, device=device)
@@ -120,6 +187,12 @@ class ThreadComm:
     def all_to_all(self, parts):
         got = self._swap(list(parts))
         return [got[r][self.rank] for r in range(self.world)]
+
+    def peer_values(self, t):
+        return self._swap(t.data_ptr())          # one process: every rank's memory as it is
+
+    def after_peer_reads(self, device):
+        self.board.barrier.wait()                # every rank's gather is enqueued (one stream)
 
 
 # ---------------------------------------------------------------------------- device ops
@@ -218,6 +291,16 @@ class CudaOps:
              ptr(out), H, L, ptr(self.status), self._stream())
         return out
 
+    def gather_peer(self, src, base, v, peers):
+        """The gather reading earlier shards' rows in place: peers[k] = rank k's values."""
+        H, L = src.shape
+        vb = v[0, 0].numel() * v.element_size()
+        out = torch.empty_like(v)
+        arr = (ctypes.c_void_p * len(peers))(*peers)
+        call("lema_shard_gather_peer", ptr(src), base, arr, len(peers), vb, ptr(out), H, L,
+             ptr(self.status), self._stream())
+        return out
+
     def check(self):
         s = int(self.status.item())
         if s:
@@ -250,6 +333,11 @@ def sharded_prefill(qc: torch.Tensor, kc: torch.Tensor, v: torch.Tensor, comm=No
         raise ValueError("the sequence must stay below 2^31 - 1 positions")
     qc, kc, v = qc.contiguous(), kc.contiguous(), v.contiguous()
     base = comm.rank * L
+    # the same decision on every rank: same comm and ops types and environment, then a
+    # collective answer; LEMA_SHARD_PEER=0 keeps the request + all-to-all path (same results)
+    peers = (comm.peer_values(v) if comm.world > 1 and hasattr(ops, "gather_peer")
+             and hasattr(comm, "peer_values") and os.environ.get("LEMA_SHARD_PEER", "1")[:1] != "0"
+             else None)
 
     # 1-2: local work, no rank waits for another
     src, ltc, ltp, ltn = ops.segment_match(qc, kc, seg_len)
@@ -264,6 +352,15 @@ def sharded_prefill(qc: torch.Tensor, kc: torch.Tensor, v: torch.Tensor, comm=No
     ops.resolve(qc, src, earlier)
     del tables, earlier
     _mark(marks, "resolve")
+
+    if peers is not None:
+        # 5-6: rows of earlier shards read in place (peer memory), own rows, zeros
+        out = ops.gather_peer(src, base, v, peers)
+        _mark(marks, "gather")
+        comm.after_peer_reads(src.device)
+        _mark(marks, "release")
+        ops.check()
+        return src, out
 
     # 5: rows at earlier shards' positions, requested once each, in groups of heads
     vflat = v.view(H * L, -1).view(torch.uint8)           # rows as bytes, for transport

@@ -30,7 +30,10 @@ BIG_POOL = synth.CodeSpec(bits=32, pool=1 << 18, alpha=1.05, fresh=0.05)
     (1, 1024, SMALL_POOL), (2, 1024, SMALL_POOL), (4, 512, SMALL_POOL),
     (3, 2048, BIG_POOL), (2, 8192, BIG_POOL),   # 8192-position segments: some overflow K2's table
 ])
-def test_sharded_equals_one_pass(cuda, n_shards, seg_len, spec):
+@pytest.mark.parametrize("peer", ["1", "0"])
+def test_sharded_equals_one_pass(cuda, monkeypatch, n_shards, seg_len, spec, peer):
+    # peer=1: earlier shards' rows read in place by the gather; 0: requested and exchanged
+    monkeypatch.setenv("LEMA_SHARD_PEER", peer)
     H = 4
     T = n_shards * seg_len * 12
     q, k, v = case(H, T, spec, seed=n_shards * 10 + seg_len)
@@ -59,8 +62,10 @@ def test_sharded_vs_oracle_small(cuda):
     assert np.array_equal(out.float().cpu().numpy(), oracle.gather(ref, vf))
 
 
+@pytest.mark.parametrize("peer", ["1", "0"])
 @pytest.mark.parametrize("kind", ["all_equal", "all_distinct", "q_is_k"])
-def test_sharded_edge_cases(cuda, kind):
+def test_sharded_edge_cases(cuda, monkeypatch, kind, peer):
+    monkeypatch.setenv("LEMA_SHARD_PEER", peer)
     H, T, n_sh, seg = 2, 4 * 1024, 4, 256
     rng = np.random.default_rng(3)
     if kind == "all_equal":
