@@ -304,7 +304,8 @@ def run_b200(args):
     # the public host-buffer call: batches of --e2e-batch streams, copies both ways overlapped
     # with the kernels (attention.HostPrefill); one untimed call first
     from latest_exact_match_attention_b200.attention import HostPrefill
-    hp = HostPrefill(dev, T, torch.int32, (D_V,), torch.bfloat16, batch=min(args.e2e_batch, n_rank))
+    hp = HostPrefill(dev, T, torch.int32, (D_V,), torch.bfloat16, batch=min(args.e2e_batch, n_rank),
+                     slots=args.e2e_slots)
     if e2e_steps:
         hp(hq, hk, hv, hs, ho)
     barrier()
@@ -378,7 +379,7 @@ def run_b200(args):
                      "launch_ms": round(per_launch_ms, 4)},
         "e2e": {"value": e2e_value and round(e2e_value, 2), "unit": UNIT, "h2d_bytes_per_step": h2d,
                 "d2h_bytes_per_step": d2h, "steps": e2e_steps,
-                "batch_streams": min(args.e2e_batch, n_rank)},
+                "batch_streams": min(args.e2e_batch, n_rank), "device_slots": args.e2e_slots},
         "cpu_baseline": cpu,
         "decode": decode,
         # per step: the shared-memory match kernel (pipelined: it also copies the rows), the
@@ -999,6 +1000,8 @@ def main():
     ap.add_argument("--impl", choices=["b200", "reference"], default="b200")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-e2e", action="store_true")
+    ap.add_argument("--e2e-slots", type=int, default=3,
+                    help="batches in flight on the device in the host-buffer call (e2e)")
     ap.add_argument("--e2e-batch", type=int, default=64,
                     help="streams per batch of the host-buffer call (e2e): smaller batches shorten "
                          "the copy pipeline's fill and drain")

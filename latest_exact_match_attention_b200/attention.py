@@ -208,23 +208,26 @@ class HostPrefill:
     through the device in batches of `batch` streams. The host->device copies of batch b+1,
     the kernels of batch b and the device->host copies of batch b-1 run at once on three CUDA
     streams, so the call costs about the slower copy direction instead of the sum of both.
-    Device buffers (two batches in flight) and the three streams are allocated once; one
-    instance serves calls of its shape. The call returns once the work is queued; the host
-    outputs are complete when the caller's current stream reaches that point."""
+    Device buffers (`slots` batches in flight, so that neither copy direction waits for the
+    other's slot) and the three streams are allocated once; one instance serves calls of its
+    shape. The call returns once the work is queued; the host outputs are complete when the
+    caller's current stream reaches that point."""
 
     def __init__(self, device, T: int, code_dtype=torch.int32, row_shape=(), row_dtype=None,
-                 batch: int = 64, want_src: bool = True):
+                 batch: int = 64, want_src: bool = True, slots: int = 3):
         self.device = torch.device(device)
         self.T, self.batch, self.want_src = T, batch, want_src
+        self.slots = max(2, int(slots))
         self.code_dtype = code_dtype
         self.cb = torch.empty((), dtype=code_dtype).element_size()
-        mk = lambda shape, dt: [torch.empty(shape, dtype=dt, device=self.device) for _ in range(2)]
+        mk = lambda shape, dt: [torch.empty(shape, dtype=dt, device=self.device) for _ in range(self.slots)]
         self.dq = mk((batch, T), code_dtype)
         self.dk = mk((batch, T), code_dtype)
-        self.dsrc = mk((batch, T), torch.int32) if want_src else [None, None]
+        none = [None] * self.slots
+        self.dsrc = mk((batch, T), torch.int32) if want_src else none
         self.has_v = row_dtype is not None
-        self.dv = mk((batch, T) + tuple(row_shape), row_dtype) if self.has_v else [None, None]
-        self.dout = mk((batch, T) + tuple(row_shape), row_dtype) if self.has_v else [None, None]
+        self.dv = mk((batch, T) + tuple(row_shape), row_dtype) if self.has_v else none
+        self.dout = mk((batch, T) + tuple(row_shape), row_dtype) if self.has_v else none
         self.vbytes = (self.dv[0][0, 0].numel() * self.dv[0].element_size()) if self.has_v else 0
         nb = int(_lib.lib().lema_prefill_workspace_bytes(batch, T, self.cb))
         self.ws = _workspace(nb, self.device)
@@ -239,11 +242,12 @@ class HostPrefill:
         for s in self.streams:
             s.wait_stream(cur)
         ev_cp, ev_out = [], []
+        S = self.slots
         for b, n0 in enumerate(range(0, N, self.batch)):
-            n, j = min(self.batch, N - n0), b % 2
+            n, j = min(self.batch, N - n0), b % S
             with torch.cuda.stream(s_in):
-                if b >= 2:
-                    s_in.wait_event(ev_cp[b - 2])        # slot j's inputs were read
+                if b >= S:
+                    s_in.wait_event(ev_cp[b - S])        # slot j's inputs were read
                 self.dq[j][:n].copy_(qc[n0:n0 + n], non_blocking=True)
                 self.dk[j][:n].copy_(kc[n0:n0 + n], non_blocking=True)
                 if self.has_v:
@@ -252,8 +256,8 @@ class HostPrefill:
                 e_in.record(s_in)
             with torch.cuda.stream(s_cp):
                 s_cp.wait_event(e_in)
-                if b >= 2:
-                    s_cp.wait_event(ev_out[b - 2])       # slot j's outputs were copied out
+                if b >= S:
+                    s_cp.wait_event(ev_out[b - S])       # slot j's outputs were copied out
                 call("lema_prefill_match", ptr(self.dq[j]), ptr(self.dk[j]), self.cb, n, self.T,
                      ptr(self.dsrc[j]), ptr(self.dv[j]), self.vbytes, ptr(self.dout[j]),
                      ptr(self.ws), 0 if self.ws is None else self.ws.numel(), ptr(status),
