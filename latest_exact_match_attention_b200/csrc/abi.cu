@@ -63,6 +63,11 @@ unsigned long long wait_limit_ns() {
   return 4000000000ull;
 }
 
+bool pdl_enabled() {
+  const char* e = std::getenv("LEMA_PDL");
+  return e == nullptr || e[0] != '0';
+}
+
 const DeviceInfo* current_device_info() {
   int dev = -1;
   cudaError_t e = cudaGetDevice(&dev);

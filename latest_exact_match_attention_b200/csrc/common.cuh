@@ -124,4 +124,36 @@ inline size_t round_up(size_t x, size_t a) { return (x + a - 1) / a * a; }
 
 namespace lema {
 __host__ __device__ constexpr size_t round_up16(size_t x) { return (x + 15) / 16 * 16; }
+
+// Programmatic dependent launch. A kernel launched by launch_dependent may start while the
+// kernel before it in the stream is finishing (its launch and CTA placement overlap that
+// kernel's tail); it calls griddep_wait() before its first global memory access, which returns
+// once the previous kernel has completed and its writes are visible. Launched the ordinary
+// way, griddep_wait() returns at once. LEMA_PDL=0 in the environment launches ordinarily.
+__device__ __forceinline__ void griddep_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+// In the kernel before it: lets the dependent kernel be placed on free SM slots once every CTA
+// of this grid has started (it still waits in griddep_wait for this grid to complete).
+__device__ __forceinline__ void griddep_launch() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
+
+bool pdl_enabled();
+
+template <typename... KArgs, typename... Args>
+cudaError_t launch_dependent(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem,
+                             cudaStream_t stream, Args... args) {
+  if (!pdl_enabled()) {
+    kernel<<<grid, block, smem, stream>>>(args...);
+    return cudaGetLastError();
+  }
+  cudaLaunchConfig_t cfg{};
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = stream;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return cudaLaunchKernelEx(&cfg, kernel, args...);
+}
 }  // namespace lema

@@ -611,6 +611,8 @@ __device__ void seg_resolve(const Params& p, const Tab& tab, int64_t n, int64_t 
 template <typename CodeT, bool kSmemTable, bool kPipe = false, bool kSeg = false>
 __global__ void __launch_bounds__(kThreads, 2) match_kernel(const Params p) {
   static_assert(!kSeg || (kSmemTable && !kPipe), "segments: shared-memory tables, two-kernel path");
+  griddep_wait();  // launched as a dependent (the overflow path): the matcher's results first
+  griddep_launch();
   using Tab = Table<CodeT, uint32_t>;
   extern __shared__ __align__(16) unsigned char smem[];
   constexpr uint32_t kCap = SmemCap<CodeT>::kSlots;
@@ -1090,6 +1092,7 @@ __device__ __forceinline__ void sweep_warp(uint32_t* ids, uint32_t T, uint32_t* 
 
 template <typename CodeT>
 __global__ void __launch_bounds__(kSwThreads, kSwPerSm) sweep_kernel(const Params p) {
+  griddep_launch();  // the overflow path may be placed once every sweep CTA runs
   using L = SweepLayout<CodeT>;
   using Tab = Table<CodeT, uint32_t>;
   extern __shared__ __align__(16) unsigned char smem[];
@@ -1165,6 +1168,7 @@ __global__ void __launch_bounds__(kSwThreads, kSwPerSm) sweep_kernel(const Param
 constexpr int kGThreads = 256;
 template <typename Vec>
 __global__ void __launch_bounds__(kGThreads) gather_kernel(const GatherParams g) {
+  griddep_wait();  // the indices of the kernels before it
   const uint32_t w0 = blockIdx.x * (kGThreads * kGUnroll) + threadIdx.x;
   for (int64_t n = blockIdx.y; n < g.N; n += gridDim.y) {
     const int32_t* src = g.src + n * g.T;
@@ -1238,8 +1242,7 @@ int launch_gather(const MatchLaunch& a, const int32_t* src) {
   const uint64_t per_cta = kGThreads * kGUnroll;
   const dim3 grid(static_cast<unsigned>((words + per_cta - 1) / per_cta),
                   static_cast<unsigned>(std::min<int64_t>(a.N, 65535)));
-  gather_kernel<Vec><<<grid, kGThreads, 0, a.stream>>>(g);
-  LEMA_CUDA_TRY(cudaGetLastError());
+  LEMA_CUDA_TRY(launch_dependent(gather_kernel<Vec>, grid, dim3(kGThreads), 0, a.stream, g));
   return LEMA_OK;
 }
 
@@ -1387,8 +1390,7 @@ int run_pipe(const MatchLaunch& a, const Plan& pl, const DeviceInfo& dev, Params
     auto gk = match_kernel<CodeT, false>;
     const size_t gsm = smem_bytes<CodeT>(false);
     LEMA_CUDA_TRY(cudaFuncSetAttribute(gk, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(gsm)));
-    gk<<<static_cast<unsigned>(pl.n_gtables), kThreads, gsm, a.stream>>>(p);
-    LEMA_CUDA_TRY(cudaGetLastError());
+    LEMA_CUDA_TRY(launch_dependent(gk, dim3(static_cast<unsigned>(pl.n_gtables)), dim3(kThreads), gsm, a.stream, p));
   }
   return LEMA_OK;
 }
@@ -1421,8 +1423,7 @@ int run_sweep(const MatchLaunch& a, const Plan& pl, const DeviceInfo& dev, Param
     auto gk = match_kernel<CodeT, false>;
     const size_t gsm = smem_bytes<CodeT>(false);
     LEMA_CUDA_TRY(cudaFuncSetAttribute(gk, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(gsm)));
-    gk<<<static_cast<unsigned>(pl.n_gtables), kThreads, gsm, a.stream>>>(p);
-    LEMA_CUDA_TRY(cudaGetLastError());
+    LEMA_CUDA_TRY(launch_dependent(gk, dim3(static_cast<unsigned>(pl.n_gtables)), dim3(kThreads), gsm, a.stream, p));
   }
   if (a.out != nullptr) return run_gather(a, p.src);
   return LEMA_OK;
@@ -1516,8 +1517,7 @@ int run(const MatchLaunch& a, const Plan& pl, const DeviceInfo& dev) {
     auto kern = match_kernel<CodeT, false>;
     const size_t sm = smem_bytes<CodeT>(false);
     LEMA_CUDA_TRY(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(sm)));
-    kern<<<static_cast<unsigned>(pl.n_gtables), kThreads, sm, a.stream>>>(p);
-    LEMA_CUDA_TRY(cudaGetLastError());
+    LEMA_CUDA_TRY(launch_dependent(kern, dim3(static_cast<unsigned>(pl.n_gtables)), dim3(kThreads), sm, a.stream, p));
   }
   if (a.out != nullptr) return run_gather(a, p.src);
   return LEMA_OK;
