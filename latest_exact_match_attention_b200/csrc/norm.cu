@@ -65,6 +65,8 @@ __device__ __forceinline__ uint4 scale8(const uint4& v, const uint4& w, float rs
 template <typename T>
 __global__ void __launch_bounds__(32 * kRowsPerBlock) rms_norm_x8_kernel(const uint4* x, const uint4* w, uint4* out,
                                                                         int64_t M, uint32_t C, float d, float eps) {
+  griddep_wait();    // launched as a dependent: the rows' producer first
+  griddep_launch();  // and the next kernel (K1 after norm1) may set itself up meanwhile
   const int lane = threadIdx.x & 31;
   const int64_t m = static_cast<int64_t>(blockIdx.x) * kRowsPerBlock + (threadIdx.x >> 5);
   if (m >= M) return;
@@ -113,13 +115,14 @@ extern "C" int lema_rms_norm(const void* x, const void* weight, int dtype, int64
   const cudaStream_t s = static_cast<cudaStream_t>(stream);
   const uint32_t C = static_cast<uint32_t>(D / 8);
   const float d = static_cast<float>(D);
+  const dim3 grid(static_cast<unsigned>(blocks)), block(32 * kRowsPerBlock);
+  const uint4* xv = static_cast<const uint4*>(x);
+  const uint4* wv = static_cast<const uint4*>(weight);
+  uint4* ov = static_cast<uint4*>(out);
   if (dtype == LEMA_BF16) {
-    rms_norm_x8_kernel<__nv_bfloat16><<<static_cast<unsigned>(blocks), 32 * kRowsPerBlock, 0, s>>>(
-        static_cast<const uint4*>(x), static_cast<const uint4*>(weight), static_cast<uint4*>(out), M, C, d, eps);
+    LEMA_CUDA_TRY(launch_dependent(rms_norm_x8_kernel<__nv_bfloat16>, grid, block, 0, s, xv, wv, ov, M, C, d, eps));
   } else {
-    rms_norm_x8_kernel<__half><<<static_cast<unsigned>(blocks), 32 * kRowsPerBlock, 0, s>>>(
-        static_cast<const uint4*>(x), static_cast<const uint4*>(weight), static_cast<uint4*>(out), M, C, d, eps);
+    LEMA_CUDA_TRY(launch_dependent(rms_norm_x8_kernel<__half>, grid, block, 0, s, xv, wv, ov, M, C, d, eps));
   }
-  LEMA_CUDA_TRY(cudaGetLastError());
   return LEMA_OK;
 }

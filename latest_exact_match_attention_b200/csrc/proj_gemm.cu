@@ -270,6 +270,9 @@ __global__ void __launch_bounds__(kThreads, 1)
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem_base = *s_tmem;
+  // launched as a dependent: the set-up above overlaps the previous kernel; its outputs (x)
+  // are read only from here on
+  griddep_wait();
 
   if (warp == 0) {
     // ------------------------------------------------------------ TMA producer
@@ -475,8 +478,8 @@ template <int BN>
 int launch(const CUtensorMap& map_x, const CUtensorMap& map_w, const Params& prm, int64_t grid, cudaStream_t stream) {
   LEMA_CUDA_TRY(cudaFuncSetAttribute(proj_codes_kernel<BN>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                      static_cast<int>(Tile<BN>::kSmemBytes)));
-  proj_codes_kernel<BN><<<static_cast<unsigned>(grid), kThreads, Tile<BN>::kSmemBytes, stream>>>(map_x, map_w, prm);
-  LEMA_CUDA_TRY(cudaGetLastError());
+  LEMA_CUDA_TRY(launch_dependent(proj_codes_kernel<BN>, dim3(static_cast<unsigned>(grid)), dim3(kThreads),
+                                 Tile<BN>::kSmemBytes, stream, map_x, map_w, prm));
   return LEMA_OK;
 }
 

@@ -258,6 +258,7 @@ __device__ __forceinline__ uint64_t load_code(const void* p, int64_t i) {
 // T == 1: item i is partition i; look up, then insert. G lanes per item.
 template <typename CodeT, typename Vec, int G>
 __global__ void __launch_bounds__(kThreads) exchange_step(const Args a) {
+  griddep_wait();  // launched as a dependent: the codes and values first
   const int64_t i = (static_cast<int64_t>(blockIdx.x) * kThreads + threadIdx.x) / G;
   if (i >= a.n) return;  // whole groups
   const Lane<G> L = group_lane<G>();
@@ -283,6 +284,7 @@ __global__ void __launch_bounds__(kThreads) exchange_step(const Args a) {
 // reads the old row word before it writes the new one.
 template <typename CodeT, typename Vec, int G>
 __global__ void __launch_bounds__(kThreads, 4) exchange_both(const Args a) {
+  griddep_wait();  // launched as a dependent: the codes and values first
   const int64_t i = (static_cast<int64_t>(blockIdx.x) * kThreads + threadIdx.x) / G;
   if (i >= a.n) return;  // whole groups
   const Lane<G> L = group_lane<G>();
@@ -394,6 +396,7 @@ __global__ void __launch_bounds__(kThreads, 4) exchange_both(const Args a) {
 // T > 1, phase (2): in-chunk match or store lookup. G lanes per item.
 template <typename CodeT, typename Vec, int G>
 __global__ void __launch_bounds__(kThreads) exchange_resolve(const Args a) {
+  griddep_wait();  // launched as a dependent: the codes and values first
   const int64_t i = (static_cast<int64_t>(blockIdx.x) * kThreads + threadIdx.x) / G;
   if (i >= a.n) return;
   const Lane<G> L = group_lane<G>();
@@ -411,6 +414,7 @@ __global__ void __launch_bounds__(kThreads) exchange_resolve(const Args a) {
 // T > 1, phase (3): insert each partition's distinct key codes with their last row.
 template <typename CodeT, typename Vec, int G>
 __global__ void __launch_bounds__(kThreads) exchange_insert(const Args a) {
+  griddep_wait();  // launched as a dependent: the codes and values first
   const int64_t i = (static_cast<int64_t>(blockIdx.x) * kThreads + threadIdx.x) / G;
   if (i >= a.n) return;
   const int64_t p = i / a.T;
@@ -465,10 +469,9 @@ int run(Args a, int64_t T, void* ws, size_t ws_bytes, int code_bytes, cudaStream
   const unsigned blocks = static_cast<unsigned>((a.n * G + kThreads - 1) / kThreads);
   if (T == 1) {
     if (a.phase == 3 && interleave())
-      exchange_both<CodeT, Vec, G><<<blocks, kThreads, 0, stream>>>(a);
+      LEMA_CUDA_TRY(launch_dependent(exchange_both<CodeT, Vec, G>, dim3(blocks), dim3(kThreads), 0, stream, a));
     else
-      exchange_step<CodeT, Vec, G><<<blocks, kThreads, 0, stream>>>(a);
-    LEMA_CUDA_TRY(cudaGetLastError());
+      LEMA_CUDA_TRY(launch_dependent(exchange_step<CodeT, Vec, G>, dim3(blocks), dim3(kThreads), 0, stream, a));
     return LEMA_OK;
   }
   const WsLayout w = layout(a.n, T, code_bytes);
@@ -493,10 +496,8 @@ int run(Args a, int64_t T, void* ws, size_t ws_bytes, int code_bytes, cudaStream
   a.lt_code = m.lt_code;
   a.lt_pos = m.lt_pos;
   a.lt_count = m.lt_count;
-  exchange_resolve<CodeT, Vec, G><<<blocks, kThreads, 0, stream>>>(a);
-  LEMA_CUDA_TRY(cudaGetLastError());
-  exchange_insert<CodeT, Vec, G><<<blocks, kThreads, 0, stream>>>(a);
-  LEMA_CUDA_TRY(cudaGetLastError());
+  LEMA_CUDA_TRY(launch_dependent(exchange_resolve<CodeT, Vec, G>, dim3(blocks), dim3(kThreads), 0, stream, a));
+  LEMA_CUDA_TRY(launch_dependent(exchange_insert<CodeT, Vec, G>, dim3(blocks), dim3(kThreads), 0, stream, a));
   return LEMA_OK;
 }
 

@@ -23,6 +23,7 @@ template <> __device__ __forceinline__ __half from_f<__half>(float v) { return _
 
 template <typename T>
 __global__ void swiglu_kernel(const T* gu, T* out, int64_t M, int64_t F) {
+  griddep_wait();  // launched as a dependent: the gate/up GEMM first
   const int64_t n = M * F;
   for (int64_t i = blockIdx.x * int64_t(blockDim.x) + threadIdx.x; i < n; i += int64_t(gridDim.x) * blockDim.x) {
     const int64_t m = i / F, f = i - m * F;
@@ -34,6 +35,7 @@ __global__ void swiglu_kernel(const T* gu, T* out, int64_t M, int64_t F) {
 
 // bf16, F % 8 == 0, 16-byte aligned: 8 outputs per thread from two 16-byte loads.
 __global__ void swiglu_bf16x8_kernel(const uint4* gu, uint4* out, uint32_t M, uint32_t F8) {
+  griddep_wait();  // launched as a dependent: the gate/up GEMM first
   const uint32_t n = M * F8;
   for (uint32_t i = blockIdx.x * blockDim.x + threadIdx.x; i < n; i += gridDim.x * blockDim.x) {
     const uint32_t m = i / F8, f = i - m * F8;
@@ -69,9 +71,9 @@ extern "C" int lema_swiglu(const void* gu, int dtype, int64_t M, int64_t F, void
   if (dtype == LEMA_BF16 && F % 8 == 0 && aligned(gu, 16) && aligned(out, 16) && M * (F / 8) < (int64_t(1) << 31)) {
     const int64_t n = M * (F / 8);
     const int64_t b8 = std::max<int64_t>(1, std::min<int64_t>((n + 255) / 256, int64_t(dev->sms) * 16));
-    swiglu_bf16x8_kernel<<<static_cast<unsigned>(b8), 256, 0, s>>>(static_cast<const uint4*>(gu), static_cast<uint4*>(out),
-                                                                   static_cast<uint32_t>(M), static_cast<uint32_t>(F / 8));
-    LEMA_CUDA_TRY(cudaGetLastError());
+    LEMA_CUDA_TRY(launch_dependent(swiglu_bf16x8_kernel, dim3(static_cast<unsigned>(b8)), dim3(256), 0, s,
+                                   static_cast<const uint4*>(gu), static_cast<uint4*>(out),
+                                   static_cast<uint32_t>(M), static_cast<uint32_t>(F / 8)));
     return LEMA_OK;
   }
   switch (dtype) {
