@@ -262,7 +262,6 @@ __global__ void __launch_bounds__(kThreads) exchange_step(const Args a) {
   const int64_t i = (static_cast<int64_t>(blockIdx.x) * kThreads + threadIdx.x) / G;
   if (i >= a.n) return;  // whole groups
   const Lane<G> L = group_lane<G>();
-  const int64_t wpr = a.vbytes / static_cast<int64_t>(sizeof(Vec));
   const uint64_t g = a.g0 + static_cast<uint64_t>(i);
   if (a.phase & 1) lookup<G, Vec>(a, load_code<CodeT>(a.qc, i), g, out_row<Vec>(a, i, 0), L);
   if (!(a.phase & 2)) return;
@@ -421,7 +420,6 @@ __global__ void __launch_bounds__(kThreads) exchange_insert(const Args a) {
   const int64_t e = i - p * a.T;
   if (e >= a.lt_count[p]) return;  // whole groups
   const Lane<G> L = group_lane<G>();
-  const int64_t wpr = a.vbytes / static_cast<int64_t>(sizeof(Vec));
   const int32_t pos = a.lt_pos[i];
   const int r = insert<G, Vec>(a, load_code<CodeT>(a.lt_code, i), a.g0 + static_cast<uint64_t>(p),
                             v_row<Vec>(a, p, pos), L);
