@@ -112,10 +112,14 @@ __device__ __forceinline__ void st_release(uint64_t* p, uint64_t v) {
 // A chain of c slots then costs about c / 8 dependent round trips instead of c: at load 0.95
 // an unsuccessful linear probe averages ~200 slots. Calls with few items (a batch-1 decode
 // step has 64 per layer) use whole warps instead (kWideG = 32 slots per round trip): the
-// lanes are there for free.
+// lanes are there for free; mid-sized calls (a batch-256 decode step: 16384 items per layer)
+// use 16 lanes, measured 3.5% faster per step than 32 (fewer waves of warps) and 8% faster
+// than 8 (fewer round trips at load 0.65).
 constexpr int kG = 8;
 constexpr int kWideG = 32;
-constexpr int64_t kWideMaxItems = 16384;  // up to this many items per call: 32-lane groups
+constexpr int kMidG = 16;
+constexpr int64_t kWideMaxItems = 4096;   // up to this many items per call: 32-lane groups
+constexpr int64_t kMidMaxItems = 16384;   // up to this many: 16-lane groups
 
 template <int G>
 struct Lane {
@@ -588,7 +592,7 @@ int store_exchange(void* table, int64_t cap, int64_t vbytes, const void* qc, con
   // LEMA_K3_WIDE_MAX overrides the item count up to which 32-lane groups probe (same results)
   int64_t wide_max = k3::kWideMaxItems;
   if (const char* e = std::getenv("LEMA_K3_WIDE_MAX")) wide_max = std::atoll(e);
-  int G = n <= wide_max ? k3::kWideG : k3::kG;
+  int G = n <= wide_max ? k3::kWideG : (n <= k3::kMidMaxItems ? k3::kMidG : k3::kG);
   // LEMA_K3_GROUP=8/16/32 sets the lanes per item for every call (same results)
   if (const char* e = std::getenv("LEMA_K3_GROUP")) {
     const int g = std::atoi(e);
