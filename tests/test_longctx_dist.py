@@ -5,8 +5,10 @@ their concatenated result must equal the oracle's single pass over the whole seq
 
 This pins the host logic: shard offsets, the last-occurrence exchange, the deduplicated row
 requests routed to their owners and the rows coming back in request order."""
+import ctypes
 import os
 import socket
+import threading
 
 import numpy as np
 import pytest
@@ -99,6 +101,28 @@ class PlainOps:
         pass
 
 
+class PeerPlainOps(PlainOps):
+    """PlainOps plus the peer gather, restated: a position before this shard is read from its
+    owner rank's [H, L, d] values (owner = s // L, row s - owner * L) through the address the
+    comm hands out -- what lema_shard_gather_peer does on the GPU (test-only)."""
+
+    @staticmethod
+    def gather_peer(src, base, v, peers):
+        H, L = src.shape
+        d = v.shape[-1]
+        n = H * L * d
+        views = [np.ctypeslib.as_array((ctypes.c_float * n).from_address(a)).reshape(H, L, d) if a else None
+                 for a in peers]
+        out = np.zeros((H, L, d), np.float32)
+        s = src.numpy()
+        for h in range(H):
+            for i in range(L):
+                if s[h, i] >= 0:
+                    owner = int(s[h, i]) // L
+                    out[h, i] = views[owner][h, int(s[h, i]) - owner * L]
+        return torch.from_numpy(out)
+
+
 def inputs(H, T):
     rng = np.random.default_rng(5)
     kc = rng.integers(0, 40, size=(H, T)).astype(np.uint32) * np.uint32(2654435761)  # wraps
@@ -107,7 +131,7 @@ def inputs(H, T):
     return qc.astype(np.uint32), kc.astype(np.uint32), v
 
 
-def _rank(rank, world, port, H, T, seg, q):
+def _rank(rank, world, port, H, T, seg, q, peer_ops=False):
     import torch.distributed as dist
 
     from latest_exact_match_attention_b200.longctx import TorchComm, sharded_prefill
@@ -119,7 +143,8 @@ def _rank(rank, world, port, H, T, seg, q):
         sl = slice(rank * L, (rank + 1) * L)
         src, out = sharded_prefill(torch.from_numpy(qc[:, sl].view(np.int32).copy()),
                                    torch.from_numpy(kc[:, sl].view(np.int32).copy()),
-                                   torch.from_numpy(v[:, sl].copy()), TorchComm(), PlainOps(), seg)
+                                   torch.from_numpy(v[:, sl].copy()), TorchComm(),
+                                   PeerPlainOps() if peer_ops else PlainOps(), seg)
         q.put((rank, src.numpy(), out.numpy()))
     finally:
         dist.destroy_process_group()
@@ -131,13 +156,16 @@ def free_port():
         return s.getsockname()[1]
 
 
+@pytest.mark.parametrize("peer_ops", [False, True])
 @pytest.mark.parametrize("world", [2, 3])
-def test_two_gloo_ranks_match_one_pass(world):
+def test_two_gloo_ranks_match_one_pass(world, peer_ops):
+    # peer_ops: the ops can read peers' memory, but over gloo TorchComm.peer_values answers
+    # None on every rank (no collective is left unmatched) and the rows travel by all-to-all
     H, T, seg = 3, 2 * 6 * 64, 64
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
     port = free_port()
-    procs = [ctx.Process(target=_rank, args=(r, world, port, H, T, seg, q)) for r in range(world)]
+    procs = [ctx.Process(target=_rank, args=(r, world, port, H, T, seg, q, peer_ops)) for r in range(world)]
     for p in procs:
         p.start()
     got = dict()
@@ -155,3 +183,40 @@ def test_two_gloo_ranks_match_one_pass(world):
     assert np.array_equal(out, oracle.gather(ref, v))
     L = T // world
     assert (ref[:, L:] < L).any() and (ref[:, L:] >= 0).any()   # matches cross the boundary
+
+
+@pytest.mark.parametrize("world", [2, 3, 4])
+def test_peer_rows_with_thread_ranks(world):
+    """The peer path's host protocol: ranks as threads (ThreadComm hands every rank the others'
+    value addresses), the gather reading earlier shards' rows in place, the release barrier
+    after it; the concatenated result equals the oracle's single pass."""
+    from latest_exact_match_attention_b200.longctx import ThreadComm, _Board, sharded_prefill
+    H, T, seg = 3, world * 6 * 64, 64
+    qc, kc, v = inputs(H, T)
+    L = T // world
+    board = _Board(world)
+    res, errs = [None] * world, []
+    vs = [torch.from_numpy(v[:, r * L:(r + 1) * L].copy()) for r in range(world)]   # kept alive
+
+    def run(r):
+        try:
+            sl = slice(r * L, (r + 1) * L)
+            res[r] = sharded_prefill(torch.from_numpy(qc[:, sl].view(np.int32).copy()),
+                                     torch.from_numpy(kc[:, sl].view(np.int32).copy()), vs[r],
+                                     ThreadComm(board, r), PeerPlainOps(), seg)
+        except BaseException as e:  # noqa: BLE001 -- re-raised below
+            errs.append(e)
+            board.barrier.abort()
+
+    threads = [threading.Thread(target=run, args=(r,)) for r in range(world)]
+    for t in threads:
+        t.start()
+    for t in threads:
+        t.join(timeout=120)
+    assert not errs, errs
+    src = np.concatenate([res[r][0].numpy() for r in range(world)], 1)
+    out = np.concatenate([res[r][1].numpy() for r in range(world)], 1)
+    ref = oracle.latest_prev_match(qc, kc)
+    assert np.array_equal(src, ref)
+    assert np.array_equal(out, oracle.gather(ref, v))
+    assert (ref[:, L:] < L).any() and (ref[:, L:] >= 0).any()
