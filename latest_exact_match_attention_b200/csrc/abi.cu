@@ -6,6 +6,7 @@
 #include <cstdlib>
 #include <cstdio>
 #include <mutex>
+#include <vector>
 
 #include "common.cuh"
 #include "match.cuh"
@@ -66,6 +67,52 @@ unsigned long long wait_limit_ns() {
 bool pdl_enabled() {
   const char* e = std::getenv("LEMA_PDL");
   return e == nullptr || e[0] != '0';
+}
+
+int kernel_facts(const void* kernel, size_t smem, int threads, int cluster, int* out) {
+  int dev = -1;
+  LEMA_CUDA_TRY(cudaGetDevice(&dev));
+  struct Fact {
+    const void* kernel;
+    int dev;
+    size_t smem;
+    int threads, cluster, value;
+  };
+  static std::mutex mu;
+  static std::vector<Fact> memo;
+  {
+    std::lock_guard<std::mutex> g(mu);
+    for (const Fact& f : memo) {
+      if (f.kernel == kernel && f.dev == dev && f.smem == smem && f.threads == threads && f.cluster == cluster) {
+        if (out != nullptr) *out = f.value;
+        return LEMA_OK;
+      }
+    }
+  }
+  LEMA_CUDA_TRY(cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem)));
+  int value = 0;
+  if (cluster > 0) {
+    cudaLaunchConfig_t cfg{};
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeClusterDimension;
+    attr[0].val.clusterDim.x = static_cast<unsigned>(cluster);
+    attr[0].val.clusterDim.y = 1;
+    attr[0].val.clusterDim.z = 1;
+    cfg.gridDim = dim3(static_cast<unsigned>(cluster), 1, 1);
+    cfg.blockDim = dim3(static_cast<unsigned>(threads), 1, 1);
+    cfg.dynamicSmemBytes = smem;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    LEMA_CUDA_TRY(cudaOccupancyMaxActiveClusters(&value, kernel, &cfg));
+  } else if (threads > 0) {
+    LEMA_CUDA_TRY(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&value, kernel, threads, smem));
+  }
+  {
+    std::lock_guard<std::mutex> g(mu);
+    memo.push_back(Fact{kernel, dev, smem, threads, cluster, value});
+  }
+  if (out != nullptr) *out = value;
+  return LEMA_OK;
 }
 
 const DeviceInfo* current_device_info() {

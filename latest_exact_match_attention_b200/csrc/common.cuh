@@ -96,6 +96,13 @@ const DeviceInfo* current_device_info();
 // LEMA_STATUS_PROBE_LIMIT and returns; it never traps.
 unsigned long long wait_limit_ns();
 
+// Propagates a LEMA_* status code (not a CUDA error) from a call of this library.
+#define LEMA_TRY(expr)                \
+  do {                                \
+    const int _rc = (expr);           \
+    if (_rc != LEMA_OK) return _rc;   \
+  } while (0)
+
 #define LEMA_CUDA_TRY(expr)                                \
   do {                                                     \
     cudaError_t _e = (expr);                               \
@@ -136,6 +143,13 @@ __device__ __forceinline__ void griddep_wait() { asm volatile("griddepcontrol.wa
 __device__ __forceinline__ void griddep_launch() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
 
 bool pdl_enabled();
+
+// Launch facts of a kernel on the current device, worked out on the first call per (kernel,
+// device, dynamic shared memory, threads, cluster size) and remembered: the first call sets
+// the kernel's dynamic shared memory limit, then `out` (if not null) receives the resident
+// CTAs per SM (cluster == 0, threads > 0) or the resident clusters of `cluster` CTAs. A call
+// after the first costs a lookup instead of runtime queries (small launches are host-bound).
+int kernel_facts(const void* kernel, size_t smem, int threads, int cluster, int* out);
 
 template <typename... KArgs, typename... Args>
 cudaError_t launch_dependent(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem,

@@ -1375,9 +1375,8 @@ int run_pipe(const MatchLaunch& a, const Plan& pl, const DeviceInfo& dev, Params
   LEMA_CUDA_TRY(cudaMemsetAsync(ws + pl.off_ctl, 0, pl.ctl_bytes, a.stream));
   auto kern = match_kernel<CodeT, true, true>;
   const size_t sm = smem_bytes<CodeT>(true);
-  LEMA_CUDA_TRY(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(sm)));
   int per_sm = 0;
-  LEMA_CUDA_TRY(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kern, kThreads, sm));
+  LEMA_TRY(kernel_facts(reinterpret_cast<const void*>(kern), sm, kThreads, 0, &per_sm));
   per_sm = std::max(per_sm, 1);
   p.match_sms = match_sms(a.N, per_sm, dev.sms);
   p.wave = p.match_sms * static_cast<uint32_t>(per_sm);
@@ -1389,7 +1388,7 @@ int run_pipe(const MatchLaunch& a, const Plan& pl, const DeviceInfo& dev, Params
     p.gather_inline = 1;
     auto gk = match_kernel<CodeT, false>;
     const size_t gsm = smem_bytes<CodeT>(false);
-    LEMA_CUDA_TRY(cudaFuncSetAttribute(gk, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(gsm)));
+    LEMA_TRY(kernel_facts(reinterpret_cast<const void*>(gk), gsm, 0, 0, nullptr));
     LEMA_CUDA_TRY(launch_dependent(gk, dim3(static_cast<unsigned>(pl.n_gtables)), dim3(kThreads), gsm, a.stream, p));
   }
   return LEMA_OK;
@@ -1410,9 +1409,8 @@ template <typename CodeT>
 int run_sweep(const MatchLaunch& a, const Plan& pl, const DeviceInfo& dev, Params p) {
   auto kern = sweep_kernel<CodeT>;
   const size_t sm = SweepLayout<CodeT>::kBytes;
-  LEMA_CUDA_TRY(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(sm)));
   int per_sm = 0;
-  LEMA_CUDA_TRY(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kern, kSwThreads, sm));
+  LEMA_TRY(kernel_facts(reinterpret_cast<const void*>(kern), sm, kSwThreads, 0, &per_sm));
   const int64_t grid = std::min<int64_t>(a.N, static_cast<int64_t>(std::max(per_sm, 1)) * dev.sms);
   kern<<<static_cast<unsigned>(grid), kSwThreads, sm, a.stream>>>(p);
   LEMA_CUDA_TRY(cudaGetLastError());
@@ -1422,7 +1420,7 @@ int run_sweep(const MatchLaunch& a, const Plan& pl, const DeviceInfo& dev, Param
     p.gather_inline = 0;
     auto gk = match_kernel<CodeT, false>;
     const size_t gsm = smem_bytes<CodeT>(false);
-    LEMA_CUDA_TRY(cudaFuncSetAttribute(gk, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(gsm)));
+    LEMA_TRY(kernel_facts(reinterpret_cast<const void*>(gk), gsm, 0, 0, nullptr));
     LEMA_CUDA_TRY(launch_dependent(gk, dim3(static_cast<unsigned>(pl.n_gtables)), dim3(kThreads), gsm, a.stream, p));
   }
   if (a.out != nullptr) return run_gather(a, p.src);
@@ -1481,7 +1479,6 @@ int run(const MatchLaunch& a, const Plan& pl, const DeviceInfo& dev) {
   if (segs > 1) {
     auto kern = match_kernel<CodeT, true, false, true>;
     const size_t sm = smem_bytes<CodeT>(true);
-    LEMA_CUDA_TRY(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(sm)));
     cudaLaunchConfig_t cfg{};
     cudaLaunchAttribute attr[1];
     attr[0].id = cudaLaunchAttributeClusterDimension;
@@ -1495,7 +1492,7 @@ int run(const MatchLaunch& a, const Plan& pl, const DeviceInfo& dev) {
     cfg.numAttrs = 1;
     cfg.gridDim = dim3(static_cast<unsigned>(a.N * segs), 1, 1);
     int clusters = 0;
-    LEMA_CUDA_TRY(cudaOccupancyMaxActiveClusters(&clusters, kern, &cfg));
+    LEMA_TRY(kernel_facts(reinterpret_cast<const void*>(kern), sm, kThreads, segs, &clusters));
     if (clusters >= 1) {  // else: one CTA per stream
       cfg.gridDim = dim3(static_cast<unsigned>(std::min<int64_t>(a.N, clusters) * segs), 1, 1);
       LEMA_CUDA_TRY(cudaLaunchKernelEx(&cfg, kern, p));
@@ -1505,9 +1502,8 @@ int run(const MatchLaunch& a, const Plan& pl, const DeviceInfo& dev) {
   if (pl.fast && !seg_done) {
     auto kern = match_kernel<CodeT, true>;
     const size_t sm = smem_bytes<CodeT>(true);
-    LEMA_CUDA_TRY(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(sm)));
     int per_sm = 0;
-    LEMA_CUDA_TRY(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kern, kThreads, sm));
+    LEMA_TRY(kernel_facts(reinterpret_cast<const void*>(kern), sm, kThreads, 0, &per_sm));
     const int64_t grid = std::min<int64_t>(a.N, static_cast<int64_t>(std::max(per_sm, 1)) * dev.sms);
     kern<<<static_cast<unsigned>(grid), kThreads, sm, a.stream>>>(p);
     LEMA_CUDA_TRY(cudaGetLastError());
@@ -1516,7 +1512,7 @@ int run(const MatchLaunch& a, const Plan& pl, const DeviceInfo& dev) {
     p.list_mode = pl.list_mode ? 1 : 0;
     auto kern = match_kernel<CodeT, false>;
     const size_t sm = smem_bytes<CodeT>(false);
-    LEMA_CUDA_TRY(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(sm)));
+    LEMA_TRY(kernel_facts(reinterpret_cast<const void*>(kern), sm, 0, 0, nullptr));
     LEMA_CUDA_TRY(launch_dependent(kern, dim3(static_cast<unsigned>(pl.n_gtables)), dim3(kThreads), sm, a.stream, p));
   }
   if (a.out != nullptr) return run_gather(a, p.src);

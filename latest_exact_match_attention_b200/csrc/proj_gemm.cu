@@ -476,8 +476,7 @@ bool encode_kmajor(EncodeTiledFn enc, CUtensorMap* map, const void* base, int64_
 
 template <int BN>
 int launch(const CUtensorMap& map_x, const CUtensorMap& map_w, const Params& prm, int64_t grid, cudaStream_t stream) {
-  LEMA_CUDA_TRY(cudaFuncSetAttribute(proj_codes_kernel<BN>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                     static_cast<int>(Tile<BN>::kSmemBytes)));
+  LEMA_TRY(kernel_facts(reinterpret_cast<const void*>(proj_codes_kernel<BN>), Tile<BN>::kSmemBytes, 0, 0, nullptr));
   LEMA_CUDA_TRY(launch_dependent(proj_codes_kernel<BN>, dim3(static_cast<unsigned>(grid)), dim3(kThreads),
                                  Tile<BN>::kSmemBytes, stream, map_x, map_w, prm));
   return LEMA_OK;
