@@ -257,9 +257,13 @@ def run_b200(args):
 
     ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
           for _ in range(args.steps)]
-    barrier()
-    torch.cuda.synchronize()
     with ClockSampler(local) as clk:
+        # the sampler's start-up pause leaves the GPU idle: warm it up again, untimed, right
+        # before the barrier and synchronisation that open the timed region
+        for _ in range(max(3, args.warmup)):
+            step()
+        barrier()
+        torch.cuda.synchronize()
         t0 = torch.cuda.Event(enable_timing=True)
         t1 = torch.cuda.Event(enable_timing=True)
         t0.record(stream)
@@ -632,12 +636,12 @@ def decode_record(args, rank: int, world: int, dev, small: bool = False, worst_l
     cache.check()
     counts = cache.counts().float()            # [depth, batch, heads]
     d = decoder(model, cache, tok=idx[:, prefix:prefix + 1])
-    for _ in range(warm):
-        d.step()
-    torch.cuda.synchronize()
-    if world > 1:
-        torch.distributed.barrier()
     with ClockSampler(dev.index) as clk:
+        for _ in range(warm):            # after the sampler's start-up pause, untimed
+            d.step()
+        torch.cuda.synchronize()
+        if world > 1:
+            torch.distributed.barrier()
         a.record(stream)
         for _ in range(steps):
             d.step()
