@@ -425,10 +425,10 @@ def run_match(args):
         def step():
             call("lema_prefill_match", ptr(q), ptr(k), 4, n, T, ptr(src), None, 0, None, ptr(ws), nb,
                  ptr(st), stream.cuda_stream)
-        for _ in range(max(3, args.warmup)):
-            step()
-        torch.cuda.synchronize()
         with ClockSampler(dev.index) as clk:
+            for _ in range(max(3, args.warmup)):     # after the sampler's start-up pause
+                step()
+            torch.cuda.synchronize()
             a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
             a.record(stream)
             for _ in range(args.steps):
