@@ -19,8 +19,9 @@
 // by a multiply-high (Lemire's range reduction), so the capacity is any slot count.
 //
 // Exchange on the GPU:
-//   T == 1 (decode step): every item is its own partition; one thread per item looks up and
-//           then inserts. No ordering between items is needed.
+//   T == 1 (decode step): every item is its own partition; a group of lanes per item (below)
+//           walks its lookup and its insert probes, interleaved round trip by round trip. No
+//           ordering between items is needed.
 //   T > 1 (prefill chunk): the order inside a partition only matters between equal codes, so
 //           the call is decomposed exactly:
 //             (1) the matcher (K2) finds each query's latest earlier key INSIDE the chunk and
