@@ -160,19 +160,54 @@ struct ResolveTablesParams {
   int32_t* src;
 };
 
-__global__ void resolve_tables_kernel(const ResolveTablesParams p) {
-  const int64_t total = p.n_heads * p.L;
-  for (int64_t i = blockIdx.x * int64_t(blockDim.x) + threadIdx.x; i < total; i += int64_t(gridDim.x) * blockDim.x) {
-    if (p.src[i] >= 0) continue;
-    const int64_t h = i / p.L;
-    const uint32_t q = p.qc[i];
-    int32_t r = -1;
-    for (int t = p.n_tables - 1; t >= 0 && r < 0; --t) {
-      const int64_t sl = p.slots[t];
-      r = lt_find(p.tables[t] + h * sl, static_cast<uint32_t>(sl - 1), q);
-    }
-    p.src[i] = r;
+__device__ __forceinline__ void resolve_one(const ResolveTablesParams& p, int64_t i) {
+  const int64_t h = i / p.L;
+  const uint32_t q = p.qc[i];
+  int32_t r = -1;
+  for (int t = p.n_tables - 1; t >= 0 && r < 0; --t) {
+    const int64_t sl = p.slots[t];
+    r = lt_find(p.tables[t] + h * sl, static_cast<uint32_t>(sl - 1), q);
   }
+  p.src[i] = r;
+}
+
+// Only a few positions in a hundred are still unmatched, so instead of one thread per
+// position (each waiting on its index load, then on a rare dependent probe chain), every warp
+// scans 4 x 32 positions per round (four coalesced loads in flight), queues the unmatched ones
+// in shared memory, and probes them 32 at a time, one per lane: the probes of a warp are
+// independent and in flight together.
+constexpr int kResolveThreads = 256;
+__global__ void __launch_bounds__(kResolveThreads) resolve_tables_kernel(const ResolveTablesParams p) {
+  constexpr int kWarps = kResolveThreads / 32, kLoads = 4;
+  __shared__ int64_t queue[kWarps][64];
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  const int64_t total = p.n_heads * p.L;
+  const uint32_t below = (1u << lane) - 1u;
+  int n = 0;  // queued, the same in every lane
+  const int64_t stride = int64_t(gridDim.x) * kWarps * 32 * kLoads;
+  for (int64_t base = (int64_t(blockIdx.x) * kWarps + warp) * 32 * kLoads; base < total; base += stride) {
+    int32_t sv[kLoads];
+#pragma unroll
+    for (int u = 0; u < kLoads; ++u) {
+      const int64_t i = base + u * 32 + lane;
+      sv[u] = i < total ? __ldcs(p.src + i) : 0;
+    }
+#pragma unroll
+    for (int u = 0; u < kLoads; ++u) {
+      const int64_t i = base + u * 32 + lane;
+      const bool miss = i < total && sv[u] < 0;
+      const uint32_t m = __ballot_sync(0xFFFFFFFFu, miss);
+      if (miss) queue[warp][n + __popc(m & below)] = i;
+      n += __popc(m);
+      __syncwarp();
+      if (n >= 32) {  // 32 probes at once; the rest (< 32) stay queued
+        n -= 32;
+        resolve_one(p, queue[warp][n + lane]);
+        __syncwarp();
+      }
+    }
+  }
+  if (lane < n) resolve_one(p, queue[warp][lane]);
 }
 
 // A head swept as vrows rows (sub-shards) of L positions: queries of row r (v = r % vrows)
@@ -533,7 +568,8 @@ extern "C" int lema_lt_resolve_tables(const uint64_t* const* tables, const int64
   const DeviceInfo* dev = k5::sm100();
   if (dev == nullptr) return LEMA_ERR_UNSUPPORTED;
   k5::ResolveTablesParams p{tables, slots, n_tables, n_heads, L, qcodes, src};
-  k5::resolve_tables_kernel<<<k5::grid_for(n_heads * L, 256, *dev), 256, 0, static_cast<cudaStream_t>(stream)>>>(p);
+  k5::resolve_tables_kernel<<<k5::grid_for((n_heads * L + 3) / 4, k5::kResolveThreads, *dev), k5::kResolveThreads, 0,
+                              static_cast<cudaStream_t>(stream)>>>(p);
   LEMA_CUDA_TRY(cudaGetLastError());
   return LEMA_OK;
 }
