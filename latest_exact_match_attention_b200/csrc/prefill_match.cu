@@ -376,7 +376,10 @@ __device__ __forceinline__ unsigned long long global_ns() {
 
 // Rows [t0, t1) of stream n by the kThr threads of a CTA, kGUnroll loads in flight per thread.
 // The indices come through L2 (__ldcg): other CTAs of the same launch may have written them.
-constexpr int kGUnroll = 4;   // loads in flight per thread (measured: 8 -> 4 took the call 0.428 -> 0.384 ms)
+// loads in flight per thread in the gather kernel (the two-kernel path: calls below one wave of
+// matchers). Measured on config 2's streams with the current matcher: 2 / 4 / 8 give 0.1039 /
+// 0.1068 / 0.1135 ms per call at 128 streams and 0.1657 / 0.1697 / 0.1826 at 256
+constexpr int kGUnroll = 2;
 template <typename Vec, int kThr>
 __device__ __forceinline__ void gather_span(const GatherParams& g, int64_t n, uint32_t t0, uint32_t t1,
                                             int tid) {
