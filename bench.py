@@ -822,9 +822,10 @@ def run_longctx(args):
         "dtype": "u32", "data": "synthetic (device-generated, chunk-seeded)",
         "config": {"workload": f"cfg5: T={T} H={H} 32-bit codes pool 2^20 Zipf 1.05 5% fresh, d_v 64 bf16",
                    "positions_per_gpu": n // world, "seg_len": args.seg_len, "hit_rate": round(hit, 4),
-                   "parallelism": f"sequence x{world}, NCCL all-gather + " + (
+                   "parallelism": "one GPU, no collective" if world == 1 else
+                   f"sequence x{world}, NCCL all-gather + " + (
                        "all-to-all of rows" if "row_all_to_all" in phases else
-                       "rows read from peer GPUs' memory (CUDA IPC, NVLink)" if world > 1 else "none")},
+                       "rows read from peer GPUs' memory (CUDA IPC, NVLink)")},
         "parity_check": check,
         "phases_ms_rank0": {k: round(x, 3) for k, x in phases.items()},
         "phases_ms_max_over_ranks": {k: round(x, 3) for k, x in pmax.items()},

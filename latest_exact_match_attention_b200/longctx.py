@@ -23,7 +23,8 @@ Per rank (kernels in csrc/shard.cu, K2 in csrc/prefill_match.cu):
 Where every rank can map every other rank's values (one node: CUDA IPC over NVLink; ranks as
 threads of one process: the same memory), steps 5 and 6 are one kernel instead: the gather
 reads an earlier shard's row where it lies, with plain loads of the peer GPU's memory, and a
-collective after it keeps every rank's values in place until the last read.
+collective after it keeps every rank's values in place until the last read. A single rank
+takes that kernel too: all its sources are its own, so there are no requests to build.
 
 Only steps 3 and 5 talk to other ranks, and nothing waits for another rank before step 3.
 The collectives go through a `Comm`: `TorchComm` (torch.distributed: NCCL on the GPU, gloo
@@ -335,9 +336,12 @@ def sharded_prefill(qc: torch.Tensor, kc: torch.Tensor, v: torch.Tensor, comm=No
     base = comm.rank * L
     # the same decision on every rank: same comm and ops types and environment, then a
     # collective answer; LEMA_SHARD_PEER=0 keeps the request + all-to-all path (same results)
-    peers = (comm.peer_values(v) if comm.world > 1 and hasattr(ops, "gather_peer")
-             and hasattr(comm, "peer_values") and os.environ.get("LEMA_SHARD_PEER", "1")[:1] != "0"
-             else None)
+    peers = None
+    if hasattr(ops, "gather_peer") and os.environ.get("LEMA_SHARD_PEER", "1")[:1] != "0":
+        if comm.world == 1:
+            peers = [v.data_ptr()]      # one rank: every source is its own (no requests to build)
+        elif hasattr(comm, "peer_values"):
+            peers = comm.peer_values(v)
 
     # 1-2: local work, no rank waits for another
     src, ltc, ltp, ltn = ops.segment_match(qc, kc, seg_len)
@@ -357,8 +361,9 @@ def sharded_prefill(qc: torch.Tensor, kc: torch.Tensor, v: torch.Tensor, comm=No
         # 5-6: rows of earlier shards read in place (peer memory), own rows, zeros
         out = ops.gather_peer(src, base, v, peers)
         _mark(marks, "gather")
-        comm.after_peer_reads(src.device)
-        _mark(marks, "release")
+        if comm.world > 1:
+            comm.after_peer_reads(src.device)
+            _mark(marks, "release")
         ops.check()
         return src, out
 
